@@ -1,0 +1,380 @@
+#!/usr/bin/env python3
+"""Benchmark of the BFP SmolLM2-135M greedy decode path on B200.
+
+Metric: BFP decode tok/s at bs1 and bs256, with the fraction
+of the HBM roofline.  One JSON line on rank 0.
+
+Workload (config.workload): configs[1] = "cfg2": synthetic SmolLM2-135M
+(seeded random weights, BFP fixed points, packed like the reference), a
+48-token prompt, 256 greedy tokens, KV up to 304 positions, batch 1.  A step
+is one full generate call (prefill + 256 decode steps).  ``value`` =
+generated tokens/s over all ranks (each rank decodes its own replica: bs1
+does not shard, so N GPUs run N independent streams -- weak scaling).
+The same line carries ``bs256``: configs[2] = "cfg3", 256 ragged sequences
+x 128 tokens, sequences split over the ranks with no collectives.
+
+``--impl reference`` times the reference algorithm on the host cores (the
+numpy restatement under oracle/, since the reference is Python that cannot
+be installed on the GPU box) with the same metric and unit.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "tinyllm-fpga_b200"))
+
+import numpy as np  # noqa: E402
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# algorithmic bytes (packed BFP: 2 B mantissa + 1/16 B exponent per element)
+# ---------------------------------------------------------------------------
+def weight_bytes_per_token(cfg):
+    kvd = cfg.H_KV * cfg.HD
+    per_layer = 0
+    for dout, din in ((cfg.D, cfg.D), (kvd, cfg.D), (kvd, cfg.D), (cfg.D, cfg.D), (cfg.FFN, cfg.D),
+                      (cfg.FFN, cfg.D), (cfg.D, cfg.FFN)):
+        per_layer += dout * din * 2 + dout * din // 16
+    head = cfg.VOCAB * cfg.D * 2 + cfg.VOCAB * cfg.D // 16
+    return cfg.NL * per_layer, head
+
+
+def kv_bytes_per_position(cfg):
+    return cfg.NL * 2 * cfg.H_KV * cfg.HD * 2 + cfg.NL * 2 * cfg.H_KV * cfg.HD // 16   # 23,760 B
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.3)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, nm in enumerate(names):
+                if len(r) > 5 + i and r[5 + i].lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------------------
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    from bfp200 import BfpConfig, Decoder, synth, _lib
+
+    pk, pk_kind = peaks()
+    cfg2 = BfpConfig(MAX_CTX=48 + 256, max_seqs=256)
+    t0 = time.time()
+    img = synth.synthetic_image(BfpConfig(), seed=0)
+    build_s = time.time() - t0
+    dec = Decoder(cfg2, device=local)
+    dec.load_image(img)
+    del img
+    prompts2, ngen2 = synth.config_prompts(2)
+    prompts3, ngen3 = synth.config_prompts(3)
+    lo, hi = rank * len(prompts3) // world, (rank + 1) * len(prompts3) // world
+    part3 = prompts3[lo:hi]
+
+    # ---- cfg2 (bs1): device time of each generate (events on the library's stream)
+    for _ in range(args.warmup):
+        dec.generate(prompts2, ngen2)
+    barrier(world)
+    with ClockSampler(local) as clk:
+        dev_ms = []
+        for _ in range(args.steps):
+            dec.generate(prompts2, ngen2)
+            t = dec.last_timing()
+            dev_ms.append(t["prefill_ms"] + t["decode_ms"])
+        # e2e through the public API: host prompt ids in, host tokens out,
+        # H2D/D2H inside the timed region (synchronous call, host clock)
+        e2e_s = []
+        for _ in range(max(1, args.steps // 2)):
+            ts = time.perf_counter()
+            out = dec.generate(prompts2, ngen2)
+            e2e_s.append(time.perf_counter() - ts)
+    barrier(world)
+    uncert = dec.uncertified_steps()
+    step_ms = max_over_ranks(statistics.mean(dev_ms), world)
+    e2e_step_s = max_over_ranks(statistics.mean(e2e_s), world)
+    tokens_per_step = ngen2 * world
+    value = tokens_per_step / (step_ms / 1e3)
+    e2e = tokens_per_step / e2e_step_s
+    last = dec.last_timing()
+    decode_tok_ms = last["decode_ms"] / ngen2
+
+    # ---- roofline of the dominant kernel: the BFP matmul.  Its device time
+    # for one token's 120 launches (4 per layer) is measured with events on
+    # the library stream by replaying the decode-step matmuls.
+    wbytes, hbytes = weight_bytes_per_token(cfg2)
+    mm = matmul_timing(dec, ncols=1, reps=50)
+    achieved_gbs = wbytes / (mm["ms_per_token"] / 1e3) / 1e9
+    peak = pk["hbm_gbs"]
+    roof = {"kernel": "bfp_matmul_kernel (QKV/O/GU/D, bs1)", "bound": "hbm", "achieved": round(achieved_gbs, 1),
+            "peak": peak, "unit": "GB/s", "frac": round(achieved_gbs / peak, 4), "traffic": None,
+            "peak_kind": pk_kind, "launches_per_token": mm["launches"],
+            "us_per_launch": round(mm["ms_per_token"] * 1e3 / mm["launches"], 3)}
+    # whole-path roofline: weights + KV per token over the decode time
+    mean_pos = 48 + ngen2 / 2
+    path_bytes = wbytes + hbytes + kv_bytes_per_position(cfg2) * (mean_pos + 1)
+    path_frac = path_bytes / (decode_tok_ms / 1e3) / 1e9 / peak
+
+    # ---- bs256 (cfg3), sequences split over ranks
+    for _ in range(max(1, args.warmup // 3)):
+        dec.generate(part3, ngen3)
+    barrier(world)
+    b_ms = []
+    for _ in range(max(1, args.steps // 4)):
+        dec.generate(part3, ngen3)
+        t = dec.last_timing()
+        b_ms.append(t["prefill_ms"] + t["decode_ms"])
+    barrier(world)
+    b_step = max_over_ranks(statistics.mean(b_ms), world)
+    bs256 = {"value": round(len(prompts3) * ngen3 / (b_step / 1e3), 1), "unit": "tok/s",
+             "ms_per_step": round(b_step, 3), "sequences": len(prompts3), "n_gen": ngen3,
+             "scaling": "strong", "uncertified_steps": dec.uncertified_steps()}
+
+    launches = launches_per_generate(cfg2, 1, 48, ngen2)
+    res = {
+        "metric": "BFP decode tok/s (bs1, cfg2)", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int16-BFP/int64/f64", "data": "synthetic",
+        "config": {"workload": "cfg2: 48-token prompt + 256 greedy tokens, bs1, KV<=304",
+                   "model": "SmolLM2-135M arch, seeded random BFP weights", "global_batch": world,
+                   "seq_len": 48 + 256, "parallelism": f"replicas{world}",
+                   "l2": "inputs larger than L2 (277 MB of weights streamed per token)"},
+        "decode_us_per_token": round(decode_tok_ms * 1e3, 2),
+        "prefill_ms": round(last["prefill_ms"], 3),
+        "path_roofline_frac": round(path_frac, 4),
+        "roofline": roof,
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 48 * 4 + 4,
+                "d2h_bytes_per_step": (48 + ngen2) * 4 + 8},
+        "gpu_launches": launches * args.steps,
+        "bs256": bs256,
+        "uncertified_steps": uncert,
+        "image_build_s": round(build_s, 1),
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        res["cpu_baseline"] = cpu_baseline(args)
+    dec.close()
+    return res
+
+
+def launches_per_generate(cfg, n_seq, plen, n_gen):
+    per_fwd = 1 + cfg.NL * 8              # embed + 8 kernels per layer
+    prefill = per_fwd                     # one chunk (sim feed: no head)
+    decode = n_gen * (per_fwd + 3 + 1)    # + head (prep, logits, reduce) + advance
+    return prefill + decode
+
+
+def matmul_timing(dec, ncols, reps):
+    import ctypes as C
+    from bfp200 import _lib
+    L = _lib.lib()
+    ms = C.c_double()
+    n = C.c_int()
+    _lib.check(L.bfp200_time_matmuls(dec.handle, ncols, reps, C.byref(ms), C.byref(n)))
+    return {"ms_per_token": ms.value, "launches": n.value}
+
+
+def cpu_baseline(args):
+    """The oracle port (numpy restatement of the reference simulator) on the
+    host: steady-state decode of the cfg2 stream at its mean context (KV
+    length 176), 1 stream.  Sample: 6 decode steps."""
+    sys.path.insert(0, REPO)
+    from oracle import bfp_oracle as O
+    from oracle import synth as OS
+    model = OS.make_model(0)
+    model.cache_float_weights()
+    cfg = O.Cfg()
+    kv = O.new_kv(cfg, 304)
+    rng = np.random.default_rng(0)
+    for li in range(cfg.NL):       # a KV cache of 176 positions (values do not change the cost)
+        kv[li]["k"][:176] = O.fp_quantize_vec(rng.standard_normal(176 * 192)).reshape(176, 3, 64)
+        kv[li]["v"][:176] = O.fp_quantize_vec(rng.standard_normal(176 * 192)).reshape(176, 3, 64)
+    n = 6
+    t = time.perf_counter()
+    tok = 123
+    for s in range(n):
+        pos = 176 + s
+        h = model.embed_q(tok)
+        cs = O.rope_cos_sin(pos)
+        for li in range(cfg.NL):
+            h = O.fwd_layer(h, model.layers[li], pos, kv[li], pos, cfg, cs=cs)
+        tok = int(np.argmax(O.head_logits(h, model.norm_w_q, model.embed)))
+    dt = time.perf_counter() - t
+    return {"value": round(n / dt, 4), "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": f"{n} decode steps of one cfg2 stream at KV length 176..{176 + n - 1}, numpy oracle, 1 process"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference algorithm (oracle port) on host cores."""
+    if rank != 0:
+        return None
+    sys.path.insert(0, REPO)
+    from oracle import bfp_oracle as O
+    from oracle import synth as OS
+    model = OS.make_model(0)
+    model.cache_float_weights()
+    cfg = O.Cfg()
+    prompt = OS.config_prompts(2)[0][0]
+    kv = O.new_kv(cfg, 304)
+    # prefill the 48-token prompt once (untimed), then time decode steps
+    h = None
+    for pos, tid in enumerate(prompt):
+        h = model.embed_q(tid)
+        cs = O.rope_cos_sin(pos)
+        for li in range(cfg.NL):
+            h = O.fwd_layer(h, model.layers[li], pos, kv[li], pos, cfg, cs=cs)
+    tok, pos = prompt[-1], len(prompt)
+    per_step = 2
+    times = []
+    for it in range(args.warmup + args.steps):
+        t = time.perf_counter()
+        for _ in range(per_step):
+            h = model.embed_q(tok)
+            cs = O.rope_cos_sin(pos)
+            for li in range(cfg.NL):
+                h = O.fwd_layer(h, model.layers[li], pos, kv[li], pos, cfg, cs=cs)
+            tok = int(np.argmax(O.head_logits(h, model.norm_w_q, model.embed)))
+            pos += 1
+            if pos >= 304:
+                kv = O.new_kv(cfg, 304)
+                pos = 0
+        if it >= args.warmup:
+            times.append(time.perf_counter() - t)
+    step_s = statistics.mean(times)
+    v = per_step / step_s
+    return {"impl": "reference", "metric": "BFP decode tok/s (bs1, cfg2)", "value": round(v, 4), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64/f64",
+            "data": "synthetic",
+            "config": {"workload": "cfg2: 48-token prompt + greedy decode, bs1, KV<=304",
+                       "model": "SmolLM2-135M arch, seeded random BFP weights", "global_batch": 1, "seq_len": 304,
+                       "parallelism": "host"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": 1, "kind": "port",
+                             "sample": f"{per_step} decode steps per timed step of the cfg2 stream "
+                                       "(numpy restatement of the reference simulator)"},
+            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        res = run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    world, rank, local = dist_init()
+    res = run_ours(args, world, rank, local)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

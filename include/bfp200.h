@@ -1,0 +1,163 @@
+/* bfp200.h -- C ABI of libbfp200.so, the B200 (sm_100a) implementation of the
+ * block-floating-point (BFP) SmolLM2-135M greedy decode path of
+ * jrrk2/tinyllm-fpga.
+ *
+ * The reference has no FFI on this path: its surfaces are the Python module
+ * rtl/vc707/host/gen_smollm_blockfp_full.py (packer + bit-exact simulator)
+ * and the files the packers write (<PREFIX>DDR3.bin, <PREFIX>*_m/_e.hex,
+ * <PREFIX>PROMPT.hex) that rtl/vc707/host/bfp_client.cpp uploads.  Each entry
+ * point below names the reference interface it replaces.
+ *
+ * Conventions: every function returns 0 on success or a negative BFP200_E*
+ * code; bfp200_last_error() gives the message of the calling thread's last
+ * failure.  All pointers are HOST pointers unless a name ends in _dev.  A
+ * handle owns one CUDA device, one stream and all device memory it needs;
+ * one call may be in flight per handle, handles on different devices (or
+ * threads) are independent.  Nothing here falls back to the CPU: without a
+ * usable sm_100 device bfp200_open fails with BFP200_ENODEV.
+ */
+#ifndef BFP200_H
+#define BFP200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  BFP200_OK = 0,
+  BFP200_EINVAL = -1,    /* bad argument (shape, length, range) */
+  BFP200_ENODEV = -2,    /* no usable CUDA device */
+  BFP200_ECUDA = -3,     /* CUDA runtime error */
+  BFP200_EIMAGE = -4,    /* image / ROM content does not match the config */
+  BFP200_ESTATE = -5,    /* call order (e.g. generate before load_image) */
+  BFP200_ETIMEOUT = -6,  /* a bounded device-side wait gave up */
+  BFP200_ENOMEM = -7,    /* device allocation failed */
+};
+
+/* Model / run configuration.  Field names follow the reference's environment
+ * variables (gen_smollm_blockfp_full.py:53-64, gen_smollm_blockfp_cfg.py:44). */
+typedef struct bfp200_cfg {
+  int D;            /* model width (576) */
+  int H_Q;          /* query heads (9) */
+  int H_KV;         /* key/value heads (3) */
+  int HD;           /* head dim (64; the only supported value) */
+  int FFN;          /* MLP width (1536) */
+  int NL;           /* layers (30) */
+  int VOCAB;        /* vocabulary rows in the image (49152, multiple of 16) */
+  int MAX_CTX;      /* KV positions per sequence (<= 3072) */
+  int NPROMPT_MAX;  /* longest prompt accepted (48) */
+  int max_seqs;     /* sequences one generate call may carry */
+  double rope_base; /* 10000.0: the simulator's rope_fp default (:250) */
+  double eps;       /* 1e-5 (:236, :438) */
+} bfp200_cfg;
+
+typedef struct bfp200_handle bfp200_handle;
+
+/* Fills *cfg with the SmolLM2-135M defaults of the reference. */
+void bfp200_default_cfg(bfp200_cfg* cfg);
+
+/* Text of the calling thread's last error. */
+int bfp200_last_error(char* buf, size_t len);
+
+/* Replaces: the reference's process-level setup (module import, :53-85). */
+int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out);
+int bfp200_close(bfp200_handle* h);
+
+/* Replaces: `bfp_client upload <DDR3.bin>` (bfp_client.cpp:1696-1701) feeding
+ * the DDR3 image written by gen_smollm_blockfp_ddr.py:155-241 (region order
+ * and 4 KiB alignment of lbfp_ddr3.svh:45-86).  The buffer is only read
+ * during the call. */
+int bfp200_load_image(bfp200_handle* h, const void* ddr3_bin, size_t len);
+
+/* Replaces: `bfp_client load-roms` (bfp_client.cpp:1381-1437) -- same kind
+ * numbering: 0 G1_m, 1 G1_e, 2 G2_m, 3 G2_e, 4 NORM_W_m, 5 NORM_W_e,
+ * 6 PROMPT.  Entries are the 16-bit values of the .hex lines
+ * (parse_hex_file, :1162-1183); exponents use the low 8 bits. */
+int bfp200_load_rom(bfp200_handle* h, int kind, const uint16_t* entries, size_t n);
+
+/* Replaces: the golden driver loop of gen_smollm_blockfp_full.py:425-449
+ * (feed_mode 0 = "sim": prompt + n_gen ids, the argmax of the last prompt
+ * step is discarded and the last prompt token is fed again) or the RTL feed
+ * rule of autoregress_bfp_top.sv:358-384 (feed_mode 1 = "rtl": one argmax
+ * per step, len + n_gen ids).
+ *   prompt_ids   concatenated prompts (NULL: the ROM prompt, n_seq must be 1)
+ *   prompt_lens  n_seq lengths, 1..NPROMPT_MAX (NULL with prompt_ids NULL)
+ *   out_tokens   concatenated per-sequence outputs of len_i + n_gen ids
+ * Requires len_i + n_gen <= MAX_CTX. */
+int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq, int n_gen,
+                    int feed_mode, int32_t* out_tokens);
+
+/* Same as bfp200_generate, with the sequences split into contiguous blocks
+ * over n_dev handles (one per GPU), run concurrently with no collectives.
+ * Replaces: nothing in the reference (single FPGA, single stream). */
+int bfp200_generate_multi(bfp200_handle* const* hs, int n_dev, const int32_t* prompt_ids, const int32_t* prompt_lens,
+                          int n_seq, int n_gen, int feed_mode, int32_t* out_tokens);
+
+/* Number of head argmax decisions of the last generate call whose fp64
+ * margin did not certify agreement with every summation order (0 means the
+ * token stream is independent of the reference's BLAS). */
+int bfp200_uncertified_steps(bfp200_handle* h, long long* count);
+
+/* Device time of the last generate call's phases, in milliseconds. */
+int bfp200_last_timing(bfp200_handle* h, double* prefill_ms, double* decode_ms);
+
+/* Measurement: device time of one token's BFP matmuls (the 4 per layer of
+ * every layer, production epilogues, `ncols` columns), replayed `reps` times
+ * from a CUDA graph on the handle's stream between CUDA events.  Requires a
+ * loaded image.  Replaces nothing in the reference. */
+int bfp200_time_matmuls(bfp200_handle* h, int ncols, int reps, double* ms_per_token, int* launches_per_token);
+
+/* ---- op-level entry points (the reference's module functions) ---------- */
+
+/* tile_quantize (gen_smollm_blockfp_full.py:90-97): n doubles (n % 16 == 0)
+ * -> m[n] int16, e[n/16] int8. */
+int bfp200_tile_quantize(bfp200_handle* h, const double* v, size_t n, int16_t* m, int8_t* e);
+/* tile_decode (:100-102). */
+int bfp200_tile_decode(bfp200_handle* h, const int16_t* m, const int8_t* e, size_t n, double* v);
+
+/* matvec_hw_golden (:217-233) on `batch` independent columns.
+ *   x_m [batch][D_in], x_e [batch][D_in/16]; W_m [D_out][D_in/16][16],
+ *   W_e [D_out][D_in/16] (the reference's quantize_W layout);
+ *   out_m [batch][D_out], out_e [batch][D_out/16] = tile_quantize of the
+ *   result (decode gives the reference's fp_quantize_vec(out_real)). */
+int bfp200_matvec(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m, const int8_t* W_e,
+                  int D_out, int D_in, int batch, int16_t* out_m, int8_t* out_e);
+
+/* rmsnorm_fp (:236-238) on ncols vectors of n doubles. */
+int bfp200_rmsnorm_fp(bfp200_handle* h, const double* x, const double* gamma, int n, int ncols, double eps,
+                      double* out);
+/* silu_fp (:241-242), n % 16 == 0. */
+int bfp200_silu_fp(bfp200_handle* h, const double* x, size_t n, double* out);
+/* softmax_fp (:245-247) on ncols vectors of n doubles. */
+int bfp200_softmax_fp(bfp200_handle* h, const double* x, int n, int ncols, double* out);
+/* rope_fp (:250-258) on nvec vectors of HD doubles at positions pos[]. */
+int bfp200_rope_fp(bfp200_handle* h, const double* x, const int32_t* pos, int nvec, int HD, double base,
+                   double* out);
+/* The (cos, sin) pairs rope_fp evaluates (:253-254), [n_pos][HD/2][2],
+ * computed with the host libm exactly as Python's math module does. */
+int bfp200_rope_table(double* out, int n_pos, int HD, double base);
+
+/* One layer, fwd_layer (:261-293), for ncols independent columns using
+ * layer `layer` of the loaded image.  h_in/h_out are [ncols][D] doubles on
+ * the BFP grid.  k_cache/v_cache are the reference's per-layer float64
+ * caches [ncols][max_ctx][H_KV][HD]: positions < kv_pos[c] are read, slot
+ * kv_pos[c] is written back (fwd_layer mutates kv in place, :270-272).
+ * pos[c] is the RoPE position.  If stages is non-NULL it receives, per
+ * column, BFP200_NSTAGES vectors of D_stage doubles (see bfp200_stage_dims). */
+int bfp200_fwd_layer(bfp200_handle* h, int layer, const double* h_in, const int32_t* pos, const int32_t* kv_pos,
+                     int ncols, double* k_cache, double* v_cache, int max_ctx, double* h_out, double* stages);
+
+/* Stage dump layout of bfp200_fwd_layer (mirrors the N1..D dumps of
+ * gen_smollm_blockfp_bfp.py:393-426): n1 q k v attn o h1 n2 g u mlp d, where
+ * n1/n2/attn/mlp are the matvec inputs tile_quantize(.) decoded, q/k are
+ * post-RoPE and every other stage is the matvec output. */
+#define BFP200_NSTAGES 12
+int bfp200_stage_dims(bfp200_handle* h, int32_t* dims_out /* [BFP200_NSTAGES] */);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BFP200_H */

@@ -1,0 +1,121 @@
+"""GPU op-level parity: the kernels behind bfp200's C ABI against the golden
+fixtures and the oracle.  Bit-exact for integer and IEEE-exact stages;
+stages that call exp (silu_fp, softmax_fp) use CUDA's exp where the
+reference uses numpy's, so they are held to a stated tolerance."""
+import math
+
+import numpy as np
+import pytest
+
+import inputs
+from common import golden_path, manifest, sha
+from oracle import bfp_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from bfp200 import ops as _ops
+    return _ops
+
+
+def test_tile_quantize_golden(ops):
+    z = np.load(golden_path("quant.npz"))
+    m, e = ops.tile_quantize(z["v"])
+    assert np.array_equal(m, z["m"]) and np.array_equal(e, z["e"])
+    assert np.array_equal(ops.tile_decode(m, e), z["d"])
+
+
+def test_tile_quantize_random_and_thresholds(ops):
+    rng = np.random.default_rng(21)
+    v = np.concatenate([inputs.outlier_normal(rng, 16 * 4096),
+                        rng.standard_normal(16 * 4096) * np.exp2(rng.integers(-200, 200, size=16 * 4096))])
+    # doubles within 100 ulps below every power of two in the exponent range
+    p = np.ldexp(1.0, np.repeat(np.arange(-140, 140), 16))
+    k = np.tile(np.arange(16), 280) * 7
+    near = p * (1.0 - k * 2.0 ** -53)
+    v = np.concatenate([v, near, -near])
+    m, e = ops.tile_quantize(v)
+    mo, eo = O.tile_quantize(v)
+    assert np.array_equal(m, mo) and np.array_equal(e, eo)
+
+
+def _sweep_sha(Y):
+    ym, ye = O.tile_quantize(Y.reshape(-1))
+    return sha(ym, ye)
+
+
+@pytest.mark.parametrize("shape", inputs.SWEEP_SHAPES)
+def test_matvec_sweep(ops, shape):
+    """cfg4: every weight shape at batch 1..1024, bit-exact: against the
+    reference's own outputs (hash) where it was run, the oracle otherwise."""
+    D_out, D_in = shape
+    W_m, W_e = inputs.sweep_weights(D_out, D_in)
+    gold = manifest()["matvec_sha"]
+    for B in inputs.SWEEP_BATCHES:
+        X_m, X_e = inputs.sweep_x(D_in, B, D_out)
+        om, oe = ops.matvec(X_m, X_e, W_m, W_e)
+        Y = ops.tile_decode(om.reshape(-1), oe.reshape(-1)).reshape(B, D_out)
+        key = f"{D_out}x{D_in}_b{B}"
+        if key in gold:
+            assert _sweep_sha(Y) == gold[key], key
+        cols = np.arange(B) if D_out * B <= 64 * 1536 else np.linspace(0, B - 1, 6).astype(int)
+        ref = O.matvec_cols(X_m[cols], X_e[cols], W_m, W_e)
+        assert np.array_equal(Y[cols], ref), key
+
+
+@pytest.mark.parametrize("name", ["shift_mask", "saturate", "mixed", "zero_x"])
+def test_matvec_edges(ops, name):
+    z = np.load(golden_path(f"matvec_edge_{name}.npz"))
+    assert np.array_equal(ops.matvec_hw_golden(z["x_m"], z["x_e"], z["W_m"], z["W_e"]), z["y"])
+
+
+def test_rmsnorm_fp_exact(ops):
+    """cfg5-style activations (N(0,1), 1% x30): bit-exact (IEEE ops + numpy
+    pairwise mean reproduced)."""
+    rng = np.random.default_rng(5)
+    x = O.fp_quantize_vec(inputs.outlier_normal(rng, 64 * 576)).reshape(64, 576)
+    g = O.fp_quantize_vec(1.0 + 0.05 * rng.standard_normal(576))
+    got = ops.rmsnorm_fp(x, g)
+    want = np.stack([O.rmsnorm_fp(x[i], g) for i in range(64)])
+    assert np.array_equal(got, want)
+
+
+def test_rope_fp_exact(ops):
+    """RoPE at positions 0..2047 on 64-dim heads: bit-exact."""
+    rng = np.random.default_rng(6)
+    x = O.fp_quantize_vec(inputs.outlier_normal(rng, 2048 * 64)).reshape(2048, 64)
+    pos = np.arange(2048)
+    got = ops.rope_fp(x, pos)
+    want = np.stack([O.rope_fp(x[i], int(pos[i])) for i in range(2048)])
+    assert np.array_equal(got, want)
+
+
+def test_silu_fp_tolerance(ops):
+    """silu_fp = fpq(x / (1 + exp(-x))): CUDA exp vs numpy exp may differ in
+    the last ulp, which can move a BFP mantissa only when the quotient sits
+    on a rounding boundary.  Tolerance: at most 1 mantissa LSB, on at most
+    1e-5 of the elements."""
+    rng = np.random.default_rng(7)
+    x = O.fp_quantize_vec(inputs.outlier_normal(rng, 64 * 1536))
+    got = ops.silu_fp(x)
+    want = O.silu_fp(x)
+    diff = got != want
+    assert diff.mean() <= 1e-5
+    if diff.any():
+        _, e = O.tile_quantize(want)
+        lsb = np.repeat(np.power(2.0, e.astype(np.float64) - 15), 16)
+        assert (np.abs(got - want)[diff] <= lsb[diff]).all()
+
+
+def test_softmax_fp_tolerance(ops):
+    """softmax_fp over T=2048 scores: max |rel err| <= 4 ulp (exp differs by
+    at most ~1 ulp between libraries; the sum and division are reproduced)."""
+    rng = np.random.default_rng(8)
+    x = inputs.outlier_normal(rng, 64 * 2048).reshape(64, 2048)
+    got = ops.softmax_fp(x)
+    want = np.stack([O.softmax_fp(x[i]) for i in range(64)])
+    rel = np.abs(got - want) / np.maximum(np.abs(want), np.finfo(float).tiny)
+    assert rel.max() <= 4 * 2.0 ** -52
+    assert (got == want).mean() > 0.99

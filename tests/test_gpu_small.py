@@ -1,0 +1,93 @@
+"""GPU parity on small random models (fast, many shapes): token streams of
+the C-ABI decoder against the oracle for several seeds, ragged batches, both
+feed modes and KV lengths up to MAX_CTX; error paths of the ABI."""
+import numpy as np
+import pytest
+
+from oracle import bfp_oracle as O
+from oracle import synth as OS
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(D=128, H_Q=2, H_KV=1, HD=64, FFN=256, NL=3, VOCAB=512)
+
+
+def _pair(seed, max_ctx, max_seqs, **kw):
+    from bfp200 import BfpConfig, Decoder, synth
+    dims = dict(SMALL, **kw)
+    cfg = BfpConfig(MAX_CTX=max_ctx, max_seqs=max_seqs, **dims)
+    dec = Decoder(cfg)
+    dec.load_image(synth.synthetic_image(cfg, seed))
+    ocfg = O.Cfg(**dims)
+    return dec, OS.make_model(seed, ocfg), ocfg
+
+
+@pytest.mark.parametrize("seed", [1, 2])
+def test_small_model_ragged_batch(seed):
+    dec, model, ocfg = _pair(seed, 40, 5)
+    rng = np.random.default_rng(seed)
+    prompts = [rng.integers(0, 512, size=int(n)).tolist() for n in (1, 2, 7, 16, 30)]
+    got = dec.generate(prompts, 10)
+    for p, g in zip(prompts, got):
+        assert g == O.generate(model, p, 10, max_ctx=40, cfg=ocfg)
+    got_rtl = dec.generate(prompts[:2], 5, feed_mode="rtl")
+    for p, g in zip(prompts[:2], got_rtl):
+        assert g == O.generate(model, p, 5, max_ctx=40, cfg=ocfg, feed_mode="rtl")
+    dec.close()
+
+
+def test_small_model_full_context():
+    """prompt + n_gen == MAX_CTX exactly; GQA with 3 query heads per KV head."""
+    dec, model, ocfg = _pair(3, 64, 2, H_Q=3, D=192, FFN=384)
+    prompts = [[5, 6, 7, 8], list(range(20, 44))]
+    got = dec.generate(prompts, 40)
+    assert got[0] == O.generate(model, prompts[0], 40, max_ctx=64, cfg=ocfg)
+    got1 = dec.generate(prompts[1:], 40)[0]
+    assert got1 == O.generate(model, prompts[1], 40, max_ctx=64, cfg=ocfg)
+    dec.close()
+
+
+def test_error_paths():
+    from bfp200 import BfpConfig, BfpError, Decoder, _lib, synth
+    cfg = BfpConfig(MAX_CTX=16, max_seqs=2, **SMALL)
+    dec = Decoder(cfg)
+    with pytest.raises(BfpError) as e:
+        dec.generate([[1, 2]], 4)
+    assert e.value.code == _lib.ESTATE
+    with pytest.raises(BfpError) as e:
+        dec.load_image(b"\0" * 1000)
+    assert e.value.code == _lib.EIMAGE
+    dec.load_image(synth.synthetic_image(cfg, 1))
+    with pytest.raises(BfpError) as e:
+        dec.generate([[1, 2]], 15)                 # 2 + 15 > MAX_CTX
+    assert e.value.code == _lib.EINVAL
+    with pytest.raises(BfpError):
+        dec.generate([[600]], 2)                   # token outside the vocabulary
+    with pytest.raises(BfpError):
+        dec.generate([[1]] * 3, 2)                 # more sequences than max_seqs
+    with pytest.raises(BfpError):
+        dec.generate([list(range(49))], 1)         # longer than NPROMPT_MAX
+    with pytest.raises(BfpError):
+        dec.load_rom(6, [])                        # empty prompt ROM
+    with pytest.raises(BfpError):
+        dec.load_rom(0, [0] * 10)                  # wrong gamma ROM length
+    assert dec.generate([[1, 2]], 3)[0][:2] == [1, 2]
+    dec.close()
+
+
+def test_rom_prompt_and_gamma_roms():
+    """load-roms path: prompt from the PROMPT ROM; gammas re-loaded from ROM
+    entries give the same stream as the image's gammas."""
+    from bfp200 import BfpConfig, Decoder, pack, synth
+    cfg = BfpConfig(MAX_CTX=32, max_seqs=1, **SMALL)
+    img = synth.synthetic_image(cfg, 4)
+    g1, g2, nw = pack.unpack_image(cfg, img)
+    dec = Decoder(cfg)
+    dec.load_image(img)
+    dec.load_rom(6, [9, 8, 7])
+    a = dec.generate(None, 5)
+    dec.load_rom(0, np.concatenate([m for m, _ in g1]).view(np.uint16))
+    dec.load_rom(1, np.concatenate([e for _, e in g1]).astype(np.uint8).astype(np.uint16))
+    b = dec.generate(None, 5)
+    assert a == b and a[0][:3] == [9, 8, 7]
+    dec.close()

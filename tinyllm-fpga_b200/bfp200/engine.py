@@ -1,0 +1,161 @@
+"""Decoder: one libbfp200 handle on one GPU (the drop-in for the reference's
+golden driver loop, rtl/vc707/host/gen_smollm_blockfp_full.py:406-449, fed by
+the packed image and ROM files of the packers)."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import _lib
+from ._lib import arr, check, ptr
+from .config import BfpConfig
+from .image import ROM_KINDS, read_roms
+
+FEED_MODES = {"sim": 0, "rtl": 1}
+
+
+class Decoder:
+    def __init__(self, cfg: BfpConfig | None = None, device: int = 0):
+        self.cfg = cfg or BfpConfig()
+        self.device = device
+        self._h = C.c_void_p()
+        self._rom_prompt_len = 0
+        check(_lib.lib().bfp200_open(C.byref(self.cfg.to_c()), int(device), C.byref(self._h)))
+
+    # -- lifecycle ------------------------------------------------------------
+    def close(self):
+        if self._h:
+            _lib.lib().bfp200_close(self._h)
+            self._h = C.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    # -- loading ----------------------------------------------------------------
+    def load_image(self, image):
+        """<PREFIX>DDR3.bin contents (bytes) or a path to it."""
+        if isinstance(image, (str, os.PathLike)):
+            with open(image, "rb") as f:
+                image = f.read()
+        buf = np.frombuffer(image, dtype=np.uint8)
+        check(_lib.lib().bfp200_load_image(self._h, buf.ctypes.data, buf.size))
+
+    def load_rom(self, kind: int, entries):
+        e = arr(entries, np.uint16)
+        check(_lib.lib().bfp200_load_rom(self._h, int(kind), ptr(e), e.size))
+        if int(kind) == 6:
+            self._rom_prompt_len = int(e.size)
+
+    def load_roms(self, directory, prefix="lbfp_full_"):
+        """The client's load-roms (bfp_client.cpp:1381-1437) from a release dir."""
+        for kind, entries in read_roms(directory, prefix).items():
+            self.load_rom(kind, entries)
+
+    # -- decode -----------------------------------------------------------------
+    def generate(self, prompts=None, n_gen=None, feed_mode="sim"):
+        """prompts: list of token-id lists (None: the loaded PROMPT ROM).
+        Returns one list per sequence: prompt + n_gen ids (sim) or one argmax
+        per step (rtl)."""
+        n_gen = self.cfg.N_GEN if n_gen is None else int(n_gen)
+        mode = FEED_MODES[feed_mode]
+        if prompts is None:
+            if not self._rom_prompt_len:
+                raise ValueError("no prompt given and no PROMPT ROM loaded")
+            out = np.empty(self._rom_prompt_len + n_gen, np.int32)
+            check(_lib.lib().bfp200_generate(self._h, None, None, 1, n_gen, mode, ptr(out)))
+            return [out.tolist()]
+        lens = arr([len(p) for p in prompts], np.int32)
+        ids = arr(np.concatenate([np.asarray(p, dtype=np.int64) for p in prompts]), np.int32)
+        out = np.empty(int(lens.sum()) + len(prompts) * n_gen, np.int32)
+        check(_lib.lib().bfp200_generate(self._h, ptr(ids), ptr(lens), len(prompts), n_gen, mode, ptr(out)))
+        res, o = [], 0
+        for L in lens:
+            res.append(out[o:o + L + n_gen].tolist())
+            o += L + n_gen
+        return res
+
+    def uncertified_steps(self) -> int:
+        n = C.c_longlong()
+        check(_lib.lib().bfp200_uncertified_steps(self._h, C.byref(n)))
+        return n.value
+
+    def last_timing(self):
+        a, b = C.c_double(), C.c_double()
+        check(_lib.lib().bfp200_last_timing(self._h, C.byref(a), C.byref(b)))
+        return {"prefill_ms": a.value, "decode_ms": b.value}
+
+    # -- one layer (fwd_layer, :261-293) ----------------------------------------
+    def stage_dims(self):
+        d = np.empty(_lib.NSTAGES, np.int32)
+        check(_lib.lib().bfp200_stage_dims(self._h, ptr(d)))
+        return d
+
+    def fwd_layer(self, layer, h, pos, k_cache, v_cache, kv_pos=None, stages=False):
+        """h (ncols, D) grid doubles; k_cache/v_cache (ncols, max_ctx, H_KV, HD)
+        float64, updated in place at kv_pos.  Returns h_out (and a list of
+        per-stage dicts if stages)."""
+        h = arr(h, np.float64)
+        one = h.ndim == 1
+        h2 = h.reshape(1, -1) if one else h
+        ncols = h2.shape[0]
+        pos_a = arr(np.broadcast_to(np.asarray(pos), (ncols,)), np.int32)
+        kvp = pos_a if kv_pos is None else arr(np.broadcast_to(np.asarray(kv_pos), (ncols,)), np.int32)
+        kc = k_cache if k_cache.ndim == 4 else k_cache[None]
+        vc = v_cache if v_cache.ndim == 4 else v_cache[None]
+        if not (kc.flags["C_CONTIGUOUS"] and kc.dtype == np.float64 and vc.flags["C_CONTIGUOUS"]
+                and vc.dtype == np.float64):
+            raise ValueError("k_cache / v_cache must be C-contiguous float64")
+        out = np.empty_like(h2)
+        st = None
+        if stages:
+            dims = self.stage_dims()
+            st = np.empty(ncols * int(dims.sum()), np.float64)
+        check(_lib.lib().bfp200_fwd_layer(self._h, int(layer), ptr(h2), ptr(pos_a), ptr(kvp), ncols, ptr(kc),
+                                          ptr(vc), kc.shape[1], ptr(out), ptr(st)))
+        res = out[0] if one else out
+        if not stages:
+            return res
+        names = ["n1", "q", "k", "v", "attn", "o", "h1", "n2", "g", "u", "mlp", "d"]
+        per = []
+        o = 0
+        for _ in range(ncols):
+            dct = {}
+            for nm, dd in zip(names, dims):
+                dct[nm] = st[o:o + dd].copy()
+                o += dd
+            per.append(dct)
+        return res, per
+
+
+def generate_multi(decoders, prompts, n_gen, feed_mode="sim"):
+    """Sequences split into contiguous blocks over the decoders (one per GPU),
+    run concurrently, no collectives (bfp200_generate_multi)."""
+    hs = (C.c_void_p * len(decoders))(*[d.handle.value for d in decoders])
+    lens = arr([len(p) for p in prompts], np.int32)
+    ids = arr(np.concatenate([np.asarray(p, dtype=np.int64) for p in prompts]), np.int32)
+    out = np.empty(int(lens.sum()) + len(prompts) * n_gen, np.int32)
+    check(_lib.lib().bfp200_generate_multi(C.cast(hs, C.c_void_p), len(decoders), ptr(ids), ptr(lens), len(prompts),
+                                           int(n_gen), FEED_MODES[feed_mode], ptr(out)))
+    res, o = [], 0
+    for L in lens:
+        res.append(out[o:o + L + n_gen].tolist())
+        o += L + n_gen
+    return res
+
+
+__all__ = ["Decoder", "generate_multi", "ROM_KINDS"]

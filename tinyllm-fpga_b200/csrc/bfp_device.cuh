@@ -1,0 +1,293 @@
+// bfp_device.cuh -- device-side arithmetic that reproduces the reference BFP
+// simulator bit for bit (jrrk2/tinyllm-fpga rtl/vc707/host/
+// gen_smollm_blockfp_full.py).  Everything here is exact IEEE-754 double or
+// integer arithmetic; the file must be compiled with -fmad=false so no
+// multiply/add pair is contracted into an FMA the simulator never performs.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace bfp {
+
+constexpr int TILE = 16;        // elements per shared exponent (bfp_format.svh:1-27)
+constexpr int ALIGN_MAX = 47;   // gen_smollm_blockfp_full.py:214
+constexpr long long SAT_HI = (1LL << 47) - 1;   // :229
+constexpr long long SAT_LO = -(1LL << 47);      // :230
+
+// 2^k as a double, exact for k in [-1022, 1023].
+__host__ __device__ __forceinline__ double pow2(int k) {
+#ifdef __CUDA_ARCH__
+  return __longlong_as_double((long long)(k + 1023) << 52);
+#else
+  union { long long i; double d; } u;
+  u.i = (long long)(k + 1023) << 52;
+  return u.d;
+#endif
+}
+
+__host__ __device__ __forceinline__ int ilog2_u32(unsigned v) {
+#ifdef __CUDA_ARCH__
+  return 31 - __clz((int)v);
+#else
+  return 31 - __builtin_clz(v);
+#endif
+}
+
+// Number of doubles directly below 2^j that a correctly rounded log2 maps to
+// exactly j (so floor(log2(x)) jumps to j before x reaches 2^j).  Derived
+// from log2(2^j (1 - n 2^-53)) = j - n 2^-53 / ln 2 rounding to j; the
+// values below are floor(ln2 * 2^b) for the ulp exponent b of the result's
+// binade.  numpy's float64 log2 follows this exactly (checked by the tests on
+// every host that generates or compares golden data).
+__host__ __device__ __forceinline__ int log2_roundup_count(int j) {
+  if (j == 0) return 0;
+  int aj = j < 0 ? -j : j;
+  int a = ilog2_u32((unsigned)aj);
+  int b = (j > 0 && (aj & (aj - 1)) == 0) ? a - 1 : a;
+  switch (b) {
+    case 1: return 1;    case 2: return 2;    case 3: return 5;    case 4: return 11;
+    case 5: return 22;   case 6: return 44;   case 7: return 88;   case 8: return 177;
+    case 9: return 354;  case 10: return 709;
+    default: return 0;
+  }
+}
+
+// floor(np.log2(x)) for a finite positive normal double, numpy-exact.
+__host__ __device__ __forceinline__ int floor_log2_np(double x) {
+#ifdef __CUDA_ARCH__
+  unsigned long long bits = (unsigned long long)__double_as_longlong(x);
+#else
+  union { double d; unsigned long long i; } u; u.d = x;
+  unsigned long long bits = u.i;
+#endif
+  int k = (int)((bits >> 52) & 0x7FF) - 1023;
+  unsigned long long F = bits & ((1ULL << 52) - 1);
+  int n = log2_roundup_count(k + 1);
+  return (n > 0 && F >= (1ULL << 52) - (unsigned long long)n) ? k + 1 : k;
+}
+
+// Tile exponent of tile_quantize (:92-93) from the tile's max |v|.
+// NaN/Inf follow numpy's x86 cast (INT32_MIN + 1, clipped to -127).
+__host__ __device__ __forceinline__ int tile_exponent(double max_abs) {
+  if (!(max_abs <= 1.7976931348623157e308)) return -127;     // NaN or +Inf
+  if (max_abs < 1e-300) max_abs = 1e-300;
+  int e = floor_log2_np(max_abs) + 1;
+  return e < -127 ? -127 : (e > 127 ? 127 : e);
+}
+
+// Mantissa of tile_quantize (:94-96): clip(rint(v / 2^e * 32768)).  Values
+// whose int64 cast is undefined in numpy (NaN, |x| >= 2^63) give x86's
+// INT64_MIN, i.e. -32768 after the clip.
+__host__ __device__ __forceinline__ int16_t tile_mantissa(double v, int e) {
+  double x = v * pow2(15 - e);
+  if (!(x > -9.2233720368547758e18 && x < 9.2233720368547758e18)) return (int16_t)-32768;
+  double r = rint(x);
+  if (r > 32767.0) r = 32767.0;
+  if (r < -32768.0) r = -32768.0;
+  return (int16_t)(int)r;
+}
+
+// tile_decode (:100-102): m/32768 * 2^e, exact.
+__host__ __device__ __forceinline__ double bfp_decode(int m, int e) {
+  return (double)m * pow2(e - 15);
+}
+
+// tile_quantize applied to a grid value already held as (m, e): identity
+// unless the tile holds -32768 (decoded -2^e), which bumps the exponent and
+// halves every mantissa with round-half-even.  `has_min` = tile contains
+// -32768.
+__host__ __device__ __forceinline__ int requant_exp(int e, bool has_min) {
+  return (has_min && e < 127) ? e + 1 : e;
+}
+__host__ __device__ __forceinline__ int16_t requant_mant(int m, bool bumped) {
+  if (!bumped) return (int16_t)m;
+  int k = m >> 1;                       // floor(m / 2)
+  int odd = m & 1;                      // m/2 = k + 0.5 when odd -> round half to even
+  return (int16_t)(k + (odd & (k & 1)));
+}
+
+#ifdef __CUDACC__
+// ---------------------------------------------------------------------------
+// Cooperative tile quantize: 16 consecutive lanes hold one tile (lane & 15 =
+// element index).  Returns this lane's mantissa; *e_out gets the exponent.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int16_t tile_quantize_16lanes(double v, int* e_out) {
+  double a = fabs(v);
+  // NaN-propagating max (np.max returns NaN when any element is NaN)
+  #pragma unroll
+  for (int off = 8; off >= 1; off >>= 1) {
+    double o = __shfl_xor_sync(0xffffffffu, a, off, 16);
+    a = (a != a || o != o) ? __longlong_as_double(0x7FF8000000000000LL) : (o > a ? o : a);
+  }
+  int e = tile_exponent(a);
+  *e_out = e;
+  return tile_mantissa(v, e);
+}
+
+// ---------------------------------------------------------------------------
+// numpy pairwise summation (numpy/_core/src/umath/loops_utils.h.src,
+// pairwise_sum): blocks of <= 128 summed with 8 strided accumulators, larger
+// ranges split at n/2 rounded down to a multiple of 8; the reduction adds the
+// result to the identity +0.0.  Valid for n <= 8192 (one ufunc buffer).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ double np_pw_leaf(const double* a, int n) {
+  if (n < 8) {
+    double res = 0.0;
+    for (int i = 0; i < n; ++i) res = __dadd_rn(res, a[i]);
+    return res;
+  }
+  double r0 = a[0], r1 = a[1], r2 = a[2], r3 = a[3], r4 = a[4], r5 = a[5], r6 = a[6], r7 = a[7];
+  int i = 8;
+  int lim = n - (n % 8);
+  for (; i < lim; i += 8) {
+    r0 = __dadd_rn(r0, a[i + 0]); r1 = __dadd_rn(r1, a[i + 1]);
+    r2 = __dadd_rn(r2, a[i + 2]); r3 = __dadd_rn(r3, a[i + 3]);
+    r4 = __dadd_rn(r4, a[i + 4]); r5 = __dadd_rn(r5, a[i + 5]);
+    r6 = __dadd_rn(r6, a[i + 6]); r7 = __dadd_rn(r7, a[i + 7]);
+  }
+  double res = __dadd_rn(__dadd_rn(__dadd_rn(r0, r1), __dadd_rn(r2, r3)),
+                         __dadd_rn(__dadd_rn(r4, r5), __dadd_rn(r6, r7)));
+  for (; i < n; ++i) res = __dadd_rn(res, a[i]);
+  return res;
+}
+
+// Enumerates the leaves of the pairwise tree of size n in order, writing
+// (start, len) pairs; returns the count.  Single thread.
+__device__ __forceinline__ int np_pw_leaves(int n, int* lo_out, int* len_out, int max_leaves) {
+  int st_lo[24], st_n[24];
+  int sp = 0, nl = 0;
+  st_lo[sp] = 0; st_n[sp] = n; ++sp;
+  while (sp > 0) {
+    --sp;
+    int lo = st_lo[sp], len = st_n[sp];
+    if (len <= 128) {
+      if (nl < max_leaves) { lo_out[nl] = lo; len_out[nl] = len; }
+      ++nl;
+    } else {
+      int n2 = len / 2;
+      n2 -= n2 % 8;
+      st_lo[sp] = lo + n2; st_n[sp] = len - n2; ++sp;   // right (visited second)
+      st_lo[sp] = lo;      st_n[sp] = n2;       ++sp;   // left (visited first)
+    }
+  }
+  return nl;
+}
+
+// Combines leaf values in the exact order of the recursive tree (post-order
+// stack machine: a node's value is left + right once both children are done).
+__device__ __forceinline__ double np_pw_combine(int n, const double* leafval) {
+  int st_n[24], st_s[24];
+  double vals[24];
+  int sp = 0, vsp = 0, li = 0;
+  st_n[0] = n; st_s[0] = 0; sp = 1;
+  while (sp > 0) {
+    const int top = sp - 1;
+    const int len = st_n[top];
+    if (len <= 128) {
+      vals[vsp++] = leafval[li++];
+      --sp;
+      continue;
+    }
+    int n2 = len / 2;
+    n2 -= n2 % 8;
+    if (st_s[top] == 0) {
+      st_s[top] = 1;
+      st_n[sp] = n2; st_s[sp] = 0; ++sp;
+    } else if (st_s[top] == 1) {
+      st_s[top] = 2;
+      st_n[sp] = len - n2; st_s[sp] = 0; ++sp;
+    } else {
+      const double r = vals[--vsp];
+      const double l = vals[--vsp];
+      vals[vsp++] = __dadd_rn(l, r);
+      --sp;
+    }
+  }
+  return vals[0];
+}
+
+// Single-thread numpy sum of a[0..n) (the full reduction: 0.0 + pairwise).
+__device__ __forceinline__ double np_sum_serial(const double* a, int n) {
+  if (n <= 128) return __dadd_rn(0.0, np_pw_leaf(a, n));
+  int lo[64], len[64];
+  double val[64];
+  int nl = np_pw_leaves(n, lo, len, 64);
+  for (int i = 0; i < nl; ++i) val[i] = np_pw_leaf(a + lo[i], len[i]);
+  return __dadd_rn(0.0, np_pw_combine(n, val));
+}
+
+// Warp-cooperative numpy sum of a shared-memory array (n <= 8192).  All 32
+// lanes must call it; scratch needs 3*64 words of shared memory.  Returns the
+// sum on every lane.
+__device__ __forceinline__ double np_sum_warp(const double* a, int n, int* s_lo, int* s_len,
+                                              double* s_val) {
+  const int lane = threadIdx.x & 31;
+  if (n <= 128) {
+    double r = 0.0;
+    if (lane == 0) r = __dadd_rn(0.0, np_pw_leaf(a, n));
+    return __shfl_sync(0xffffffffu, r, 0);
+  }
+  int nl = 0;
+  if (lane == 0) nl = np_pw_leaves(n, s_lo, s_len, 64);
+  nl = __shfl_sync(0xffffffffu, nl, 0);
+  __syncwarp();
+  for (int i = lane; i < nl; i += 32) s_val[i] = np_pw_leaf(a + s_lo[i], s_len[i]);
+  __syncwarp();
+  double r = 0.0;
+  if (lane == 0) r = __dadd_rn(0.0, np_pw_combine(n, s_val));
+  return __shfl_sync(0xffffffffu, r, 0);
+}
+
+// ---------------------------------------------------------------------------
+// Correct rounding of (signed 128-bit integer) * 2^scale to double.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ double i128_to_double_scaled(__int128 x, int scale) {
+  if (x == 0) return 0.0;
+  bool neg = x < 0;
+  unsigned __int128 u = neg ? (unsigned __int128)(-x) : (unsigned __int128)x;
+  unsigned long long hi = (unsigned long long)(u >> 64), lo = (unsigned long long)u;
+  int p = hi ? 127 - __clzll((long long)hi) : 63 - __clzll((long long)lo);  // top bit index
+  double r;
+  if (p < 53) {
+    r = (double)lo;                                  // exact
+    r = r * pow2(scale);
+  } else {
+    int sh = p - 52;
+    unsigned __int128 mant = u >> sh;
+    unsigned __int128 rem = u - (mant << sh);
+    unsigned __int128 half = (unsigned __int128)1 << (sh - 1);
+    unsigned long long m = (unsigned long long)mant;
+    if (rem > half || (rem == half && (m & 1))) ++m;
+    if (m >> 53) { m >>= 1; ++sh; }
+    r = (double)m * pow2(sh + scale);                // exact: m < 2^53, power-of-two scale
+  }
+  return neg ? -r : r;
+}
+
+// Exact BFP dot of two 64-element head vectors given as 4 tiles each:
+// sum_j S_j * 2^(E_j - 30) with S_j = sum_k qm*km (|S_j| <= 2^34) and
+// E_j = qe_j + ke_j, rounded once to double.  This equals the reference's
+// BLAS np.dot whenever the pair-exponent spread is <= 17 (then every partial
+// sum is exact in double); wider spreads are rounded exactly here.
+__device__ __forceinline__ double exact_tile_dot4(const long long S[4], const int E[4]) {
+  int emax = -100000, emin = 100000;
+  #pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (S[j] != 0) { emax = E[j] > emax ? E[j] : emax; emin = E[j] < emin ? E[j] : emin; }
+  if (emax == -100000) return 0.0;
+  if (emax - emin <= 17) {
+    double s = 0.0;
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) s = __dadd_rn(s, (double)S[j] * pow2(E[j] - 30));
+    return s;
+  }
+  int base = emax - 90 > emin ? emax - 90 : emin;   // terms below 2^-90 of the top are dropped
+  __int128 acc = 0;
+  #pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (S[j] != 0 && E[j] >= base) acc += ((__int128)S[j]) << (E[j] - base);
+  return i128_to_double_scaled(acc, base - 30);
+}
+#endif  // __CUDACC__
+
+}  // namespace bfp

@@ -1,0 +1,1085 @@
+// engine.cu -- host runtime and C ABI (include/bfp200.h) of libbfp200.so.
+//
+// A handle owns one device: the repacked weight image, a per-sequence BFP KV
+// arena, activation buffers and a captured CUDA graph of one decode step.
+// generate() = causal prefill of every prompt position (chunked, position
+// ordered, so each chunk only reads KV written by earlier chunks or earlier
+// in the same layer), then n_gen decode steps replayed from the graph with
+// the token feedback kept on the device.
+#include "../../include/bfp200.h"
+#include "bfp_device.cuh"
+#include "kernels.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <string>
+#include <thread>
+#include <vector>
+
+using namespace bfp;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define CK(x)                                                                                  \
+  do {                                                                                         \
+    cudaError_t _e = (x);                                                                      \
+    if (_e != cudaSuccess) return fail(BFP200_ECUDA, std::string(#x) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+
+#define CKR(x)                       \
+  do {                               \
+    int _r = (x);                    \
+    if (_r != BFP200_OK) return _r;  \
+  } while (0)
+
+template <typename T>
+struct DBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  DBuf() = default;
+  DBuf(const DBuf&) = delete;
+  DBuf& operator=(const DBuf&) = delete;
+  ~DBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+  // (Re)allocates to at least `count` elements, zero-filled.
+  cudaError_t ensure(size_t count) {
+    if (count <= n && p) return cudaSuccess;
+    release();
+    cudaError_t e = cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T));
+    if (e != cudaSuccess) { p = nullptr; return e; }
+    n = count;
+    return cudaMemset(p, 0, std::max<size_t>(count, 1) * sizeof(T));
+  }
+};
+
+struct MMPlan {
+  int rg = 1, bn = 1, ks = 1;
+};
+
+constexpr size_t MM_SMEM_LIMIT = 200 * 1024;
+
+MMPlan plan_matmul(int G, int NT, int ncols, bool swiglu, int nsm) {
+  MMPlan p;
+  p.rg = swiglu ? 2 : 1;
+  p.bn = ncols <= 32 ? ncols : 32;
+  const long rows_t = G / p.rg, cols_t = (ncols + p.bn - 1) / p.bn;
+  const long target = 2L * nsm;
+  int best = -1;
+  for (int ks = 1; ks <= NT; ++ks) {
+    if (NT % ks) continue;
+    const int ntc = NT / ks;
+    if (matmul_smem_bytes(p.rg, p.bn, ntc, NT) > MM_SMEM_LIMIT) continue;
+    if (best < 0) best = ks;
+    else if (rows_t * cols_t * ks <= target && ntc >= 4) best = ks;
+  }
+  p.ks = best < 0 ? NT : best;
+  return p;
+}
+
+// Layout of the packed DDR3 image (gen_smollm_blockfp_ddr.py:155-221,
+// lbfp_ddr3.svh:45-86): each region padded to 4 KiB, in this order.
+struct Region {
+  std::string name;
+  size_t off = 0, size = 0;
+};
+
+size_t align4k(size_t n) { return (n + 4095) & ~size_t(4095); }
+
+std::vector<Region> image_regions(const bfp200_cfg& c) {
+  std::vector<Region> r;
+  size_t off = 0;
+  auto add = [&](const std::string& name, size_t size) {
+    r.push_back({name, off, size});
+    off += align4k(size);
+  };
+  const int KVD = c.H_KV * c.HD;
+  const struct { const char* tag; int dout, din; } mats[] = {
+      {"WQ", c.D, c.D}, {"WK", KVD, c.D}, {"WV", KVD, c.D}, {"WO", c.D, c.D},
+      {"WG", c.FFN, c.D}, {"WU", c.FFN, c.D}, {"WDN", c.D, c.FFN}};
+  for (auto& m : mats) {
+    add(std::string(m.tag) + "_m", (size_t)c.NL * (m.dout / 16) * m.din * 32);
+    add(std::string(m.tag) + "_e", (size_t)c.NL * (m.dout / 16) * (m.din / 16) * 16);
+  }
+  const int NTD = c.D / 16;
+  add("G1_m", (size_t)c.NL * c.D * 2);
+  add("G1_e", (size_t)c.NL * NTD);
+  add("G2_m", (size_t)c.NL * c.D * 2);
+  add("G2_e", (size_t)c.NL * NTD);
+  add("EMBED_m", (size_t)c.VOCAB / 16 * c.D * 32);
+  add("EMBED_e", (size_t)c.VOCAB / 16 * NTD * 16);
+  add("EMBED_LU_m", (size_t)c.VOCAB * c.D * 2);
+  add("EMBED_LU_e", (size_t)c.VOCAB * 64);
+  add("NORM_W_m", (size_t)c.D * 2);
+  add("NORM_W_e", (size_t)NTD);
+  r.push_back({"END", off, 0});
+  return r;
+}
+
+const Region* find_region(const std::vector<Region>& rs, const std::string& name) {
+  for (auto& r : rs)
+    if (r.name == name) return &r;
+  return nullptr;
+}
+
+// Exact (m, e) form of a tile of BFP grid values (lossless; a tile whose
+// minimum is -2^e keeps exponent e and mantissa -32768).  Returns false if
+// the values are not on a 16-bit BFP grid.
+bool grid_encode_tile(const double* v, int16_t* m, int8_t* e) {
+  double mx = 0.0;
+  for (int i = 0; i < 16; ++i) mx = std::max(mx, std::fabs(v[i]));
+  const int e1 = tile_exponent(mx);
+  for (int ee : {e1, e1 - 1}) {
+    if (ee < -127) continue;
+    bool ok = true;
+    int16_t mm[16];
+    for (int i = 0; i < 16 && ok; ++i) {
+      const double x = v[i] * pow2(15 - ee);
+      if (x != std::rint(x) || x < -32768.0 || x > 32767.0) ok = false;
+      else mm[i] = (int16_t)(int)x;
+    }
+    if (ok) {
+      std::memcpy(m, mm, sizeof(mm));
+      *e = (int8_t)ee;
+      return true;
+    }
+  }
+  return false;
+}
+
+__global__ void advance_kernel(const int* tok, const int* cert, int ncols, int n_gen, int* gen_out, int* col_tok,
+                               int* col_pos, int* dec_step, long long* uncert) {
+  __shared__ int s_step;
+  if (threadIdx.x == 0) s_step = *dec_step;
+  __syncthreads();
+  const int step = s_step;
+  int bad = 0;
+  for (int c = threadIdx.x; c < ncols; c += blockDim.x) {
+    const int t = tok[c];
+    if (step < n_gen) gen_out[(size_t)c * n_gen + step] = t;
+    col_tok[c] = t;
+    col_pos[c] += 1;
+    bad += cert[c] ? 0 : 1;
+  }
+  if (bad) atomicAdd(reinterpret_cast<unsigned long long*>(uncert), (unsigned long long)bad);
+  __syncthreads();
+  if (threadIdx.x == 0) *dec_step = step + 1;
+}
+
+__global__ void scatter_tokens_kernel(const int* tok, const int* cert, const int* slot, const int* pos, int ncols,
+                                      int stride, int* out, long long* uncert) {
+  int bad = 0;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < ncols; c += gridDim.x * blockDim.x) {
+    out[(size_t)slot[c] * stride + pos[c]] = tok[c];
+    bad += cert[c] ? 0 : 1;
+  }
+  if (bad) atomicAdd(reinterpret_cast<unsigned long long*>(uncert), (unsigned long long)bad);
+}
+
+}  // namespace
+
+struct bfp200_handle {
+  bfp200_cfg cfg{};
+  int device = 0;
+  int nsm = 148;
+  cudaStream_t stream = nullptr;
+  int D = 0, HQ = 0, HKV = 0, HD = 0, FFN = 0, NL = 0, V = 0, MAXC = 0, NTD = 0, NTF = 0, KVD = 0, QD = 0;
+  int RQKV = 0, GQKV = 0, GO = 0, GGU = 0, GD = 0;
+  bool pdl = true;
+  // weights
+  DBuf<uint8_t> wm_qkv, wm_o, wm_gu, wm_d;
+  DBuf<int8_t> we_qkv, we_o, we_gu, we_d;
+  DBuf<double> g1, g2, nw;
+  DBuf<int16_t> emb_m;
+  DBuf<int8_t> emb_e;
+  DBuf<double> emb_norm;
+  double emb_norm_max = 0.0;
+  DBuf<double> rope_cs;
+  std::vector<int16_t> g1m, g2m, nwm;
+  std::vector<int8_t> g1e, g2e, nwe;
+  std::vector<int32_t> rom_prompt;
+  bool have_image = false;
+  // KV arena
+  DBuf<int16_t> km, vm;
+  DBuf<int8_t> ke, ve;
+  // activations (column capacity cap)
+  int cap = 0;
+  DBuf<int16_t> h_m, h1_m, n_m, qkv_m, qr_m, a_m, mlp_m, dbg_m;
+  DBuf<int8_t> h_e, h1_e, n_e, qkv_e, qr_e, a_e, mlp_e, dbg_e;
+  DBuf<long long> acc;
+  DBuf<unsigned> counters;
+  DBuf<double> hn, hn_norm, part_val, part_sec;
+  DBuf<int> part_idx, tok, cert;
+  DBuf<int> col_slot, col_pos, col_kvpos, col_tok;
+  DBuf<int> gen_out, dec_step, rtl_out;
+  DBuf<long long> uncert_dev;
+  cudaGraphExec_t graph = nullptr;
+  int graph_cols = -1, graph_ngen = -1;
+  long long uncert = 0;
+  double t_prefill = 0.0, t_decode = 0.0;
+
+  ~bfp200_handle() {
+    if (graph) cudaGraphExecDestroy(graph);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  size_t layer_stride_m(int G, int NT) const { return (size_t)G * NT * 512; }
+  size_t layer_stride_e(int G, int NT) const { return (size_t)G * NT * 16; }
+  DevMat mat(const DBuf<uint8_t>& wm, const DBuf<int8_t>& we, int G, int NT, int l) const {
+    DevMat m;
+    m.wm = wm.p + layer_stride_m(G, NT) * l;
+    m.we = we.p + layer_stride_e(G, NT) * l;
+    m.G = G;
+    m.NT = NT;
+    return m;
+  }
+  Dims dims() const { return Dims{D, HQ, HKV, HD, FFN, NL, V, MAXC}; }
+  KvArena kv() const {
+    KvArena k;
+    k.km = km.p; k.ke = ke.p; k.vm = vm.p; k.ve = ve.p;
+    k.NL = NL; k.HKV = HKV; k.HD = HD; k.MAX_CTX = MAXC;
+    return k;
+  }
+  ColDesc cols() const {
+    ColDesc c;
+    c.slot = col_slot.p;
+    c.pos = col_pos.p;
+    return c;
+  }
+};
+
+namespace {
+
+int ensure_cols(bfp200_handle* h, int ncols) {
+  if (ncols <= h->cap) return BFP200_OK;
+  const int cap = std::max(ncols, 64);
+  const int R_MAX = std::max({h->RQKV, 2 * h->FFN, h->D});
+  CK(h->h_m.ensure((size_t)cap * h->D)); CK(h->h_e.ensure((size_t)cap * h->NTD));
+  CK(h->h1_m.ensure((size_t)cap * h->D)); CK(h->h1_e.ensure((size_t)cap * h->NTD));
+  CK(h->n_m.ensure((size_t)cap * h->D)); CK(h->n_e.ensure((size_t)cap * h->NTD));
+  CK(h->qkv_m.ensure((size_t)cap * h->RQKV)); CK(h->qkv_e.ensure((size_t)cap * h->RQKV / 16));
+  CK(h->qr_m.ensure((size_t)cap * h->QD)); CK(h->qr_e.ensure((size_t)cap * h->QD / 16));
+  CK(h->a_m.ensure((size_t)cap * h->QD)); CK(h->a_e.ensure((size_t)cap * h->QD / 16));
+  CK(h->mlp_m.ensure((size_t)cap * h->FFN)); CK(h->mlp_e.ensure((size_t)cap * h->NTF));
+  CK(h->dbg_m.ensure((size_t)cap * R_MAX)); CK(h->dbg_e.ensure((size_t)cap * R_MAX / 16));
+  CK(h->acc.ensure((size_t)R_MAX * cap));
+  CK(h->counters.ensure((size_t)(R_MAX / 16) * (cap + 1)));
+  const int nrb_max = (h->V + 63) / 64;
+  CK(h->hn.ensure((size_t)cap * h->D)); CK(h->hn_norm.ensure(cap));
+  CK(h->part_val.ensure((size_t)cap * nrb_max)); CK(h->part_sec.ensure((size_t)cap * nrb_max));
+  CK(h->part_idx.ensure((size_t)cap * nrb_max));
+  CK(h->tok.ensure(cap)); CK(h->cert.ensure(cap));
+  CK(h->col_slot.ensure(cap)); CK(h->col_pos.ensure(cap)); CK(h->col_kvpos.ensure(cap)); CK(h->col_tok.ensure(cap));
+  h->cap = cap;
+  if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; h->graph_cols = -1; }
+  return BFP200_OK;
+}
+
+int ensure_kv(bfp200_handle* h, int nslots) {
+  const size_t per = (size_t)nslots * h->NL * h->HKV * h->MAXC;
+  if (h->km.n >= per * h->HD) return BFP200_OK;
+  CK(h->km.ensure(per * h->HD)); CK(h->vm.ensure(per * h->HD));
+  CK(h->ke.ensure(per * (h->HD / 16))); CK(h->ve.ensure(per * (h->HD / 16)));
+  if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; h->graph_cols = -1; }
+  return BFP200_OK;
+}
+
+int enqueue_matmul(bfp200_handle* h, DevMat W, const int16_t* xm, const int8_t* xe, int x_ld, int x_lde,
+                   int ncols, int epi, int16_t* om, int8_t* oe, int o_ld, int o_lde, const int16_t* rm,
+                   const int8_t* re, long long* acc, unsigned* counters, int acc_ld) {
+  MatmulArgs a;
+  a.W = W;
+  a.xm = xm; a.xe = xe; a.x_ld = x_ld; a.x_lde = x_lde;
+  a.ncols = ncols;
+  a.epi = epi;
+  a.om = om; a.oe = oe; a.o_ld = o_ld; a.o_lde = o_lde;
+  a.rm = rm; a.re = re;
+  const MMPlan p = plan_matmul(W.G, W.NT, ncols, epi == EPI_SWIGLU, h->nsm);
+  a.rg = p.rg; a.bn = p.bn; a.ksplit = p.ks;
+  a.acc = acc; a.counters = counters; a.acc_ld = acc_ld;
+  if (p.ks > 1 && (acc == nullptr || counters == nullptr))
+    return fail(BFP200_EINVAL, "matmul needs K-split scratch");
+  CK(launch_matmul(a, h->stream, h->pdl));
+  return BFP200_OK;
+}
+
+// Stage capture for bfp200_fwd_layer (nullptr in the fast path).
+struct StageSink {
+  std::vector<std::vector<double>> st;  // [stage][ncols * dim]
+};
+
+int download_decoded(bfp200_handle* h, const int16_t* m, const int8_t* e, int ld, int n_per_col, int off,
+                     int ncols, std::vector<double>& out) {
+  // copies columns [0, ncols) elements [off, off + n_per_col) of a (m, e) buffer
+  std::vector<int16_t> hm((size_t)ncols * ld);
+  std::vector<int8_t> he((size_t)ncols * ld / 16);
+  CK(cudaMemcpyAsync(hm.data(), m, hm.size() * 2, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaMemcpyAsync(he.data(), e, he.size(), cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  out.assign((size_t)ncols * n_per_col, 0.0);
+  for (int c = 0; c < ncols; ++c)
+    for (int i = 0; i < n_per_col; ++i) {
+      const size_t src = (size_t)c * ld + off + i;
+      out[(size_t)c * n_per_col + i] = bfp_decode(hm[src], he[src / 16]);
+    }
+  return BFP200_OK;
+}
+
+int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink) {
+  const Dims d = h->dims();
+  const bool pdl = h->pdl;
+  cudaStream_t s = h->stream;
+  long long* acc = h->acc.p;
+  unsigned* cnt = h->counters.p;
+  const int accld = h->cap;
+  // n1 = tile_quantize(rmsnorm_fp(h, g1))               (:263-264)
+  CK(launch_rmsnorm(h->h_m.p, h->h_e.p, h->g1.p + (size_t)l * h->D, h->cfg.eps, h->D, ncols, h->n_m.p, h->n_e.p, s, pdl));
+  if (sink) CKR(download_decoded(h, h->n_m.p, h->n_e.p, h->D, h->D, 0, ncols, sink->st[0]));
+  // q, k, v = matvec(n1, Wq|Wk|Wv)                         (:265-267)
+  CKR(enqueue_matmul(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
+                     EPI_STORE, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->RQKV / 16, nullptr, nullptr, acc, cnt, accld));
+  if (sink) CKR(download_decoded(h, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->KVD, h->QD + h->KVD, ncols, sink->st[3]));
+  // rope on q, k; KV write                                (:268-272)
+  CK(launch_rope_kv(h->qkv_m.p, h->qkv_e.p, h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), h->rope_cs.p, d, ncols, s, pdl));
+  // attention -> tile_quantize(fpq(attn))                 (:273-283)
+  CK(launch_attention(h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), d, ncols, h->a_m.p, h->a_e.p, s, pdl));
+  if (sink) {
+    CKR(download_decoded(h, h->qr_m.p, h->qr_e.p, h->QD, h->QD, 0, ncols, sink->st[1]));
+    CKR(download_decoded(h, h->a_m.p, h->a_e.p, h->QD, h->QD, 0, ncols, sink->st[4]));
+    CKR(enqueue_matmul(h, h->mat(h->wm_o, h->we_o, h->GO, h->QD / 16, l), h->a_m.p, h->a_e.p, h->QD, h->QD / 16,
+                       ncols, EPI_STORE, h->dbg_m.p, h->dbg_e.p, h->D, h->NTD, nullptr, nullptr, acc, cnt, accld));
+    CKR(download_decoded(h, h->dbg_m.p, h->dbg_e.p, h->D, h->D, 0, ncols, sink->st[5]));
+  }
+  // h1 = fpq(h + matvec(attn, Wo))                          (:284-285)
+  CKR(enqueue_matmul(h, h->mat(h->wm_o, h->we_o, h->GO, h->QD / 16, l), h->a_m.p, h->a_e.p, h->QD, h->QD / 16, ncols,
+                     EPI_RESIDUAL, h->h1_m.p, h->h1_e.p, h->D, h->NTD, h->h_m.p, h->h_e.p, acc, cnt, accld));
+  if (sink) CKR(download_decoded(h, h->h1_m.p, h->h1_e.p, h->D, h->D, 0, ncols, sink->st[6]));
+  // n2 = tile_quantize(rmsnorm_fp(h1, g2))                 (:286-287)
+  CK(launch_rmsnorm(h->h1_m.p, h->h1_e.p, h->g2.p + (size_t)l * h->D, h->cfg.eps, h->D, ncols, h->n_m.p, h->n_e.p, s, pdl));
+  if (sink) {
+    CKR(download_decoded(h, h->n_m.p, h->n_e.p, h->D, h->D, 0, ncols, sink->st[7]));
+    CKR(enqueue_matmul(h, h->mat(h->wm_gu, h->we_gu, h->GGU, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
+                       EPI_STORE, h->dbg_m.p, h->dbg_e.p, 2 * h->FFN, 2 * h->FFN / 16, nullptr, nullptr, acc, cnt,
+                       accld));
+    std::vector<double> gu;
+    CKR(download_decoded(h, h->dbg_m.p, h->dbg_e.p, 2 * h->FFN, 2 * h->FFN, 0, ncols, gu));
+    sink->st[8].assign((size_t)ncols * h->FFN, 0.0);
+    sink->st[9].assign((size_t)ncols * h->FFN, 0.0);
+    for (int c = 0; c < ncols; ++c)
+      for (int i = 0; i < h->FFN; ++i) {
+        const int grp = i / 16, r = i % 16;
+        sink->st[8][(size_t)c * h->FFN + i] = gu[(size_t)c * 2 * h->FFN + (2 * grp) * 16 + r];
+        sink->st[9][(size_t)c * h->FFN + i] = gu[(size_t)c * 2 * h->FFN + (2 * grp + 1) * 16 + r];
+      }
+  }
+  // mlp = tile_quantize(fpq(silu_fp(g) * u))                (:288-291)
+  CKR(enqueue_matmul(h, h->mat(h->wm_gu, h->we_gu, h->GGU, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
+                     EPI_SWIGLU, h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF, nullptr, nullptr, acc, cnt, accld));
+  if (sink) {
+    CKR(download_decoded(h, h->mlp_m.p, h->mlp_e.p, h->FFN, h->FFN, 0, ncols, sink->st[10]));
+    CKR(enqueue_matmul(h, h->mat(h->wm_d, h->we_d, h->GD, h->NTF, l), h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF, ncols,
+                       EPI_STORE, h->dbg_m.p, h->dbg_e.p, h->D, h->NTD, nullptr, nullptr, acc, cnt, accld));
+    CKR(download_decoded(h, h->dbg_m.p, h->dbg_e.p, h->D, h->D, 0, ncols, sink->st[11]));
+  }
+  // h = fpq(h1 + matvec(mlp, Wd))                           (:292-293)
+  CKR(enqueue_matmul(h, h->mat(h->wm_d, h->we_d, h->GD, h->NTF, l), h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF, ncols,
+                     EPI_RESIDUAL, h->h_m.p, h->h_e.p, h->D, h->NTD, h->h1_m.p, h->h1_e.p, acc, cnt, accld));
+  return BFP200_OK;
+}
+
+int enqueue_head(bfp200_handle* h, int ncols) {
+  cudaStream_t s = h->stream;
+  CK(launch_head_prep(h->h_m.p, h->h_e.p, h->nw.p, h->cfg.eps, h->D, ncols, h->hn.p, h->hn_norm.p, s, h->pdl));
+  int nrb = 0;
+  CK(launch_head_logits(h->emb_m.p, h->emb_e.p, h->V, h->D, h->hn.p, ncols, h->part_val.p, h->part_idx.p,
+                        h->part_sec.p, &nrb, s, h->pdl));
+  CK(launch_head_reduce(h->part_val.p, h->part_idx.p, h->part_sec.p, nrb, h->hn_norm.p, h->emb_norm_max, h->D, ncols,
+                        h->tok.p, h->cert.p, s, h->pdl));
+  return BFP200_OK;
+}
+
+int enqueue_forward(bfp200_handle* h, int ncols, bool head) {
+  CK(launch_embed(h->emb_m.p, h->emb_e.p, h->col_tok.p, h->D, ncols, h->h_m.p, h->h_e.p, h->stream, h->pdl));
+  for (int l = 0; l < h->NL; ++l) CKR(enqueue_layer(h, l, ncols, nullptr));
+  if (head) CKR(enqueue_head(h, ncols));
+  return BFP200_OK;
+}
+
+int check_cfg(const bfp200_cfg& c) {
+  if (c.D <= 0 || c.D % 16 || c.FFN <= 0 || c.FFN % 16 || c.H_Q <= 0 || c.H_KV <= 0 || c.H_Q % c.H_KV ||
+      c.HD != 64 || c.H_Q * c.HD != c.D || c.NL <= 0 || c.VOCAB <= 0 || c.VOCAB % 16 || c.MAX_CTX <= 0 ||
+      c.MAX_CTX > 3072 || c.NPROMPT_MAX <= 0 || c.max_seqs <= 0 || c.D > 8192)
+    return fail(BFP200_EINVAL,
+                "unsupported config (need HD=64, H_Q*HD=D, D/FFN/VOCAB multiples of 16, H_Q % H_KV == 0, "
+                "MAX_CTX <= 3072)");
+  return BFP200_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+void bfp200_default_cfg(bfp200_cfg* c) {
+  c->D = 576; c->H_Q = 9; c->H_KV = 3; c->HD = 64; c->FFN = 1536; c->NL = 30; c->VOCAB = 49152;
+  c->MAX_CTX = 64; c->NPROMPT_MAX = 48; c->max_seqs = 1;
+  c->rope_base = 10000.0;
+  c->eps = 1e-5;
+}
+
+int bfp200_last_error(char* buf, size_t len) {
+  if (buf && len) {
+    std::strncpy(buf, g_err.c_str(), len - 1);
+    buf[len - 1] = 0;
+  }
+  return BFP200_OK;
+}
+
+int bfp200_rope_table(double* out, int n_pos, int HD, double base) {
+  if (!out || n_pos < 0 || HD <= 0 || HD % 2) return fail(BFP200_EINVAL, "rope_table: bad arguments");
+  const int H2 = HD / 2;
+  for (int p = 0; p < n_pos; ++p)
+    for (int j = 0; j < H2; ++j) {
+      // theta = 1.0 / (base ** (2*j/HD)) * pos   (gen_smollm_blockfp_full.py:253)
+      const double expo = (double)(2 * j) / (double)HD;
+      const double pw = (expo == 0.0) ? 1.0 : std::pow(base, expo);
+      const double theta = 1.0 / pw * (double)p;
+      out[((size_t)p * H2 + j) * 2 + 0] = std::cos(theta);
+      out[((size_t)p * H2 + j) * 2 + 1] = std::sin(theta);
+    }
+  return BFP200_OK;
+}
+
+int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
+  if (!cfg || !out) return fail(BFP200_EINVAL, "open: null argument");
+  CKR(check_cfg(*cfg));
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) return fail(BFP200_ENODEV, "no CUDA device");
+  if (device < 0 || device >= ndev) return fail(BFP200_ENODEV, "device index out of range");
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) return fail(BFP200_ENODEV, "libbfp200 is built for sm_100a (B200); device is sm_" +
+                                                       std::to_string(prop.major) + std::to_string(prop.minor));
+  CK(cudaSetDevice(device));
+  CK(init_kernel_attributes());
+  auto* h = new bfp200_handle();
+  h->cfg = *cfg;
+  h->device = device;
+  h->nsm = prop.multiProcessorCount;
+  h->D = cfg->D; h->HQ = cfg->H_Q; h->HKV = cfg->H_KV; h->HD = cfg->HD; h->FFN = cfg->FFN; h->NL = cfg->NL;
+  h->V = cfg->VOCAB; h->MAXC = cfg->MAX_CTX;
+  h->NTD = h->D / 16; h->NTF = h->FFN / 16; h->KVD = h->HKV * h->HD; h->QD = h->HQ * h->HD;
+  h->RQKV = h->QD + 2 * h->KVD;
+  h->GQKV = h->RQKV / 16; h->GO = h->D / 16; h->GGU = 2 * h->FFN / 16; h->GD = h->D / 16;
+  if (const char* e = std::getenv("BFP200_NO_PDL")) h->pdl = !(e[0] == '1');
+  cudaError_t ce = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
+  if (ce != cudaSuccess) { delete h; return fail(BFP200_ECUDA, cudaGetErrorString(ce)); }
+  std::vector<double> cs((size_t)h->MAXC * h->HD);
+  bfp200_rope_table(cs.data(), h->MAXC, h->HD, cfg->rope_base);
+  if (h->rope_cs.ensure(cs.size()) != cudaSuccess ||
+      cudaMemcpy(h->rope_cs.p, cs.data(), cs.size() * 8, cudaMemcpyHostToDevice) != cudaSuccess) {
+    delete h;
+    return fail(BFP200_ENOMEM, "open: rope table allocation failed");
+  }
+  *out = h;
+  return BFP200_OK;
+}
+
+int bfp200_close(bfp200_handle* h) {
+  if (!h) return BFP200_OK;
+  cudaSetDevice(h->device);
+  cudaStreamSynchronize(h->stream);
+  delete h;
+  return BFP200_OK;
+}
+
+static void decode_vec(const int16_t* m, const int8_t* e, size_t n, double* out) {
+  for (size_t i = 0; i < n; ++i) out[i] = bfp_decode(m[i], e[i / 16]);
+}
+
+static int upload_gammas(bfp200_handle* h) {
+  std::vector<double> g1(h->g1m.size()), g2(h->g2m.size()), nw(h->nwm.size());
+  decode_vec(h->g1m.data(), h->g1e.data(), g1.size(), g1.data());
+  decode_vec(h->g2m.data(), h->g2e.data(), g2.size(), g2.data());
+  decode_vec(h->nwm.data(), h->nwe.data(), nw.size(), nw.data());
+  CK(h->g1.ensure(g1.size())); CK(h->g2.ensure(g2.size())); CK(h->nw.ensure(nw.size()));
+  CK(cudaMemcpy(h->g1.p, g1.data(), g1.size() * 8, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(h->g2.p, g2.data(), g2.size() * 8, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(h->nw.p, nw.data(), nw.size() * 8, cudaMemcpyHostToDevice));
+  return BFP200_OK;
+}
+
+int bfp200_load_image(bfp200_handle* h, const void* img, size_t len) {
+  if (!h || !img) return fail(BFP200_EINVAL, "load_image: null argument");
+  CK(cudaSetDevice(h->device));
+  const auto rs = image_regions(h->cfg);
+  const size_t total = find_region(rs, "END")->off;
+  if (len != total)
+    return fail(BFP200_EIMAGE, "image is " + std::to_string(len) + " bytes; this config needs " + std::to_string(total));
+  const uint8_t* b = static_cast<const uint8_t*>(img);
+  // weights: raw image to the device, then repacked per matrix
+  DBuf<uint8_t> staging;
+  const size_t wbytes = find_region(rs, "G1_m")->off;
+  CK(staging.ensure(wbytes));
+  CK(cudaMemcpyAsync(staging.p, b, wbytes, cudaMemcpyHostToDevice, h->stream));
+  CK(h->wm_qkv.ensure((size_t)h->NL * h->GQKV * h->NTD * 512)); CK(h->we_qkv.ensure((size_t)h->NL * h->GQKV * h->NTD * 16));
+  CK(h->wm_o.ensure((size_t)h->NL * h->GO * (h->QD / 16) * 512)); CK(h->we_o.ensure((size_t)h->NL * h->GO * (h->QD / 16) * 16));
+  CK(h->wm_gu.ensure((size_t)h->NL * h->GGU * h->NTD * 512)); CK(h->we_gu.ensure((size_t)h->NL * h->GGU * h->NTD * 16));
+  CK(h->wm_d.ensure((size_t)h->NL * h->GD * h->NTF * 512)); CK(h->we_d.ensure((size_t)h->NL * h->GD * h->NTF * 16));
+  struct Spec { const char* tag; int dout, din; DBuf<uint8_t>* wm; DBuf<int8_t>* we; int Gtot, gstride, goff; };
+  const Spec specs[] = {
+      {"WQ", h->QD, h->D, &h->wm_qkv, &h->we_qkv, h->GQKV, 1, 0},
+      {"WK", h->KVD, h->D, &h->wm_qkv, &h->we_qkv, h->GQKV, 1, h->QD / 16},
+      {"WV", h->KVD, h->D, &h->wm_qkv, &h->we_qkv, h->GQKV, 1, (h->QD + h->KVD) / 16},
+      {"WO", h->D, h->QD, &h->wm_o, &h->we_o, h->GO, 1, 0},
+      {"WG", h->FFN, h->D, &h->wm_gu, &h->we_gu, h->GGU, 2, 0},
+      {"WU", h->FFN, h->D, &h->wm_gu, &h->we_gu, h->GGU, 2, 1},
+      {"WDN", h->D, h->FFN, &h->wm_d, &h->we_d, h->GD, 1, 0}};
+  for (const auto& sp : specs) {
+    const Region* rm = find_region(rs, std::string(sp.tag) + "_m");
+    const Region* re = find_region(rs, std::string(sp.tag) + "_e");
+    const int G = sp.dout / 16, NT = sp.din / 16;
+    const size_t lm = (size_t)G * sp.din * 32, le = (size_t)G * NT * 16;
+    for (int l = 0; l < h->NL; ++l) {
+      CK(launch_pack_from_ddr(reinterpret_cast<const int16_t*>(staging.p + rm->off + l * lm),
+                              reinterpret_cast<const int8_t*>(staging.p + re->off + l * le), sp.dout, NT,
+                              sp.wm->p + (size_t)l * sp.Gtot * NT * 512, sp.we->p + (size_t)l * sp.Gtot * NT * 16,
+                              sp.gstride, sp.goff, h->stream));
+    }
+  }
+  // gammas and final norm (host copies kept for load_rom)
+  auto take16 = [&](const char* nm, size_t n, std::vector<int16_t>& v) {
+    v.resize(n);
+    std::memcpy(v.data(), b + find_region(rs, nm)->off, n * 2);
+  };
+  auto take8 = [&](const char* nm, size_t n, std::vector<int8_t>& v) {
+    v.resize(n);
+    std::memcpy(v.data(), b + find_region(rs, nm)->off, n);
+  };
+  take16("G1_m", (size_t)h->NL * h->D, h->g1m); take8("G1_e", (size_t)h->NL * h->NTD, h->g1e);
+  take16("G2_m", (size_t)h->NL * h->D, h->g2m); take8("G2_e", (size_t)h->NL * h->NTD, h->g2e);
+  take16("NORM_W_m", h->D, h->nwm); take8("NORM_W_e", h->NTD, h->nwe);
+  CKR(upload_gammas(h));
+  // embedding table: row-major mantissas (EMBED_LU_m) and per-row exponents
+  // (EMBED_LU_e, rows padded to 64 B); the head reads the same rows.
+  CK(h->emb_m.ensure((size_t)h->V * h->D));
+  CK(cudaMemcpyAsync(h->emb_m.p, b + find_region(rs, "EMBED_LU_m")->off, (size_t)h->V * h->D * 2,
+                     cudaMemcpyHostToDevice, h->stream));
+  std::vector<int8_t> ee((size_t)h->V * h->NTD);
+  const uint8_t* lue = b + find_region(rs, "EMBED_LU_e")->off;
+  for (int r = 0; r < h->V; ++r) std::memcpy(ee.data() + (size_t)r * h->NTD, lue + (size_t)r * 64, h->NTD);
+  CK(h->emb_e.ensure(ee.size()));
+  CK(cudaMemcpyAsync(h->emb_e.p, ee.data(), ee.size(), cudaMemcpyHostToDevice, h->stream));
+  CK(h->emb_norm.ensure(h->V));
+  CK(launch_row_norms(h->emb_m.p, h->emb_e.p, h->V, h->D, h->emb_norm.p, h->stream));
+  std::vector<double> norms(h->V);
+  CK(cudaMemcpyAsync(norms.data(), h->emb_norm.p, h->V * 8, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  h->emb_norm_max = *std::max_element(norms.begin(), norms.end());
+  h->have_image = true;
+  return BFP200_OK;
+}
+
+int bfp200_load_rom(bfp200_handle* h, int kind, const uint16_t* entries, size_t n) {
+  if (!h || (!entries && n)) return fail(BFP200_EINVAL, "load_rom: null argument");
+  CK(cudaSetDevice(h->device));
+  const size_t nld = (size_t)h->NL * h->D, nlt = (size_t)h->NL * h->NTD;
+  auto put16 = [&](std::vector<int16_t>& v, size_t want) -> int {
+    if (n != want) return fail(BFP200_EIMAGE, "load_rom kind " + std::to_string(kind) + ": " + std::to_string(n) +
+                                                  " entries, expected " + std::to_string(want));
+    v.resize(n);
+    for (size_t i = 0; i < n; ++i) v[i] = (int16_t)entries[i];
+    return BFP200_OK;
+  };
+  auto put8 = [&](std::vector<int8_t>& v, size_t want) -> int {
+    if (n != want) return fail(BFP200_EIMAGE, "load_rom kind " + std::to_string(kind) + ": " + std::to_string(n) +
+                                                  " entries, expected " + std::to_string(want));
+    v.resize(n);
+    for (size_t i = 0; i < n; ++i) v[i] = (int8_t)(entries[i] & 0xFF);
+    return BFP200_OK;
+  };
+  switch (kind) {
+    case 0: CKR(put16(h->g1m, nld)); break;
+    case 1: CKR(put8(h->g1e, nlt)); break;
+    case 2: CKR(put16(h->g2m, nld)); break;
+    case 3: CKR(put8(h->g2e, nlt)); break;
+    case 4: CKR(put16(h->nwm, h->D)); break;
+    case 5: CKR(put8(h->nwe, h->NTD)); break;
+    case 6:
+      if (n == 0 || n > (size_t)h->cfg.NPROMPT_MAX)
+        return fail(BFP200_EINVAL, "prompt ROM length must be 1..NPROMPT_MAX");
+      h->rom_prompt.assign(entries, entries + n);
+      return BFP200_OK;
+    default: return fail(BFP200_EINVAL, "load_rom: kind must be 0..6");
+  }
+  if (h->g1m.size() == nld && h->g1e.size() == nlt && h->g2m.size() == nld && h->g2e.size() == nlt &&
+      h->nwm.size() == (size_t)h->D && h->nwe.size() == (size_t)h->NTD)
+    CKR(upload_gammas(h));
+  return BFP200_OK;
+}
+
+int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq, int n_gen,
+                    int feed_mode, int32_t* out_tokens) {
+  if (!h || !out_tokens) return fail(BFP200_EINVAL, "generate: null argument");
+  if (!h->have_image) return fail(BFP200_ESTATE, "generate before load_image");
+  if (feed_mode != 0 && feed_mode != 1) return fail(BFP200_EINVAL, "feed_mode must be 0 (sim) or 1 (rtl)");
+  if (n_gen < 0) return fail(BFP200_EINVAL, "n_gen < 0");
+  std::vector<int32_t> ids, lens;
+  if (!prompt_ids) {
+    if (h->rom_prompt.empty() || n_seq != 1) return fail(BFP200_EINVAL, "no prompt given and no prompt ROM loaded");
+    ids = h->rom_prompt;
+    lens = {(int32_t)ids.size()};
+  } else {
+    if (!prompt_lens || n_seq <= 0) return fail(BFP200_EINVAL, "generate: bad prompt arguments");
+    lens.assign(prompt_lens, prompt_lens + n_seq);
+    const size_t tot = std::accumulate(lens.begin(), lens.end(), (size_t)0);
+    ids.assign(prompt_ids, prompt_ids + tot);
+  }
+  if (n_seq > h->cfg.max_seqs) return fail(BFP200_EINVAL, "n_seq > max_seqs");
+  for (int s = 0; s < n_seq; ++s) {
+    if (lens[s] <= 0 || lens[s] > h->cfg.NPROMPT_MAX) return fail(BFP200_EINVAL, "prompt length outside 1..NPROMPT_MAX");
+    if (lens[s] + n_gen > h->MAXC) return fail(BFP200_EINVAL, "prompt length + n_gen exceeds MAX_CTX");
+  }
+  for (int32_t t : ids)
+    if (t < 0 || t >= h->V) return fail(BFP200_EINVAL, "token id outside the vocabulary");
+  CK(cudaSetDevice(h->device));
+  CKR(ensure_kv(h, n_seq));
+  // ---- prefill: every prompt position, position-major
+  const int PREFILL_CHUNK = 1024;
+  std::vector<int32_t> off(n_seq + 1, 0);
+  for (int s = 0; s < n_seq; ++s) off[s + 1] = off[s] + lens[s];
+  std::vector<int> cs, cp, ct;
+  const int maxlen = *std::max_element(lens.begin(), lens.end());
+  for (int p = 0; p < maxlen; ++p)
+    for (int s = 0; s < n_seq; ++s)
+      if (p < lens[s]) { cs.push_back(s); cp.push_back(p); ct.push_back(ids[off[s] + p]); }
+  const int ncp = (int)cs.size();
+  CKR(ensure_cols(h, std::max(std::min(ncp, PREFILL_CHUNK), n_seq)));
+  const bool rtl = feed_mode == 1;
+  if (rtl) CK(h->rtl_out.ensure((size_t)n_seq * h->cfg.NPROMPT_MAX));
+  CK(h->uncert_dev.ensure(1));
+  CK(cudaMemsetAsync(h->uncert_dev.p, 0, 8, h->stream));
+  cudaEvent_t ev0, ev1, ev2;
+  cudaEventCreate(&ev0); cudaEventCreate(&ev1); cudaEventCreate(&ev2);
+  CK(cudaEventRecord(ev0, h->stream));
+  for (int c0 = 0; c0 < ncp; c0 += h->cap) {
+    const int nc = std::min(h->cap, ncp - c0);
+    CK(cudaMemcpyAsync(h->col_slot.p, cs.data() + c0, nc * 4, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(h->col_pos.p, cp.data() + c0, nc * 4, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(h->col_tok.p, ct.data() + c0, nc * 4, cudaMemcpyHostToDevice, h->stream));
+    CKR(enqueue_forward(h, nc, rtl));
+    if (rtl)
+      scatter_tokens_kernel<<<(nc + 255) / 256, 256, 0, h->stream>>>(h->tok.p, h->cert.p, h->col_slot.p,
+                                                                     h->col_pos.p, nc, h->cfg.NPROMPT_MAX,
+                                                                     h->rtl_out.p, h->uncert_dev.p);
+    CK(cudaStreamSynchronize(h->stream));   // host column arrays are reused by the next chunk
+  }
+  CK(cudaEventRecord(ev1, h->stream));
+  std::vector<int32_t> rtl_host;
+  if (rtl) {
+    rtl_host.resize((size_t)n_seq * h->cfg.NPROMPT_MAX);
+    CK(cudaMemcpyAsync(rtl_host.data(), h->rtl_out.p, rtl_host.size() * 4, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+  }
+  // ---- decode: column s = sequence s at position len_s, fed its last token
+  std::vector<int> dslot(n_seq), dpos(n_seq), dtok(n_seq);
+  for (int s = 0; s < n_seq; ++s) {
+    dslot[s] = s;
+    dpos[s] = lens[s];
+    dtok[s] = rtl ? rtl_host[(size_t)s * h->cfg.NPROMPT_MAX + lens[s] - 1] : ids[off[s] + lens[s] - 1];
+  }
+  if (n_gen > 0) {
+    CK(h->gen_out.ensure((size_t)n_seq * n_gen));
+    CK(h->dec_step.ensure(1));
+    CK(cudaMemcpyAsync(h->col_slot.p, dslot.data(), n_seq * 4, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(h->col_pos.p, dpos.data(), n_seq * 4, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(h->col_tok.p, dtok.data(), n_seq * 4, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemsetAsync(h->dec_step.p, 0, 4, h->stream));
+    if (!h->graph || h->graph_cols != n_seq || h->graph_ngen != n_gen) {
+      if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; }
+      CK(cudaStreamSynchronize(h->stream));
+      cudaGraph_t g;
+      CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+      int r = enqueue_forward(h, n_seq, true);
+      advance_kernel<<<1, 256, 0, h->stream>>>(h->tok.p, h->cert.p, n_seq, n_gen, h->gen_out.p, h->col_tok.p,
+                                               h->col_pos.p, h->dec_step.p, h->uncert_dev.p);
+      cudaError_t ce = cudaStreamEndCapture(h->stream, &g);
+      if (r != BFP200_OK) { if (ce == cudaSuccess) cudaGraphDestroy(g); return r; }
+      CK(ce);
+      ce = cudaGraphInstantiate(&h->graph, g, 0);
+      cudaGraphDestroy(g);
+      CK(ce);
+      h->graph_cols = n_seq;
+      h->graph_ngen = n_gen;
+    }
+    for (int i = 0; i < n_gen; ++i) CK(cudaGraphLaunch(h->graph, h->stream));
+  }
+  CK(cudaEventRecord(ev2, h->stream));
+  std::vector<int32_t> gen((size_t)n_seq * n_gen);
+  if (n_gen > 0) CK(cudaMemcpyAsync(gen.data(), h->gen_out.p, gen.size() * 4, cudaMemcpyDeviceToHost, h->stream));
+  long long unc = 0;
+  CK(cudaMemcpyAsync(&unc, h->uncert_dev.p, 8, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  float ms1 = 0, ms2 = 0;
+  cudaEventElapsedTime(&ms1, ev0, ev1);
+  cudaEventElapsedTime(&ms2, ev1, ev2);
+  cudaEventDestroy(ev0); cudaEventDestroy(ev1); cudaEventDestroy(ev2);
+  h->t_prefill = ms1;
+  h->t_decode = ms2;
+  h->uncert = unc;
+  if (read_and_clear_error_flag(h->stream)) return fail(BFP200_ETIMEOUT, "a bounded device wait timed out");
+  // ---- assemble: sim = prompt + generated; rtl = one argmax per step
+  size_t o = 0;
+  for (int s = 0; s < n_seq; ++s) {
+    for (int p = 0; p < lens[s]; ++p)
+      out_tokens[o++] = rtl ? rtl_host[(size_t)s * h->cfg.NPROMPT_MAX + p] : ids[off[s] + p];
+    for (int i = 0; i < n_gen; ++i) out_tokens[o++] = gen[(size_t)s * n_gen + i];
+  }
+  return BFP200_OK;
+}
+
+int bfp200_generate_multi(bfp200_handle* const* hs, int n_dev, const int32_t* prompt_ids, const int32_t* prompt_lens,
+                          int n_seq, int n_gen, int feed_mode, int32_t* out_tokens) {
+  if (!hs || n_dev <= 0 || !prompt_ids || !prompt_lens || n_seq <= 0)
+    return fail(BFP200_EINVAL, "generate_multi: bad arguments");
+  // contiguous blocks balanced by total steps
+  std::vector<long long> cum(n_seq + 1, 0);
+  for (int s = 0; s < n_seq; ++s) cum[s + 1] = cum[s] + prompt_lens[s] + n_gen;
+  std::vector<int> b(n_dev + 1, 0);
+  b[n_dev] = n_seq;
+  for (int d = 1; d < n_dev; ++d) {
+    const long long target = cum[n_seq] * d / n_dev;
+    b[d] = (int)(std::lower_bound(cum.begin(), cum.end(), target) - cum.begin());
+    b[d] = std::max(b[d], b[d - 1]);
+  }
+  std::vector<size_t> id_off(n_seq + 1, 0), out_off(n_seq + 1, 0);
+  for (int s = 0; s < n_seq; ++s) {
+    id_off[s + 1] = id_off[s] + prompt_lens[s];
+    out_off[s + 1] = out_off[s] + prompt_lens[s] + n_gen;
+  }
+  std::vector<int> rc(n_dev, BFP200_OK);
+  std::vector<std::string> errs(n_dev);
+  std::vector<std::thread> th;
+  for (int d = 0; d < n_dev; ++d) {
+    if (b[d + 1] == b[d]) continue;
+    th.emplace_back([&, d] {
+      rc[d] = bfp200_generate(hs[d], prompt_ids + id_off[b[d]], prompt_lens + b[d], b[d + 1] - b[d], n_gen,
+                              feed_mode, out_tokens + out_off[b[d]]);
+      if (rc[d] != BFP200_OK) errs[d] = g_err;
+    });
+  }
+  for (auto& t : th) t.join();
+  for (int d = 0; d < n_dev; ++d)
+    if (rc[d] != BFP200_OK) return fail(rc[d], "device " + std::to_string(d) + ": " + errs[d]);
+  return BFP200_OK;
+}
+
+int bfp200_uncertified_steps(bfp200_handle* h, long long* count) {
+  if (!h || !count) return fail(BFP200_EINVAL, "null argument");
+  *count = h->uncert;
+  return BFP200_OK;
+}
+
+int bfp200_last_timing(bfp200_handle* h, double* prefill_ms, double* decode_ms) {
+  if (!h) return fail(BFP200_EINVAL, "null handle");
+  if (prefill_ms) *prefill_ms = h->t_prefill;
+  if (decode_ms) *decode_ms = h->t_decode;
+  return BFP200_OK;
+}
+
+int bfp200_time_matmuls(bfp200_handle* h, int ncols, int reps, double* ms_per_token, int* launches_per_token) {
+  if (!h || ncols <= 0 || reps <= 0 || !ms_per_token) return fail(BFP200_EINVAL, "time_matmuls: bad arguments");
+  if (!h->have_image) return fail(BFP200_ESTATE, "time_matmuls before load_image");
+  CK(cudaSetDevice(h->device));
+  CKR(ensure_cols(h, ncols));
+  long long* acc = h->acc.p;
+  unsigned* cnt = h->counters.p;
+  const int accld = h->cap;
+  auto body = [&]() -> int {
+    for (int l = 0; l < h->NL; ++l) {
+      CKR(enqueue_matmul(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD,
+                         ncols, EPI_STORE, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->RQKV / 16, nullptr, nullptr, acc, cnt,
+                         accld));
+      CKR(enqueue_matmul(h, h->mat(h->wm_o, h->we_o, h->GO, h->QD / 16, l), h->a_m.p, h->a_e.p, h->QD, h->QD / 16,
+                         ncols, EPI_RESIDUAL, h->h1_m.p, h->h1_e.p, h->D, h->NTD, h->h_m.p, h->h_e.p, acc, cnt,
+                         accld));
+      CKR(enqueue_matmul(h, h->mat(h->wm_gu, h->we_gu, h->GGU, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
+                         EPI_SWIGLU, h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF, nullptr, nullptr, acc, cnt, accld));
+      CKR(enqueue_matmul(h, h->mat(h->wm_d, h->we_d, h->GD, h->NTF, l), h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF,
+                         ncols, EPI_RESIDUAL, h->dbg_m.p, h->dbg_e.p, h->D, h->NTD, h->h1_m.p, h->h1_e.p, acc, cnt,
+                         accld));
+    }
+    return BFP200_OK;
+  };
+  CK(cudaStreamSynchronize(h->stream));
+  cudaGraph_t g;
+  CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+  const int r = body();
+  cudaError_t ce = cudaStreamEndCapture(h->stream, &g);
+  if (r != BFP200_OK) { if (ce == cudaSuccess) cudaGraphDestroy(g); return r; }
+  CK(ce);
+  cudaGraphExec_t ge;
+  ce = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  CK(ce);
+  for (int i = 0; i < 3; ++i) CK(cudaGraphLaunch(ge, h->stream));
+  cudaEvent_t a, b;
+  cudaEventCreate(&a); cudaEventCreate(&b);
+  CK(cudaEventRecord(a, h->stream));
+  for (int i = 0; i < reps; ++i) CK(cudaGraphLaunch(ge, h->stream));
+  CK(cudaEventRecord(b, h->stream));
+  CK(cudaEventSynchronize(b));
+  float ms = 0;
+  cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a); cudaEventDestroy(b);
+  cudaGraphExecDestroy(ge);
+  *ms_per_token = ms / reps;
+  if (launches_per_token) *launches_per_token = 4 * h->NL;
+  if (read_and_clear_error_flag(h->stream)) return fail(BFP200_ETIMEOUT, "a bounded device wait timed out");
+  return BFP200_OK;
+}
+
+// ---------------------------------------------------------------------------
+// op-level entry points
+// ---------------------------------------------------------------------------
+int bfp200_tile_quantize(bfp200_handle* h, const double* v, size_t n, int16_t* m, int8_t* e) {
+  if (!h || (n && (!v || !m || !e)) || n % 16) return fail(BFP200_EINVAL, "tile_quantize: bad arguments");
+  if (!n) return BFP200_OK;
+  CK(cudaSetDevice(h->device));
+  DBuf<double> dv; DBuf<int16_t> dm; DBuf<int8_t> de;
+  CK(dv.ensure(n)); CK(dm.ensure(n)); CK(de.ensure(n / 16));
+  CK(cudaMemcpyAsync(dv.p, v, n * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(launch_tile_quantize(dv.p, (long long)(n / 16), dm.p, de.p, h->stream));
+  CK(cudaMemcpyAsync(m, dm.p, n * 2, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaMemcpyAsync(e, de.p, n / 16, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_tile_decode(bfp200_handle* h, const int16_t* m, const int8_t* e, size_t n, double* v) {
+  if (!h || (n && (!v || !m || !e)) || n % 16) return fail(BFP200_EINVAL, "tile_decode: bad arguments");
+  if (!n) return BFP200_OK;
+  CK(cudaSetDevice(h->device));
+  DBuf<double> dv; DBuf<int16_t> dm; DBuf<int8_t> de;
+  CK(dv.ensure(n)); CK(dm.ensure(n)); CK(de.ensure(n / 16));
+  CK(cudaMemcpyAsync(dm.p, m, n * 2, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(de.p, e, n / 16, cudaMemcpyHostToDevice, h->stream));
+  CK(launch_tile_decode(dm.p, de.p, (long long)(n / 16), dv.p, h->stream));
+  CK(cudaMemcpyAsync(v, dv.p, n * 8, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_matvec(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m, const int8_t* W_e,
+                  int D_out, int D_in, int batch, int16_t* out_m, int8_t* out_e) {
+  if (!h || !x_m || !x_e || !W_m || !W_e || !out_m || !out_e || D_out <= 0 || D_in <= 0 || D_out % 16 ||
+      D_in % 16 || batch <= 0)
+    return fail(BFP200_EINVAL, "matvec: bad arguments (D_out, D_in multiples of 16, batch >= 1)");
+  CK(cudaSetDevice(h->device));
+  const int NT = D_in / 16, G = D_out / 16;
+  DBuf<int16_t> dWm, dxm, dom; DBuf<int8_t> dWe, dxe, doe; DBuf<uint8_t> wm; DBuf<int8_t> we;
+  CK(dWm.ensure((size_t)D_out * D_in)); CK(dWe.ensure((size_t)D_out * NT));
+  CK(dxm.ensure((size_t)batch * D_in)); CK(dxe.ensure((size_t)batch * NT));
+  CK(dom.ensure((size_t)batch * D_out)); CK(doe.ensure((size_t)batch * G));
+  CK(wm.ensure((size_t)G * NT * 512)); CK(we.ensure((size_t)G * NT * 16));
+  CK(cudaMemcpyAsync(dWm.p, W_m, (size_t)D_out * D_in * 2, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(dWe.p, W_e, (size_t)D_out * NT, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(dxm.p, x_m, (size_t)batch * D_in * 2, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(dxe.p, x_e, (size_t)batch * NT, cudaMemcpyHostToDevice, h->stream));
+  CK(launch_pack_weights(dWm.p, dWe.p, D_out, NT, wm.p, we.p, 1, 0, h->stream));
+  DevMat W;
+  W.wm = wm.p; W.we = we.p; W.G = G; W.NT = NT;
+  const MMPlan p = plan_matmul(G, NT, batch, false, h->nsm);
+  DBuf<long long> acc; DBuf<unsigned> cnt;
+  if (p.ks > 1) {
+    CK(acc.ensure((size_t)D_out * batch));
+    CK(cnt.ensure((size_t)G * ((batch + p.bn - 1) / p.bn)));
+  }
+  CKR(enqueue_matmul(h, W, dxm.p, dxe.p, D_in, NT, batch, EPI_STORE, dom.p, doe.p, D_out, G, nullptr, nullptr, acc.p,
+                     cnt.p, batch));
+  CK(cudaMemcpyAsync(out_m, dom.p, (size_t)batch * D_out * 2, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaMemcpyAsync(out_e, doe.p, (size_t)batch * G, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  if (read_and_clear_error_flag(h->stream)) return fail(BFP200_ETIMEOUT, "a bounded device wait timed out");
+  return BFP200_OK;
+}
+
+int bfp200_rmsnorm_fp(bfp200_handle* h, const double* x, const double* gamma, int n, int ncols, double eps,
+                      double* out) {
+  if (!h || !x || !gamma || !out || n <= 0 || n % 16 || ncols <= 0 || n > 8192)
+    return fail(BFP200_EINVAL, "rmsnorm_fp: bad arguments");
+  CK(cudaSetDevice(h->device));
+  DBuf<double> dx, dg, dout;
+  CK(dx.ensure((size_t)n * ncols)); CK(dg.ensure(n)); CK(dout.ensure((size_t)n * ncols));
+  CK(cudaMemcpyAsync(dx.p, x, (size_t)n * ncols * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(dg.p, gamma, (size_t)n * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(launch_rmsnorm_fp(dx.p, dg.p, eps, n, ncols, dout.p, h->stream));
+  CK(cudaMemcpyAsync(out, dout.p, (size_t)n * ncols * 8, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_silu_fp(bfp200_handle* h, const double* x, size_t n, double* out) {
+  if (!h || (n && (!x || !out)) || n % 16) return fail(BFP200_EINVAL, "silu_fp: bad arguments");
+  if (!n) return BFP200_OK;
+  CK(cudaSetDevice(h->device));
+  DBuf<double> dx, dout;
+  CK(dx.ensure(n)); CK(dout.ensure(n));
+  CK(cudaMemcpyAsync(dx.p, x, n * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(launch_silu_fp(dx.p, (long long)n, dout.p, h->stream));
+  CK(cudaMemcpyAsync(out, dout.p, n * 8, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_softmax_fp(bfp200_handle* h, const double* x, int n, int ncols, double* out) {
+  if (!h || !x || !out || n <= 0 || ncols <= 0 || n > 4096) return fail(BFP200_EINVAL, "softmax_fp: bad arguments");
+  CK(cudaSetDevice(h->device));
+  DBuf<double> dx, dout;
+  CK(dx.ensure((size_t)n * ncols)); CK(dout.ensure((size_t)n * ncols));
+  CK(cudaMemcpyAsync(dx.p, x, (size_t)n * ncols * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(launch_softmax_fp(dx.p, n, ncols, dout.p, h->stream));
+  CK(cudaMemcpyAsync(out, dout.p, (size_t)n * ncols * 8, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_rope_fp(bfp200_handle* h, const double* x, const int32_t* pos, int nvec, int HD, double base, double* out) {
+  if (!h || !x || !pos || !out || nvec <= 0 || HD <= 0 || HD % 32) return fail(BFP200_EINVAL, "rope_fp: bad arguments");
+  CK(cudaSetDevice(h->device));
+  std::vector<double> cs((size_t)nvec * HD);
+  for (int i = 0; i < nvec; ++i) {
+    if (pos[i] < 0) return fail(BFP200_EINVAL, "rope_fp: negative position");
+    // one row of the table for this position
+    const int H2 = HD / 2;
+    for (int j = 0; j < H2; ++j) {
+      const double expo = (double)(2 * j) / (double)HD;
+      const double pw = (expo == 0.0) ? 1.0 : std::pow(base, expo);
+      const double theta = 1.0 / pw * (double)pos[i];
+      cs[(size_t)i * HD + 2 * j] = std::cos(theta);
+      cs[(size_t)i * HD + 2 * j + 1] = std::sin(theta);
+    }
+  }
+  DBuf<double> dx, dcs, dout;
+  CK(dx.ensure((size_t)nvec * HD)); CK(dcs.ensure(cs.size())); CK(dout.ensure((size_t)nvec * HD));
+  CK(cudaMemcpyAsync(dx.p, x, (size_t)nvec * HD * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(dcs.p, cs.data(), cs.size() * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(launch_rope_fp(dx.p, dcs.p, HD, nvec, dout.p, h->stream));
+  CK(cudaMemcpyAsync(out, dout.p, (size_t)nvec * HD * 8, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_stage_dims(bfp200_handle* h, int32_t* dims) {
+  if (!h || !dims) return fail(BFP200_EINVAL, "null argument");
+  const int32_t v[BFP200_NSTAGES] = {h->D, h->QD, h->KVD, h->KVD, h->QD, h->D, h->D, h->D, h->FFN, h->FFN, h->FFN, h->D};
+  std::memcpy(dims, v, sizeof(v));
+  return BFP200_OK;
+}
+
+int bfp200_fwd_layer(bfp200_handle* h, int layer, const double* h_in, const int32_t* pos, const int32_t* kv_pos,
+                     int ncols, double* k_cache, double* v_cache, int max_ctx, double* h_out, double* stages) {
+  if (!h || !h_in || !pos || !kv_pos || !k_cache || !v_cache || !h_out || ncols <= 0)
+    return fail(BFP200_EINVAL, "fwd_layer: null argument");
+  if (!h->have_image) return fail(BFP200_ESTATE, "fwd_layer before load_image");
+  if (layer < 0 || layer >= h->NL) return fail(BFP200_EINVAL, "fwd_layer: layer out of range");
+  if (ncols > h->cfg.max_seqs || max_ctx <= 0) return fail(BFP200_EINVAL, "fwd_layer: ncols > max_seqs");
+  for (int c = 0; c < ncols; ++c)
+    if (pos[c] < 0 || pos[c] >= h->MAXC || kv_pos[c] < 0 || kv_pos[c] >= h->MAXC || kv_pos[c] >= max_ctx ||
+        pos[c] != kv_pos[c])
+      return fail(BFP200_EINVAL, "fwd_layer: positions must satisfy pos == kv_pos < min(MAX_CTX, max_ctx)");
+  CK(cudaSetDevice(h->device));
+  CKR(ensure_kv(h, ncols));
+  CKR(ensure_cols(h, ncols));
+  const int D = h->D, HKV = h->HKV, HD = h->HD;
+  // h_in and the cache prefix in exact BFP form
+  std::vector<int16_t> hm((size_t)ncols * D);
+  std::vector<int8_t> he((size_t)ncols * h->NTD);
+  for (size_t t = 0; t < (size_t)ncols * h->NTD; ++t)
+    if (!grid_encode_tile(h_in + t * 16, hm.data() + t * 16, he.data() + t))
+      return fail(BFP200_EINVAL, "fwd_layer: h_in is not on the BFP grid");
+  CK(cudaMemcpyAsync(h->h_m.p, hm.data(), hm.size() * 2, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(h->h_e.p, he.data(), he.size(), cudaMemcpyHostToDevice, h->stream));
+  const size_t slot_stride = (size_t)h->NL * HKV * h->MAXC;   // rows of HD per slot
+  for (int c = 0; c < ncols; ++c) {
+    for (int kvh = 0; kvh < HKV; ++kvh) {
+      const int T = kv_pos[c];
+      if (T == 0) continue;
+      std::vector<int16_t> kmh((size_t)T * HD), vmh((size_t)T * HD);
+      std::vector<int8_t> keh((size_t)T * HD / 16), veh((size_t)T * HD / 16);
+      for (int t = 0; t < T; ++t)
+        for (int q = 0; q < HD / 16; ++q) {
+          const size_t src = (((size_t)c * max_ctx + t) * HKV + kvh) * HD + q * 16;
+          if (!grid_encode_tile(k_cache + src, kmh.data() + (size_t)t * HD + q * 16, keh.data() + (size_t)t * HD / 16 + q) ||
+              !grid_encode_tile(v_cache + src, vmh.data() + (size_t)t * HD + q * 16, veh.data() + (size_t)t * HD / 16 + q))
+            return fail(BFP200_EINVAL, "fwd_layer: KV cache value not on the BFP grid");
+        }
+      const size_t row0 = (size_t)c * slot_stride + ((size_t)layer * HKV + kvh) * h->MAXC;
+      CK(cudaMemcpyAsync(h->km.p + row0 * HD, kmh.data(), kmh.size() * 2, cudaMemcpyHostToDevice, h->stream));
+      CK(cudaMemcpyAsync(h->vm.p + row0 * HD, vmh.data(), vmh.size() * 2, cudaMemcpyHostToDevice, h->stream));
+      CK(cudaMemcpyAsync(h->ke.p + row0 * HD / 16, keh.data(), keh.size(), cudaMemcpyHostToDevice, h->stream));
+      CK(cudaMemcpyAsync(h->ve.p + row0 * HD / 16, veh.data(), veh.size(), cudaMemcpyHostToDevice, h->stream));
+    }
+  }
+  std::vector<int> slots(ncols);
+  std::iota(slots.begin(), slots.end(), 0);
+  CK(cudaMemcpyAsync(h->col_slot.p, slots.data(), ncols * 4, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(h->col_pos.p, pos, ncols * 4, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  StageSink sink;
+  sink.st.resize(BFP200_NSTAGES);
+  CKR(enqueue_layer(h, layer, ncols, stages ? &sink : nullptr));
+  std::vector<double> hout;
+  CKR(download_decoded(h, h->h_m.p, h->h_e.p, D, D, 0, ncols, hout));
+  std::memcpy(h_out, hout.data(), hout.size() * 8);
+  // KV slot kv_pos written back (post-RoPE k, raw v)
+  for (int c = 0; c < ncols; ++c)
+    for (int kvh = 0; kvh < HKV; ++kvh) {
+      const size_t row = (size_t)c * slot_stride + ((size_t)layer * HKV + kvh) * h->MAXC + kv_pos[c];
+      int16_t km_[64], vm_[64];
+      int8_t ke_[4], ve_[4];
+      CK(cudaMemcpyAsync(km_, h->km.p + row * HD, HD * 2, cudaMemcpyDeviceToHost, h->stream));
+      CK(cudaMemcpyAsync(vm_, h->vm.p + row * HD, HD * 2, cudaMemcpyDeviceToHost, h->stream));
+      CK(cudaMemcpyAsync(ke_, h->ke.p + row * HD / 16, HD / 16, cudaMemcpyDeviceToHost, h->stream));
+      CK(cudaMemcpyAsync(ve_, h->ve.p + row * HD / 16, HD / 16, cudaMemcpyDeviceToHost, h->stream));
+      CK(cudaStreamSynchronize(h->stream));
+      const size_t dst = (((size_t)c * max_ctx + kv_pos[c]) * HKV + kvh) * HD;
+      for (int i = 0; i < HD; ++i) {
+        k_cache[dst + i] = bfp_decode(km_[i], ke_[i / 16]);
+        v_cache[dst + i] = bfp_decode(vm_[i], ve_[i / 16]);
+      }
+    }
+  if (stages) {
+    // k stage = post-RoPE k (just read back), per column
+    sink.st[2].assign((size_t)ncols * h->KVD, 0.0);
+    for (int c = 0; c < ncols; ++c)
+      for (int i = 0; i < h->KVD; ++i)
+        sink.st[2][(size_t)c * h->KVD + i] = k_cache[(((size_t)c * max_ctx + kv_pos[c]) * HKV + i / HD) * HD + i % HD];
+    int32_t dims[BFP200_NSTAGES];
+    bfp200_stage_dims(h, dims);
+    size_t o = 0;
+    for (int c = 0; c < ncols; ++c)
+      for (int s = 0; s < BFP200_NSTAGES; ++s) {
+        std::memcpy(stages + o, sink.st[s].data() + (size_t)c * dims[s], (size_t)dims[s] * 8);
+        o += dims[s];
+      }
+  }
+  if (read_and_clear_error_flag(h->stream)) return fail(BFP200_ETIMEOUT, "a bounded device wait timed out");
+  return BFP200_OK;
+}
+
+}  // extern "C"

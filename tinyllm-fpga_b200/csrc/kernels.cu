@@ -1,0 +1,1083 @@
+// kernels.cu -- sm_100a kernels of the BFP SmolLM2-135M decode path.
+//
+// Each kernel restates one stage of the reference simulator
+// (jrrk2/tinyllm-fpga rtl/vc707/host/gen_smollm_blockfp_full.py, cited by
+// line) with bit-identical results.  Compile with -fmad=false.
+#include "bfp_device.cuh"
+#include "kernels.cuh"
+
+#include <cmath>
+#include <cstdio>
+
+namespace bfp {
+
+// ---------------------------------------------------------------------------
+// PTX helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// d = c + a.h0*b.b0 + a.h1*b.b1 (lo) / a.h0*b.b2 + a.h1*b.b3 (hi); a: 2 x s16
+__device__ __forceinline__ int dp2a_lo_ss(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int dp2a_hi_ss(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int dp2a_lo_su(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int dp2a_hi_su(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned phase) {
+  unsigned ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(phase) : "memory");
+  return ok != 0;
+}
+// 1-D bulk copy global -> shared (TMA engine), completion on an mbarrier.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait on an mbarrier phase (the copy is local and always completes;
+// the bound only guarantees the kernel cannot spin forever).  Returns false
+// on timeout after a second bounded wait for the copy still in flight.
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned phase) {
+  for (long long it = 0; it < (1LL << 26); ++it)
+    if (mbar_try_wait(bar, phase)) return true;
+  for (long long it = 0; it < (1LL << 26); ++it)
+    if (mbar_try_wait(bar, phase)) break;
+  return false;
+}
+
+__device__ int g_error_flag;   // set by a kernel whose bounded wait timed out
+
+// ---------------------------------------------------------------------------
+// bfp_matmul: out[c][r] = quant( clip(sum_t floor_shift(S[r,c,t])) * 2^(M-30) )
+// restating matvec_hw_golden (:217-233) for many columns, with the
+// residual (:285,:293) or SwiGLU (:290-291) stage fused into the epilogue.
+//
+// Exactness: tile sums S = sum_k x_k w_k are formed as 256*A + B with
+//   A = sum x_k * (w_k >> 8)   (dp2a s16 x s8, |A| < 2^26)
+//   B = sum x_k * (w_k & 255)  (dp2a s16 x u8, |B| < 2^27)
+// in int32, combined in int64; each tile is floor-shifted by its own
+// exponent gap and accumulated in int64, like the reference's int64 numpy.
+// ---------------------------------------------------------------------------
+constexpr int MM_THREADS = 256;
+constexpr int MM_BC = 8;   // columns per register chunk
+
+struct MMSmem {
+  size_t ws, xs, weall, xeall, ms, red, tot, bar, total;
+  bool stage_all;   // all NT exponents of the CTA's rows/columns fit in shared memory
+};
+
+__host__ __device__ inline MMSmem mm_layout(int rg, int bn, int ntc, int NT) {
+  MMSmem L;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off = (off + bytes + 15) & ~size_t(15); return o; };
+  L.bar = take(16);
+  L.ws = take((size_t)rg * ntc * 512);
+  L.xs = take((size_t)bn * ntc * 32);
+  L.stage_all = ((size_t)rg * NT * 16 + (size_t)bn * NT) <= 24 * 1024;
+  const int ne = L.stage_all ? NT : ntc;
+  L.weall = take((size_t)rg * ne * 16);
+  L.xeall = take((size_t)bn * ne);
+  L.ms = take((size_t)16 * rg * bn * 4);
+  L.red = take((size_t)MM_THREADS * MM_BC * 8);
+  L.tot = take((size_t)16 * rg * bn * 8);
+  L.total = off;
+  return L;
+}
+
+size_t matmul_smem_bytes(int rg, int bn, int ntc, int NT) { return mm_layout(rg, bn, ntc, NT).total; }
+
+template <int RG>
+__global__ void __launch_bounds__(MM_THREADS)
+bfp_matmul_kernel(MatmulArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int ROWS = 16 * RG;
+  constexpr int TL = MM_THREADS / ROWS;
+  const int NT = a.W.NT;
+  const int ntc = (NT + a.ksplit - 1) / a.ksplit;
+  const int t0 = blockIdx.z * ntc;
+  const int nt_here = min(ntc, NT - t0);
+  const int g0 = blockIdx.x * RG;
+  const int c0 = blockIdx.y * a.bn;
+  const int ncol = min(a.bn, a.ncols - c0);
+  const int tid = threadIdx.x;
+  const MMSmem L = mm_layout(RG, a.bn, ntc, NT);
+  unsigned long long* bar = reinterpret_cast<unsigned long long*>(smem + L.bar);
+  unsigned char* Ws = smem + L.ws;
+  unsigned char* Xs = smem + L.xs;
+  int8_t* WeAll = reinterpret_cast<int8_t*>(smem + L.weall);
+  int8_t* XeAll = reinterpret_cast<int8_t*>(smem + L.xeall);
+  int* Ms = reinterpret_cast<int*>(smem + L.ms);
+  long long* red = reinterpret_cast<long long*>(smem + L.red);
+  long long* tot = reinterpret_cast<long long*>(smem + L.tot);
+
+  pdl_trigger();
+  // ---- weights do not depend on earlier kernels: start streaming them now
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0 && nt_here > 0) {
+    const unsigned bytes = (unsigned)nt_here * 512u;
+    mbar_expect_tx(bar, bytes * RG);
+    #pragma unroll
+    for (int gi = 0; gi < RG; ++gi)
+      bulk_g2s(Ws + (size_t)gi * ntc * 512, a.W.wm + ((size_t)(g0 + gi) * NT + t0) * 512, bytes, bar);
+  }
+  const bool stage_all = L.stage_all;
+  if (stage_all) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.W.we + (size_t)g0 * NT * 16);
+    uint4* dst = reinterpret_cast<uint4*>(WeAll);
+    for (int i = tid; i < RG * NT; i += MM_THREADS) dst[i] = src[i];
+  } else {
+    for (int i = tid; i < RG * ntc; i += MM_THREADS) {
+      const int gi = i / ntc, t = i % ntc;
+      if (t < nt_here)
+        reinterpret_cast<uint4*>(WeAll)[i] =
+            reinterpret_cast<const uint4*>(a.W.we + ((size_t)(g0 + gi) * NT + t0 + t) * 16)[0];
+    }
+  }
+  for (int i = tid; i < ROWS * a.bn; i += MM_THREADS) Ms[i] = -100000;
+  // ---- activations come from the previous kernel
+  pdl_wait();
+  for (int i = tid; i < ncol * nt_here * 2; i += MM_THREADS) {
+    const int b = i / (nt_here * 2), r = i % (nt_here * 2);
+    const uint4* src = reinterpret_cast<const uint4*>(a.xm + (size_t)(c0 + b) * a.x_ld + (size_t)t0 * 16);
+    reinterpret_cast<uint4*>(Xs + (size_t)b * ntc * 32)[r] = src[r];
+  }
+  const int xe_n = stage_all ? NT : ntc;
+  for (int i = tid; i < ncol * xe_n; i += MM_THREADS) {
+    const int b = i / xe_n, t = i % xe_n;
+    if (stage_all || t < nt_here) XeAll[b * xe_n + t] = a.xe[(size_t)(c0 + b) * a.x_lde + (stage_all ? t : t0 + t)];
+  }
+  __syncthreads();
+  // ---- per (row, column) max tile exponent over the FULL K (:221-222);
+  //      several threads per pair when there are few pairs
+  {
+    const int pairs = ROWS * ncol;
+    const int tsplit = pairs >= MM_THREADS ? 1 : MM_THREADS / pairs;
+    const int nworkers = (MM_THREADS / tsplit) * tsplit;
+    if (tid < nworkers) {
+      const int sub = tid % tsplit;
+      for (int p = tid / tsplit; p < pairs; p += MM_THREADS / tsplit) {
+        const int row = p % ROWS, b = p / ROWS;
+        const int gi = row >> 4, ri = row & 15;
+        int m = -100000;
+        if (stage_all) {
+          for (int t = sub; t < NT; t += tsplit) {
+            const int e = (int)XeAll[b * NT + t] + (int)WeAll[(gi * NT + t) * 16 + ri];
+            m = e > m ? e : m;
+          }
+        } else {
+          const int8_t* xe = a.xe + (size_t)(c0 + b) * a.x_lde;
+          const int8_t* we = a.W.we + (size_t)(g0 + gi) * NT * 16 + ri;
+          for (int t = sub; t < NT; t += tsplit) {
+            const int e = (int)xe[t] + (int)we[(size_t)t * 16];
+            m = e > m ? e : m;
+          }
+        }
+        atomicMax(&Ms[row * a.bn + b], m);
+      }
+    }
+  }
+  __syncthreads();
+  if (nt_here > 0 && !mbar_wait_bounded(bar, 0)) {
+    if (tid == 0) atomicExch(&g_error_flag, 1);
+  }
+  __syncthreads();
+
+  // ---- main loop
+  const int i = tid % ROWS;
+  const int j = tid / ROWS;
+  const int gi = i >> 4, ri = i & 15;
+  for (int cb = 0; cb < ncol; cb += MM_BC) {
+    const int nb = min(MM_BC, ncol - cb);
+    long long acc[MM_BC];
+    int Mr[MM_BC];
+    #pragma unroll
+    for (int b = 0; b < MM_BC; ++b) {
+      acc[b] = 0;
+      Mr[b] = (b < nb) ? Ms[i * a.bn + cb + b] : 0;
+    }
+    for (int t = j; t < nt_here; t += TL) {
+      const uint4* wp = reinterpret_cast<const uint4*>(Ws + ((size_t)gi * ntc + t) * 512);
+      const uint4 wh = wp[ri];
+      const uint4 wl = wp[16 + ri];
+      const int we = stage_all ? (int)WeAll[(gi * NT + t0 + t) * 16 + ri] : (int)WeAll[(gi * ntc + t) * 16 + ri];
+      #pragma unroll
+      for (int b = 0; b < MM_BC; ++b) {
+        if (b < nb) {
+          const uint4* xp = reinterpret_cast<const uint4*>(Xs + ((size_t)(cb + b) * ntc + t) * 32);
+          const uint4 x0 = xp[0], x1 = xp[1];
+          int A = 0, B = 0;
+          A = dp2a_lo_ss(x0.x, wh.x, A); A = dp2a_hi_ss(x0.y, wh.x, A);
+          A = dp2a_lo_ss(x0.z, wh.y, A); A = dp2a_hi_ss(x0.w, wh.y, A);
+          A = dp2a_lo_ss(x1.x, wh.z, A); A = dp2a_hi_ss(x1.y, wh.z, A);
+          A = dp2a_lo_ss(x1.z, wh.w, A); A = dp2a_hi_ss(x1.w, wh.w, A);
+          B = dp2a_lo_su(x0.x, wl.x, B); B = dp2a_hi_su(x0.y, wl.x, B);
+          B = dp2a_lo_su(x0.z, wl.y, B); B = dp2a_hi_su(x0.w, wl.y, B);
+          B = dp2a_lo_su(x1.x, wl.z, B); B = dp2a_hi_su(x1.y, wl.z, B);
+          B = dp2a_lo_su(x1.z, wl.w, B); B = dp2a_hi_su(x1.w, wl.w, B);
+          const long long S = ((long long)A << 8) + (long long)B;
+          const int sh = Mr[b] - (stage_all ? (int)XeAll[(cb + b) * NT + t0 + t] : (int)XeAll[(cb + b) * ntc + t]) - we;
+          acc[b] += (sh > ALIGN_MAX) ? 0LL : (S >> sh);
+        }
+      }
+    }
+    #pragma unroll
+    for (int b = 0; b < MM_BC; ++b) red[((size_t)j * ROWS + i) * MM_BC + b] = acc[b];
+    __syncthreads();
+    for (int o = tid; o < ROWS * MM_BC; o += MM_THREADS) {
+      const int row = o % ROWS, b = o / ROWS;
+      if (b < nb) {
+        long long s = 0;
+        for (int jj = 0; jj < TL; ++jj) s += red[((size_t)jj * ROWS + row) * MM_BC + b];
+        if (a.ksplit == 1) {
+          tot[row * a.bn + cb + b] = s;
+        } else {
+          atomicAdd(reinterpret_cast<unsigned long long*>(
+                        &a.acc[(size_t)(g0 * 16 + row) * a.acc_ld + c0 + cb + b]),
+                    (unsigned long long)s);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- K split: the last CTA to arrive owns the epilogue
+  if (a.ksplit > 1) {
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned id = blockIdx.y * gridDim.x + blockIdx.x;
+      const unsigned old = atomicAdd(&a.counters[id], 1u);
+      s_last = (old == (unsigned)a.ksplit - 1);
+      if (s_last) a.counters[id] = 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int o = tid; o < ROWS * ncol; o += MM_THREADS) {
+      const int row = o % ROWS, b = o / ROWS;
+      tot[row * a.bn + b] = (long long)atomicExch(
+          reinterpret_cast<unsigned long long*>(&a.acc[(size_t)(g0 * 16 + row) * a.acc_ld + c0 + b]), 0ULL);
+    }
+    __syncthreads();
+  }
+
+  // ---- epilogue: 16 lanes per (row group, column)
+  const int lane = tid & 31;
+  const int l16 = tid & 15;
+  const int slot16 = tid >> 4;   // 16 slots per pass
+  const int ngroups_out = (a.epi == EPI_SWIGLU) ? RG / 2 : RG;
+  const int npairs = ngroups_out * ncol;
+  const int npairs_pad = (npairs + 15) & ~15;
+  for (int p = slot16; p < npairs_pad; p += 16) {
+    const bool valid = p < npairs;
+    const int go = valid ? p % ngroups_out : 0;
+    const int b = valid ? p / ngroups_out : 0;
+    const int col = c0 + b;
+    if (a.epi != EPI_SWIGLU) {
+      const int row = go * 16 + l16;
+      double out_real = 0.0;
+      if (valid) {
+        long long acc = tot[row * a.bn + b];
+        acc = acc > SAT_HI ? SAT_HI : (acc < SAT_LO ? SAT_LO : acc);        // :229-231
+        out_real = (double)acc * pow2(Ms[row * a.bn + b] - 30);            // :232, exact
+      }
+      int qe;
+      int16_t qm = tile_quantize_16lanes(out_real, &qe);                    // :233
+      const size_t orow = (size_t)(g0 + go) * 16 + l16;
+      if (a.epi == EPI_STORE) {
+        if (valid) {
+          a.om[(size_t)col * a.o_ld + orow] = qm;
+          if (l16 == 0) a.oe[(size_t)col * a.o_lde + g0 + go] = (int8_t)qe;
+        }
+      } else {  // EPI_RESIDUAL: fpq(h + o)
+        double hv = 0.0;
+        if (valid) hv = bfp_decode(a.rm[(size_t)col * a.o_ld + orow], a.re[(size_t)col * a.o_lde + g0 + go]);
+        const double y = __dadd_rn(hv, bfp_decode(qm, qe));
+        int ye;
+        int16_t ym = tile_quantize_16lanes(y, &ye);
+        if (valid) {
+          a.om[(size_t)col * a.o_ld + orow] = ym;
+          if (l16 == 0) a.oe[(size_t)col * a.o_lde + g0 + go] = (int8_t)ye;
+        }
+      }
+    } else {
+      // rows of the pair: g = group 2*go, u = group 2*go+1
+      double gr = 0.0, ur = 0.0;
+      if (valid) {
+        const int rowg = (2 * go) * 16 + l16, rowu = (2 * go + 1) * 16 + l16;
+        long long ag = tot[rowg * a.bn + b], au = tot[rowu * a.bn + b];
+        ag = ag > SAT_HI ? SAT_HI : (ag < SAT_LO ? SAT_LO : ag);
+        au = au > SAT_HI ? SAT_HI : (au < SAT_LO ? SAT_LO : au);
+        gr = (double)ag * pow2(Ms[rowg * a.bn + b] - 30);
+        ur = (double)au * pow2(Ms[rowu * a.bn + b] - 30);
+      }
+      int ge, ue, se, pe;
+      const int16_t gm = tile_quantize_16lanes(gr, &ge);
+      const int16_t um = tile_quantize_16lanes(ur, &ue);
+      const double gv = bfp_decode(gm, ge), uv = bfp_decode(um, ue);
+      // silu_fp (:241-242): fpq(x / (1 + exp(-x)))
+      const double s = __ddiv_rn(gv, __dadd_rn(1.0, exp(-gv)));
+      const int16_t sm = tile_quantize_16lanes(s, &se);
+      // mlp = fpq(silu * u) (:290), then tile_quantize(mlp) (:291)
+      const double prod = __dmul_rn(bfp_decode(sm, se), uv);
+      int16_t pm = tile_quantize_16lanes(prod, &pe);
+      const unsigned bal = __ballot_sync(0xffffffffu, pm == (int16_t)-32768);
+      const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
+      const bool bump = has_min && pe < 127;
+      pm = requant_mant(pm, bump);
+      pe = requant_exp(pe, has_min);
+      if (valid) {
+        const size_t og = (size_t)g0 / 2 + go;
+        a.om[(size_t)col * a.o_ld + og * 16 + l16] = pm;
+        if (l16 == 0) a.oe[(size_t)col * a.o_lde + og] = (int8_t)pe;
+      }
+    }
+  }
+}
+
+cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s, bool pdl) {
+  const int ntc = (a.W.NT + a.ksplit - 1) / a.ksplit;
+  const size_t smem = mm_layout(a.rg, a.bn, ntc, a.W.NT).total;
+  dim3 grid(a.W.G / a.rg, (a.ncols + a.bn - 1) / a.bn, a.ksplit);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(MM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  switch (a.rg) {
+    case 1: return cudaLaunchKernelEx(&cfg, bfp_matmul_kernel<1>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, bfp_matmul_kernel<2>, a);
+    case 4: return cudaLaunchKernelEx(&cfg, bfp_matmul_kernel<4>, a);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+// Generic PDL-aware launcher for the simple kernels below.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------------------
+// rmsnorm_fp + tile_quantize (:236-238, :263-264 / :286-287).  One warp per
+// column.  Output is the matvec-ready form tile_quantize(fpq(y)).
+// ---------------------------------------------------------------------------
+constexpr int NORM_WARPS = 4;
+
+__device__ __forceinline__ void warp_rms_factor(const double* sq, int D, int* s_lo, int* s_len,
+                                                double* s_val, double eps, double* r_out) {
+  const double s = np_sum_warp(sq, D, s_lo, s_len, s_val);
+  const double mean = __ddiv_rn(s, (double)D);              // np.mean = sum / n
+  *r_out = __dsqrt_rn(__dadd_rn(mean, eps));                // np.sqrt(mean + eps)
+}
+
+__global__ void __launch_bounds__(NORM_WARPS * 32)
+rmsnorm_quant_kernel(const int16_t* xm, const int8_t* xe, const double* gamma, double eps, int D, int ncols,
+                     int16_t* om, int8_t* oe) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * NORM_WARPS + warp;
+  if (c >= ncols) return;
+  const int NT = D / 16;
+  double* sq = reinterpret_cast<double*>(smem) + (size_t)warp * (D + 64 + 96);
+  double* s_val = sq + D;
+  int* s_lo = reinterpret_cast<int*>(s_val + 64);
+  int* s_len = s_lo + 96;
+  for (int i = lane; i < D; i += 32) {
+    const double x = bfp_decode(xm[(size_t)c * D + i], xe[(size_t)c * NT + i / 16]);
+    sq[i] = __dmul_rn(x, x);
+  }
+  __syncwarp();
+  double r;
+  warp_rms_factor(sq, D, s_lo, s_len, s_val, eps, &r);
+  for (int base = 0; base < D; base += 32) {
+    const int i = base + lane;
+    const bool valid = i < D;
+    double y = 0.0;
+    if (valid) {
+      const double x = bfp_decode(xm[(size_t)c * D + i], xe[(size_t)c * NT + i / 16]);
+      y = __ddiv_rn(__dmul_rn(x, gamma[i]), r);             // x * gamma / sqrt(v)
+    }
+    int e;
+    int16_t m = tile_quantize_16lanes(y, &e);               // fpq (:238)
+    const unsigned bal = __ballot_sync(0xffffffffu, valid && m == (int16_t)-32768);
+    const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
+    m = requant_mant(m, has_min && e < 127);               // tile_quantize(n) (:264)
+    e = requant_exp(e, has_min);
+    if (valid) {
+      om[(size_t)c * D + i] = m;
+      if ((i & 15) == 0) oe[(size_t)c * NT + i / 16] = (int8_t)e;
+    }
+  }
+}
+
+cudaError_t launch_rmsnorm(const int16_t* xm, const int8_t* xe, const double* gamma, double eps, int D, int ncols,
+                           int16_t* om, int8_t* oe, cudaStream_t s, bool pdl) {
+  const size_t smem = (size_t)NORM_WARPS * (D + 64 + 96) * 8;
+  return launch_ex(rmsnorm_quant_kernel, dim3((ncols + NORM_WARPS - 1) / NORM_WARPS), dim3(NORM_WARPS * 32),
+                   smem, s, pdl, xm, xe, gamma, eps, D, ncols, om, oe);
+}
+
+// ---------------------------------------------------------------------------
+// rope_fp on every q and k head (:250-258, :268-269) + KV write (:270-272).
+// rope_cs[pos][j] = (cos, sin) of theta_j(pos), computed on the host with
+// the same libm calls as the reference's math.cos / math.sin.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+rope_kv_kernel(const int16_t* qkv_m, const int8_t* qkv_e, int16_t* qr_m, int8_t* qr_e, KvArena kv, int layer,
+               ColDesc cols, const double* rope_cs, Dims d, int ncols) {
+  __shared__ double xs[256];
+  pdl_trigger();
+  pdl_wait();
+  const int c = blockIdx.x;
+  const int slot = cols.slot[c], pos = cols.pos[c];
+  const int HD = d.HD, H2 = HD / 2;
+  const int R = (d.HQ + 2 * d.HKV) * HD;         // rows of the fused qkv output
+  const int RT = R / 16;
+  const int heads = d.HQ + d.HKV;
+  const int tid = threadIdx.x;
+  const int hpb = 256 / HD;                       // heads per pass
+  for (int hb = 0; hb < heads; hb += hpb) {
+    const int hh = hb + tid / HD;
+    const int dd = tid % HD;
+    const bool valid = hh < heads;
+    double x = 0.0;
+    if (valid) {
+      const int row = hh * HD + dd;
+      x = bfp_decode(qkv_m[(size_t)c * R + row], qkv_e[(size_t)c * RT + row / 16]);
+    }
+    xs[tid] = x;
+    __syncthreads();
+    double out = 0.0;
+    if (valid) {
+      const int jj = dd < H2 ? dd : dd - H2;
+      const double cs = rope_cs[((size_t)pos * H2 + jj) * 2 + 0];
+      const double sn = rope_cs[((size_t)pos * H2 + jj) * 2 + 1];
+      const double av = xs[(tid / HD) * HD + jj], bv = xs[(tid / HD) * HD + jj + H2];
+      out = dd < H2 ? __dsub_rn(__dmul_rn(av, cs), __dmul_rn(bv, sn))     // a*c - b*s
+                    : __dadd_rn(__dmul_rn(bv, cs), __dmul_rn(av, sn));    // b*c + a*s
+    }
+    int e;
+    const int16_t m = tile_quantize_16lanes(out, &e);
+    if (valid) {
+      if (hh < d.HQ) {
+        qr_m[(size_t)c * d.HQ * HD + hh * HD + dd] = m;
+        if ((dd & 15) == 0) qr_e[(size_t)c * (d.HQ * HD / 16) + (hh * HD + dd) / 16] = (int8_t)e;
+      } else {
+        const int kvh = hh - d.HQ;
+        const size_t base = (((size_t)slot * d.NL + layer) * d.HKV + kvh) * d.MAX_CTX + pos;
+        kv.km[base * HD + dd] = m;
+        if ((dd & 15) == 0) kv.ke[base * (HD / 16) + dd / 16] = (int8_t)e;
+      }
+    }
+    __syncthreads();
+  }
+  // v rows copied as produced by the matvec (kv['v'][kv_pos] = v, :272)
+  for (int i = tid; i < d.HKV * HD; i += 256) {
+    const int kvh = i / HD, dd = i % HD;
+    const int row = (d.HQ + d.HKV) * HD + i;
+    const size_t base = (((size_t)slot * d.NL + layer) * d.HKV + kvh) * d.MAX_CTX + pos;
+    kv.vm[base * HD + dd] = qkv_m[(size_t)c * R + row];
+    if ((dd & 15) == 0) kv.ve[base * (HD / 16) + dd / 16] = qkv_e[(size_t)c * RT + row / 16];
+  }
+}
+
+cudaError_t launch_rope_kv(const int16_t* qkv_m, const int8_t* qkv_e, int16_t* qr_m, int8_t* qr_e, KvArena kv,
+                           int layer, ColDesc cols, const double* rope_cs, Dims d, int ncols, cudaStream_t s,
+                           bool pdl) {
+  return launch_ex(rope_kv_kernel, dim3(ncols), dim3(256), 0, s, pdl, qkv_m, qkv_e, qr_m, qr_e, kv, layer, cols,
+                   rope_cs, d, ncols);
+}
+
+// ---------------------------------------------------------------------------
+// GQA attention (:273-283): exact scores, softmax_fp, sequential
+// accumulation attn += sm[t] * v[t], fpq, then tile_quantize for the O matvec.
+// ---------------------------------------------------------------------------
+constexpr int ATT_THREADS = 128;
+
+__global__ void __launch_bounds__(ATT_THREADS)
+attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
+                 double sqrt_hd, int16_t* am, int8_t* ae) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_qm[64];
+  __shared__ int s_qe[4];
+  __shared__ double s_red[ATT_THREADS / 32];
+  __shared__ double s_bcast;
+  __shared__ int s_lo[96], s_len[96];
+  __shared__ double s_val[96];
+  pdl_trigger();
+  pdl_wait();
+  const int c = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int slot = cols.slot[c], pos = cols.pos[c];
+  const int T = pos + 1;
+  const int grp = d.HQ / d.HKV;
+  const int kvh = h / grp;
+  const int HD = 64;
+  double* sc = reinterpret_cast<double*>(smem);
+  if (tid < HD) s_qm[tid] = qr_m[(size_t)c * d.HQ * HD + h * HD + tid];
+  if (tid < 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h * 4 + tid];
+  __syncthreads();
+  const size_t kbase = (((size_t)slot * d.NL + layer) * d.HKV + kvh) * d.MAX_CTX;
+  // scores[t] = float(np.dot(q, k_t)) / math.sqrt(HD)   (:278)
+  double lmax = -INFINITY;
+  for (int t = tid; t < T; t += ATT_THREADS) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
+    const int8_t* ke = kv.ke + (kbase + t) * 4;
+    long long S[4];
+    int E[4];
+    #pragma unroll
+    for (int jt = 0; jt < 4; ++jt) {
+      const uint4 k0 = kr[jt * 2], k1 = kr[jt * 2 + 1];
+      const unsigned w[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+      long long s = 0;
+      #pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int lo = (int)(int16_t)(w[u] & 0xFFFF), hi = (int)(int16_t)(w[u] >> 16);
+        s += (long long)(s_qm[jt * 16 + 2 * u] * lo) + (long long)(s_qm[jt * 16 + 2 * u + 1] * hi);
+      }
+      S[jt] = s;
+      E[jt] = s_qe[jt] + (int)ke[jt];
+    }
+    const double v = __ddiv_rn(exact_tile_dot4(S, E), sqrt_hd);
+    sc[t] = v;
+    lmax = v > lmax ? v : lmax;
+  }
+  // softmax_fp (:245-247): e = exp(x - max); e / e.sum()
+  for (int off = 16; off; off >>= 1) {
+    const double o = __shfl_xor_sync(0xffffffffu, lmax, off);
+    lmax = o > lmax ? o : lmax;
+  }
+  if (lane == 0) s_red[warp] = lmax;
+  __syncthreads();
+  double mx = s_red[0];
+  for (int w = 1; w < ATT_THREADS / 32; ++w) mx = s_red[w] > mx ? s_red[w] : mx;
+  for (int t = tid; t < T; t += ATT_THREADS) sc[t] = exp(__dsub_rn(sc[t], mx));
+  __syncthreads();
+  if (warp == 0) {
+    const double S = np_sum_warp(sc, T, s_lo, s_len, s_val);
+    if (lane == 0) s_bcast = S;
+  }
+  __syncthreads();
+  const double Ssum = s_bcast;
+  for (int t = tid; t < T; t += ATT_THREADS) sc[t] = __ddiv_rn(sc[t], Ssum);
+  __syncthreads();
+  // attn[h] += sm[t] * v[t]  sequentially in t (:280-281)
+  if (tid < 64) {
+    double acc = 0.0;
+    const int16_t* vr = kv.vm + kbase * HD + tid;
+    const int8_t* ve = kv.ve + kbase * 4 + (tid >> 4);
+    #pragma unroll 4
+    for (int t = 0; t < T; ++t) {
+      const double vv = bfp_decode(vr[(size_t)t * HD], ve[(size_t)t * 4]);
+      acc = __dadd_rn(acc, __dmul_rn(sc[t], vv));
+    }
+    int e;
+    int16_t m = tile_quantize_16lanes(acc, &e);             // fpq(attn)   (:282)
+    const unsigned bal = __ballot_sync(0xffffffffu, m == (int16_t)-32768);
+    const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
+    m = requant_mant(m, has_min && e < 127);               // tile_quantize(attn) (:283)
+    e = requant_exp(e, has_min);
+    am[(size_t)c * d.HQ * HD + h * HD + tid] = m;
+    if ((tid & 15) == 0) ae[(size_t)c * d.HQ * 4 + h * 4 + tid / 16] = (int8_t)e;
+  }
+}
+
+cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
+                             int ncols, int16_t* am, int8_t* ae, cudaStream_t s, bool pdl) {
+  const size_t smem = (size_t)d.MAX_CTX * 8;
+  return launch_ex(attention_kernel, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
+                   cols, d, std::sqrt((double)d.HD), am, ae);
+}
+
+// ---------------------------------------------------------------------------
+// Embedding row (:411-412, :434): h = embed_q[tid] (the image's BFP row).
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(const int16_t* emb_m, const int8_t* emb_e, const int* tokens, int D, int16_t* hm,
+                             int8_t* he) {
+  pdl_trigger();
+  pdl_wait();
+  const int c = blockIdx.x;
+  const int tok = tokens[c];
+  const int NT = D / 16;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) hm[(size_t)c * D + i] = emb_m[(size_t)tok * D + i];
+  for (int i = threadIdx.x; i < NT; i += blockDim.x) he[(size_t)c * NT + i] = emb_e[(size_t)tok * NT + i];
+}
+
+cudaError_t launch_embed(const int16_t* emb_m, const int8_t* emb_e, const int* tokens, int D, int ncols,
+                         int16_t* hm, int8_t* he, cudaStream_t s, bool pdl) {
+  return launch_ex(embed_kernel, dim3(ncols), dim3(128), 0, s, pdl, emb_m, emb_e, tokens, D, hm, he);
+}
+
+// ---------------------------------------------------------------------------
+// Head (:438-440).  head_prep: hn = (h / sqrt(mean(h*h) + eps)) * norm_w_q.
+// head_logits: fp64 logits = hn . embed_v, per-row-block (max, argmax,
+// runner-up).  head_reduce: global argmax (lowest index on ties) and a
+// certificate that any summation order (the reference's BLAS) picks the
+// same index.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(NORM_WARPS * 32)
+head_prep_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, double eps, int D, int ncols, double* hn,
+                 double* hn_norm) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * NORM_WARPS + warp;
+  if (c >= ncols) return;
+  const int NT = D / 16;
+  double* sq = reinterpret_cast<double*>(smem) + (size_t)warp * (D + 64 + 96);
+  double* s_val = sq + D;
+  int* s_lo = reinterpret_cast<int*>(s_val + 64);
+  int* s_len = s_lo + 96;
+  for (int i = lane; i < D; i += 32) {
+    const double x = bfp_decode(hm[(size_t)c * D + i], he[(size_t)c * NT + i / 16]);
+    sq[i] = __dmul_rn(x, x);
+  }
+  __syncwarp();
+  double r;
+  warp_rms_factor(sq, D, s_lo, s_len, s_val, eps, &r);
+  double ss = 0.0;
+  for (int i = lane; i < D; i += 32) {
+    const double x = bfp_decode(hm[(size_t)c * D + i], he[(size_t)c * NT + i / 16]);
+    const double y = __dmul_rn(__ddiv_rn(x, r), norm_w[i]);
+    hn[(size_t)c * D + i] = y;
+    ss = fma(y, y, ss);
+  }
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if (lane == 0) hn_norm[c] = sqrt(ss) * (1.0 + 1e-12);
+}
+
+cudaError_t launch_head_prep(const int16_t* hm, const int8_t* he, const double* norm_w, double eps, int D, int ncols,
+                             double* hn, double* hn_norm, cudaStream_t s, bool pdl) {
+  const size_t smem = (size_t)NORM_WARPS * (D + 64 + 96) * 8;
+  return launch_ex(head_prep_kernel, dim3((ncols + NORM_WARPS - 1) / NORM_WARPS), dim3(NORM_WARPS * 32), smem, s,
+                   pdl, hm, he, norm_w, eps, D, ncols, hn, hn_norm);
+}
+
+template <int RT, int CT, int TR, int TC>
+__global__ void __launch_bounds__(256)
+head_logits_kernel(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, const double* hn, int ncols,
+                   double* part_val, int* part_idx, double* part_second) {
+  static_assert((RT / TR) * (CT / TC) == 256, "thread tiling");
+  __shared__ double Es[16][RT + 1];
+  __shared__ double Hs[16][CT + 1];
+  __shared__ double s_val[RT / TR][CT];
+  __shared__ int s_idx[RT / TR][CT];
+  __shared__ double s_sec[RT / TR][CT];
+  pdl_trigger();
+  const int tid = threadIdx.x;
+  const int tx = tid % (CT / TC), ty = tid / (CT / TC);
+  const int v0 = blockIdx.x * RT, c0 = blockIdx.y * CT;
+  const int NT = D / 16;
+  double acc[TR][TC];
+  #pragma unroll
+  for (int a = 0; a < TR; ++a)
+    #pragma unroll
+    for (int b = 0; b < TC; ++b) acc[a][b] = 0.0;
+  pdl_wait();
+  for (int t = 0; t < NT; ++t) {
+    for (int o = tid; o < RT * 16; o += 256) {
+      const int r = o / 16, k = o % 16;
+      const int v = v0 + r;
+      double val = 0.0;
+      if (v < VOCAB) val = bfp_decode(emb_m[(size_t)v * D + t * 16 + k], emb_e[(size_t)v * NT + t]);
+      Es[k][r] = val;
+    }
+    for (int o = tid; o < CT * 16; o += 256) {
+      const int cc = o / 16, k = o % 16;
+      Hs[k][cc] = (c0 + cc < ncols) ? hn[(size_t)(c0 + cc) * D + t * 16 + k] : 0.0;
+    }
+    __syncthreads();
+    #pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      double av[TR], bv[TC];
+      #pragma unroll
+      for (int a = 0; a < TR; ++a) av[a] = Es[k][ty * TR + a];
+      #pragma unroll
+      for (int b = 0; b < TC; ++b) bv[b] = Hs[k][tx * TC + b];
+      #pragma unroll
+      for (int a = 0; a < TR; ++a)
+        #pragma unroll
+        for (int b = 0; b < TC; ++b) acc[a][b] = fma(av[a], bv[b], acc[a][b]);
+    }
+    __syncthreads();
+  }
+  // per thread: best / runner-up among its TR rows, per column
+  #pragma unroll
+  for (int b = 0; b < TC; ++b) {
+    double best = -INFINITY, sec = -INFINITY;
+    int bi = 0x7fffffff;
+    #pragma unroll
+    for (int a = 0; a < TR; ++a) {
+      const int v = v0 + ty * TR + a;
+      if (v >= VOCAB) continue;
+      const double x = acc[a][b];
+      if (x > best) { sec = best; best = x; bi = v; }
+      else if (x > sec) sec = x;
+    }
+    s_val[ty][tx * TC + b] = best;
+    s_idx[ty][tx * TC + b] = bi;
+    s_sec[ty][tx * TC + b] = sec;
+  }
+  __syncthreads();
+  for (int cc = tid; cc < CT; cc += 256) {
+    if (c0 + cc >= ncols) continue;
+    double best = -INFINITY, sec = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int y = 0; y < RT / TR; ++y) {   // ascending row order: ties keep the lowest index
+      const double x = s_val[y][cc];
+      const int xi = s_idx[y][cc];
+      const double xs = s_sec[y][cc];
+      if (x > best || (x == best && xi < bi)) {
+        sec = fmax(sec, best);
+        best = x; bi = xi;
+      } else {
+        sec = fmax(sec, x);
+      }
+      sec = fmax(sec, xs);
+    }
+    const size_t o = (size_t)(c0 + cc) * gridDim.x + blockIdx.x;
+    part_val[o] = best; part_idx[o] = bi; part_second[o] = sec;
+  }
+}
+
+cudaError_t launch_head_logits(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, const double* hn,
+                               int ncols, double* part_val, int* part_idx, double* part_second, int* n_rowblocks,
+                               cudaStream_t s, bool pdl) {
+  if (ncols <= 4) {
+    constexpr int RT = 256, CT = 4;
+    *n_rowblocks = (VOCAB + RT - 1) / RT;
+    return launch_ex(head_logits_kernel<RT, CT, 4, 1>, dim3(*n_rowblocks, (ncols + CT - 1) / CT), dim3(256), 0, s,
+                     pdl, emb_m, emb_e, VOCAB, D, hn, ncols, part_val, part_idx, part_second);
+  }
+  constexpr int RT = 64, CT = 64;
+  *n_rowblocks = (VOCAB + RT - 1) / RT;
+  return launch_ex(head_logits_kernel<RT, CT, 4, 4>, dim3(*n_rowblocks, (ncols + CT - 1) / CT), dim3(256), 0, s,
+                   pdl, emb_m, emb_e, VOCAB, D, hn, ncols, part_val, part_idx, part_second);
+}
+
+__global__ void head_reduce_kernel(const double* part_val, const int* part_idx, const double* part_second, int nrb,
+                                   const double* hn_norm, double emb_norm_max, int D, int* tok_out, int* cert_out) {
+  pdl_trigger();
+  pdl_wait();
+  const int c = blockIdx.x;
+  const int lane = threadIdx.x;
+  double best = -INFINITY, sec = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int r = lane; r < nrb; r += 32) {
+    const size_t o = (size_t)c * nrb + r;
+    const double x = part_val[o];
+    const int xi = part_idx[o];
+    if (x > best || (x == best && xi < bi)) { sec = fmax(sec, best); best = x; bi = xi; }
+    else sec = fmax(sec, x);
+    sec = fmax(sec, part_second[o]);
+  }
+  for (int off = 16; off; off >>= 1) {
+    const double ob = __shfl_xor_sync(0xffffffffu, best, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    const double os = __shfl_xor_sync(0xffffffffu, sec, off);
+    if (ob > best || (ob == best && oi < bi)) { sec = fmax(sec, best); best = ob; bi = oi; }
+    else sec = fmax(sec, ob);
+    sec = fmax(sec, os);
+  }
+  if (lane == 0) {
+    // |fl(dot) - dot| <= gamma_D * sum|a_i b_i| <= gamma_D * ||hn|| * ||e_v|| for
+    // every summation order; two orders differ by at most twice that per logit.
+    const double u = 1.1102230246251565e-16;
+    const double gam = (D + 2) * u / (1.0 - (D + 2) * u);
+    const double margin = 4.0 * gam * hn_norm[c] * emb_norm_max * (1.0 + 1e-6);
+    tok_out[c] = bi;
+    cert_out[c] = (best - sec) > margin ? 1 : 0;
+  }
+}
+
+cudaError_t launch_head_reduce(const double* part_val, const int* part_idx, const double* part_second,
+                               int n_rowblocks, const double* hn_norm, double emb_norm_max, int D, int ncols,
+                               int* tok_out, int* cert_out, cudaStream_t s, bool pdl) {
+  return launch_ex(head_reduce_kernel, dim3(ncols), dim3(32), 0, s, pdl, part_val, part_idx, part_second,
+                   n_rowblocks, hn_norm, emb_norm_max, D, tok_out, cert_out);
+}
+
+// ---------------------------------------------------------------------------
+// Standalone ops (module-level functions of the reference)
+// ---------------------------------------------------------------------------
+__global__ void tile_quantize_kernel(const double* v, long long ntiles, int16_t* m, int8_t* e) {
+  const long long total = ntiles * 16;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long base = (long long)blockIdx.x * blockDim.x; base < ((total + 31) / 32) * 32; base += stride) {
+    const long long i = base + threadIdx.x;
+    const bool valid = i < total;
+    int ee;
+    const int16_t mm = tile_quantize_16lanes(valid ? v[i] : 0.0, &ee);
+    if (valid) {
+      m[i] = mm;
+      if ((i & 15) == 0) e[i / 16] = (int8_t)ee;
+    }
+  }
+}
+
+cudaError_t launch_tile_quantize(const double* v, long long ntiles, int16_t* m, int8_t* e, cudaStream_t s) {
+  if (ntiles <= 0) return cudaSuccess;
+  const long long blocks = (ntiles * 16 + 255) / 256;
+  tile_quantize_kernel<<<(unsigned)(blocks < 65535 * 16 ? blocks : 65535 * 16), 256, 0, s>>>(v, ntiles, m, e);
+  return cudaGetLastError();
+}
+
+__global__ void tile_decode_kernel(const int16_t* m, const int8_t* e, long long n, double* v) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    v[i] = bfp_decode(m[i], e[i / 16]);
+}
+
+cudaError_t launch_tile_decode(const int16_t* m, const int8_t* e, long long ntiles, double* v, cudaStream_t s) {
+  if (ntiles <= 0) return cudaSuccess;
+  const long long n = ntiles * 16;
+  const long long blocks = (n + 255) / 256;
+  tile_decode_kernel<<<(unsigned)(blocks < 1048576 ? blocks : 1048576), 256, 0, s>>>(m, e, n, v);
+  return cudaGetLastError();
+}
+
+__global__ void rmsnorm_fp_kernel(const double* x, const double* gamma, double eps, int n, int ncols, double* out) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * NORM_WARPS + warp;
+  if (c >= ncols) return;
+  double* sq = reinterpret_cast<double*>(smem) + (size_t)warp * (n + 64 + 96);
+  double* s_val = sq + n;
+  int* s_lo = reinterpret_cast<int*>(s_val + 64);
+  int* s_len = s_lo + 96;
+  const double* xc = x + (size_t)c * n;
+  for (int i = lane; i < n; i += 32) sq[i] = __dmul_rn(xc[i], xc[i]);
+  __syncwarp();
+  double r;
+  warp_rms_factor(sq, n, s_lo, s_len, s_val, eps, &r);
+  for (int base = 0; base < n; base += 32) {
+    const int i = base + lane;
+    const bool valid = i < n;
+    const double y = valid ? __ddiv_rn(__dmul_rn(xc[i], gamma[i]), r) : 0.0;
+    int e;
+    const int16_t m = tile_quantize_16lanes(y, &e);
+    if (valid) out[(size_t)c * n + i] = bfp_decode(m, e);
+  }
+}
+
+cudaError_t launch_rmsnorm_fp(const double* x, const double* gamma, double eps, int n, int ncols, double* out,
+                              cudaStream_t s) {
+  const size_t smem = (size_t)NORM_WARPS * (n + 64 + 96) * 8;
+  return launch_ex(rmsnorm_fp_kernel, dim3((ncols + NORM_WARPS - 1) / NORM_WARPS), dim3(NORM_WARPS * 32), smem, s,
+                   false, x, gamma, eps, n, ncols, out);
+}
+
+__global__ void silu_fp_kernel(const double* x, long long n, double* out) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long base = (long long)blockIdx.x * blockDim.x; base < ((n + 31) / 32) * 32; base += stride) {
+    const long long i = base + threadIdx.x;
+    const bool valid = i < n;
+    const double xv = valid ? x[i] : 0.0;
+    const double y = __ddiv_rn(xv, __dadd_rn(1.0, exp(-xv)));
+    int e;
+    const int16_t m = tile_quantize_16lanes(y, &e);
+    if (valid) out[i] = bfp_decode(m, e);
+  }
+}
+
+cudaError_t launch_silu_fp(const double* x, long long n, double* out, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const long long blocks = (n + 255) / 256;
+  silu_fp_kernel<<<(unsigned)(blocks < 65535 * 16 ? blocks : 65535 * 16), 256, 0, s>>>(x, n, out);
+  return cudaGetLastError();
+}
+
+__global__ void softmax_fp_kernel(const double* x, int n, double* out) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_lo[96], s_len[96];
+  __shared__ double s_val[96];
+  __shared__ double s_b;
+  const int c = blockIdx.x;
+  const int lane = threadIdx.x;
+  double* e = reinterpret_cast<double*>(smem);
+  const double* xc = x + (size_t)c * n;
+  double mx = -INFINITY;
+  for (int i = lane; i < n; i += 32) mx = xc[i] > mx ? xc[i] : mx;
+  for (int off = 16; off; off >>= 1) {
+    const double o = __shfl_xor_sync(0xffffffffu, mx, off);
+    mx = o > mx ? o : mx;
+  }
+  for (int i = lane; i < n; i += 32) e[i] = exp(__dsub_rn(xc[i], mx));
+  __syncwarp();
+  const double S = np_sum_warp(e, n, s_lo, s_len, s_val);
+  if (lane == 0) s_b = S;
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) out[(size_t)c * n + i] = __ddiv_rn(e[i], s_b);
+}
+
+cudaError_t launch_softmax_fp(const double* x, int n, int ncols, double* out, cudaStream_t s) {
+  return launch_ex(softmax_fp_kernel, dim3(ncols), dim3(32), (size_t)n * 8, s, false, x, n, out);
+}
+
+__global__ void rope_fp_kernel(const double* x, const double* cs, int HD, int nvec, double* out) {
+  const int H2 = HD / 2;
+  const int vec = blockIdx.x;
+  const int dd = threadIdx.x;   // blockDim.x == HD (multiple of 32)
+  const double* xv = x + (size_t)vec * HD;
+  const int jj = dd < H2 ? dd : dd - H2;
+  const double c = cs[(size_t)vec * HD + jj * 2], s = cs[(size_t)vec * HD + jj * 2 + 1];
+  const double a = xv[jj], b = xv[jj + H2];
+  const double y = dd < H2 ? __dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s)) : __dadd_rn(__dmul_rn(b, c), __dmul_rn(a, s));
+  int e;
+  const int16_t m = tile_quantize_16lanes(y, &e);
+  out[(size_t)vec * HD + dd] = bfp_decode(m, e);
+}
+
+cudaError_t launch_rope_fp(const double* x, const double* cs, int HD, int nvec, double* out, cudaStream_t s) {
+  if (HD % 32 != 0) return cudaErrorInvalidValue;
+  rope_fp_kernel<<<nvec, HD, 0, s>>>(x, cs, HD, nvec, out);
+  return cudaGetLastError();
+}
+
+__global__ void pack_weights_kernel(const int16_t* m_ref, const int8_t* e_ref, int R, int NT, uint8_t* wm, int8_t* we,
+                                    int gstride, int goff) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;   // (g, t, r)
+  const long long total = (long long)R * NT;
+  if (idx >= total) return;
+  const int r = (int)(idx % 16);
+  const long long gt = idx / 16;
+  const int t = (int)(gt % NT);
+  const int g = (int)(gt / NT);
+  const int row = g * 16 + r;
+  const size_t gd = (size_t)g * gstride + goff;
+  uint8_t* dst = wm + (gd * NT + t) * 512;
+  for (int k = 0; k < 16; ++k) {
+    const int mv = m_ref[((size_t)row * NT + t) * 16 + k];
+    dst[r * 16 + k] = (uint8_t)((mv >> 8) & 0xFF);
+    dst[256 + r * 16 + k] = (uint8_t)(mv & 0xFF);
+  }
+  we[(gd * NT + t) * 16 + r] = e_ref[(size_t)row * NT + t];
+}
+
+cudaError_t launch_pack_weights(const int16_t* m_ref, const int8_t* e_ref, int R, int NT, uint8_t* wm, int8_t* we,
+                                int gstride, int goff, cudaStream_t s) {
+  const long long total = (long long)R * NT;
+  pack_weights_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(m_ref, e_ref, R, NT, wm, we, gstride, goff);
+  return cudaGetLastError();
+}
+
+__global__ void pack_from_ddr_kernel(const int16_t* ddr_m, const int8_t* ddr_e, int R, int NT, uint8_t* wm,
+                                     int8_t* we, int gstride, int goff) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)R * NT;
+  if (idx >= total) return;
+  const int r = (int)(idx % 16);
+  const long long gt = idx / 16;
+  const int t = (int)(gt % NT);
+  const int g = (int)(gt / NT);
+  const int K = NT * 16;
+  const size_t gd = (size_t)g * gstride + goff;
+  uint8_t* dst = wm + (gd * NT + t) * 512;
+  for (int k = 0; k < 16; ++k) {
+    // mantissa entry (chunk g, col 16t+k): 16 lanes = rows 16g..16g+15
+    const int mv = ddr_m[((size_t)g * K + t * 16 + k) * 16 + r];
+    dst[r * 16 + k] = (uint8_t)((mv >> 8) & 0xFF);
+    dst[256 + r * 16 + k] = (uint8_t)(mv & 0xFF);
+  }
+  we[(gd * NT + t) * 16 + r] = ddr_e[((size_t)g * NT + t) * 16 + r];
+}
+
+cudaError_t launch_pack_from_ddr(const int16_t* ddr_m, const int8_t* ddr_e, int R, int NT, uint8_t* wm, int8_t* we,
+                                 int gstride, int goff, cudaStream_t s) {
+  const long long total = (long long)R * NT;
+  pack_from_ddr_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(ddr_m, ddr_e, R, NT, wm, we, gstride, goff);
+  return cudaGetLastError();
+}
+
+__global__ void row_norms_kernel(const int16_t* m, const int8_t* e, int rows, int D, double* out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int NT = D / 16;
+  double ss = 0.0;
+  for (int i = lane; i < D; i += 32) {
+    const double v = bfp_decode(m[(size_t)warp * D + i], e[(size_t)warp * NT + i / 16]);
+    ss = fma(v, v, ss);
+  }
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if (lane == 0) out[warp] = sqrt(ss) * (1.0 + 1e-12);
+}
+
+cudaError_t launch_row_norms(const int16_t* m, const int8_t* e, int rows, int D, double* out, cudaStream_t s) {
+  row_norms_kernel<<<(rows * 32 + 255) / 256, 256, 0, s>>>(m, e, rows, D, out);
+  return cudaGetLastError();
+}
+
+}  // namespace bfp
+
+namespace bfp {
+int read_and_clear_error_flag(cudaStream_t s) {
+  int v = 0, z = 0;
+  cudaMemcpyFromSymbolAsync(&v, g_error_flag, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  cudaMemcpyToSymbolAsync(g_error_flag, &z, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+  cudaStreamSynchronize(s);
+  return v;
+}
+}  // namespace bfp
+
+namespace bfp {
+cudaError_t init_kernel_attributes() {
+  const int mx = 227 * 1024;
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void* f) {
+    cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    if (r != cudaSuccess) e = r;
+  };
+  set((const void*)bfp_matmul_kernel<1>);
+  set((const void*)bfp_matmul_kernel<2>);
+  set((const void*)bfp_matmul_kernel<4>);
+  set((const void*)rmsnorm_quant_kernel);
+  set((const void*)head_prep_kernel);
+  set((const void*)attention_kernel);
+  set((const void*)rmsnorm_fp_kernel);
+  set((const void*)softmax_fp_kernel);
+  return e;
+}
+}  // namespace bfp

@@ -1,0 +1,113 @@
+// kernels.cuh -- argument structs and launchers for the BFP decode kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace bfp {
+
+// One BFP weight matrix in the device layout used by bfp_matmul:
+//   wm: [G][NT][2 planes][16 rows][16 k] bytes; plane 0 = m >> 8 (signed),
+//       plane 1 = m & 0xFF (unsigned).  512 B per (row group, K tile).
+//   we: [G][NT][16 rows] int8 tile exponents.
+struct DevMat {
+  const uint8_t* wm = nullptr;
+  const int8_t* we = nullptr;
+  int G = 0;    // row groups of 16 (rows = 16 G)
+  int NT = 0;   // K tiles of 16 (K = 16 NT)
+};
+
+enum MatmulEpilogue : int {
+  EPI_STORE = 0,     // out = quant(matvec)                      (q, k, v, generic)
+  EPI_RESIDUAL = 1,  // out = quant(decode(res) + decode(quant(matvec)))   (:285, :293)
+  EPI_SWIGLU = 2,    // groups (2i, 2i+1) = (g, u): out = requant(quant(quant(silu(g)) * u))  (:290-291)
+};
+
+struct MatmulArgs {
+  DevMat W;
+  // activations: column c at xm + c*x_ld (int16, K elements), xe + c*x_lde (int8, NT)
+  const int16_t* xm = nullptr;
+  const int8_t* xe = nullptr;
+  int x_ld = 0, x_lde = 0;
+  int ncols = 0;
+  int epi = EPI_STORE;
+  int16_t* om = nullptr;  // output mantissas, column stride o_ld
+  int8_t* oe = nullptr;   // output exponents, column stride o_lde
+  int o_ld = 0, o_lde = 0;
+  const int16_t* rm = nullptr;  // residual (EPI_RESIDUAL), same layout as the output
+  const int8_t* re = nullptr;
+  long long* acc = nullptr;      // K-split scratch [rows][ncols_cap], zero between uses
+  unsigned* counters = nullptr;  // K-split arrival counters, zero between uses
+  int acc_ld = 0;                // columns per accumulator row
+  int ksplit = 1;
+  int rg = 1;                    // row groups per CTA (1, 2 or 4)
+  int bn = 1;                    // columns per CTA
+};
+
+// Per-column descriptors of a forward pass.
+struct ColDesc {
+  const int* slot = nullptr;  // KV slot of the column
+  const int* pos = nullptr;   // position (step) of the column
+};
+
+struct KvArena {
+  int16_t* km = nullptr;  // [slot][layer][kvh][MAX_CTX][HD]
+  int8_t* ke = nullptr;   // [slot][layer][kvh][MAX_CTX][HD/16]
+  int16_t* vm = nullptr;
+  int8_t* ve = nullptr;
+  int NL = 0, HKV = 0, HD = 64, MAX_CTX = 0;
+};
+
+struct Dims {
+  int D, HQ, HKV, HD, FFN, NL, VOCAB, MAX_CTX;
+};
+
+size_t matmul_smem_bytes(int rg, int bn, int ntc, int NT);
+cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s, bool pdl);
+// Raises the dynamic shared memory limit of every kernel (call once per device).
+cudaError_t init_kernel_attributes();
+// Reads and clears the device flag a bounded wait sets when it gives up.
+int read_and_clear_error_flag(cudaStream_t s);
+
+cudaError_t launch_rmsnorm(const int16_t* xm, const int8_t* xe, const double* gamma, double eps,
+                           int D, int ncols, int16_t* om, int8_t* oe, cudaStream_t s, bool pdl);
+cudaError_t launch_rope_kv(const int16_t* qkv_m, const int8_t* qkv_e, int16_t* qr_m, int8_t* qr_e,
+                           KvArena kv, int layer, ColDesc cols, const double* rope_cs, Dims d,
+                           int ncols, cudaStream_t s, bool pdl);
+cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
+                             ColDesc cols, Dims d, int ncols, int16_t* am, int8_t* ae,
+                             cudaStream_t s, bool pdl);
+cudaError_t launch_embed(const int16_t* emb_m, const int8_t* emb_e, const int* tokens, int D,
+                         int ncols, int16_t* hm, int8_t* he, cudaStream_t s, bool pdl);
+cudaError_t launch_head_prep(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
+                             int D, int ncols, double* hn, double* hn_norm, cudaStream_t s, bool pdl);
+cudaError_t launch_head_logits(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D,
+                               const double* hn, int ncols, double* part_val, int* part_idx,
+                               double* part_second, int* n_rowblocks, cudaStream_t s, bool pdl);
+// Reduces per-row-block partials to the argmax; writes tok_out[c] and the
+// certification flag (1 = the margin to the runner-up exceeds the fp64 dot
+// error bound of any summation order).
+cudaError_t launch_head_reduce(const double* part_val, const int* part_idx, const double* part_second,
+                               int n_rowblocks, const double* hn_norm, double emb_norm_max, int D,
+                               int ncols, int* tok_out, int* cert_out, cudaStream_t s, bool pdl);
+
+// Standalone ops (the reference's module-level functions).
+cudaError_t launch_tile_quantize(const double* v, long long ntiles, int16_t* m, int8_t* e, cudaStream_t s);
+cudaError_t launch_tile_decode(const int16_t* m, const int8_t* e, long long ntiles, double* v, cudaStream_t s);
+cudaError_t launch_rmsnorm_fp(const double* x, const double* gamma, double eps, int n, int ncols,
+                              double* out, cudaStream_t s);
+cudaError_t launch_silu_fp(const double* x, long long n, double* out, cudaStream_t s);
+cudaError_t launch_softmax_fp(const double* x, int n, int ncols, double* out, cudaStream_t s);
+cudaError_t launch_rope_fp(const double* x, const double* cs, int HD, int nvec, double* out, cudaStream_t s);
+// Converts reference-layout weights (m [R][NT][16], e [R][NT]) to DevMat layout.
+// Destination row group of source group g is g * gstride + goff (interleaves
+// the gate/up matrices as groups 2i / 2i+1).
+cudaError_t launch_pack_weights(const int16_t* m_ref, const int8_t* e_ref, int R, int NT,
+                                uint8_t* wm, int8_t* we, int gstride, int goff, cudaStream_t s);
+// Converts the DDR3 wide-packed layout (entries [chunk][col][lane] int16 and
+// [chunk][tile][lane] int8) to DevMat layout.
+cudaError_t launch_pack_from_ddr(const int16_t* ddr_m, const int8_t* ddr_e, int R, int NT,
+                                 uint8_t* wm, int8_t* we, int gstride, int goff, cudaStream_t s);
+// L2-norm of each embedding row (for the head's error bound), in double.
+cudaError_t launch_row_norms(const int16_t* m, const int8_t* e, int rows, int D, double* out, cudaStream_t s);
+
+}  // namespace bfp
