@@ -133,6 +133,10 @@ int bfp200_rmsnorm_fp(bfp200_handle* h, const double* x, const double* gamma, in
 int bfp200_silu_fp(bfp200_handle* h, const double* x, size_t n, double* out);
 /* softmax_fp (:245-247) on ncols vectors of n doubles. */
 int bfp200_softmax_fp(bfp200_handle* h, const double* x, int n, int ncols, double* out);
+/* numpy's float64 reduction np.add.reduce / np.mean's sum (pairwise
+ * summation), the order rmsnorm_fp (:237), softmax_fp (:247) and the head
+ * (:438) sum in; ncols rows of n <= 3072 doubles. */
+int bfp200_pairwise_sum(bfp200_handle* h, const double* x, int n, int ncols, double* out);
 /* rope_fp (:250-258) on nvec vectors of HD doubles at positions pos[]. */
 int bfp200_rope_fp(bfp200_handle* h, const double* x, const int32_t* pos, int nvec, int HD, double base,
                    double* out);

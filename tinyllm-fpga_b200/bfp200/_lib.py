@@ -54,6 +54,7 @@ SIGNATURES = {
     "bfp200_silu_fp": [_P, _P, _Z, _P],
     "bfp200_softmax_fp": [_P, _P, _I, _I, _P],
     "bfp200_rope_fp": [_P, _P, _P, _I, _I, _D, _P],
+    "bfp200_pairwise_sum": [_P, _P, _I, _I, _P],
     "bfp200_rope_table": [_P, _I, _I, _D],
     "bfp200_fwd_layer": [_P, _I, _P, _P, _P, _I, _P, _P, _I, _P, _P],
     "bfp200_stage_dims": [_P, _P],

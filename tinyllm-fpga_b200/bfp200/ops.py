@@ -117,6 +117,15 @@ def softmax_fp(x):
     return out[0] if one else out
 
 
+def pairwise_sum(x):
+    """numpy's float64 np.add.reduce along the last axis (pairwise summation)."""
+    x = arr(x, np.float64)
+    x2 = x.reshape(-1, x.shape[-1])
+    out = np.empty(x2.shape[0], np.float64)
+    check(_lib.lib().bfp200_pairwise_sum(context(), ptr(x2), x2.shape[1], x2.shape[0], ptr(out)))
+    return out.reshape(x.shape[:-1])
+
+
 def rope_fp(x, pos, base=10000.0):
     """rope_fp (:250-258); x (HD,) or (nvec, HD) with pos scalar or (nvec,)."""
     x = arr(x, np.float64)

@@ -337,15 +337,23 @@ int download_decoded(bfp200_handle* h, const int16_t* m, const int8_t* e, int ld
   return BFP200_OK;
 }
 
-int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink) {
+// first_pdl: the layer's first kernel follows one of this library's kernels
+// in the stream (never a host copy), so it may use programmatic dependent
+// launch.  The stage-dump path copies to the host between kernels and runs
+// without PDL.
+int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool first_pdl = true) {
   const Dims d = h->dims();
+  const bool saved_pdl = h->pdl;
+  if (sink) h->pdl = false;
+  struct Restore { bfp200_handle* h; bool v; ~Restore() { h->pdl = v; } } restore{h, saved_pdl};
   const bool pdl = h->pdl;
   cudaStream_t s = h->stream;
   long long* acc = h->acc.p;
   unsigned* cnt = h->counters.p;
   const int accld = h->cap;
   // n1 = tile_quantize(rmsnorm_fp(h, g1))               (:263-264)
-  CK(launch_rmsnorm(h->h_m.p, h->h_e.p, h->g1.p + (size_t)l * h->D, h->cfg.eps, h->D, ncols, h->n_m.p, h->n_e.p, s, pdl));
+  CK(launch_rmsnorm(h->h_m.p, h->h_e.p, h->g1.p + (size_t)l * h->D, h->cfg.eps, h->D, ncols, h->n_m.p, h->n_e.p, s,
+                    pdl && first_pdl));
   if (sink) CKR(download_decoded(h, h->n_m.p, h->n_e.p, h->D, h->D, 0, ncols, sink->st[0]));
   // q, k, v = matvec(n1, Wq|Wk|Wv)                         (:265-267)
   CKR(enqueue_matmul(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
@@ -410,8 +418,11 @@ int enqueue_head(bfp200_handle* h, int ncols) {
   return BFP200_OK;
 }
 
+// The embedding kernel is the first kernel after host copies of the column
+// descriptors (prefill) or after the non-PDL advance kernel (decode graph):
+// it is launched without programmatic dependent launch.
 int enqueue_forward(bfp200_handle* h, int ncols, bool head) {
-  CK(launch_embed(h->emb_m.p, h->emb_e.p, h->col_tok.p, h->D, ncols, h->h_m.p, h->h_e.p, h->stream, h->pdl));
+  CK(launch_embed(h->emb_m.p, h->emb_e.p, h->col_tok.p, h->D, ncols, h->h_m.p, h->h_e.p, h->stream, false));
   for (int l = 0; l < h->NL; ++l) CKR(enqueue_layer(h, l, ncols, nullptr));
   if (head) CKR(enqueue_head(h, ncols));
   return BFP200_OK;
@@ -958,6 +969,18 @@ int bfp200_softmax_fp(bfp200_handle* h, const double* x, int n, int ncols, doubl
   return BFP200_OK;
 }
 
+int bfp200_pairwise_sum(bfp200_handle* h, const double* x, int n, int ncols, double* out) {
+  if (!h || !x || !out || n <= 0 || ncols <= 0 || n > 3072) return fail(BFP200_EINVAL, "pairwise_sum: bad arguments");
+  CK(cudaSetDevice(h->device));
+  DBuf<double> dx, dout;
+  CK(dx.ensure((size_t)n * ncols)); CK(dout.ensure(ncols));
+  CK(cudaMemcpyAsync(dx.p, x, (size_t)n * ncols * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(launch_np_sum(dx.p, n, ncols, dout.p, h->stream));
+  CK(cudaMemcpyAsync(out, dout.p, (size_t)ncols * 8, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
 int bfp200_rope_fp(bfp200_handle* h, const double* x, const int32_t* pos, int nvec, int HD, double base, double* out) {
   if (!h || !x || !pos || !out || nvec <= 0 || HD <= 0 || HD % 32) return fail(BFP200_EINVAL, "rope_fp: bad arguments");
   CK(cudaSetDevice(h->device));
@@ -1042,7 +1065,7 @@ int bfp200_fwd_layer(bfp200_handle* h, int layer, const double* h_in, const int3
   CK(cudaStreamSynchronize(h->stream));
   StageSink sink;
   sink.st.resize(BFP200_NSTAGES);
-  CKR(enqueue_layer(h, layer, ncols, stages ? &sink : nullptr));
+  CKR(enqueue_layer(h, layer, ncols, stages ? &sink : nullptr, /*first_pdl=*/false));
   std::vector<double> hout;
   CKR(download_decoded(h, h->h_m.p, h->h_e.p, D, D, 0, ncols, hout));
   std::memcpy(h_out, hout.data(), hout.size() * 8);

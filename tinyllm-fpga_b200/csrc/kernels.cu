@@ -953,6 +953,22 @@ __global__ void softmax_fp_kernel(const double* x, int n, double* out) {
   for (int i = lane; i < n; i += 32) out[(size_t)c * n + i] = __ddiv_rn(e[i], s_b);
 }
 
+__global__ void np_sum_kernel(const double* x, int n, double* out) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_lo[96], s_len[96];
+  __shared__ double s_val[96];
+  const int c = blockIdx.x, lane = threadIdx.x;
+  double* a = reinterpret_cast<double*>(smem);
+  for (int i = lane; i < n; i += 32) a[i] = x[(size_t)c * n + i];
+  __syncwarp();
+  const double S = np_sum_warp(a, n, s_lo, s_len, s_val);
+  if (lane == 0) out[c] = S;
+}
+
+cudaError_t launch_np_sum(const double* x, int n, int ncols, double* out, cudaStream_t s) {
+  return launch_ex(np_sum_kernel, dim3(ncols), dim3(32), (size_t)n * 8, s, false, x, n, out);
+}
+
 cudaError_t launch_softmax_fp(const double* x, int n, int ncols, double* out, cudaStream_t s) {
   return launch_ex(softmax_fp_kernel, dim3(ncols), dim3(32), (size_t)n * 8, s, false, x, n, out);
 }
@@ -1064,10 +1080,16 @@ int read_and_clear_error_flag(cudaStream_t s) {
 
 namespace bfp {
 cudaError_t init_kernel_attributes() {
-  const int mx = 227 * 1024;
-  cudaError_t e = cudaSuccess;
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return e;
   auto set = [&](const void* f) {
-    cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncAttributes fa;
+    cudaError_t r = cudaFuncGetAttributes(&fa, f);
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
     if (r != cudaSuccess) e = r;
   };
   set((const void*)bfp_matmul_kernel<1>);
@@ -1078,6 +1100,7 @@ cudaError_t init_kernel_attributes() {
   set((const void*)attention_kernel);
   set((const void*)rmsnorm_fp_kernel);
   set((const void*)softmax_fp_kernel);
+  set((const void*)np_sum_kernel);
   return e;
 }
 }  // namespace bfp

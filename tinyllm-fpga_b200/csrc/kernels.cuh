@@ -96,6 +96,8 @@ cudaError_t launch_tile_decode(const int16_t* m, const int8_t* e, long long ntil
 cudaError_t launch_rmsnorm_fp(const double* x, const double* gamma, double eps, int n, int ncols,
                               double* out, cudaStream_t s);
 cudaError_t launch_silu_fp(const double* x, long long n, double* out, cudaStream_t s);
+// numpy's float64 add.reduce (pairwise summation) of ncols rows of n values.
+cudaError_t launch_np_sum(const double* x, int n, int ncols, double* out, cudaStream_t s);
 cudaError_t launch_softmax_fp(const double* x, int n, int ncols, double* out, cudaStream_t s);
 cudaError_t launch_rope_fp(const double* x, const double* cs, int HD, int nvec, double* out, cudaStream_t s);
 // Converts reference-layout weights (m [R][NT][16], e [R][NT]) to DevMat layout.
