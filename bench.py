@@ -167,6 +167,7 @@ def run_ours(args, world, rank, local):
     dec.load_image(img)
     del img
     prompts2, ngen2 = synth.config_prompts(2)
+    ngen2 = args.n_gen
     prompts3, ngen3 = synth.config_prompts(3)
     lo, hi = rank * len(prompts3) // world, (rank + 1) * len(prompts3) // world
     part3 = prompts3[lo:hi]
@@ -215,19 +216,21 @@ def run_ours(args, world, rank, local):
     path_frac = path_bytes / (decode_tok_ms / 1e3) / 1e9 / peak
 
     # ---- bs256 (cfg3), sequences split over ranks
-    for _ in range(max(1, args.warmup // 3)):
+    bs256 = None
+    for _ in range(0 if args.no_bs256 else max(1, args.warmup // 3)):
         dec.generate(part3, ngen3)
-    barrier(world)
-    b_ms = []
-    for _ in range(max(1, args.steps // 4)):
-        dec.generate(part3, ngen3)
-        t = dec.last_timing()
-        b_ms.append(t["prefill_ms"] + t["decode_ms"])
-    barrier(world)
-    b_step = max_over_ranks(statistics.mean(b_ms), world)
-    bs256 = {"value": round(len(prompts3) * ngen3 / (b_step / 1e3), 1), "unit": "tok/s",
-             "ms_per_step": round(b_step, 3), "sequences": len(prompts3), "n_gen": ngen3,
-             "scaling": "strong", "uncertified_steps": dec.uncertified_steps()}
+    if not args.no_bs256:
+        barrier(world)
+        b_ms = []
+        for _ in range(max(1, args.steps // 4)):
+            dec.generate(part3, ngen3)
+            t = dec.last_timing()
+            b_ms.append(t["prefill_ms"] + t["decode_ms"])
+        barrier(world)
+        b_step = max_over_ranks(statistics.mean(b_ms), world)
+        bs256 = {"value": round(len(prompts3) * ngen3 / (b_step / 1e3), 1), "unit": "tok/s",
+                 "ms_per_step": round(b_step, 3), "sequences": len(prompts3), "n_gen": ngen3,
+                 "scaling": "strong", "uncertified_steps": dec.uncertified_steps()}
 
     launches = launches_per_generate(cfg2, 1, 48, ngen2)
     res = {
@@ -250,7 +253,7 @@ def run_ours(args, world, rank, local):
         "image_build_s": round(build_s, 1),
         "clocks": clk.summary(),
     }
-    if rank == 0:
+    if rank == 0 and not args.no_cpu:
         res["cpu_baseline"] = cpu_baseline(args)
     dec.close()
     return res
@@ -360,6 +363,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n-gen", type=int, default=256, help="generated tokens of the bs1 workload (profiling runs)")
+    ap.add_argument("--no-bs256", action="store_true", help="skip the bs256 measurement (profiling runs)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
