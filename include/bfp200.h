@@ -154,6 +154,24 @@ int bfp200_rope_table(double* out, int n_pos, int HD, double base);
 int bfp200_fwd_layer(bfp200_handle* h, int layer, const double* h_in, const int32_t* pos, const int32_t* kv_pos,
                      int ncols, double* k_cache, double* v_cache, int max_ctx, double* h_out, double* stages);
 
+/* No counterpart in the reference.  bfp200_matvec for callers that cannot
+ * allocate device memory -- a framework that owns every byte through its own
+ * caching allocator or fixed pool, or a latency-critical loop that cannot
+ * take cudaMalloc/cudaFree's implicit device synchronisation.  Every pointer
+ * is a DEVICE pointer on the current device, in the layouts of
+ * bfp200_matvec; the call is asynchronous on `stream` (a cudaStream_t, NULL
+ * for the default stream) and allocates nothing.  Its scratch (the matmul's
+ * K-split accumulators and counters) is a fixed file-scope device array of
+ * 2 MiB + 64 KiB that every GPU loading the library holds until exit:
+ * D_out * batch must not exceed 262144 (larger sizes fail with
+ * BFP200_EINVAL).  The first call on a device does a one-time set-up (it
+ * looks up the scratch array's device address and sets kernel attributes),
+ * so make that first call before any stream capture.  All calls share the
+ * scratch: calls that overlap on the GPU (different streams, threads or
+ * processes sharing the library) race and must be serialised by the caller. */
+int bfp200_matvec_noalloc(const int16_t* x_m, const int8_t* x_e, const int16_t* W_m, const int8_t* W_e, int D_out,
+                          int D_in, int batch, int16_t* out_m, int8_t* out_e, void* stream);
+
 /* Stage dump layout of bfp200_fwd_layer (mirrors the N1..D dumps of
  * gen_smollm_blockfp_bfp.py:393-426): n1 q k v attn o h1 n2 g u mlp d, where
  * n1/n2/attn/mlp are the matvec inputs tile_quantize(.) decoded, q/k are

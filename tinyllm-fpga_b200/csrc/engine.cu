@@ -190,6 +190,8 @@ __global__ void scatter_tokens_kernel(const int* tok, const int* cert, const int
 
 }  // namespace
 
+int bfp200_set_error(int code, const std::string& msg) { return fail(code, msg); }
+
 struct bfp200_handle {
   bfp200_cfg cfg{};
   int device = 0;

@@ -84,12 +84,14 @@ struct MMSmem {
   bool stage_all;   // all NT exponents of the CTA's rows/columns fit in shared memory
 };
 
-__host__ __device__ inline MMSmem mm_layout(int rg, int bn, int ntc, int NT) {
+// refw: weights staged from the reference layout (one padded row of ntc
+// tiles per matrix row) instead of the packed 512 B (group, tile) blocks.
+__host__ __device__ inline MMSmem mm_layout(int rg, int bn, int ntc, int NT, bool refw = false) {
   MMSmem L;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = (off + bytes + 15) & ~size_t(15); return o; };
   L.bar = take(16);
-  L.ws = take((size_t)rg * ntc * 512);
+  L.ws = take(refw ? (size_t)rg * 16 * ((size_t)ntc * 32 + 16) : (size_t)rg * ntc * 512);
   L.xs = take((size_t)bn * ntc * 32);
   L.stage_all = ((size_t)rg * NT * 16 + (size_t)bn * NT) <= 24 * 1024;
   const int ne = L.stage_all ? NT : ntc;
@@ -104,7 +106,11 @@ __host__ __device__ inline MMSmem mm_layout(int rg, int bn, int ntc, int NT) {
 
 size_t matmul_smem_bytes(int rg, int bn, int ntc, int NT) { return mm_layout(rg, bn, ntc, NT).total; }
 
-template <int RG>
+// REFW = false: a.W holds the packed DevMat layout (the decode path).
+// REFW = true: a.W.wm points at int16 mantissas [rows][NT][16] and a.W.we at
+// int8 exponents [rows][NT] -- the reference's quantize_W layout -- and the
+// hi/lo byte planes are formed in registers.
+template <int RG, bool REFW = false>
 __global__ void __launch_bounds__(MM_THREADS)
 bfp_matmul_kernel(MatmulArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -118,7 +124,8 @@ bfp_matmul_kernel(MatmulArgs a) {
   const int c0 = blockIdx.y * a.bn;
   const int ncol = min(a.bn, a.ncols - c0);
   const int tid = threadIdx.x;
-  const MMSmem L = mm_layout(RG, a.bn, ntc, NT);
+  const MMSmem L = mm_layout(RG, a.bn, ntc, NT, REFW);
+  const size_t wrow = (size_t)ntc * 32 + 16;   // REFW: padded smem stride of one matrix row
   unsigned long long* bar = reinterpret_cast<unsigned long long*>(smem + L.bar);
   unsigned char* Ws = smem + L.ws;
   unsigned char* Xs = smem + L.xs;
@@ -138,12 +145,24 @@ bfp_matmul_kernel(MatmulArgs a) {
   if (tid == 0 && nt_here > 0) {
     const unsigned bytes = (unsigned)nt_here * 512u;
     mbar_expect_tx(bar, bytes * RG);
-    #pragma unroll
-    for (int gi = 0; gi < RG; ++gi)
-      bulk_g2s(Ws + (size_t)gi * ntc * 512, a.W.wm + ((size_t)(g0 + gi) * NT + t0) * 512, bytes, bar);
+    if constexpr (REFW) {
+      for (int r = 0; r < ROWS; ++r)
+        bulk_g2s(Ws + r * wrow, a.W.wm + (((size_t)g0 * 16 + r) * NT + t0) * 32, (unsigned)nt_here * 32u, bar);
+    } else {
+      #pragma unroll
+      for (int gi = 0; gi < RG; ++gi)
+        bulk_g2s(Ws + (size_t)gi * ntc * 512, a.W.wm + ((size_t)(g0 + gi) * NT + t0) * 512, bytes, bar);
+    }
   }
   const bool stage_all = L.stage_all;
-  if (stage_all) {
+  if constexpr (REFW) {
+    const int ne = stage_all ? NT : ntc;
+    for (int i = tid; i < RG * ne * 16; i += MM_THREADS) {
+      const int ri = i & 15, t = (i >> 4) % ne, gi = (i >> 4) / ne;
+      const int tg = stage_all ? t : t0 + t;
+      if (tg < NT) WeAll[i] = a.W.we[((size_t)(g0 + gi) * 16 + ri) * NT + tg];
+    }
+  } else if (stage_all) {
     const uint4* src = reinterpret_cast<const uint4*>(a.W.we + (size_t)g0 * NT * 16);
     uint4* dst = reinterpret_cast<uint4*>(WeAll);
     for (int i = tid; i < RG * NT; i += MM_THREADS) dst[i] = src[i];
@@ -188,9 +207,11 @@ bfp_matmul_kernel(MatmulArgs a) {
           }
         } else {
           const int8_t* xe = a.xe + (size_t)(c0 + b) * a.x_lde;
-          const int8_t* we = a.W.we + (size_t)(g0 + gi) * NT * 16 + ri;
+          const int8_t* we = REFW ? a.W.we + ((size_t)(g0 + gi) * 16 + ri) * NT
+                                  : a.W.we + (size_t)(g0 + gi) * NT * 16 + ri;
+          const size_t wst = REFW ? 1 : 16;
           for (int t = sub; t < NT; t += tsplit) {
-            const int e = (int)xe[t] + (int)we[(size_t)t * 16];
+            const int e = (int)xe[t] + (int)we[(size_t)t * wst];
             m = e > m ? e : m;
           }
         }
@@ -218,9 +239,20 @@ bfp_matmul_kernel(MatmulArgs a) {
       Mr[b] = (b < nb) ? Ms[i * a.bn + cb + b] : 0;
     }
     for (int t = j; t < nt_here; t += TL) {
-      const uint4* wp = reinterpret_cast<const uint4*>(Ws + ((size_t)gi * ntc + t) * 512);
-      const uint4 wh = wp[ri];
-      const uint4 wl = wp[16 + ri];
+      uint4 wh, wl;
+      if constexpr (REFW) {
+        // 16 int16 mantissas -> hi-byte word and lo-byte word per 4 k
+        const uint4* wp = reinterpret_cast<const uint4*>(Ws + (size_t)i * wrow + (size_t)t * 32);
+        const uint4 v0 = wp[0], v1 = wp[1];
+        wh = make_uint4(__byte_perm(v0.x, v0.y, 0x7531), __byte_perm(v0.z, v0.w, 0x7531),
+                        __byte_perm(v1.x, v1.y, 0x7531), __byte_perm(v1.z, v1.w, 0x7531));
+        wl = make_uint4(__byte_perm(v0.x, v0.y, 0x6420), __byte_perm(v0.z, v0.w, 0x6420),
+                        __byte_perm(v1.x, v1.y, 0x6420), __byte_perm(v1.z, v1.w, 0x6420));
+      } else {
+        const uint4* wp = reinterpret_cast<const uint4*>(Ws + ((size_t)gi * ntc + t) * 512);
+        wh = wp[ri];
+        wl = wp[16 + ri];
+      }
       const int we = stage_all ? (int)WeAll[(gi * NT + t0 + t) * 16 + ri] : (int)WeAll[(gi * ntc + t) * 16 + ri];
       #pragma unroll
       for (int b = 0; b < MM_BC; ++b) {
@@ -380,6 +412,21 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s, bool pdl) {
       return cudaErrorInvalidValue;
   }
 }
+
+cudaError_t launch_matmul_refw(const MatmulArgs& a, cudaStream_t s) {
+  if (a.epi != EPI_STORE) return cudaErrorInvalidValue;
+  const int ntc = (a.W.NT + a.ksplit - 1) / a.ksplit;
+  const size_t smem = mm_layout(a.rg, a.bn, ntc, a.W.NT, true).total;
+  dim3 grid(a.W.G / a.rg, (a.ncols + a.bn - 1) / a.bn, a.ksplit);
+  switch (a.rg) {
+    case 1: bfp_matmul_kernel<1, true><<<grid, MM_THREADS, smem, s>>>(a); break;
+    case 2: bfp_matmul_kernel<2, true><<<grid, MM_THREADS, smem, s>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+size_t matmul_refw_smem_bytes(int rg, int bn, int ntc, int NT) { return mm_layout(rg, bn, ntc, NT, true).total; }
 
 // Generic PDL-aware launcher for the simple kernels below.
 template <typename... KArgs, typename... Args>
@@ -1095,6 +1142,8 @@ cudaError_t init_kernel_attributes() {
   set((const void*)bfp_matmul_kernel<1>);
   set((const void*)bfp_matmul_kernel<2>);
   set((const void*)bfp_matmul_kernel<4>);
+  set((const void*)bfp_matmul_kernel<1, true>);
+  set((const void*)bfp_matmul_kernel<2, true>);
   set((const void*)rmsnorm_quant_kernel);
   set((const void*)head_prep_kernel);
   set((const void*)attention_kernel);

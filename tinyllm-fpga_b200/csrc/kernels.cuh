@@ -63,6 +63,11 @@ struct Dims {
 
 size_t matmul_smem_bytes(int rg, int bn, int ntc, int NT);
 cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s, bool pdl);
+// The matmul reading weights in the reference's quantize_W layout
+// (a.W.wm = int16 [rows][NT][16], a.W.we = int8 [rows][NT]); EPI_STORE only,
+// rg 1 or 2, no programmatic dependent launch.
+cudaError_t launch_matmul_refw(const MatmulArgs& a, cudaStream_t s);
+size_t matmul_refw_smem_bytes(int rg, int bn, int ntc, int NT);
 // Raises the dynamic shared memory limit of every kernel (call once per device).
 cudaError_t init_kernel_attributes();
 // Reads and clears the device flag a bounded wait sets when it gives up.
