@@ -203,7 +203,7 @@ def run_ours(args, world, rank, local):
     # for one token's 120 launches (4 per layer) is measured with events on
     # the library stream by replaying the decode-step matmuls.
     wbytes, hbytes = weight_bytes_per_token(cfg2)
-    mm = matmul_timing(dec, ncols=1, reps=50)
+    mm = matmul_timing(dec, ncols=1, reps=args.mm_reps)
     achieved_gbs = wbytes / (mm["ms_per_token"] / 1e3) / 1e9
     peak = pk["hbm_gbs"]
     roof = {"kernel": "bfp_matmul_kernel (QKV/O/GU/D, bs1)", "bound": "hbm", "achieved": round(achieved_gbs, 1),
@@ -233,6 +233,9 @@ def run_ours(args, world, rank, local):
                  "scaling": "strong", "uncertified_steps": dec.uncertified_steps()}
 
     launches = launches_per_generate(cfg2, 1, 48, ngen2)
+    profile = {"bs1_pos176": dec.profile_forward(1, 176)}
+    if not args.no_bs256:
+        profile["bs256_pos100"] = dec.profile_forward(len(part3), 100)
     res = {
         "metric": "BFP decode tok/s (bs1, cfg2)", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
@@ -249,6 +252,7 @@ def run_ours(args, world, rank, local):
                 "d2h_bytes_per_step": (48 + ngen2) * 4 + 8},
         "gpu_launches": launches * args.steps,
         "bs256": bs256,
+        "kernel_profile_ms": profile,
         "uncertified_steps": uncert,
         "image_build_s": round(build_s, 1),
         "clocks": clk.summary(),
@@ -366,6 +370,7 @@ def main():
     ap.add_argument("--n-gen", type=int, default=256, help="generated tokens of the bs1 workload (profiling runs)")
     ap.add_argument("--no-bs256", action="store_true", help="skip the bs256 measurement (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
+    ap.add_argument("--mm-reps", type=int, default=50, help="graph replays for the matmul roofline timing")
     args = ap.parse_args()
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))

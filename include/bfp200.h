@@ -110,6 +110,15 @@ int bfp200_last_timing(bfp200_handle* h, double* prefill_ms, double* decode_ms);
  * loaded image.  Replaces nothing in the reference. */
 int bfp200_time_matmuls(bfp200_handle* h, int ncols, int reps, double* ms_per_token, int* launches_per_token);
 
+/* Measurement: one forward pass (embedding, every layer, head) of `ncols`
+ * columns at position `pos`, launched without programmatic overlap and with
+ * a CUDA event before every kernel; per kernel kind k (0 embed, 1 rmsnorm,
+ * 2 qkv matmul, 3 rope+kv, 4 attention, 5 o matmul, 6 gate/up matmul,
+ * 7 down matmul, 8 head prep, 9 head logits, 10 head reduce) returns the
+ * summed milliseconds and launch count (arrays of 11).  The KV content is
+ * whatever the slots hold.  Replaces nothing in the reference. */
+int bfp200_profile_forward(bfp200_handle* h, int ncols, int pos, double* ms_by_kind, int* launches_by_kind);
+
 /* ---- op-level entry points (the reference's module functions) ---------- */
 
 /* tile_quantize (gen_smollm_blockfp_full.py:90-97): n doubles (n % 16 == 0)

@@ -91,3 +91,28 @@ def test_rom_prompt_and_gamma_roms():
     b = dec.generate(None, 5)
     assert a == b and a[0][:3] == [9, 8, 7]
     dec.close()
+
+
+@pytest.mark.parametrize("nseq", [1, 2, 4])
+def test_small_batch_kernels_match_general_kernels(nseq, monkeypatch):
+    """1..4 columns run the fused small-batch kernels (gemv.cu); the general
+    matmul path (forced with BFP200_NO_SMALL) and the oracle agree with them."""
+    from bfp200 import BfpConfig, Decoder, synth
+    cfg = BfpConfig(MAX_CTX=48, max_seqs=4, **SMALL)
+    img = synth.synthetic_image(cfg, 5)
+    rng = np.random.default_rng(50 + nseq)
+    prompts = [rng.integers(0, 512, size=int(n)).tolist() for n in (3, 11, 1, 20)[:nseq]]
+    fast = Decoder(cfg)
+    fast.load_image(img)
+    got_fast = fast.generate(prompts, 12)
+    got_fast_rtl = fast.generate(prompts, 5, feed_mode="rtl")
+    fast.close()
+    monkeypatch.setenv("BFP200_NO_SMALL", "1")
+    slow = Decoder(cfg)
+    slow.load_image(img)
+    assert slow.generate(prompts, 12) == got_fast
+    assert slow.generate(prompts, 5, feed_mode="rtl") == got_fast_rtl
+    slow.close()
+    ocfg = O.Cfg(**SMALL)
+    model = OS.make_model(5, ocfg)
+    assert got_fast[0] == O.generate(model, prompts[0], 12, max_ctx=48, cfg=ocfg)

@@ -99,6 +99,17 @@ class Decoder:
         check(_lib.lib().bfp200_last_timing(self._h, C.byref(a), C.byref(b)))
         return {"prefill_ms": a.value, "decode_ms": b.value}
 
+    PROFILE_KINDS = ("embed", "rmsnorm", "mm_qkv", "rope_kv", "attention", "mm_o", "mm_gu", "mm_d", "head_prep",
+                     "head_logits", "head_reduce")
+
+    def profile_forward(self, ncols, pos):
+        """Per-kernel-kind device time (ms) and launch counts of one forward
+        pass of ncols columns at position pos (serialised launches)."""
+        ms = np.zeros(len(self.PROFILE_KINDS), np.float64)
+        n = np.zeros(len(self.PROFILE_KINDS), np.int32)
+        check(_lib.lib().bfp200_profile_forward(self._h, int(ncols), int(pos), ptr(ms), ptr(n)))
+        return {k: (round(float(a), 4), int(b)) for k, a, b in zip(self.PROFILE_KINDS, ms, n)}
+
     # -- one layer (fwd_layer, :261-293) ----------------------------------------
     def stage_dims(self):
         d = np.empty(_lib.NSTAGES, np.int32)

@@ -216,12 +216,59 @@ __device__ __forceinline__ double np_sum_serial(const double* a, int n) {
   return __dadd_rn(0.0, np_pw_combine(n, val));
 }
 
+// numpy's pairwise tree is "perfect" for n when every split is an exact half
+// that stays a multiple of 8 down to leaves of L <= 128 (L % 8 == 0, so no
+// tail): e.g. n = 576 -> 8 leaves of 72.  Returns the number of halvings k
+// (<= 3, i.e. <= 8 leaves) and the leaf size, or -1.
+__host__ __device__ __forceinline__ int np_pw_perfect(int n, int* leaf) {
+  int k = 0;
+  while (n > 128) {
+    const int n2 = n / 2;
+    if ((n & 1) || (n2 % 8)) return -1;
+    n = n2;
+    if (++k > 3) return -1;
+  }
+  if (n < 8 || (n % 8)) return -1;
+  *leaf = n;
+  return k;
+}
+
+// Warp-parallel numpy sum for a perfect tree (k halvings, leaves of L): lane
+// 4*l + q holds accumulators 2q, 2q+1 of leaf l; the accumulator pairs, the
+// 8-accumulator combine ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) and the leaf
+// tree are all evaluated by xor shuffles with the lower lane as the left
+// operand, i.e. in exactly numpy's order.  Returns 0.0 + sum on every lane.
+__device__ __forceinline__ double np_sum_warp_perfect(const double* a, int k, int L) {
+  const int lane = threadIdx.x & 31;
+  const int leaf = lane >> 2, q = lane & 3;
+  double v = 0.0;
+  if (leaf < (1 << k)) {
+    const double* b = a + leaf * L + 2 * q;
+    double r0 = b[0], r1 = b[1];
+    for (int i = 8; i < L; i += 8) { r0 = __dadd_rn(r0, b[i]); r1 = __dadd_rn(r1, b[i + 1]); }
+    v = __dadd_rn(r0, r1);
+  }
+  double o = __shfl_xor_sync(0xffffffffu, v, 1);
+  if ((q & 1) == 0) v = __dadd_rn(v, o);
+  o = __shfl_xor_sync(0xffffffffu, v, 2);
+  if ((q & 2) == 0) v = __dadd_rn(v, o);
+  for (int lev = 0; lev < k; ++lev) {
+    const int m = 4 << lev;
+    o = __shfl_xor_sync(0xffffffffu, v, m);
+    if ((lane & m) == 0) v = __dadd_rn(v, o);
+  }
+  return __dadd_rn(0.0, __shfl_sync(0xffffffffu, v, 0));
+}
+
 // Warp-cooperative numpy sum of a shared-memory array (n <= 8192).  All 32
 // lanes must call it; scratch needs 3*64 words of shared memory.  Returns the
 // sum on every lane.
 __device__ __forceinline__ double np_sum_warp(const double* a, int n, int* s_lo, int* s_len,
                                               double* s_val) {
   const int lane = threadIdx.x & 31;
+  int pl = 0;
+  const int pk = np_pw_perfect(n, &pl);
+  if (pk >= 0) return np_sum_warp_perfect(a, pk, pl);
   if (n <= 128) {
     double r = 0.0;
     if (lane == 0) r = __dadd_rn(0.0, np_pw_leaf(a, n));

@@ -71,7 +71,7 @@ struct MMPlan {
 
 constexpr size_t MM_SMEM_LIMIT = 200 * 1024;
 
-MMPlan plan_matmul(int G, int NT, int ncols, bool swiglu, int nsm) {
+MMPlan plan_matmul(int G, int NT, int ncols, bool swiglu, int nsm, int max_ks = 1 << 30) {
   MMPlan p;
   p.rg = swiglu ? 2 : 1;
   p.bn = ncols <= 32 ? ncols : 32;
@@ -83,7 +83,7 @@ MMPlan plan_matmul(int G, int NT, int ncols, bool swiglu, int nsm) {
     const int ntc = NT / ks;
     if (matmul_smem_bytes(p.rg, p.bn, ntc, NT) > MM_SMEM_LIMIT) continue;
     if (best < 0) best = ks;
-    else if (rows_t * cols_t * ks <= target && ntc >= 4) best = ks;
+    else if (rows_t * cols_t * ks <= target && ntc >= 4 && ks <= max_ks) best = ks;
   }
   p.ks = best < 0 ? NT : best;
   return p;
@@ -200,6 +200,8 @@ struct bfp200_handle {
   int D = 0, HQ = 0, HKV = 0, HD = 0, FFN = 0, NL = 0, V = 0, MAXC = 0, NTD = 0, NTF = 0, KVD = 0, QD = 0;
   int RQKV = 0, GQKV = 0, GO = 0, GGU = 0, GD = 0;
   bool pdl = true;
+  bool use_clusters = true;   // K-split reduction through distributed shared memory
+  bool use_small = true;      // 1..4 columns: the fused small-batch kernels (gemv.cu)
   // weights
   DBuf<uint8_t> wm_qkv, wm_o, wm_gu, wm_d;
   DBuf<int8_t> we_qkv, we_o, we_gu, we_d;
@@ -231,6 +233,8 @@ struct bfp200_handle {
   int graph_cols = -1, graph_ngen = -1;
   long long uncert = 0;
   double t_prefill = 0.0, t_decode = 0.0;
+  // per-kernel profiling (bfp200_profile_forward): an event before every launch
+  std::vector<std::pair<int, cudaEvent_t>>* prof = nullptr;
 
   ~bfp200_handle() {
     if (graph) cudaGraphExecDestroy(graph);
@@ -278,7 +282,7 @@ int ensure_cols(bfp200_handle* h, int ncols) {
   CK(h->dbg_m.ensure((size_t)cap * R_MAX)); CK(h->dbg_e.ensure((size_t)cap * R_MAX / 16));
   CK(h->acc.ensure((size_t)R_MAX * cap));
   CK(h->counters.ensure((size_t)(R_MAX / 16) * (cap + 1)));
-  const int nrb_max = (h->V + 63) / 64;
+  const int nrb_max = std::max((h->V + 63) / 64, 2 * h->nsm);
   CK(h->hn.ensure((size_t)cap * h->D)); CK(h->hn_norm.ensure(cap));
   CK(h->part_val.ensure((size_t)cap * nrb_max)); CK(h->part_sec.ensure((size_t)cap * nrb_max));
   CK(h->part_idx.ensure((size_t)cap * nrb_max));
@@ -298,6 +302,18 @@ int ensure_kv(bfp200_handle* h, int nslots) {
   return BFP200_OK;
 }
 
+// Kernel kinds of the per-kernel profile (bfp200_profile_forward).
+enum ProfKind { PK_EMBED, PK_RMSNORM, PK_MM_QKV, PK_ROPE_KV, PK_ATTENTION, PK_MM_O, PK_MM_GU, PK_MM_D, PK_HEAD_PREP,
+                PK_HEAD_LOGITS, PK_HEAD_REDUCE, PK_COUNT };
+
+void mark(bfp200_handle* h, int kind) {
+  if (!h->prof) return;
+  cudaEvent_t ev;
+  cudaEventCreate(&ev);
+  cudaEventRecord(ev, h->stream);
+  h->prof->push_back({kind, ev});
+}
+
 int enqueue_matmul(bfp200_handle* h, DevMat W, const int16_t* xm, const int8_t* xe, int x_ld, int x_lde,
                    int ncols, int epi, int16_t* om, int8_t* oe, int o_ld, int o_lde, const int16_t* rm,
                    const int8_t* re, long long* acc, unsigned* counters, int acc_ld) {
@@ -308,10 +324,11 @@ int enqueue_matmul(bfp200_handle* h, DevMat W, const int16_t* xm, const int8_t* 
   a.epi = epi;
   a.om = om; a.oe = oe; a.o_ld = o_ld; a.o_lde = o_lde;
   a.rm = rm; a.re = re;
-  const MMPlan p = plan_matmul(W.G, W.NT, ncols, epi == EPI_SWIGLU, h->nsm);
+  const MMPlan p = plan_matmul(W.G, W.NT, ncols, epi == EPI_SWIGLU, h->nsm, h->use_clusters ? 8 : (1 << 30));
   a.rg = p.rg; a.bn = p.bn; a.ksplit = p.ks;
+  a.cluster = (p.ks > 1 && p.ks <= 8 && h->use_clusters) ? 1 : 0;
   a.acc = acc; a.counters = counters; a.acc_ld = acc_ld;
-  if (p.ks > 1 && (acc == nullptr || counters == nullptr))
+  if (p.ks > 1 && !a.cluster && (acc == nullptr || counters == nullptr))
     return fail(BFP200_EINVAL, "matmul needs K-split scratch");
   CK(launch_matmul(a, h->stream, h->pdl));
   return BFP200_OK;
@@ -354,16 +371,20 @@ int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool firs
   unsigned* cnt = h->counters.p;
   const int accld = h->cap;
   // n1 = tile_quantize(rmsnorm_fp(h, g1))               (:263-264)
+  mark(h, PK_RMSNORM);
   CK(launch_rmsnorm(h->h_m.p, h->h_e.p, h->g1.p + (size_t)l * h->D, h->cfg.eps, h->D, ncols, h->n_m.p, h->n_e.p, s,
                     pdl && first_pdl));
   if (sink) CKR(download_decoded(h, h->n_m.p, h->n_e.p, h->D, h->D, 0, ncols, sink->st[0]));
   // q, k, v = matvec(n1, Wq|Wk|Wv)                         (:265-267)
+  mark(h, PK_MM_QKV);
   CKR(enqueue_matmul(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
                      EPI_STORE, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->RQKV / 16, nullptr, nullptr, acc, cnt, accld));
   if (sink) CKR(download_decoded(h, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->KVD, h->QD + h->KVD, ncols, sink->st[3]));
   // rope on q, k; KV write                                (:268-272)
+  mark(h, PK_ROPE_KV);
   CK(launch_rope_kv(h->qkv_m.p, h->qkv_e.p, h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), h->rope_cs.p, d, ncols, s, pdl));
   // attention -> tile_quantize(fpq(attn))                 (:273-283)
+  mark(h, PK_ATTENTION);
   CK(launch_attention(h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), d, ncols, h->a_m.p, h->a_e.p, s, pdl));
   if (sink) {
     CKR(download_decoded(h, h->qr_m.p, h->qr_e.p, h->QD, h->QD, 0, ncols, sink->st[1]));
@@ -373,10 +394,12 @@ int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool firs
     CKR(download_decoded(h, h->dbg_m.p, h->dbg_e.p, h->D, h->D, 0, ncols, sink->st[5]));
   }
   // h1 = fpq(h + matvec(attn, Wo))                          (:284-285)
+  mark(h, PK_MM_O);
   CKR(enqueue_matmul(h, h->mat(h->wm_o, h->we_o, h->GO, h->QD / 16, l), h->a_m.p, h->a_e.p, h->QD, h->QD / 16, ncols,
                      EPI_RESIDUAL, h->h1_m.p, h->h1_e.p, h->D, h->NTD, h->h_m.p, h->h_e.p, acc, cnt, accld));
   if (sink) CKR(download_decoded(h, h->h1_m.p, h->h1_e.p, h->D, h->D, 0, ncols, sink->st[6]));
   // n2 = tile_quantize(rmsnorm_fp(h1, g2))                 (:286-287)
+  mark(h, PK_RMSNORM);
   CK(launch_rmsnorm(h->h1_m.p, h->h1_e.p, h->g2.p + (size_t)l * h->D, h->cfg.eps, h->D, ncols, h->n_m.p, h->n_e.p, s, pdl));
   if (sink) {
     CKR(download_decoded(h, h->n_m.p, h->n_e.p, h->D, h->D, 0, ncols, sink->st[7]));
@@ -395,6 +418,7 @@ int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool firs
       }
   }
   // mlp = tile_quantize(fpq(silu_fp(g) * u))                (:288-291)
+  mark(h, PK_MM_GU);
   CKR(enqueue_matmul(h, h->mat(h->wm_gu, h->we_gu, h->GGU, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
                      EPI_SWIGLU, h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF, nullptr, nullptr, acc, cnt, accld));
   if (sink) {
@@ -404,17 +428,92 @@ int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool firs
     CKR(download_decoded(h, h->dbg_m.p, h->dbg_e.p, h->D, h->D, 0, ncols, sink->st[11]));
   }
   // h = fpq(h1 + matvec(mlp, Wd))                           (:292-293)
+  mark(h, PK_MM_D);
   CKR(enqueue_matmul(h, h->mat(h->wm_d, h->we_d, h->GD, h->NTF, l), h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF, ncols,
                      EPI_RESIDUAL, h->h_m.p, h->h_e.p, h->D, h->NTD, h->h1_m.p, h->h1_e.p, acc, cnt, accld));
   return BFP200_OK;
 }
 
+// Small-batch layer (1..4 columns): 5 kernels -- fused RMSNorm+QKV+RoPE+KV
+// write, attention, O+residual, RMSNorm+gate/up+SwiGLU, down+residual.
+bool small_path_ok(bfp200_handle* h, int ncols) {
+  return h->use_small && ncols >= 1 && ncols <= 4 && gemv_supported(GV_QKV_ROPE, true, h->NTD, ncols) &&
+         gemv_supported(GV_RESIDUAL, false, h->QD / 16, ncols) && gemv_supported(GV_SWIGLU, true, h->NTD, ncols) &&
+         gemv_supported(GV_RESIDUAL, false, h->NTF, ncols);
+}
+
+GemvArgs gemv_args(bfp200_handle* h, DevMat W, int ncols, int mode) {
+  GemvArgs a;
+  a.W = W;
+  a.ncols = ncols;
+  a.mode = mode;
+  a.eps = h->cfg.eps;
+  return a;
+}
+
+int enqueue_gemv_qkv(bfp200_handle* h, int l, int ncols, bool pdl) {
+  GemvArgs a = gemv_args(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), ncols, GV_QKV_ROPE);
+  a.xm = h->h_m.p; a.xe = h->h_e.p; a.x_ld = h->D; a.x_lde = h->NTD;
+  a.norm = 1; a.gamma = h->g1.p + (size_t)l * h->D;
+  a.rope_cs = h->rope_cs.p; a.col_slot = h->col_slot.p; a.col_pos = h->col_pos.p;
+  a.kv = h->kv(); a.layer = l; a.HQ = h->HQ; a.HKV = h->HKV;
+  a.qr_m = h->qr_m.p; a.qr_e = h->qr_e.p;
+  CK(launch_gemv(a, h->stream, pdl));
+  return BFP200_OK;
+}
+
+int enqueue_gemv_o(bfp200_handle* h, int l, int ncols, bool pdl, int16_t* om, int8_t* oe) {
+  GemvArgs a = gemv_args(h, h->mat(h->wm_o, h->we_o, h->GO, h->QD / 16, l), ncols, GV_RESIDUAL);
+  a.xm = h->a_m.p; a.xe = h->a_e.p; a.x_ld = h->QD; a.x_lde = h->QD / 16;
+  a.rm = h->h_m.p; a.re = h->h_e.p;
+  a.om = om; a.oe = oe; a.o_ld = h->D; a.o_lde = h->NTD;
+  CK(launch_gemv(a, h->stream, pdl));
+  return BFP200_OK;
+}
+
+int enqueue_gemv_gu(bfp200_handle* h, int l, int ncols, bool pdl) {
+  GemvArgs a = gemv_args(h, h->mat(h->wm_gu, h->we_gu, h->GGU, h->NTD, l), ncols, GV_SWIGLU);
+  a.xm = h->h1_m.p; a.xe = h->h1_e.p; a.x_ld = h->D; a.x_lde = h->NTD;
+  a.norm = 1; a.gamma = h->g2.p + (size_t)l * h->D;
+  a.om = h->mlp_m.p; a.oe = h->mlp_e.p; a.o_ld = h->FFN; a.o_lde = h->NTF;
+  CK(launch_gemv(a, h->stream, pdl));
+  return BFP200_OK;
+}
+
+int enqueue_gemv_d(bfp200_handle* h, int l, int ncols, bool pdl, int16_t* om, int8_t* oe) {
+  GemvArgs a = gemv_args(h, h->mat(h->wm_d, h->we_d, h->GD, h->NTF, l), ncols, GV_RESIDUAL);
+  a.xm = h->mlp_m.p; a.xe = h->mlp_e.p; a.x_ld = h->FFN; a.x_lde = h->NTF;
+  a.rm = h->h1_m.p; a.re = h->h1_e.p;
+  a.om = om; a.oe = oe; a.o_ld = h->D; a.o_lde = h->NTD;
+  CK(launch_gemv(a, h->stream, pdl));
+  return BFP200_OK;
+}
+
+int enqueue_layer_small(bfp200_handle* h, int l, int ncols, bool first_pdl) {
+  const bool pdl = h->pdl;
+  mark(h, PK_MM_QKV);
+  CKR(enqueue_gemv_qkv(h, l, ncols, pdl && first_pdl));
+  mark(h, PK_ATTENTION);
+  CK(launch_attention(h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), h->dims(), ncols, h->a_m.p, h->a_e.p, h->stream,
+                      pdl));
+  mark(h, PK_MM_O);
+  CKR(enqueue_gemv_o(h, l, ncols, pdl, h->h1_m.p, h->h1_e.p));
+  mark(h, PK_MM_GU);
+  CKR(enqueue_gemv_gu(h, l, ncols, pdl));
+  mark(h, PK_MM_D);
+  CKR(enqueue_gemv_d(h, l, ncols, pdl, h->h_m.p, h->h_e.p));
+  return BFP200_OK;
+}
+
 int enqueue_head(bfp200_handle* h, int ncols) {
   cudaStream_t s = h->stream;
+  mark(h, PK_HEAD_PREP);
   CK(launch_head_prep(h->h_m.p, h->h_e.p, h->nw.p, h->cfg.eps, h->D, ncols, h->hn.p, h->hn_norm.p, s, h->pdl));
   int nrb = 0;
+  mark(h, PK_HEAD_LOGITS);
   CK(launch_head_logits(h->emb_m.p, h->emb_e.p, h->V, h->D, h->hn.p, ncols, h->part_val.p, h->part_idx.p,
                         h->part_sec.p, &nrb, s, h->pdl));
+  mark(h, PK_HEAD_REDUCE);
   CK(launch_head_reduce(h->part_val.p, h->part_idx.p, h->part_sec.p, nrb, h->hn_norm.p, h->emb_norm_max, h->D, ncols,
                         h->tok.p, h->cert.p, s, h->pdl));
   return BFP200_OK;
@@ -424,8 +523,13 @@ int enqueue_head(bfp200_handle* h, int ncols) {
 // descriptors (prefill) or after the non-PDL advance kernel (decode graph):
 // it is launched without programmatic dependent launch.
 int enqueue_forward(bfp200_handle* h, int ncols, bool head) {
+  mark(h, PK_EMBED);
   CK(launch_embed(h->emb_m.p, h->emb_e.p, h->col_tok.p, h->D, ncols, h->h_m.p, h->h_e.p, h->stream, false));
-  for (int l = 0; l < h->NL; ++l) CKR(enqueue_layer(h, l, ncols, nullptr));
+  const bool small = small_path_ok(h, ncols);
+  for (int l = 0; l < h->NL; ++l) {
+    if (small) CKR(enqueue_layer_small(h, l, ncols, /*first_pdl=*/true));
+    else CKR(enqueue_layer(h, l, ncols, nullptr));
+  }
   if (head) CKR(enqueue_head(h, ncols));
   return BFP200_OK;
 }
@@ -499,6 +603,8 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
   h->RQKV = h->QD + 2 * h->KVD;
   h->GQKV = h->RQKV / 16; h->GO = h->D / 16; h->GGU = 2 * h->FFN / 16; h->GD = h->D / 16;
   if (const char* e = std::getenv("BFP200_NO_PDL")) h->pdl = !(e[0] == '1');
+  if (const char* e = std::getenv("BFP200_NO_CLUSTER")) h->use_clusters = !(e[0] == '1');
+  if (const char* e = std::getenv("BFP200_NO_SMALL")) h->use_small = !(e[0] == '1');
   cudaError_t ce = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
   if (ce != cudaSuccess) { delete h; return fail(BFP200_ECUDA, cudaGetErrorString(ce)); }
   std::vector<double> cs((size_t)h->MAXC * h->HD);
@@ -814,6 +920,45 @@ int bfp200_last_timing(bfp200_handle* h, double* prefill_ms, double* decode_ms) 
   return BFP200_OK;
 }
 
+int bfp200_profile_forward(bfp200_handle* h, int ncols, int pos, double* ms_by_kind, int* launches_by_kind) {
+  if (!h || ncols <= 0 || !ms_by_kind) return fail(BFP200_EINVAL, "profile_forward: bad arguments");
+  if (!h->have_image) return fail(BFP200_ESTATE, "profile_forward before load_image");
+  if (ncols > h->cfg.max_seqs || pos < 0 || pos >= h->MAXC) return fail(BFP200_EINVAL, "profile_forward: ncols/pos");
+  CK(cudaSetDevice(h->device));
+  CKR(ensure_kv(h, ncols));
+  CKR(ensure_cols(h, ncols));
+  std::vector<int> slots(ncols), poss(ncols, pos), toks(ncols, 0);
+  std::iota(slots.begin(), slots.end(), 0);
+  CK(cudaMemcpyAsync(h->col_slot.p, slots.data(), ncols * 4, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(h->col_pos.p, poss.data(), ncols * 4, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(h->col_tok.p, toks.data(), ncols * 4, cudaMemcpyHostToDevice, h->stream));
+  const bool saved = h->pdl;
+  h->pdl = false;   // serialised launches: each kernel's time stands alone
+  std::vector<std::pair<int, cudaEvent_t>> evs;
+  int r = BFP200_OK;
+  for (int pass = 0; pass < 2 && r == BFP200_OK; ++pass) {   // pass 0 warms caches and code
+    for (auto& pe : evs) cudaEventDestroy(pe.second);
+    evs.clear();
+    h->prof = &evs;
+    r = enqueue_forward(h, ncols, true);
+    mark(h, PK_COUNT);
+    h->prof = nullptr;
+    cudaStreamSynchronize(h->stream);
+  }
+  h->pdl = saved;
+  if (r != BFP200_OK) { for (auto& pe : evs) cudaEventDestroy(pe.second); return r; }
+  for (int k = 0; k < PK_COUNT; ++k) { ms_by_kind[k] = 0.0; if (launches_by_kind) launches_by_kind[k] = 0; }
+  for (size_t i = 0; i + 1 < evs.size(); ++i) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, evs[i].second, evs[i + 1].second);
+    ms_by_kind[evs[i].first] += ms;
+    if (launches_by_kind) launches_by_kind[evs[i].first] += 1;
+  }
+  for (auto& pe : evs) cudaEventDestroy(pe.second);
+  CK(cudaGetLastError());
+  return BFP200_OK;
+}
+
 int bfp200_time_matmuls(bfp200_handle* h, int ncols, int reps, double* ms_per_token, int* launches_per_token) {
   if (!h || ncols <= 0 || reps <= 0 || !ms_per_token) return fail(BFP200_EINVAL, "time_matmuls: bad arguments");
   if (!h->have_image) return fail(BFP200_ESTATE, "time_matmuls before load_image");
@@ -822,8 +967,15 @@ int bfp200_time_matmuls(bfp200_handle* h, int ncols, int reps, double* ms_per_to
   long long* acc = h->acc.p;
   unsigned* cnt = h->counters.p;
   const int accld = h->cap;
+  const bool small = small_path_ok(h, ncols);
   auto body = [&]() -> int {
-    for (int l = 0; l < h->NL; ++l) {
+    for (int l = 0; l < h->NL && small; ++l) {
+      CKR(enqueue_gemv_qkv(h, l, ncols, h->pdl));
+      CKR(enqueue_gemv_o(h, l, ncols, h->pdl, h->dbg_m.p, h->dbg_e.p));
+      CKR(enqueue_gemv_gu(h, l, ncols, h->pdl));
+      CKR(enqueue_gemv_d(h, l, ncols, h->pdl, h->dbg_m.p, h->dbg_e.p));
+    }
+    for (int l = 0; l < h->NL && !small; ++l) {
       CKR(enqueue_matmul(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD,
                          ncols, EPI_STORE, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->RQKV / 16, nullptr, nullptr, acc, cnt,
                          accld));

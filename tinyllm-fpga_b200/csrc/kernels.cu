@@ -6,6 +6,8 @@
 #include "bfp_device.cuh"
 #include "kernels.cuh"
 
+#include <cooperative_groups.h>
+
 #include <cmath>
 #include <cstdio>
 
@@ -282,7 +284,7 @@ bfp_matmul_kernel(MatmulArgs a) {
       if (b < nb) {
         long long s = 0;
         for (int jj = 0; jj < TL; ++jj) s += red[((size_t)jj * ROWS + row) * MM_BC + b];
-        if (a.ksplit == 1) {
+        if (a.ksplit == 1 || a.cluster) {
           tot[row * a.bn + cb + b] = s;
         } else {
           atomicAdd(reinterpret_cast<unsigned long long*>(
@@ -294,8 +296,25 @@ bfp_matmul_kernel(MatmulArgs a) {
     __syncthreads();
   }
 
-  // ---- K split: the last CTA to arrive owns the epilogue
-  if (a.ksplit > 1) {
+  // ---- K split over a thread-block cluster: rank 0 sums the partial
+  //      accumulators of its peers through distributed shared memory
+  if (a.ksplit > 1 && a.cluster) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();                                   // every rank's partials are in its shared memory
+    const unsigned rank = cl.block_rank();
+    if (rank == 0) {
+      for (int o = tid; o < ROWS * ncol; o += MM_THREADS) {
+        const int row = o % ROWS, b = o / ROWS;
+        long long sum = tot[row * a.bn + b];
+        for (int r = 1; r < a.ksplit; ++r) sum += cl.map_shared_rank(tot, r)[row * a.bn + b];
+        tot[row * a.bn + b] = sum;
+      }
+    }
+    cl.sync();                                   // peers stay resident until rank 0 has read them
+    if (rank != 0) return;
+  } else if (a.ksplit > 1) {
+  // ---- K split across the grid: the last CTA to arrive owns the epilogue
     __shared__ int s_last;
     __threadfence();
     __syncthreads();
@@ -399,11 +418,22 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s, bool pdl) {
   cfg.blockDim = dim3(MM_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (a.cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = a.ksplit;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   switch (a.rg) {
     case 1: return cudaLaunchKernelEx(&cfg, bfp_matmul_kernel<1>, a);
     case 2: return cudaLaunchKernelEx(&cfg, bfp_matmul_kernel<2>, a);
@@ -449,7 +479,9 @@ static cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, size_t 
 // rmsnorm_fp + tile_quantize (:236-238, :263-264 / :286-287).  One warp per
 // column.  Output is the matvec-ready form tile_quantize(fpq(y)).
 // ---------------------------------------------------------------------------
-constexpr int NORM_WARPS = 4;
+constexpr int NORM_WARPS = 4;        // standalone rmsnorm_fp op: one warp per column
+constexpr int NORM_THREADS = 128;    // decode-path kernels: one CTA per column
+constexpr int NORM_MAXV = 8;         // elements per thread held in registers (D <= 1024)
 
 __device__ __forceinline__ void warp_rms_factor(const double* sq, int D, int* s_lo, int* s_len,
                                                 double* s_val, double eps, double* r_out) {
@@ -458,35 +490,63 @@ __device__ __forceinline__ void warp_rms_factor(const double* sq, int D, int* s_
   *r_out = __dsqrt_rn(__dadd_rn(mean, eps));                // np.sqrt(mean + eps)
 }
 
-__global__ void __launch_bounds__(NORM_WARPS * 32)
+// Decodes column c of a BFP vector into xs[] and x*x into sq[], then returns
+// r = sqrt(mean(x*x) + eps) (numpy's pairwise mean) on every thread.  All
+// loads of the column are issued before any is used (one memory round trip).
+__device__ __forceinline__ double block_rms(const int16_t* xm, const int8_t* xe, int D, double eps, double* xs,
+                                            double* sq, int* s_lo, int* s_len, double* s_val, double* s_r) {
+  const int tid = threadIdx.x, NT = D / 16;
+  for (int base = 0; base < D; base += NORM_THREADS * NORM_MAXV) {
+    int16_t mv[NORM_MAXV];
+    int8_t ev[NORM_MAXV];
+    #pragma unroll
+    for (int k = 0; k < NORM_MAXV; ++k) {
+      const int i = base + tid + k * NORM_THREADS;
+      if (i < D) { mv[k] = xm[i]; ev[k] = xe[i / 16]; }
+    }
+    #pragma unroll
+    for (int k = 0; k < NORM_MAXV; ++k) {
+      const int i = base + tid + k * NORM_THREADS;
+      if (i < D) {
+        const double x = bfp_decode(mv[k], ev[k]);
+        xs[i] = x;
+        sq[i] = __dmul_rn(x, x);
+      }
+    }
+  }
+  (void)NT;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double r;
+    warp_rms_factor(sq, D, s_lo, s_len, s_val, eps, &r);
+    if (threadIdx.x == 0) *s_r = r;
+  }
+  __syncthreads();
+  return *s_r;
+}
+
+// rmsnorm_fp + tile_quantize (:236-238, :263-264 / :286-287), one CTA per
+// column; output is the matvec-ready form tile_quantize(fpq(y)).
+__global__ void __launch_bounds__(NORM_THREADS)
 rmsnorm_quant_kernel(const int16_t* xm, const int8_t* xe, const double* gamma, double eps, int D, int ncols,
                      int16_t* om, int8_t* oe) {
   extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_lo[96], s_len[96];
+  __shared__ double s_val[96];
+  __shared__ double s_r;
   pdl_trigger();
-  pdl_wait();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x * NORM_WARPS + warp;
-  if (c >= ncols) return;
+  const int c = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
   const int NT = D / 16;
-  double* sq = reinterpret_cast<double*>(smem) + (size_t)warp * (D + 64 + 96);
-  double* s_val = sq + D;
-  int* s_lo = reinterpret_cast<int*>(s_val + 64);
-  int* s_len = s_lo + 96;
-  for (int i = lane; i < D; i += 32) {
-    const double x = bfp_decode(xm[(size_t)c * D + i], xe[(size_t)c * NT + i / 16]);
-    sq[i] = __dmul_rn(x, x);
-  }
-  __syncwarp();
-  double r;
-  warp_rms_factor(sq, D, s_lo, s_len, s_val, eps, &r);
-  for (int base = 0; base < D; base += 32) {
-    const int i = base + lane;
+  double* xs = reinterpret_cast<double*>(smem);
+  double* sq = xs + D;
+  double* gs = sq + D;
+  for (int i = tid; i < D; i += NORM_THREADS) gs[i] = gamma[i];     // weights: before the dependency wait
+  pdl_wait();
+  const double r = block_rms(xm + (size_t)c * D, xe + (size_t)c * NT, D, eps, xs, sq, s_lo, s_len, s_val, &s_r);
+  for (int base = 0; base < D; base += NORM_THREADS) {
+    const int i = base + tid;
     const bool valid = i < D;
-    double y = 0.0;
-    if (valid) {
-      const double x = bfp_decode(xm[(size_t)c * D + i], xe[(size_t)c * NT + i / 16]);
-      y = __ddiv_rn(__dmul_rn(x, gamma[i]), r);             // x * gamma / sqrt(v)
-    }
+    const double y = valid ? __ddiv_rn(__dmul_rn(xs[i], gs[i]), r) : 0.0;   // x * gamma / sqrt(v)
     int e;
     int16_t m = tile_quantize_16lanes(y, &e);               // fpq (:238)
     const unsigned bal = __ballot_sync(0xffffffffu, valid && m == (int16_t)-32768);
@@ -502,9 +562,8 @@ rmsnorm_quant_kernel(const int16_t* xm, const int8_t* xe, const double* gamma, d
 
 cudaError_t launch_rmsnorm(const int16_t* xm, const int8_t* xe, const double* gamma, double eps, int D, int ncols,
                            int16_t* om, int8_t* oe, cudaStream_t s, bool pdl) {
-  const size_t smem = (size_t)NORM_WARPS * (D + 64 + 96) * 8;
-  return launch_ex(rmsnorm_quant_kernel, dim3((ncols + NORM_WARPS - 1) / NORM_WARPS), dim3(NORM_WARPS * 32),
-                   smem, s, pdl, xm, xe, gamma, eps, D, ncols, om, oe);
+  return launch_ex(rmsnorm_quant_kernel, dim3(ncols), dim3(NORM_THREADS), (size_t)3 * D * 8, s, pdl, xm, xe, gamma,
+                   eps, D, ncols, om, oe);
 }
 
 // ---------------------------------------------------------------------------
@@ -582,7 +641,8 @@ cudaError_t launch_rope_kv(const int16_t* qkv_m, const int8_t* qkv_e, int16_t* q
 // GQA attention (:273-283): exact scores, softmax_fp, sequential
 // accumulation attn += sm[t] * v[t], fpq, then tile_quantize for the O matvec.
 // ---------------------------------------------------------------------------
-constexpr int ATT_THREADS = 128;
+constexpr int ATT_THREADS = 256;
+constexpr int ATT_VCHUNK = 256;   // V positions staged in shared memory per pass
 
 __global__ void __launch_bounds__(ATT_THREADS)
 attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
@@ -603,30 +663,36 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   const int grp = d.HQ / d.HKV;
   const int kvh = h / grp;
   const int HD = 64;
-  double* sc = reinterpret_cast<double*>(smem);
+  double* sc = reinterpret_cast<double*>(smem);                                     // [MAX_CTX]
+  const size_t sc_bytes = ((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15);
+  uint4* vs = reinterpret_cast<uint4*>(smem + sc_bytes);                           // [VCHUNK][8]
+  unsigned* ves = reinterpret_cast<unsigned*>(smem + sc_bytes + ATT_VCHUNK * 128);   // [VCHUNK]
   if (tid < HD) s_qm[tid] = qr_m[(size_t)c * d.HQ * HD + h * HD + tid];
   if (tid < 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h * 4 + tid];
   __syncthreads();
   const size_t kbase = (((size_t)slot * d.NL + layer) * d.HKV + kvh) * d.MAX_CTX;
-  // scores[t] = float(np.dot(q, k_t)) / math.sqrt(HD)   (:278)
+  // scores[t] = float(np.dot(q, k_t)) / math.sqrt(HD)   (:278), exact
   double lmax = -INFINITY;
   for (int t = tid; t < T; t += ATT_THREADS) {
     const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
-    const int8_t* ke = kv.ke + (kbase + t) * 4;
+    uint4 kk[8];
+    #pragma unroll
+    for (int u = 0; u < 8; ++u) kk[u] = kr[u];
+    const unsigned ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
     long long S[4];
     int E[4];
     #pragma unroll
     for (int jt = 0; jt < 4; ++jt) {
-      const uint4 k0 = kr[jt * 2], k1 = kr[jt * 2 + 1];
-      const unsigned w[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-      long long s = 0;
+      const unsigned w[8] = {kk[2 * jt].x, kk[2 * jt].y, kk[2 * jt].z, kk[2 * jt].w,
+                             kk[2 * jt + 1].x, kk[2 * jt + 1].y, kk[2 * jt + 1].z, kk[2 * jt + 1].w};
+      long long sacc = 0;
       #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int lo = (int)(int16_t)(w[u] & 0xFFFF), hi = (int)(int16_t)(w[u] >> 16);
-        s += (long long)(s_qm[jt * 16 + 2 * u] * lo) + (long long)(s_qm[jt * 16 + 2 * u + 1] * hi);
+        sacc += (long long)(s_qm[jt * 16 + 2 * u] * lo) + (long long)(s_qm[jt * 16 + 2 * u + 1] * hi);
       }
-      S[jt] = s;
-      E[jt] = s_qe[jt] + (int)ke[jt];
+      S[jt] = sacc;
+      E[jt] = s_qe[jt] + (int)(int8_t)(ke4 >> (8 * jt));
     }
     const double v = __ddiv_rn(exact_tile_dot4(S, E), sqrt_hd);
     sc[t] = v;
@@ -650,17 +716,29 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   __syncthreads();
   const double Ssum = s_bcast;
   for (int t = tid; t < T; t += ATT_THREADS) sc[t] = __ddiv_rn(sc[t], Ssum);
-  __syncthreads();
-  // attn[h] += sm[t] * v[t]  sequentially in t (:280-281)
-  if (tid < 64) {
-    double acc = 0.0;
-    const int16_t* vr = kv.vm + kbase * HD + tid;
-    const int8_t* ve = kv.ve + kbase * 4 + (tid >> 4);
-    #pragma unroll 4
-    for (int t = 0; t < T; ++t) {
-      const double vv = bfp_decode(vr[(size_t)t * HD], ve[(size_t)t * 4]);
-      acc = __dadd_rn(acc, __dmul_rn(sc[t], vv));
+  // attn[h] += sm[t] * v[t], sequential in t (:280-281); V rows staged in
+  // shared memory so the dependent chain only waits on shared loads
+  double acc = 0.0;
+  for (int c0 = 0; c0 < T; c0 += ATT_VCHUNK) {
+    const int n = min(ATT_VCHUNK, T - c0);
+    __syncthreads();
+    const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + (kbase + c0) * HD);
+    for (int i = tid; i < n * 8; i += ATT_THREADS) vs[i] = vsrc[i];
+    const unsigned* esrc = reinterpret_cast<const unsigned*>(kv.ve + (kbase + c0) * 4);
+    for (int i = tid; i < n; i += ATT_THREADS) ves[i] = esrc[i];
+    __syncthreads();
+    if (tid < HD) {
+      const int16_t* vrow = reinterpret_cast<const int16_t*>(vs) + tid;
+      const int sh = 8 * (tid >> 4);
+      #pragma unroll 8
+      for (int t = 0; t < n; ++t) {
+        const int e = (int)(int8_t)(ves[t] >> sh);
+        const double vv = bfp_decode(vrow[(size_t)t * HD], e);
+        acc = __dadd_rn(acc, __dmul_rn(sc[c0 + t], vv));
+      }
     }
+  }
+  if (tid < HD) {
     int e;
     int16_t m = tile_quantize_16lanes(acc, &e);             // fpq(attn)   (:282)
     const unsigned bal = __ballot_sync(0xffffffffu, m == (int16_t)-32768);
@@ -674,7 +752,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
 
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
                              int ncols, int16_t* am, int8_t* ae, cudaStream_t s, bool pdl) {
-  const size_t smem = (size_t)d.MAX_CTX * 8;
+  const size_t smem = (((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15)) + ATT_VCHUNK * 128 + ATT_VCHUNK * 4;
   return launch_ex(attention_kernel, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
                    cols, d, std::sqrt((double)d.HD), am, ae);
 }
@@ -705,43 +783,41 @@ cudaError_t launch_embed(const int16_t* emb_m, const int8_t* emb_e, const int* t
 // certificate that any summation order (the reference's BLAS) picks the
 // same index.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(NORM_WARPS * 32)
+__global__ void __launch_bounds__(NORM_THREADS)
 head_prep_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, double eps, int D, int ncols, double* hn,
                  double* hn_norm) {
   extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_lo[96], s_len[96];
+  __shared__ double s_val[96];
+  __shared__ double s_r;
+  __shared__ double s_ss[NORM_THREADS / 32];
   pdl_trigger();
-  pdl_wait();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x * NORM_WARPS + warp;
-  if (c >= ncols) return;
+  const int c = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
   const int NT = D / 16;
-  double* sq = reinterpret_cast<double*>(smem) + (size_t)warp * (D + 64 + 96);
-  double* s_val = sq + D;
-  int* s_lo = reinterpret_cast<int*>(s_val + 64);
-  int* s_len = s_lo + 96;
-  for (int i = lane; i < D; i += 32) {
-    const double x = bfp_decode(hm[(size_t)c * D + i], he[(size_t)c * NT + i / 16]);
-    sq[i] = __dmul_rn(x, x);
-  }
-  __syncwarp();
-  double r;
-  warp_rms_factor(sq, D, s_lo, s_len, s_val, eps, &r);
+  double* xs = reinterpret_cast<double*>(smem);
+  double* sq = xs + D;
+  pdl_wait();
+  const double r = block_rms(hm + (size_t)c * D, he + (size_t)c * NT, D, eps, xs, sq, s_lo, s_len, s_val, &s_r);
   double ss = 0.0;
-  for (int i = lane; i < D; i += 32) {
-    const double x = bfp_decode(hm[(size_t)c * D + i], he[(size_t)c * NT + i / 16]);
-    const double y = __dmul_rn(__ddiv_rn(x, r), norm_w[i]);
+  for (int i = tid; i < D; i += NORM_THREADS) {
+    const double y = __dmul_rn(__ddiv_rn(xs[i], r), norm_w[i]);     // (h / sqrt(...)) * norm_w_q  (:438)
     hn[(size_t)c * D + i] = y;
     ss = fma(y, y, ss);
   }
   for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  if (lane == 0) hn_norm[c] = sqrt(ss) * (1.0 + 1e-12);
+  if (lane == 0) s_ss[tid >> 5] = ss;
+  __syncthreads();
+  if (tid == 0) {
+    double t = 0.0;
+    for (int w = 0; w < NORM_THREADS / 32; ++w) t += s_ss[w];
+    hn_norm[c] = sqrt(t) * (1.0 + 1e-12);
+  }
 }
 
 cudaError_t launch_head_prep(const int16_t* hm, const int8_t* he, const double* norm_w, double eps, int D, int ncols,
                              double* hn, double* hn_norm, cudaStream_t s, bool pdl) {
-  const size_t smem = (size_t)NORM_WARPS * (D + 64 + 96) * 8;
-  return launch_ex(head_prep_kernel, dim3((ncols + NORM_WARPS - 1) / NORM_WARPS), dim3(NORM_WARPS * 32), smem, s,
-                   pdl, hm, he, norm_w, eps, D, ncols, hn, hn_norm);
+  return launch_ex(head_prep_kernel, dim3(ncols), dim3(NORM_THREADS), (size_t)2 * D * 8, s, pdl, hm, he, norm_w, eps,
+                   D, ncols, hn, hn_norm);
 }
 
 template <int RT, int CT, int TR, int TC>
@@ -831,14 +907,109 @@ head_logits_kernel(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, 
   }
 }
 
+// Few columns: one warp streams a whole embedding row (coalesced 1152 B) and
+// dots it with every column's hn (kept in shared memory); two rows in flight
+// per warp.  Per CTA: best / runner-up per column over the rows it visited.
+template <int NC>
+__global__ void __launch_bounds__(256)
+head_gemv_kernel(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, const double* hn, int ncols,
+                 double* part_val, int* part_idx, double* part_second) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ double w_best[8][NC], w_sec[8][NC];
+  __shared__ int w_idx[8][NC];
+  pdl_trigger();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  double* hs = reinterpret_cast<double*>(smem);     // [NC][D]
+  const int NT = D / 16, NU = D / 8;                // uint4 per row
+  pdl_wait();
+  for (int i = tid; i < NC * D; i += 256) {
+    const int cc = i / D, k = i % D;
+    hs[i] = cc < ncols ? hn[(size_t)cc * D + k] : 0.0;
+  }
+  __syncthreads();
+  double best[NC], sec[NC];
+  int bidx[NC];
+  #pragma unroll
+  for (int cc = 0; cc < NC; ++cc) { best[cc] = -INFINITY; sec[cc] = -INFINITY; bidx[cc] = 0x7fffffff; }
+  const int gw = blockIdx.x * 8 + warp, nw = gridDim.x * 8;
+  for (int v0 = gw; v0 < VOCAB; v0 += 2 * nw) {
+    const int vr[2] = {v0, v0 + nw};
+    uint4 w[2][3];
+    int ex[2][3];
+    #pragma unroll
+    for (int q = 0; q < 2; ++q)
+      #pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int u = lane + 32 * j;
+        if (vr[q] < VOCAB && u < NU) {
+          w[q][j] = reinterpret_cast<const uint4*>(emb_m + (size_t)vr[q] * D)[u];
+          ex[q][j] = emb_e[(size_t)vr[q] * NT + u / 2];
+        }
+      }
+    #pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (vr[q] >= VOCAB) break;
+      double acc[NC];
+      #pragma unroll
+      for (int cc = 0; cc < NC; ++cc) acc[cc] = 0.0;
+      #pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int u = lane + 32 * j;
+        if (u < NU) {
+          const double sc = pow2(ex[q][j] - 15);
+          const unsigned ww[4] = {w[q][j].x, w[q][j].y, w[q][j].z, w[q][j].w};
+          #pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const int mv = (int)(int16_t)((ww[t >> 1] >> (16 * (t & 1))) & 0xFFFF);
+            const double ev = (double)mv * sc;
+            #pragma unroll
+            for (int cc = 0; cc < NC; ++cc) acc[cc] = fma(ev, hs[cc * D + u * 8 + t], acc[cc]);
+          }
+        }
+      }
+      #pragma unroll
+      for (int cc = 0; cc < NC; ++cc) {
+        #pragma unroll
+        for (int off = 16; off; off >>= 1) acc[cc] += __shfl_xor_sync(0xffffffffu, acc[cc], off);
+        const double x = acc[cc];
+        if (x > best[cc]) { sec[cc] = best[cc]; best[cc] = x; bidx[cc] = vr[q]; }
+        else if (x > sec[cc]) sec[cc] = x;
+      }
+    }
+  }
+  if (lane == 0)
+    #pragma unroll
+    for (int cc = 0; cc < NC; ++cc) { w_best[warp][cc] = best[cc]; w_sec[warp][cc] = sec[cc]; w_idx[warp][cc] = bidx[cc]; }
+  __syncthreads();
+  if (tid < NC && tid < ncols) {
+    double b = -INFINITY, sc2 = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int ww = 0; ww < 8; ++ww) {
+      const double x = w_best[ww][tid];
+      const int xi = w_idx[ww][tid];
+      if (x > b || (x == b && xi < bi)) { sc2 = fmax(sc2, b); b = x; bi = xi; }
+      else sc2 = fmax(sc2, x);
+      sc2 = fmax(sc2, w_sec[ww][tid]);
+    }
+    const size_t o = (size_t)tid * gridDim.x + blockIdx.x;
+    part_val[o] = b; part_idx[o] = bi; part_second[o] = sc2;
+  }
+}
+
 cudaError_t launch_head_logits(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, const double* hn,
                                int ncols, double* part_val, int* part_idx, double* part_second, int* n_rowblocks,
                                cudaStream_t s, bool pdl) {
-  if (ncols <= 4) {
-    constexpr int RT = 256, CT = 4;
-    *n_rowblocks = (VOCAB + RT - 1) / RT;
-    return launch_ex(head_logits_kernel<RT, CT, 4, 1>, dim3(*n_rowblocks, (ncols + CT - 1) / CT), dim3(256), 0, s,
-                     pdl, emb_m, emb_e, VOCAB, D, hn, ncols, part_val, part_idx, part_second);
+  if (ncols <= 4 && D % 8 == 0 && D <= 768) {
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    *n_rowblocks = 2 * nsm;
+    const size_t smem = (size_t)(ncols <= 1 ? 1 : 4) * D * 8;
+    if (ncols <= 1)
+      return launch_ex(head_gemv_kernel<1>, dim3(*n_rowblocks), dim3(256), smem, s, pdl, emb_m, emb_e, VOCAB, D, hn,
+                       ncols, part_val, part_idx, part_second);
+    return launch_ex(head_gemv_kernel<4>, dim3(*n_rowblocks), dim3(256), smem, s, pdl, emb_m, emb_e, VOCAB, D, hn,
+                     ncols, part_val, part_idx, part_second);
   }
   constexpr int RT = 64, CT = 64;
   *n_rowblocks = (VOCAB + RT - 1) / RT;
@@ -1150,6 +1321,9 @@ cudaError_t init_kernel_attributes() {
   set((const void*)rmsnorm_fp_kernel);
   set((const void*)softmax_fp_kernel);
   set((const void*)np_sum_kernel);
-  return e;
+  set((const void*)head_gemv_kernel<1>);
+  set((const void*)head_gemv_kernel<4>);
+  const cudaError_t g = init_gemv_attributes();
+  return e != cudaSuccess ? e : g;
 }
 }  // namespace bfp

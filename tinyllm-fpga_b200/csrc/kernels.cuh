@@ -39,14 +39,10 @@ struct MatmulArgs {
   unsigned* counters = nullptr;  // K-split arrival counters, zero between uses
   int acc_ld = 0;                // columns per accumulator row
   int ksplit = 1;
+  int cluster = 0;               // 1: the ksplit CTAs of a tile form a cluster and reduce through
+                                 //    distributed shared memory (ksplit <= 8); 0: global atomics
   int rg = 1;                    // row groups per CTA (1, 2 or 4)
   int bn = 1;                    // columns per CTA
-};
-
-// Per-column descriptors of a forward pass.
-struct ColDesc {
-  const int* slot = nullptr;  // KV slot of the column
-  const int* pos = nullptr;   // position (step) of the column
 };
 
 struct KvArena {
@@ -56,6 +52,46 @@ struct KvArena {
   int8_t* ve = nullptr;
   int NL = 0, HKV = 0, HD = 64, MAX_CTX = 0;
 };
+
+// Small-batch matvec family (gemv.cu), 1..4 columns.
+enum GemvMode : int {
+  GV_STORE = 0,     // out = quant(matvec)
+  GV_RESIDUAL = 1,  // out = quant(res + quant(matvec))
+  GV_SWIGLU = 2,    // interleaved gate/up groups -> requant(quant(quant(silu(g)) * u))
+  GV_QKV_ROPE = 3,  // fused Q/K/V rows: RoPE on q/k heads, q -> qr buffer, k/v -> KV arena
+};
+
+struct GemvArgs {
+  DevMat W;
+  const int16_t* xm = nullptr;   // input columns (NORM: un-normalised)
+  const int8_t* xe = nullptr;
+  int x_ld = 0, x_lde = 0;
+  int ncols = 0;
+  int mode = GV_STORE;
+  int norm = 0;                  // 1: tile_quantize(rmsnorm_fp(x, gamma)) prologue
+  const double* gamma = nullptr;
+  double eps = 1e-5;
+  int16_t* om = nullptr;
+  int8_t* oe = nullptr;
+  int o_ld = 0, o_lde = 0;
+  const int16_t* rm = nullptr;   // residual (GV_RESIDUAL)
+  const int8_t* re = nullptr;
+  // GV_QKV_ROPE
+  const double* rope_cs = nullptr;
+  const int* col_slot = nullptr;
+  const int* col_pos = nullptr;
+  KvArena kv;
+  int layer = 0, HQ = 0, HKV = 0;
+  int16_t* qr_m = nullptr;
+  int8_t* qr_e = nullptr;
+};
+
+// Per-column descriptors of a forward pass.
+struct ColDesc {
+  const int* slot = nullptr;  // KV slot of the column
+  const int* pos = nullptr;   // position (step) of the column
+};
+
 
 struct Dims {
   int D, HQ, HKV, HD, FFN, NL, VOCAB, MAX_CTX;
@@ -68,6 +104,9 @@ cudaError_t launch_matmul(const MatmulArgs& a, cudaStream_t s, bool pdl);
 // rg 1 or 2, no programmatic dependent launch.
 cudaError_t launch_matmul_refw(const MatmulArgs& a, cudaStream_t s);
 size_t matmul_refw_smem_bytes(int rg, int bn, int ntc, int NT);
+cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl);
+bool gemv_supported(int mode, bool norm, int NT, int ncols);
+cudaError_t init_gemv_attributes();
 // Raises the dynamic shared memory limit of every kernel (call once per device).
 cudaError_t init_kernel_attributes();
 // Reads and clears the device flag a bounded wait sets when it gives up.
