@@ -260,6 +260,37 @@ __device__ __forceinline__ double np_sum_warp_perfect(const double* a, int k, in
   return __dadd_rn(0.0, __shfl_sync(0xffffffffu, v, 0));
 }
 
+// numpy sum driven by a precomputed plan of its pairwise tree (built on the
+// host by build_pw_plan for every length): plan = [L, H, leaf starts (L),
+// internal nodes per height (H), then (left, right) value slots of every
+// internal node ordered by height].  Leaves are summed by separate lanes,
+// then each height level is combined in parallel; value slots: leaves
+// 0..L-1, internal node j -> L + j.  sval needs 2L - 1 doubles.
+__device__ __forceinline__ double np_sum_warp_plan(const double* a, int n, const unsigned short* plan, double* sval) {
+  const int lane = threadIdx.x & 31;
+  const int L = plan[0], H = plan[1];
+  const unsigned short* starts = plan + 2;
+  const unsigned short* lvl = starts + L;
+  const unsigned short* ops = lvl + H;
+  for (int k = lane; k < L; k += 32) {
+    const int s0 = starts[k], e0 = (k + 1 < L) ? starts[k + 1] : n;
+    sval[k] = np_pw_leaf(a + s0, e0 - s0);
+  }
+  __syncwarp();
+  int base = 0;
+  for (int h = 0; h < H; ++h) {
+    const int cnt = lvl[h];
+    for (int j = lane; j < cnt; j += 32) {
+      const int o = base + j;
+      sval[L + o] = __dadd_rn(sval[ops[2 * o]], sval[ops[2 * o + 1]]);
+    }
+    base += cnt;
+    __syncwarp();
+  }
+  const double r = H ? sval[L + base - 1] : sval[0];
+  return __dadd_rn(0.0, r);
+}
+
 // Warp-cooperative numpy sum of a shared-memory array (n <= 8192).  All 32
 // lanes must call it; scratch needs 3*64 words of shared memory.  Returns the
 // sum on every lane.

@@ -54,14 +54,18 @@ struct DBuf {
     p = nullptr;
     n = 0;
   }
-  // (Re)allocates to at least `count` elements, zero-filled.
+  // (Re)allocates to at least `count` elements, zero-filled.  The fill runs on
+  // the legacy default stream, which does not order against the handle's
+  // non-blocking stream: wait for it before the buffer is used.
   cudaError_t ensure(size_t count) {
     if (count <= n && p) return cudaSuccess;
     release();
     cudaError_t e = cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T));
     if (e != cudaSuccess) { p = nullptr; return e; }
     n = count;
-    return cudaMemset(p, 0, std::max<size_t>(count, 1) * sizeof(T));
+    e = cudaMemset(p, 0, std::max<size_t>(count, 1) * sizeof(T));
+    if (e != cudaSuccess) return e;
+    return cudaStreamSynchronize(0);
   }
 };
 
@@ -132,6 +136,51 @@ const Region* find_region(const std::vector<Region>& rs, const std::string& name
   for (auto& r : rs)
     if (r.name == name) return &r;
   return nullptr;
+}
+
+// numpy pairwise-summation plan of a length n (see np_sum_warp_plan): the
+// recursive tree of pairwise_sum (leaves <= 128, split at n/2 rounded down to
+// a multiple of 8), flattened to leaf starts and internal nodes by height.
+void build_pw_plan_one(int n, std::vector<unsigned short>& out) {
+  struct Node { int lo, len, left, right, height; };
+  std::vector<Node> nodes;
+  std::vector<int> leaves;
+  auto build = [&](auto&& self, int lo, int len) -> int {
+    if (len <= 128) {
+      nodes.push_back({lo, len, -1, -1, 0});
+      leaves.push_back((int)nodes.size() - 1);
+      return (int)nodes.size() - 1;
+    }
+    int n2 = len / 2;
+    n2 -= n2 % 8;
+    const int l = self(self, lo, n2);
+    const int r = self(self, lo + n2, len - n2);
+    nodes.push_back({lo, len, l, r, std::max(nodes[l].height, nodes[r].height) + 1});
+    return (int)nodes.size() - 1;
+  };
+  build(build, 0, n);
+  std::vector<int> internal;
+  for (int i = 0; i < (int)nodes.size(); ++i)
+    if (nodes[i].left >= 0) internal.push_back(i);
+  std::stable_sort(internal.begin(), internal.end(),
+                   [&](int a, int b) { return nodes[a].height < nodes[b].height; });
+  std::vector<int> slot(nodes.size(), -1);
+  const int L = (int)leaves.size();
+  for (int k = 0; k < L; ++k) slot[leaves[k]] = k;
+  for (int j = 0; j < (int)internal.size(); ++j) slot[internal[j]] = L + j;
+  const int H = internal.empty() ? 0 : nodes[internal.back()].height;
+  out.push_back((unsigned short)L);
+  out.push_back((unsigned short)H);
+  for (int k = 0; k < L; ++k) out.push_back((unsigned short)nodes[leaves[k]].lo);
+  for (int hgt = 1; hgt <= H; ++hgt) {
+    int cnt = 0;
+    for (int i : internal) cnt += nodes[i].height == hgt;
+    out.push_back((unsigned short)cnt);
+  }
+  for (int i : internal) {
+    out.push_back((unsigned short)slot[nodes[i].left]);
+    out.push_back((unsigned short)slot[nodes[i].right]);
+  }
 }
 
 // Exact (m, e) form of a tile of BFP grid values (lossless; a tile whose
@@ -211,6 +260,8 @@ struct bfp200_handle {
   DBuf<double> emb_norm;
   double emb_norm_max = 0.0;
   DBuf<double> rope_cs;
+  DBuf<int> pw_off;                 // numpy pairwise-sum plans for lengths 0..MAX_CTX
+  DBuf<unsigned short> pw_data;
   std::vector<int16_t> g1m, g2m, nwm;
   std::vector<int8_t> g1e, g2e, nwe;
   std::vector<int32_t> rom_prompt;
@@ -385,7 +436,8 @@ int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool firs
   CK(launch_rope_kv(h->qkv_m.p, h->qkv_e.p, h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), h->rope_cs.p, d, ncols, s, pdl));
   // attention -> tile_quantize(fpq(attn))                 (:273-283)
   mark(h, PK_ATTENTION);
-  CK(launch_attention(h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), d, ncols, h->a_m.p, h->a_e.p, s, pdl));
+  CK(launch_attention(h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), d, ncols, h->a_m.p, h->a_e.p, s, pdl,
+                      h->pw_off.p, h->pw_data.p));
   if (sink) {
     CKR(download_decoded(h, h->qr_m.p, h->qr_e.p, h->QD, h->QD, 0, ncols, sink->st[1]));
     CKR(download_decoded(h, h->a_m.p, h->a_e.p, h->QD, h->QD, 0, ncols, sink->st[4]));
@@ -495,7 +547,7 @@ int enqueue_layer_small(bfp200_handle* h, int l, int ncols, bool first_pdl) {
   CKR(enqueue_gemv_qkv(h, l, ncols, pdl && first_pdl));
   mark(h, PK_ATTENTION);
   CK(launch_attention(h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), h->dims(), ncols, h->a_m.p, h->a_e.p, h->stream,
-                      pdl));
+                      pdl, h->pw_off.p, h->pw_data.p));
   mark(h, PK_MM_O);
   CKR(enqueue_gemv_o(h, l, ncols, pdl, h->h1_m.p, h->h1_e.p));
   mark(h, PK_MM_GU);
@@ -610,9 +662,25 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
   std::vector<double> cs((size_t)h->MAXC * h->HD);
   bfp200_rope_table(cs.data(), h->MAXC, h->HD, cfg->rope_base);
   if (h->rope_cs.ensure(cs.size()) != cudaSuccess ||
-      cudaMemcpy(h->rope_cs.p, cs.data(), cs.size() * 8, cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaMemcpyAsync(h->rope_cs.p, cs.data(), cs.size() * 8, cudaMemcpyHostToDevice, h->stream) != cudaSuccess ||
+      cudaStreamSynchronize(h->stream) != cudaSuccess) {
     delete h;
     return fail(BFP200_ENOMEM, "open: rope table allocation failed");
+  }
+  {
+    std::vector<int> offs(h->MAXC + 1, 0);
+    std::vector<unsigned short> data;
+    for (int n = 1; n <= h->MAXC; ++n) {
+      offs[n] = (int)data.size();
+      build_pw_plan_one(n, data);
+    }
+    if (h->pw_off.ensure(offs.size()) != cudaSuccess || h->pw_data.ensure(data.size()) != cudaSuccess ||
+        cudaMemcpyAsync(h->pw_off.p, offs.data(), offs.size() * 4, cudaMemcpyHostToDevice, h->stream) != cudaSuccess ||
+        cudaMemcpyAsync(h->pw_data.p, data.data(), data.size() * 2, cudaMemcpyHostToDevice, h->stream) != cudaSuccess ||
+        cudaStreamSynchronize(h->stream) != cudaSuccess) {
+      delete h;
+      return fail(BFP200_ENOMEM, "open: pairwise-sum plan allocation failed");
+    }
   }
   *out = h;
   return BFP200_OK;
@@ -636,9 +704,10 @@ static int upload_gammas(bfp200_handle* h) {
   decode_vec(h->g2m.data(), h->g2e.data(), g2.size(), g2.data());
   decode_vec(h->nwm.data(), h->nwe.data(), nw.size(), nw.data());
   CK(h->g1.ensure(g1.size())); CK(h->g2.ensure(g2.size())); CK(h->nw.ensure(nw.size()));
-  CK(cudaMemcpy(h->g1.p, g1.data(), g1.size() * 8, cudaMemcpyHostToDevice));
-  CK(cudaMemcpy(h->g2.p, g2.data(), g2.size() * 8, cudaMemcpyHostToDevice));
-  CK(cudaMemcpy(h->nw.p, nw.data(), nw.size() * 8, cudaMemcpyHostToDevice));
+  CK(cudaMemcpyAsync(h->g1.p, g1.data(), g1.size() * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(h->g2.p, g2.data(), g2.size() * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemcpyAsync(h->nw.p, nw.data(), nw.size() * 8, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
   return BFP200_OK;
 }
 
@@ -1129,7 +1198,14 @@ int bfp200_pairwise_sum(bfp200_handle* h, const double* x, int n, int ncols, dou
   DBuf<double> dx, dout;
   CK(dx.ensure((size_t)n * ncols)); CK(dout.ensure(ncols));
   CK(cudaMemcpyAsync(dx.p, x, (size_t)n * ncols * 8, cudaMemcpyHostToDevice, h->stream));
-  CK(launch_np_sum(dx.p, n, ncols, dout.p, h->stream));
+  // the plan-driven reduction the attention kernel uses; the generic
+  // single-lane tree walk is exercised by softmax_fp
+  std::vector<unsigned short> plan;
+  build_pw_plan_one(n, plan);
+  DBuf<unsigned short> dplan;
+  CK(dplan.ensure(plan.size()));
+  CK(cudaMemcpyAsync(dplan.p, plan.data(), plan.size() * 2, cudaMemcpyHostToDevice, h->stream));
+  CK(launch_np_sum_plan(dx.p, n, ncols, dplan.p, dout.p, h->stream));
   CK(cudaMemcpyAsync(out, dout.p, (size_t)ncols * 8, cudaMemcpyDeviceToHost, h->stream));
   CK(cudaStreamSynchronize(h->stream));
   return BFP200_OK;

@@ -125,12 +125,26 @@ gemv_kernel(GemvArgs a) {
   gv_pdl_wait();
   // ---- input columns (optionally RMS-normalised) into shared memory
   if constexpr (NORM) {
-    for (int i = tid; i < NC * K; i += GV_THREADS) {
-      const int c = i / K, k = i % K;
-      double x = 0.0;
-      if (c < a.ncols) x = bfp_decode(a.xm[(size_t)c * a.x_ld + k], a.xe[(size_t)c * a.x_lde + k / 16]);
-      xs[i] = x;
-      sq[i] = __dmul_rn(x, x);
+    constexpr int PER = 4;            // loads in flight per thread per round
+    for (int base = 0; base < NC * K; base += GV_THREADS * PER) {
+      int16_t mv[PER];
+      int8_t ev[PER];
+      #pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int i = base + tid + q * GV_THREADS;
+        const int c = i / K, k = i % K;
+        mv[q] = 0; ev[q] = 0;
+        if (i < NC * K && c < a.ncols) { mv[q] = a.xm[(size_t)c * a.x_ld + k]; ev[q] = a.xe[(size_t)c * a.x_lde + k / 16]; }
+      }
+      #pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int i = base + tid + q * GV_THREADS;
+        if (i < NC * K) {
+          const double x = bfp_decode(mv[q], ev[q]);
+          xs[i] = x;
+          sq[i] = __dmul_rn(x, x);
+        }
+      }
     }
     __syncthreads();
     if (warp < NC) {   // column `warp`: r = sqrt(mean(x*x) + eps)   (:237)

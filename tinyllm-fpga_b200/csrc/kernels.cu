@@ -646,14 +646,14 @@ constexpr int ATT_VCHUNK = 256;   // V positions staged in shared memory per pas
 
 __global__ void __launch_bounds__(ATT_THREADS)
 attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
-                 double sqrt_hd, int16_t* am, int8_t* ae) {
+                 double sqrt_hd, int16_t* am, int8_t* ae, const int* pw_off, const unsigned short* pw_data) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_qm[64];
   __shared__ int s_qe[4];
   __shared__ double s_red[ATT_THREADS / 32];
   __shared__ double s_bcast;
   __shared__ int s_lo[96], s_len[96];
-  __shared__ double s_val[96];
+  __shared__ double s_val[160];
   pdl_trigger();
   pdl_wait();
   const int c = blockIdx.x, h = blockIdx.y;
@@ -671,6 +671,21 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   if (tid < 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h * 4 + tid];
   __syncthreads();
   const size_t kbase = (((size_t)slot * d.NL + layer) * d.HKV + kvh) * d.MAX_CTX;
+  // the first V chunk streams into shared memory while the scores are formed
+  {
+    const int n0 = min(ATT_VCHUNK, T);
+    const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + kbase * HD);
+    for (int i = tid; i < n0 * 8; i += ATT_THREADS) {
+      const unsigned dst = (unsigned)__cvta_generic_to_shared(vs + i);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(vsrc + i) : "memory");
+    }
+    const unsigned* esrc = reinterpret_cast<const unsigned*>(kv.ve + kbase * 4);
+    for (int i = tid; i < n0; i += ATT_THREADS) {
+      const unsigned dst = (unsigned)__cvta_generic_to_shared(ves + i);
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(dst), "l"(esrc + i) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   // scores[t] = float(np.dot(q, k_t)) / math.sqrt(HD)   (:278), exact
   double lmax = -INFINITY;
   for (int t = tid; t < T; t += ATT_THREADS) {
@@ -710,7 +725,8 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   for (int t = tid; t < T; t += ATT_THREADS) sc[t] = exp(__dsub_rn(sc[t], mx));
   __syncthreads();
   if (warp == 0) {
-    const double S = np_sum_warp(sc, T, s_lo, s_len, s_val);
+    const double S = pw_off ? np_sum_warp_plan(sc, T, pw_data + pw_off[T], s_val)
+                            : np_sum_warp(sc, T, s_lo, s_len, s_val);
     if (lane == 0) s_bcast = S;
   }
   __syncthreads();
@@ -721,11 +737,15 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   double acc = 0.0;
   for (int c0 = 0; c0 < T; c0 += ATT_VCHUNK) {
     const int n = min(ATT_VCHUNK, T - c0);
-    __syncthreads();
-    const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + (kbase + c0) * HD);
-    for (int i = tid; i < n * 8; i += ATT_THREADS) vs[i] = vsrc[i];
-    const unsigned* esrc = reinterpret_cast<const unsigned*>(kv.ve + (kbase + c0) * 4);
-    for (int i = tid; i < n; i += ATT_THREADS) ves[i] = esrc[i];
+    if (c0 == 0) {
+      asm volatile("cp.async.wait_all;" ::: "memory");
+    } else {
+      __syncthreads();
+      const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + (kbase + c0) * HD);
+      for (int i = tid; i < n * 8; i += ATT_THREADS) vs[i] = vsrc[i];
+      const unsigned* esrc = reinterpret_cast<const unsigned*>(kv.ve + (kbase + c0) * 4);
+      for (int i = tid; i < n; i += ATT_THREADS) ves[i] = esrc[i];
+    }
     __syncthreads();
     if (tid < HD) {
       const int16_t* vrow = reinterpret_cast<const int16_t*>(vs) + tid;
@@ -751,10 +771,11 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
 }
 
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
-                             int ncols, int16_t* am, int8_t* ae, cudaStream_t s, bool pdl) {
+                             int ncols, int16_t* am, int8_t* ae, cudaStream_t s, bool pdl, const int* pw_off,
+                             const unsigned short* pw_data) {
   const size_t smem = (((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15)) + ATT_VCHUNK * 128 + ATT_VCHUNK * 4;
   return launch_ex(attention_kernel, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
-                   cols, d, std::sqrt((double)d.HD), am, ae);
+                   cols, d, std::sqrt((double)d.HD), am, ae, pw_off, pw_data);
 }
 
 // ---------------------------------------------------------------------------
@@ -1187,6 +1208,22 @@ cudaError_t launch_np_sum(const double* x, int n, int ncols, double* out, cudaSt
   return launch_ex(np_sum_kernel, dim3(ncols), dim3(32), (size_t)n * 8, s, false, x, n, out);
 }
 
+__global__ void np_sum_plan_kernel(const double* x, int n, const unsigned short* plan, double* out) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ double s_val[160];
+  const int c = blockIdx.x, lane = threadIdx.x;
+  double* a = reinterpret_cast<double*>(smem);
+  for (int i = lane; i < n; i += 32) a[i] = x[(size_t)c * n + i];
+  __syncwarp();
+  const double S = np_sum_warp_plan(a, n, plan, s_val);
+  if (lane == 0) out[c] = S;
+}
+
+cudaError_t launch_np_sum_plan(const double* x, int n, int ncols, const unsigned short* plan, double* out,
+                               cudaStream_t s) {
+  return launch_ex(np_sum_plan_kernel, dim3(ncols), dim3(32), (size_t)n * 8, s, false, x, n, plan, out);
+}
+
 cudaError_t launch_softmax_fp(const double* x, int n, int ncols, double* out, cudaStream_t s) {
   return launch_ex(softmax_fp_kernel, dim3(ncols), dim3(32), (size_t)n * 8, s, false, x, n, out);
 }
@@ -1321,6 +1358,7 @@ cudaError_t init_kernel_attributes() {
   set((const void*)rmsnorm_fp_kernel);
   set((const void*)softmax_fp_kernel);
   set((const void*)np_sum_kernel);
+  set((const void*)np_sum_plan_kernel);
   set((const void*)head_gemv_kernel<1>);
   set((const void*)head_gemv_kernel<4>);
   const cudaError_t g = init_gemv_attributes();

@@ -117,9 +117,12 @@ cudaError_t launch_rmsnorm(const int16_t* xm, const int8_t* xe, const double* ga
 cudaError_t launch_rope_kv(const int16_t* qkv_m, const int8_t* qkv_e, int16_t* qr_m, int8_t* qr_e,
                            KvArena kv, int layer, ColDesc cols, const double* rope_cs, Dims d,
                            int ncols, cudaStream_t s, bool pdl);
+// pw_off / pw_data: numpy pairwise-sum plans for lengths 1..MAX_CTX
+// (build_pw_plan), or nullptr for the generic single-lane tree walk.
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
                              ColDesc cols, Dims d, int ncols, int16_t* am, int8_t* ae,
-                             cudaStream_t s, bool pdl);
+                             cudaStream_t s, bool pdl, const int* pw_off = nullptr,
+                             const unsigned short* pw_data = nullptr);
 cudaError_t launch_embed(const int16_t* emb_m, const int8_t* emb_e, const int* tokens, int D,
                          int ncols, int16_t* hm, int8_t* he, cudaStream_t s, bool pdl);
 cudaError_t launch_head_prep(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
@@ -142,6 +145,9 @@ cudaError_t launch_rmsnorm_fp(const double* x, const double* gamma, double eps, 
 cudaError_t launch_silu_fp(const double* x, long long n, double* out, cudaStream_t s);
 // numpy's float64 add.reduce (pairwise summation) of ncols rows of n values.
 cudaError_t launch_np_sum(const double* x, int n, int ncols, double* out, cudaStream_t s);
+// Same sum evaluated from a host-built plan of the pairwise tree (np_sum_warp_plan).
+cudaError_t launch_np_sum_plan(const double* x, int n, int ncols, const unsigned short* plan, double* out,
+                               cudaStream_t s);
 cudaError_t launch_softmax_fp(const double* x, int n, int ncols, double* out, cudaStream_t s);
 cudaError_t launch_rope_fp(const double* x, const double* cs, int HD, int nvec, double* out, cudaStream_t s);
 // Converts reference-layout weights (m [R][NT][16], e [R][NT]) to DevMat layout.
