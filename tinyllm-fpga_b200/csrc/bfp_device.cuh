@@ -33,59 +33,80 @@ __host__ __device__ __forceinline__ int ilog2_u32(unsigned v) {
 #endif
 }
 
-// Number of doubles directly below 2^j that a correctly rounded log2 maps to
-// exactly j (so floor(log2(x)) jumps to j before x reaches 2^j).  Derived
-// from log2(2^j (1 - n 2^-53)) = j - n 2^-53 / ln 2 rounding to j; the
-// values below are floor(ln2 * 2^b) for the ulp exponent b of the result's
-// binade.  numpy's float64 log2 follows this exactly (checked by the tests on
-// every host that generates or compares golden data).
-__host__ __device__ __forceinline__ int log2_roundup_count(int j) {
-  if (j == 0) return 0;
-  int aj = j < 0 ? -j : j;
-  int a = ilog2_u32((unsigned)aj);
-  int b = (j > 0 && (aj & (aj - 1)) == 0) ? a - 1 : a;
-  switch (b) {
-    case 1: return 1;    case 2: return 2;    case 3: return 5;    case 4: return 11;
-    case 5: return 22;   case 6: return 44;   case 7: return 88;   case 8: return 177;
-    case 9: return 354;  case 10: return 709;
-    default: return 0;
-  }
-}
-
-// floor(np.log2(x)) for a finite positive normal double, numpy-exact.
-__host__ __device__ __forceinline__ int floor_log2_np(double x) {
+__host__ __device__ __forceinline__ unsigned long long dbits(double x) {
 #ifdef __CUDA_ARCH__
-  unsigned long long bits = (unsigned long long)__double_as_longlong(x);
+  return (unsigned long long)__double_as_longlong(x);
 #else
   union { double d; unsigned long long i; } u; u.d = x;
-  unsigned long long bits = u.i;
+  return u.i;
 #endif
-  int k = (int)((bits >> 52) & 0x7FF) - 1023;
-  unsigned long long F = bits & ((1ULL << 52) - 1);
-  int n = log2_roundup_count(k + 1);
-  return (n > 0 && F >= (1ULL << 52) - (unsigned long long)n) ? k + 1 : k;
 }
 
-// Tile exponent of tile_quantize (:92-93) from the tile's max |v|.
-// NaN/Inf follow numpy's x86 cast (INT32_MIN + 1, clipped to -127).
-__host__ __device__ __forceinline__ int tile_exponent(double max_abs) {
-  if (!(max_abs <= 1.7976931348623157e308)) return -127;     // NaN or +Inf
-  if (max_abs < 1e-300) max_abs = 1e-300;
-  int e = floor_log2_np(max_abs) + 1;
+// Number of doubles directly below 2^j that a correctly rounded log2 maps to
+// exactly j (so floor(log2(x)) jumps to j before x reaches 2^j):
+// log2(2^j (1 - n 2^-53)) = j - n 2^-53 / ln 2 rounds to j while n < ln2 * 2^b,
+// b the ulp exponent of the result's binade, i.e. n = floor(ln2 * 2^b) =
+// 0xB17217F7 >> (32 - b) (ln 2 in 0.32 fixed point; no fractional part of
+// ln2 * 2^b is close enough to an integer for the truncation to matter).
+// numpy's float64 log2 follows this exactly (checked by the tests on every
+// host that generates or compares golden data).
+__host__ __device__ __forceinline__ unsigned log2_roundup_count(int j) {
+  const unsigned aj = (unsigned)(j < 0 ? -j : j);
+  const int a = aj ? ilog2_u32(aj) : 0;
+  const int b = a - ((j > 0 && (aj & (aj - 1)) == 0) ? 1 : 0);
+  return (j != 0 && b >= 1) ? (0xB17217F7u >> (32 - b)) : 0u;
+}
+
+// Tile exponent of tile_quantize (:92-93) from the bit pattern of the tile's
+// max |v| (sign cleared): e = clip(floor(np.log2(max(max_abs, 1e-300))) + 1).
+// NaN/Inf follow numpy's x86 cast (INT32_MIN + 1, clipped to -127).  32-bit
+// arithmetic on the two halves of the pattern.
+__host__ __device__ __forceinline__ int tile_exponent_bits(unsigned long long abits) {
+  unsigned hi = (unsigned)(abits >> 32), lo = (unsigned)abits;
+  if (hi >= 0x7FF00000u) return -127;
+  constexpr unsigned FHI = 0x01a56e1fu, FLO = 0xc2f8f359u;        // bits of 1e-300
+  if (hi < FHI || (hi == FHI && lo < FLO)) { hi = FHI; lo = FLO; }
+  const int k = (int)(hi >> 20) - 1023;                           // x in [2^k, 2^(k+1))
+  const unsigned n = log2_roundup_count(k + 1);
+  // fraction F >= 2^52 - n  (n < 2^10): top 20 fraction bits all ones and lo >= 2^32 - n
+  const bool up = n > 0 && (hi & 0xFFFFFu) == 0xFFFFFu && lo >= 0u - n;
+  const int e = k + (up ? 1 : 0) + 1;
   return e < -127 ? -127 : (e > 127 ? 127 : e);
 }
 
-// Mantissa of tile_quantize (:94-96): clip(rint(v / 2^e * 32768)).  Values
-// whose int64 cast is undefined in numpy (NaN, |x| >= 2^63) give x86's
-// INT64_MIN, i.e. -32768 after the clip.
-__host__ __device__ __forceinline__ int16_t tile_mantissa(double v, int e) {
-  double x = v * pow2(15 - e);
-  if (!(x > -9.2233720368547758e18 && x < 9.2233720368547758e18)) return (int16_t)-32768;
-  double r = rint(x);
-  if (r > 32767.0) r = 32767.0;
-  if (r < -32768.0) r = -32768.0;
-  return (int16_t)(int)r;
+__host__ __device__ __forceinline__ int tile_exponent(double max_abs) {
+  return tile_exponent_bits(dbits(max_abs) & 0x7FFFFFFFFFFFFFFFULL);
 }
+
+// Mantissa of tile_quantize (:94-96): clip(rint(v / 2^e * 32768)), from v's
+// bit pattern: the 53-bit significand shifted right by >= 37 bits with
+// round-half-even, so only its high word enters the quotient.  Values whose
+// int64 cast is undefined in numpy (NaN, Inf, |x| >= 2^63) give x86's
+// INT64_MIN, i.e. -32768 after the clip.
+__host__ __device__ __forceinline__ int16_t tile_mantissa_bits(unsigned long long vb, int e) {
+  const unsigned hi = (unsigned)(vb >> 32), lo = (unsigned)vb;
+  const int ex = (int)((hi >> 20) & 0x7FF);
+  if (ex == 0x7FF) return (int16_t)-32768;
+  if (ex == 0) return 0;                                     // zero / subnormal: |x| < 2^-880
+  const bool neg = (hi >> 31) != 0;
+  const int p = ex - 1023 + 15 - e;                          // x = +-M * 2^(p - 52)
+  if (p >= 63) return (int16_t)-32768;
+  if (p >= 16) return neg ? (int16_t)-32768 : (int16_t)32767;
+  const int sft = 52 - p;                                    // 37 .. 53 when |x| >= 0.5
+  if (sft >= 54) return 0;                                   // |x| < 0.5
+  const unsigned Mh = (hi & 0xFFFFFu) | 0x100000u;           // significand bits 32..52
+  const int sh = sft - 32;                                   // 5 .. 21
+  unsigned q = Mh >> sh;
+  const unsigned rh = Mh & ((1u << sh) - 1u), hh = 1u << (sh - 1);
+  const bool above = rh > hh || (rh == hh && lo != 0u);
+  const bool tie = rh == hh && lo == 0u;
+  q += (above || (tie && (q & 1u))) ? 1u : 0u;
+  int val = neg ? -(int)q : (int)q;
+  val = val > 32767 ? 32767 : (val < -32768 ? -32768 : val);
+  return (int16_t)val;
+}
+
+__host__ __device__ __forceinline__ int16_t tile_mantissa(double v, int e) { return tile_mantissa_bits(dbits(v), e); }
 
 // tile_decode (:100-102): m/32768 * 2^e, exact.
 __host__ __device__ __forceinline__ double bfp_decode(int m, int e) {
@@ -111,17 +132,58 @@ __host__ __device__ __forceinline__ int16_t requant_mant(int m, bool bumped) {
 // Cooperative tile quantize: 16 consecutive lanes hold one tile (lane & 15 =
 // element index).  Returns this lane's mantissa; *e_out gets the exponent.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int16_t tile_quantize_16lanes(double v, int* e_out) {
-  double a = fabs(v);
-  // NaN-propagating max (np.max returns NaN when any element is NaN)
+// N independent tiles per 16-lane group quantized together: one shuffle tree
+// carries all N maxima, so their latencies overlap.
+template <int N>
+__device__ __forceinline__ void tile_quantize_16lanes_n(const double (&v)[N], int16_t (&m)[N], int (&e)[N]) {
+  unsigned long long vb[N], a[N];
+  #pragma unroll
+  for (int i = 0; i < N; ++i) { vb[i] = dbits(v[i]); a[i] = vb[i] & 0x7FFFFFFFFFFFFFFFULL; }
   #pragma unroll
   for (int off = 8; off >= 1; off >>= 1) {
-    double o = __shfl_xor_sync(0xffffffffu, a, off, 16);
-    a = (a != a || o != o) ? __longlong_as_double(0x7FF8000000000000LL) : (o > a ? o : a);
+    #pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const unsigned long long o = __shfl_xor_sync(0xffffffffu, a[i], off, 16);
+      a[i] = o > a[i] ? o : a[i];
+    }
   }
-  int e = tile_exponent(a);
+  #pragma unroll
+  for (int i = 0; i < N; ++i) {
+    e[i] = tile_exponent_bits(a[i]);
+    m[i] = tile_mantissa_bits(vb[i], e[i]);
+  }
+}
+
+// tile_quantize of fpq(v) for N tiles at once: the matvec-ready form (a tile
+// holding -32768 bumps its exponent and halves its mantissas).
+template <int N>
+__device__ __forceinline__ void tile_quantize_requant_16lanes_n(const double (&v)[N], const bool (&valid)[N],
+                                                                int16_t (&m)[N], int (&e)[N]) {
+  tile_quantize_16lanes_n<N>(v, m, e);
+  const int lane = threadIdx.x & 31;
+  #pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const unsigned bal = __ballot_sync(0xffffffffu, valid[i] && m[i] == (int16_t)-32768);
+    const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
+    m[i] = requant_mant(m[i], has_min && e[i] < 127);
+    e[i] = requant_exp(e[i], has_min);
+  }
+}
+
+__device__ __forceinline__ int16_t tile_quantize_16lanes(double v, int* e_out) {
+  // max |v| over the 16 lanes as an unsigned max of the sign-cleared bit
+  // patterns (the order of |v| for finite values; NaN > Inf > finite, so a
+  // NaN propagates like np.max)
+  const unsigned long long vb = dbits(v);
+  unsigned long long a = vb & 0x7FFFFFFFFFFFFFFFULL;
+  #pragma unroll
+  for (int off = 8; off >= 1; off >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, a, off, 16);
+    a = o > a ? o : a;
+  }
+  const int e = tile_exponent_bits(a);
   *e_out = e;
-  return tile_mantissa(v, e);
+  return tile_mantissa_bits(vb, e);
 }
 
 // ---------------------------------------------------------------------------

@@ -152,20 +152,28 @@ gemv_kernel(GemvArgs a) {
       if (lane == 0) rs[warp] = __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)K), a.eps));
     }
     __syncthreads();
-    for (int base = 0; base < NC * K; base += GV_THREADS) {
-      const int i = base + tid;                              // tiles never straddle columns (K % 16 == 0)
-      const bool valid = i < NC * K;
-      const int c = valid ? i / K : 0, k = valid ? i % K : 0;
-      const double y = valid ? __ddiv_rn(__dmul_rn(xs[i], gs[k]), rs[c]) : 0.0;
-      int e;
-      int16_t m = tile_quantize_16lanes(y, &e);               // fpq (:238)
-      const unsigned bal = __ballot_sync(0xffffffffu, valid && m == (int16_t)-32768);
-      const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
-      m = requant_mant(m, has_min && e < 127);               // tile_quantize(n)
-      e = requant_exp(e, has_min);
-      if (valid) {
-        nm[i] = m;
-        if ((k & 15) == 0) ne[c * NT + k / 16] = (int8_t)e;
+    constexpr int QN = 3;             // tiles quantized together per lane (overlapping latencies)
+    for (int base = 0; base < NC * K; base += GV_THREADS * QN) {
+      double y[QN];
+      bool valid[QN];
+      #pragma unroll
+      for (int q = 0; q < QN; ++q) {                         // tiles never straddle columns (K % 16 == 0)
+        const int i = base + tid + q * GV_THREADS;
+        valid[q] = i < NC * K;
+        const int c = valid[q] ? i / K : 0, k = valid[q] ? i % K : 0;
+        y[q] = valid[q] ? __ddiv_rn(__dmul_rn(xs[i], gs[k]), rs[c]) : 0.0;
+      }
+      int16_t m[QN];
+      int e[QN];
+      tile_quantize_requant_16lanes_n<QN>(y, valid, m, e);   // tile_quantize(fpq(y)) (:238, :264)
+      #pragma unroll
+      for (int q = 0; q < QN; ++q) {
+        const int i = base + tid + q * GV_THREADS;
+        if (valid[q]) {
+          const int c = i / K, k = i % K;
+          nm[i] = m[q];
+          if ((k & 15) == 0) ne[c * NT + k / 16] = (int8_t)e[q];
+        }
       }
     }
   } else {
@@ -263,11 +271,11 @@ gemv_kernel(GemvArgs a) {
     }
   } else if constexpr (MODE == GV_SWIGLU) {
     const int c = p;
-    const double gr = valid ? total(l16, c) : 0.0, ur = valid ? total(16 + l16, c) : 0.0;
-    int ge, ue, se, pe;
-    const int16_t gm = tile_quantize_16lanes(gr, &ge);
-    const int16_t um = tile_quantize_16lanes(ur, &ue);
-    const double gv = bfp_decode(gm, ge), uv = bfp_decode(um, ue);
+    const double gu_r[2] = {valid ? total(l16, c) : 0.0, valid ? total(16 + l16, c) : 0.0};
+    int16_t gu_m[2];
+    int gu_e[2], se, pe;
+    tile_quantize_16lanes_n<2>(gu_r, gu_m, gu_e);                    // g, u = matvec (:288-289)
+    const double gv = bfp_decode(gu_m[0], gu_e[0]), uv = bfp_decode(gu_m[1], gu_e[1]);
     const double sv = __ddiv_rn(gv, __dadd_rn(1.0, exp(-gv)));       // silu_fp (:241-242)
     const int16_t sm = tile_quantize_16lanes(sv, &se);
     const double prod = __dmul_rn(bfp_decode(sm, se), uv);           // fpq(silu * u) (:290)
@@ -361,7 +369,7 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
   X(1, 1, GV_QKV_ROPE, true, 3) X(4, 1, GV_QKV_ROPE, true, 3)
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s, bool pdl) {
-  if (a.ncols < 1 || a.ncols > 4) return cudaErrorInvalidValue;
+  if (a.ncols < 1 || a.ncols > 4 || a.W.NT > GV_MAX_NT) return cudaErrorInvalidValue;
   const int NC = a.ncols == 1 ? 1 : 4;
   const int RG = a.mode == GV_SWIGLU ? 2 : 1;
   const int tpr = GV_THREADS / (16 * RG);

@@ -535,7 +535,7 @@ rmsnorm_quant_kernel(const int16_t* xm, const int8_t* xe, const double* gamma, d
   __shared__ double s_val[96];
   __shared__ double s_r;
   pdl_trigger();
-  const int c = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  const int c = blockIdx.x, tid = threadIdx.x;
   const int NT = D / 16;
   double* xs = reinterpret_cast<double*>(smem);
   double* sq = xs + D;
@@ -543,19 +543,26 @@ rmsnorm_quant_kernel(const int16_t* xm, const int8_t* xe, const double* gamma, d
   for (int i = tid; i < D; i += NORM_THREADS) gs[i] = gamma[i];     // weights: before the dependency wait
   pdl_wait();
   const double r = block_rms(xm + (size_t)c * D, xe + (size_t)c * NT, D, eps, xs, sq, s_lo, s_len, s_val, &s_r);
-  for (int base = 0; base < D; base += NORM_THREADS) {
-    const int i = base + tid;
-    const bool valid = i < D;
-    const double y = valid ? __ddiv_rn(__dmul_rn(xs[i], gs[i]), r) : 0.0;   // x * gamma / sqrt(v)
-    int e;
-    int16_t m = tile_quantize_16lanes(y, &e);               // fpq (:238)
-    const unsigned bal = __ballot_sync(0xffffffffu, valid && m == (int16_t)-32768);
-    const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
-    m = requant_mant(m, has_min && e < 127);               // tile_quantize(n) (:264)
-    e = requant_exp(e, has_min);
-    if (valid) {
-      om[(size_t)c * D + i] = m;
-      if ((i & 15) == 0) oe[(size_t)c * NT + i / 16] = (int8_t)e;
+  constexpr int QN = 3;
+  for (int base = 0; base < D; base += NORM_THREADS * QN) {
+    double y[QN];
+    bool valid[QN];
+    #pragma unroll
+    for (int q = 0; q < QN; ++q) {
+      const int i = base + tid + q * NORM_THREADS;
+      valid[q] = i < D;
+      y[q] = valid[q] ? __ddiv_rn(__dmul_rn(xs[i], gs[i]), r) : 0.0;   // x * gamma / sqrt(v)
+    }
+    int16_t m[QN];
+    int e[QN];
+    tile_quantize_requant_16lanes_n<QN>(y, valid, m, e);   // tile_quantize(fpq(y)) (:238, :264)
+    #pragma unroll
+    for (int q = 0; q < QN; ++q) {
+      const int i = base + tid + q * NORM_THREADS;
+      if (valid[q]) {
+        om[(size_t)c * D + i] = m[q];
+        if ((i & 15) == 0) oe[(size_t)c * NT + i / 16] = (int8_t)e[q];
+      }
     }
   }
 }
