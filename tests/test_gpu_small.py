@@ -93,26 +93,51 @@ def test_rom_prompt_and_gamma_roms():
     dec.close()
 
 
-@pytest.mark.parametrize("nseq", [1, 2, 4])
+@pytest.mark.parametrize("nseq", [1, 2, 3, 4])
 def test_small_batch_kernels_match_general_kernels(nseq, monkeypatch):
-    """1..4 columns run the fused small-batch kernels (gemv.cu); the general
-    matmul path (forced with BFP200_NO_SMALL) and the oracle agree with them."""
+    """1..4 columns: the persistent decode kernel (persist.cu, BFP200_PERSIST=1),
+    the graph-replayed small-batch kernels (gemv.cu, the default), the general
+    matmul path (BFP200_NO_SMALL) and the oracle agree."""
     from bfp200 import BfpConfig, Decoder, synth
     cfg = BfpConfig(MAX_CTX=48, max_seqs=4, **SMALL)
     img = synth.synthetic_image(cfg, 5)
     rng = np.random.default_rng(50 + nseq)
     prompts = [rng.integers(0, 512, size=int(n)).tolist() for n in (3, 11, 1, 20)[:nseq]]
-    fast = Decoder(cfg)
-    fast.load_image(img)
-    got_fast = fast.generate(prompts, 12)
-    got_fast_rtl = fast.generate(prompts, 5, feed_mode="rtl")
-    fast.close()
-    monkeypatch.setenv("BFP200_NO_SMALL", "1")
-    slow = Decoder(cfg)
-    slow.load_image(img)
-    assert slow.generate(prompts, 12) == got_fast
-    assert slow.generate(prompts, 5, feed_mode="rtl") == got_fast_rtl
-    slow.close()
+    results = []
+    for env in ({"BFP200_PERSIST": "1"}, {}, {"BFP200_NO_SMALL": "1"}):
+        for k in ("BFP200_PERSIST", "BFP200_NO_SMALL"):
+            monkeypatch.delenv(k, raising=False)
+        for k, v in env.items():
+            monkeypatch.setenv(k, v)
+        dec = Decoder(cfg)
+        dec.load_image(img)
+        results.append((dec.generate(prompts, 12), dec.generate(prompts, 5, feed_mode="rtl")))
+        dec.close()
+    assert results[0] == results[1] == results[2]
     ocfg = O.Cfg(**SMALL)
     model = OS.make_model(5, ocfg)
-    assert got_fast[0] == O.generate(model, prompts[0], 12, max_ctx=48, cfg=ocfg)
+    for p, g in zip(prompts, results[0][0]):
+        assert g == O.generate(model, p, 12, max_ctx=48, cfg=ocfg)
+
+
+def test_persistent_decode_long_context(monkeypatch):
+    """Persistent decode past one 256-position attention chunk (positions
+    0..299), against the graph-replayed kernels and the oracle."""
+    from bfp200 import BfpConfig, Decoder, synth
+    cfg = BfpConfig(MAX_CTX=300, max_seqs=2, **SMALL)
+    img = synth.synthetic_image(cfg, 7)
+    prompts = [list(range(1, 41)), [7, 9]]
+    monkeypatch.setenv("BFP200_PERSIST", "1")
+    dec = Decoder(cfg)
+    dec.load_image(img)
+    fast = dec.generate(prompts, 258)
+    dec.close()
+    monkeypatch.delenv("BFP200_PERSIST")
+    dec = Decoder(cfg)
+    dec.load_image(img)
+    slow = dec.generate(prompts, 258)
+    dec.close()
+    assert fast == slow
+    ocfg = O.Cfg(**SMALL)
+    model = OS.make_model(7, ocfg)
+    assert fast[1] == O.generate(model, prompts[1], 258, max_ctx=300, cfg=ocfg)

@@ -356,12 +356,10 @@ __device__ __forceinline__ double np_sum_warp_plan(const double* a, int n, const
 // Warp-cooperative numpy sum of a shared-memory array (n <= 8192).  All 32
 // lanes must call it; scratch needs 3*64 words of shared memory.  Returns the
 // sum on every lane.
-__device__ __forceinline__ double np_sum_warp(const double* a, int n, int* s_lo, int* s_len,
-                                              double* s_val) {
+// The general tree (lengths without the power-of-two split) is kept out of
+// line: it is large and rarely taken.
+static __device__ __noinline__ double np_sum_warp_generic(const double* a, int n, int* s_lo, int* s_len, double* s_val) {
   const int lane = threadIdx.x & 31;
-  int pl = 0;
-  const int pk = np_pw_perfect(n, &pl);
-  if (pk >= 0) return np_sum_warp_perfect(a, pk, pl);
   if (n <= 128) {
     double r = 0.0;
     if (lane == 0) r = __dadd_rn(0.0, np_pw_leaf(a, n));
@@ -376,6 +374,14 @@ __device__ __forceinline__ double np_sum_warp(const double* a, int n, int* s_lo,
   double r = 0.0;
   if (lane == 0) r = __dadd_rn(0.0, np_pw_combine(n, s_val));
   return __shfl_sync(0xffffffffu, r, 0);
+}
+
+__device__ __forceinline__ double np_sum_warp(const double* a, int n, int* s_lo, int* s_len,
+                                              double* s_val) {
+  int pl = 0;
+  const int pk = np_pw_perfect(n, &pl);
+  if (pk >= 0) return np_sum_warp_perfect(a, pk, pl);
+  return np_sum_warp_generic(a, n, s_lo, s_len, s_val);
 }
 
 // ---------------------------------------------------------------------------

@@ -251,6 +251,8 @@ struct bfp200_handle {
   bool pdl = true;
   bool use_clusters = true;   // K-split reduction through distributed shared memory
   bool use_small = true;      // 1..4 columns: the fused small-batch kernels (gemv.cu)
+  bool use_persist = false;   // 1..4 columns: decode steps in one persistent kernel (persist.cu), opt-in
+  int smem_optin = 0;
   // weights
   DBuf<uint8_t> wm_qkv, wm_o, wm_gu, wm_d;
   DBuf<int8_t> we_qkv, we_o, we_gu, we_d;
@@ -280,6 +282,7 @@ struct bfp200_handle {
   DBuf<int> col_slot, col_pos, col_kvpos, col_tok;
   DBuf<int> gen_out, dec_step, rtl_out;
   DBuf<long long> uncert_dev;
+  DBuf<unsigned> psync;
   cudaGraphExec_t graph = nullptr;
   int graph_cols = -1, graph_ngen = -1;
   long long uncert = 0;
@@ -586,6 +589,36 @@ int enqueue_forward(bfp200_handle* h, int ncols, bool head) {
   return BFP200_OK;
 }
 
+PersistArgs persist_args(bfp200_handle* h, int ncols, int n_gen) {
+  PersistArgs a;
+  a.D = h->D; a.HQ = h->HQ; a.HKV = h->HKV; a.FFN = h->FFN; a.NL = h->NL; a.V = h->V; a.MAXC = h->MAXC;
+  a.NTD = h->NTD; a.NTF = h->NTF;
+  a.ncols = ncols; a.n_gen = n_gen;
+  a.eps = h->cfg.eps; a.sqrt_hd = std::sqrt((double)h->HD); a.emb_norm_max = h->emb_norm_max;
+  a.wm_qkv = h->wm_qkv.p; a.wm_o = h->wm_o.p; a.wm_gu = h->wm_gu.p; a.wm_d = h->wm_d.p;
+  a.we_qkv = h->we_qkv.p; a.we_o = h->we_o.p; a.we_gu = h->we_gu.p; a.we_d = h->we_d.p;
+  a.g1 = h->g1.p; a.g2 = h->g2.p; a.nw = h->nw.p; a.rope_cs = h->rope_cs.p;
+  a.emb_m = h->emb_m.p; a.emb_e = h->emb_e.p;
+  a.pw_off = h->pw_off.p; a.pw_data = h->pw_data.p;
+  a.kv = h->kv();
+  a.h_m = h->h_m.p; a.h1_m = h->h1_m.p; a.qkv_m = h->qkv_m.p; a.a_m = h->a_m.p; a.mlp_m = h->mlp_m.p;
+  a.h_e = h->h_e.p; a.h1_e = h->h1_e.p; a.qkv_e = h->qkv_e.p; a.a_e = h->a_e.p; a.mlp_e = h->mlp_e.p;
+  a.part_val = h->part_val.p; a.part_sec = h->part_sec.p; a.part_idx = h->part_idx.p;
+  a.col_slot = h->col_slot.p; a.col_pos = h->col_pos.p; a.col_tok = h->col_tok.p;
+  a.gen_out = h->gen_out.p; a.uncert = h->uncert_dev.p;
+  a.sync = h->psync.p;
+  a.err = error_flag_device_ptr();
+  return a;
+}
+
+// 1..4 columns decode in the persistent kernel when its grid (one CTA per
+// SM) covers every phase's row groups and its shared memory fits.
+bool persist_ok(bfp200_handle* h, int ncols) {
+  if (!h->use_persist || ncols < 1 || ncols > 4) return false;
+  PersistArgs a = persist_args(h, ncols, 1);
+  return a.err != nullptr && persistent_plan(a, h->nsm, h->smem_optin);
+}
+
 int check_cfg(const bfp200_cfg& c) {
   if (c.D <= 0 || c.D % 16 || c.FFN <= 0 || c.FFN % 16 || c.H_Q <= 0 || c.H_KV <= 0 || c.H_Q % c.H_KV ||
       c.HD != 64 || c.H_Q * c.HD != c.D || c.NL <= 0 || c.VOCAB <= 0 || c.VOCAB % 16 || c.MAX_CTX <= 0 ||
@@ -657,6 +690,8 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
   if (const char* e = std::getenv("BFP200_NO_PDL")) h->pdl = !(e[0] == '1');
   if (const char* e = std::getenv("BFP200_NO_CLUSTER")) h->use_clusters = !(e[0] == '1');
   if (const char* e = std::getenv("BFP200_NO_SMALL")) h->use_small = !(e[0] == '1');
+  if (const char* e = std::getenv("BFP200_PERSIST")) h->use_persist = e[0] == '1';
+  h->smem_optin = (int)prop.sharedMemPerBlockOptin;
   cudaError_t ce = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
   if (ce != cudaSuccess) { delete h; return fail(BFP200_ECUDA, cudaGetErrorString(ce)); }
   std::vector<double> cs((size_t)h->MAXC * h->HD);
@@ -897,24 +932,33 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
     CK(cudaMemcpyAsync(h->col_pos.p, dpos.data(), n_seq * 4, cudaMemcpyHostToDevice, h->stream));
     CK(cudaMemcpyAsync(h->col_tok.p, dtok.data(), n_seq * 4, cudaMemcpyHostToDevice, h->stream));
     CK(cudaMemsetAsync(h->dec_step.p, 0, 4, h->stream));
-    if (!h->graph || h->graph_cols != n_seq || h->graph_ngen != n_gen) {
-      if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; }
-      CK(cudaStreamSynchronize(h->stream));
-      cudaGraph_t g;
-      CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
-      int r = enqueue_forward(h, n_seq, true);
-      advance_kernel<<<1, 256, 0, h->stream>>>(h->tok.p, h->cert.p, n_seq, n_gen, h->gen_out.p, h->col_tok.p,
-                                               h->col_pos.p, h->dec_step.p, h->uncert_dev.p);
-      cudaError_t ce = cudaStreamEndCapture(h->stream, &g);
-      if (r != BFP200_OK) { if (ce == cudaSuccess) cudaGraphDestroy(g); return r; }
-      CK(ce);
-      ce = cudaGraphInstantiate(&h->graph, g, 0);
-      cudaGraphDestroy(g);
-      CK(ce);
-      h->graph_cols = n_seq;
-      h->graph_ngen = n_gen;
+    if (persist_ok(h, n_seq)) {
+      CK(h->psync.ensure(PERSIST_SYNC_WORDS));
+      CK(cudaMemsetAsync(h->psync.p, 0, PERSIST_SYNC_WORDS * sizeof(unsigned), h->stream));
+      PersistArgs pa = persist_args(h, n_seq, n_gen);
+      persistent_plan(pa, h->nsm, h->smem_optin);
+      CK(launch_persistent_decode(pa, h->nsm, h->stream));
+    } else {
+      // one decode step captured once as a CUDA graph, replayed n_gen times
+      if (!h->graph || h->graph_cols != n_seq || h->graph_ngen != n_gen) {
+        if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; }
+        CK(cudaStreamSynchronize(h->stream));
+        cudaGraph_t g;
+        CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+        int r = enqueue_forward(h, n_seq, true);
+        advance_kernel<<<1, 256, 0, h->stream>>>(h->tok.p, h->cert.p, n_seq, n_gen, h->gen_out.p, h->col_tok.p,
+                                                 h->col_pos.p, h->dec_step.p, h->uncert_dev.p);
+        cudaError_t ce = cudaStreamEndCapture(h->stream, &g);
+        if (r != BFP200_OK) { if (ce == cudaSuccess) cudaGraphDestroy(g); return r; }
+        CK(ce);
+        ce = cudaGraphInstantiate(&h->graph, g, 0);
+        cudaGraphDestroy(g);
+        CK(ce);
+        h->graph_cols = n_seq;
+        h->graph_ngen = n_gen;
+      }
+      for (int i = 0; i < n_gen; ++i) CK(cudaGraphLaunch(h->graph, h->stream));
     }
-    for (int i = 0; i < n_gen; ++i) CK(cudaGraphLaunch(h->graph, h->stream));
   }
   CK(cudaEventRecord(ev2, h->stream));
   std::vector<int32_t> gen((size_t)n_seq * n_gen);

@@ -1331,6 +1331,12 @@ cudaError_t launch_row_norms(const int16_t* m, const int8_t* e, int rows, int D,
 }  // namespace bfp
 
 namespace bfp {
+int* error_flag_device_ptr() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_error_flag) != cudaSuccess) return nullptr;
+  return static_cast<int*>(p);
+}
+
 int read_and_clear_error_flag(cudaStream_t s) {
   int v = 0, z = 0;
   cudaMemcpyFromSymbolAsync(&v, g_error_flag, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
