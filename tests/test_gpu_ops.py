@@ -35,7 +35,20 @@ def test_tile_quantize_random_and_thresholds(ops):
     p = np.ldexp(1.0, np.repeat(np.arange(-140, 140), 16))
     k = np.tile(np.arange(16), 280) * 7
     near = p * (1.0 - k * 2.0 ** -53)
-    v = np.concatenate([v, near, -near])
+    # tiles mixing a near-power-of-two element with others: the near element
+    # is the maximum (log2 round-up path), shares the maximum's binade without
+    # being the maximum, or sits in a lower binade (exponent from the others)
+    j = np.arange(-120, 120)
+    nr = np.ldexp(1.0 - 3 * 2.0 ** -53, j)                  # binade j-1, top fraction bits all ones
+    mixed = []
+    for lead, rest in ((nr, 0.3 * nr), (0.75 * nr, nr), (0.5 * nr, 0.75 * nr), (nr * 0.999, nr)):
+        t = np.repeat(rest[:, None], 16, axis=1) * rng.uniform(0.1, 1.0, size=(len(j), 16))
+        t[:, rng.integers(0, 16, size=len(j))] = 0.0
+        t[np.arange(len(j)), rng.integers(0, 16, size=len(j))] = lead
+        mixed.append(t.reshape(-1))
+    specials = np.array([0.0] * 16 + [np.inf] + [1.0] * 15 + [np.nan] + [2.0] * 15 + [-np.inf] + [0.0] * 15
+                        + [1e-310] * 16 + [5e-301, 1e-300] + [2e-300] * 14)
+    v = np.concatenate([v, near, -near] + mixed + [specials])
     m, e = ops.tile_quantize(v)
     mo, eo = O.tile_quantize(v)
     assert np.array_equal(m, mo) and np.array_equal(e, eo)

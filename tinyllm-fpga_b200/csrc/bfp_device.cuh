@@ -84,18 +84,14 @@ __host__ __device__ __forceinline__ int tile_exponent(double max_abs) {
 // int64 cast is undefined in numpy (NaN, Inf, |x| >= 2^63) give x86's
 // INT64_MIN, i.e. -32768 after the clip.
 __host__ __device__ __forceinline__ int16_t tile_mantissa_bits(unsigned long long vb, int e) {
+  // computed without branches: the general case with the shift clamped to
+  // its valid range, then the special cases selected in increasing precedence
   const unsigned hi = (unsigned)(vb >> 32), lo = (unsigned)vb;
   const int ex = (int)((hi >> 20) & 0x7FF);
-  if (ex == 0x7FF) return (int16_t)-32768;
-  if (ex == 0) return 0;                                     // zero / subnormal: |x| < 2^-880
   const bool neg = (hi >> 31) != 0;
   const int p = ex - 1023 + 15 - e;                          // x = +-M * 2^(p - 52)
-  if (p >= 63) return (int16_t)-32768;
-  if (p >= 16) return neg ? (int16_t)-32768 : (int16_t)32767;
-  const int sft = 52 - p;                                    // 37 .. 53 when |x| >= 0.5
-  if (sft >= 54) return 0;                                   // |x| < 0.5
+  const int sh = p > 15 ? 5 : (p < -1 ? 21 : 20 - p);       // 52 - p - 32, clamped to 5 .. 21
   const unsigned Mh = (hi & 0xFFFFFu) | 0x100000u;           // significand bits 32..52
-  const int sh = sft - 32;                                   // 5 .. 21
   unsigned q = Mh >> sh;
   const unsigned rh = Mh & ((1u << sh) - 1u), hh = 1u << (sh - 1);
   const bool above = rh > hh || (rh == hh && lo != 0u);
@@ -103,6 +99,11 @@ __host__ __device__ __forceinline__ int16_t tile_mantissa_bits(unsigned long lon
   q += (above || (tie && (q & 1u))) ? 1u : 0u;
   int val = neg ? -(int)q : (int)q;
   val = val > 32767 ? 32767 : (val < -32768 ? -32768 : val);
+  val = p <= -2 ? 0 : val;                                   // |x| < 0.5
+  val = p >= 16 ? (neg ? -32768 : 32767) : val;              // saturation
+  val = p >= 63 ? -32768 : val;                              // int64 cast overflow (x86 INT64_MIN)
+  val = ex == 0 ? 0 : val;                                   // zero / subnormal: |x| < 2^-880
+  val = ex == 0x7FF ? -32768 : val;                          // NaN / Inf
   return (int16_t)val;
 }
 
@@ -132,13 +133,22 @@ __host__ __device__ __forceinline__ int16_t requant_mant(int m, bool bumped) {
 // Cooperative tile quantize: 16 consecutive lanes hold one tile (lane & 15 =
 // element index).  Returns this lane's mantissa; *e_out gets the exponent.
 // ---------------------------------------------------------------------------
-// N independent tiles per 16-lane group quantized together: one shuffle tree
-// carries all N maxima, so their latencies overlap.
+// N independent tiles per 16-lane group quantized together.
+//
+// The tile exponent needs max|v| only through its exponent field, except in
+// numpy's log2 round-up case, where the max element's top 20 fraction bits
+// are all ones (tile_exponent_bits).  So the group maximum of the biased
+// exponent fields is taken with two 32-bit warp reductions (one per half
+// warp), and only when some lane holding that exponent has all-ones top
+// fraction bits does the warp take the exact 64-bit shuffle maximum.
 template <int N>
-__device__ __forceinline__ void tile_quantize_16lanes_n(const double (&v)[N], int16_t (&m)[N], int (&e)[N]) {
-  unsigned long long vb[N], a[N];
+__device__ __forceinline__ void tile_quantize_16lanes_exact_n(const unsigned long long (&vb)[N], int (&e)[N]) {
+  unsigned long long a[N];
   #pragma unroll
-  for (int i = 0; i < N; ++i) { vb[i] = dbits(v[i]); a[i] = vb[i] & 0x7FFFFFFFFFFFFFFFULL; }
+  for (int i = 0; i < N; ++i) a[i] = vb[i] & 0x7FFFFFFFFFFFFFFFULL;
+  // max |v| over the 16 lanes as an unsigned max of the sign-cleared bit
+  // patterns (the order of |v| for finite values; NaN > Inf > finite, so a
+  // NaN propagates like np.max)
   #pragma unroll
   for (int off = 8; off >= 1; off >>= 1) {
     #pragma unroll
@@ -148,10 +158,29 @@ __device__ __forceinline__ void tile_quantize_16lanes_n(const double (&v)[N], in
     }
   }
   #pragma unroll
+  for (int i = 0; i < N; ++i) e[i] = tile_exponent_bits(a[i]);
+}
+
+template <int N>
+__device__ __forceinline__ void tile_quantize_16lanes_n(const double (&v)[N], int16_t (&m)[N], int (&e)[N]) {
+  const bool upper = (threadIdx.x & 16) != 0;
+  unsigned long long vb[N];
+  bool round_up_case = false;
+  #pragma unroll
   for (int i = 0; i < N; ++i) {
-    e[i] = tile_exponent_bits(a[i]);
-    m[i] = tile_mantissa_bits(vb[i], e[i]);
+    vb[i] = dbits(v[i]);
+    const unsigned hi = (unsigned)(vb[i] >> 32);
+    const unsigned bx = (hi >> 20) & 0x7FFu;                        // biased exponent field
+    const unsigned r0 = __reduce_max_sync(0xffffffffu, upper ? 0u : bx);
+    const unsigned r1 = __reduce_max_sync(0xffffffffu, upper ? bx : 0u);
+    const unsigned kmax = upper ? r1 : r0;
+    // NaN / Inf in the tile (field 0x7FF): exponent -127 whatever the fraction
+    e[i] = kmax == 0x7FFu ? -127 : min(max((int)kmax - 1022, -127), 127);
+    round_up_case |= kmax != 0x7FFu && bx == kmax && (hi & 0xFFFFFu) == 0xFFFFFu;
   }
+  if (__any_sync(0xffffffffu, round_up_case)) tile_quantize_16lanes_exact_n<N>(vb, e);
+  #pragma unroll
+  for (int i = 0; i < N; ++i) m[i] = tile_mantissa_bits(vb[i], e[i]);
 }
 
 // tile_quantize of fpq(v) for N tiles at once: the matvec-ready form (a tile
@@ -171,19 +200,12 @@ __device__ __forceinline__ void tile_quantize_requant_16lanes_n(const double (&v
 }
 
 __device__ __forceinline__ int16_t tile_quantize_16lanes(double v, int* e_out) {
-  // max |v| over the 16 lanes as an unsigned max of the sign-cleared bit
-  // patterns (the order of |v| for finite values; NaN > Inf > finite, so a
-  // NaN propagates like np.max)
-  const unsigned long long vb = dbits(v);
-  unsigned long long a = vb & 0x7FFFFFFFFFFFFFFFULL;
-  #pragma unroll
-  for (int off = 8; off >= 1; off >>= 1) {
-    const unsigned long long o = __shfl_xor_sync(0xffffffffu, a, off, 16);
-    a = o > a ? o : a;
-  }
-  const int e = tile_exponent_bits(a);
-  *e_out = e;
-  return tile_mantissa_bits(vb, e);
+  const double vv[1] = {v};
+  int16_t m[1];
+  int e[1];
+  tile_quantize_16lanes_n<1>(vv, m, e);
+  *e_out = e[0];
+  return m[0];
 }
 
 // ---------------------------------------------------------------------------
@@ -376,11 +398,47 @@ static __device__ __noinline__ double np_sum_warp_generic(const double* a, int n
   return __shfl_sync(0xffffffffu, r, 0);
 }
 
+// np_sum_warp_perfect with the leaf length a compile-time constant: each
+// lane's loads are issued together ahead of its addition chain.
+template <int L>
+__device__ __forceinline__ double np_sum_warp_perfect_t(const double* a, int k) {
+  const int lane = threadIdx.x & 31;
+  const int leaf = lane >> 2, q = lane & 3;
+  double v = 0.0;
+  if (leaf < (1 << k)) {
+    const double* b = a + leaf * L + 2 * q;
+    double x0[L / 8], x1[L / 8];
+    #pragma unroll
+    for (int i = 0; i < L / 8; ++i) { x0[i] = b[8 * i]; x1[i] = b[8 * i + 1]; }
+    double r0 = x0[0], r1 = x1[0];
+    #pragma unroll
+    for (int i = 1; i < L / 8; ++i) { r0 = __dadd_rn(r0, x0[i]); r1 = __dadd_rn(r1, x1[i]); }
+    v = __dadd_rn(r0, r1);
+  }
+  double o = __shfl_xor_sync(0xffffffffu, v, 1);
+  if ((q & 1) == 0) v = __dadd_rn(v, o);
+  o = __shfl_xor_sync(0xffffffffu, v, 2);
+  if ((q & 2) == 0) v = __dadd_rn(v, o);
+  for (int lev = 0; lev < k; ++lev) {
+    const int m = 4 << lev;
+    o = __shfl_xor_sync(0xffffffffu, v, m);
+    if ((lane & m) == 0) v = __dadd_rn(v, o);
+  }
+  return __dadd_rn(0.0, __shfl_sync(0xffffffffu, v, 0));
+}
+
 __device__ __forceinline__ double np_sum_warp(const double* a, int n, int* s_lo, int* s_len,
                                               double* s_val) {
   int pl = 0;
   const int pk = np_pw_perfect(n, &pl);
-  if (pk >= 0) return np_sum_warp_perfect(a, pk, pl);
+  if (pk >= 0) {
+    switch (pl) {                                  // leaf lengths of the usual model widths
+      case 72: return np_sum_warp_perfect_t<72>(a, pk);     // 576, 1152
+      case 96: return np_sum_warp_perfect_t<96>(a, pk);     // 192, 384, 768, 1536
+      case 128: return np_sum_warp_perfect_t<128>(a, pk);   // 128, 256, 512, 1024
+      default: return np_sum_warp_perfect(a, pk, pl);
+    }
+  }
   return np_sum_warp_generic(a, n, s_lo, s_len, s_val);
 }
 

@@ -283,6 +283,7 @@ struct bfp200_handle {
   DBuf<int> gen_out, dec_step, rtl_out;
   DBuf<long long> uncert_dev;
   DBuf<unsigned> psync;
+  DBuf<unsigned> head_ctr;     // arrival counter of the single-launch head (left zeroed)
   cudaGraphExec_t graph = nullptr;
   int graph_cols = -1, graph_ngen = -1;
   long long uncert = 0;
@@ -342,6 +343,7 @@ int ensure_cols(bfp200_handle* h, int ncols) {
   CK(h->part_idx.ensure((size_t)cap * nrb_max));
   CK(h->tok.ensure(cap)); CK(h->cert.ensure(cap));
   CK(h->col_slot.ensure(cap)); CK(h->col_pos.ensure(cap)); CK(h->col_kvpos.ensure(cap)); CK(h->col_tok.ensure(cap));
+  CK(h->head_ctr.ensure(1));
   h->cap = cap;
   if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; h->graph_cols = -1; }
   return BFP200_OK;
@@ -562,6 +564,15 @@ int enqueue_layer_small(bfp200_handle* h, int l, int ncols, bool first_pdl) {
 
 int enqueue_head(bfp200_handle* h, int ncols) {
   cudaStream_t s = h->stream;
+  if (h->use_small && head_small_supported(ncols, h->D)) {
+    // one launch: hn, logits, certified argmax (last CTA); head_ctr is
+    // allocated by ensure_cols, outside any stream capture
+    mark(h, PK_HEAD_LOGITS);
+    CK(launch_head_small(h->h_m.p, h->h_e.p, h->nw.p, h->cfg.eps, h->emb_m.p, h->emb_e.p, h->V, h->D, ncols,
+                         h->emb_norm_max, h->part_val.p, h->part_idx.p, h->part_sec.p, h->head_ctr.p, h->tok.p,
+                         h->cert.p, s, h->pdl));
+    return BFP200_OK;
+  }
   mark(h, PK_HEAD_PREP);
   CK(launch_head_prep(h->h_m.p, h->h_e.p, h->nw.p, h->cfg.eps, h->D, ncols, h->hn.p, h->hn_norm.p, s, h->pdl));
   int nrb = 0;

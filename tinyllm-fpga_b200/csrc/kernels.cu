@@ -1080,6 +1080,207 @@ __global__ void head_reduce_kernel(const double* part_val, const int* part_idx, 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Small-batch head in one launch (1..4 columns, D <= 768): every CTA forms
+// hn = (h / sqrt(mean(h*h) + eps)) * norm_w_q (:438) itself, scans its
+// share of the vocabulary in fp64 (:439), and the last CTA to finish reduces
+// the shares to the argmax (lowest index on ties) with the certificate of
+// head_reduce_kernel.  hn is kept transposed in shared memory
+// (hnT[c][k/256][k%8][(k/8)%32]) so the lanes of a warp, which read
+// consecutive 8-element chunks of an embedding row, read consecutive doubles.
+// The first rows of each warp are loaded before the dependency wait.
+// ---------------------------------------------------------------------------
+constexpr int HS_RF = 4;   // embedding rows in flight per warp
+
+__host__ __device__ inline int head_hnT_stride(int D) { return ((D / 8 + 31) / 32) * 256; }
+
+template <int NC>
+__global__ void __launch_bounds__(256)
+head_small_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, double eps, const int16_t* emb_m,
+                  const int8_t* emb_e, int VOCAB, int D, int ncols, double emb_norm_max, double* part_val,
+                  int* part_idx, double* part_second, unsigned* done_ctr, int* tok_out, int* cert_out) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_lo[96], s_len[96];
+  __shared__ double s_val[96];
+  __shared__ double s_r[4];
+  __shared__ double w_best[8][NC], w_sec[8][NC];
+  __shared__ int w_idx[8][NC];
+  __shared__ int s_last;
+  pdl_trigger();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NT = D / 16, NU = D / 8, HS = head_hnT_stride(D);
+  double* xs = reinterpret_cast<double*>(smem);          // [NC][D]
+  double* sq = xs + NC * D;                              // [NC][D]
+  double* hnT = sq + NC * D;                             // [NC][HS]
+  const int gw = blockIdx.x * 8 + warp, nw = gridDim.x * 8;
+  // first batch of embedding rows: independent of the previous kernel
+  uint4 w[HS_RF][3];
+  int ex[HS_RF][3];
+  auto load_batch = [&](int v0) {
+    #pragma unroll
+    for (int q = 0; q < HS_RF; ++q)
+      #pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int v = v0 + q * nw, u = lane + 32 * j;
+        if (v < VOCAB && u < NU) {
+          w[q][j] = reinterpret_cast<const uint4*>(emb_m + (size_t)v * D)[u];
+          ex[q][j] = emb_e[(size_t)v * NT + u / 2];
+        } else {
+          w[q][j] = make_uint4(0, 0, 0, 0);
+          ex[q][j] = 0;
+        }
+      }
+  };
+  load_batch(gw);
+  for (int i = tid; i < NC * HS; i += 256) hnT[i] = 0.0;
+  pdl_wait();
+  for (int i = tid; i < NC * D; i += 256) {
+    const int c = i / D, k = i - c * D;
+    double x = 0.0;
+    if (c < ncols) x = bfp_decode(hm[(size_t)c * D + k], he[(size_t)c * NT + k / 16]);
+    xs[i] = x;
+    sq[i] = __dmul_rn(x, x);
+  }
+  __syncthreads();
+  if (warp < NC) {
+    double r;
+    warp_rms_factor(sq + (size_t)warp * D, D, s_lo, s_len, s_val, eps, &r);
+    if (lane == 0) s_r[warp] = r;
+  }
+  __syncthreads();
+  for (int i = tid; i < NC * D; i += 256) {
+    const int c = i / D, k = i - c * D, u = k >> 3;
+    hnT[c * HS + ((u >> 5) * 8 + (k & 7)) * 32 + (u & 31)] = __dmul_rn(__ddiv_rn(xs[i], s_r[c]), norm_w[k]);
+  }
+  __syncthreads();
+  double best[NC], sec[NC];
+  int bidx[NC];
+  #pragma unroll
+  for (int c = 0; c < NC; ++c) { best[c] = -INFINITY; sec[c] = -INFINITY; bidx[c] = 0x7fffffff; }
+  for (int v0 = gw; v0 < VOCAB; v0 += HS_RF * nw) {
+    double acc[HS_RF][NC];
+    #pragma unroll
+    for (int q = 0; q < HS_RF; ++q)
+      #pragma unroll
+      for (int c = 0; c < NC; ++c) acc[q][c] = 0.0;
+    #pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      if (32 * j >= NU) break;                             // chunks beyond the row (warp-uniform)
+      const double* hp = hnT + j * 256 + lane;             // zero-filled beyond D
+      #pragma unroll
+      for (int q = 0; q < HS_RF; ++q) {
+        const double scl = pow2(ex[q][j] - 15);
+        const unsigned ww[4] = {w[q][j].x, w[q][j].y, w[q][j].z, w[q][j].w};
+        #pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const double ev = (double)(int)(int16_t)((ww[t >> 1] >> (16 * (t & 1))) & 0xFFFF) * scl;
+          #pragma unroll
+          for (int c = 0; c < NC; ++c) acc[q][c] = fma(ev, hp[c * HS + t * 32], acc[q][c]);
+        }
+      }
+    }
+    if (v0 + HS_RF * nw < VOCAB) load_batch(v0 + HS_RF * nw);
+    #pragma unroll
+    for (int q = 0; q < HS_RF; ++q) {
+      const int v = v0 + q * nw;
+      #pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        double x = acc[q][c];
+        #pragma unroll
+        for (int off = 16; off; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+        if (v < VOCAB) {
+          if (x > best[c]) { sec[c] = best[c]; best[c] = x; bidx[c] = v; }
+          else if (x > sec[c]) sec[c] = x;
+        }
+      }
+    }
+  }
+  if (lane == 0)
+    #pragma unroll
+    for (int c = 0; c < NC; ++c) { w_best[warp][c] = best[c]; w_sec[warp][c] = sec[c]; w_idx[warp][c] = bidx[c]; }
+  __syncthreads();
+  if (tid < NC && tid < ncols) {
+    double b = -INFINITY, s2 = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int ww = 0; ww < 8; ++ww) {
+      const double x = w_best[ww][tid];
+      const int xi = w_idx[ww][tid];
+      if (x > b || (x == b && xi < bi)) { s2 = fmax(s2, b); b = x; bi = xi; }
+      else s2 = fmax(s2, x);
+      s2 = fmax(s2, w_sec[ww][tid]);
+    }
+    const size_t o = (size_t)tid * gridDim.x + blockIdx.x;
+    part_val[o] = b; part_idx[o] = bi; part_second[o] = s2;
+  }
+  // the last CTA to finish reduces
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(done_ctr, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (warp < NC && warp < ncols) {
+    const int c = warp, nrb = gridDim.x;
+    // ||hn|| of this column (any summation order; covered by the 1e-12 factor)
+    double ss = 0.0;
+    for (int k = lane; k < HS; k += 32) ss = fma(hnT[c * HS + k], hnT[c * HS + k], ss);
+    for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    double b = -INFINITY, s2 = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = lane; r < nrb; r += 32) {
+      const size_t o = (size_t)c * nrb + r;
+      const double x = __ldcg(part_val + o);
+      const int xi = __ldcg(part_idx + o);
+      if (x > b || (x == b && xi < bi)) { s2 = fmax(s2, b); b = x; bi = xi; }
+      else s2 = fmax(s2, x);
+      s2 = fmax(s2, __ldcg(part_second + o));
+    }
+    for (int off = 16; off; off >>= 1) {
+      const double ob = __shfl_xor_sync(0xffffffffu, b, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      const double os = __shfl_xor_sync(0xffffffffu, s2, off);
+      if (ob > b || (ob == b && oi < bi)) { s2 = fmax(s2, b); b = ob; bi = oi; }
+      else s2 = fmax(s2, ob);
+      s2 = fmax(s2, os);
+    }
+    if (lane == 0) {
+      // |fl(dot) - dot| <= gamma_D ||hn|| ||e_v|| for every summation order
+      const double u = 1.1102230246251565e-16;
+      const double gam = (D + 2) * u / (1.0 - (D + 2) * u);
+      const double margin = 4.0 * gam * (sqrt(ss) * (1.0 + 1e-12)) * emb_norm_max * (1.0 + 1e-6);
+      const bool ok = bi >= 0 && bi < VOCAB;              // no index: every logit was NaN
+      tok_out[c] = ok ? bi : 0;
+      cert_out[c] = (ok && (b - s2) > margin) ? 1 : 0;
+    }
+  }
+  if (tid == 0) *done_ctr = 0u;                          // ready for the next launch
+}
+
+bool head_small_supported(int ncols, int D) { return ncols >= 1 && ncols <= 4 && D % 16 == 0 && D <= 768; }
+
+size_t head_small_smem(int ncols, int D) {
+  const int NC = ncols <= 1 ? 1 : 4;
+  return (size_t)NC * (2 * D + head_hnT_stride(D)) * 8;
+}
+
+cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
+                              const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, int ncols,
+                              double emb_norm_max, double* part_val, int* part_idx, double* part_second,
+                              unsigned* done_ctr, int* tok_out, int* cert_out, cudaStream_t s, bool pdl) {
+  if (!head_small_supported(ncols, D)) return cudaErrorInvalidValue;
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const size_t smem = head_small_smem(ncols, D);
+  if (ncols <= 1)
+    return launch_ex(head_small_kernel<1>, dim3(nsm), dim3(256), smem, s, pdl, hm, he, norm_w, eps, emb_m, emb_e,
+                     VOCAB, D, ncols, emb_norm_max, part_val, part_idx, part_second, done_ctr, tok_out, cert_out);
+  return launch_ex(head_small_kernel<4>, dim3(nsm), dim3(256), smem, s, pdl, hm, he, norm_w, eps, emb_m, emb_e,
+                   VOCAB, D, ncols, emb_norm_max, part_val, part_idx, part_second, done_ctr, tok_out, cert_out);
+}
+
 cudaError_t launch_head_reduce(const double* part_val, const int* part_idx, const double* part_second,
                                int n_rowblocks, const double* hn_norm, double emb_norm_max, int D, int ncols,
                                int* tok_out, int* cert_out, cudaStream_t s, bool pdl) {
@@ -1374,6 +1575,8 @@ cudaError_t init_kernel_attributes() {
   set((const void*)np_sum_plan_kernel);
   set((const void*)head_gemv_kernel<1>);
   set((const void*)head_gemv_kernel<4>);
+  set((const void*)head_small_kernel<1>);
+  set((const void*)head_small_kernel<4>);
   const cudaError_t g = init_gemv_attributes();
   return e != cudaSuccess ? e : g;
 }

@@ -176,6 +176,14 @@ cudaError_t launch_head_reduce(const double* part_val, const int* part_idx, cons
                                int n_rowblocks, const double* hn_norm, double emb_norm_max, int D,
                                int ncols, int* tok_out, int* cert_out, cudaStream_t s, bool pdl);
 
+// Head of 1..4 columns in one launch: hn, fp64 logits, and (last CTA) the
+// certified argmax.  done_ctr: a zeroed word, left zeroed on return.
+bool head_small_supported(int ncols, int D);
+cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
+                              const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, int ncols,
+                              double emb_norm_max, double* part_val, int* part_idx, double* part_second,
+                              unsigned* done_ctr, int* tok_out, int* cert_out, cudaStream_t s, bool pdl);
+
 // Standalone ops (the reference's module-level functions).
 cudaError_t launch_tile_quantize(const double* v, long long ntiles, int16_t* m, int8_t* e, cudaStream_t s);
 cudaError_t launch_tile_decode(const int16_t* m, const int8_t* e, long long ntiles, double* v, cudaStream_t s);
