@@ -416,7 +416,7 @@ int download_decoded(bfp200_handle* h, const int16_t* m, const int8_t* e, int ld
 // in the stream (never a host copy), so it may use programmatic dependent
 // launch.  The stage-dump path copies to the host between kernels and runs
 // without PDL.
-int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool first_pdl = true) {
+int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool first_pdl = true, bool early_kv = false) {
   const Dims d = h->dims();
   const bool saved_pdl = h->pdl;
   if (sink) h->pdl = false;
@@ -442,7 +442,7 @@ int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool firs
   // attention -> tile_quantize(fpq(attn))                 (:273-283)
   mark(h, PK_ATTENTION);
   CK(launch_attention(h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), d, ncols, h->a_m.p, h->a_e.p, s, pdl,
-                      h->pw_off.p, h->pw_data.p));
+                      h->pw_off.p, h->pw_data.p, early_kv));
   if (sink) {
     CKR(download_decoded(h, h->qr_m.p, h->qr_e.p, h->QD, h->QD, 0, ncols, sink->st[1]));
     CKR(download_decoded(h, h->a_m.p, h->a_e.p, h->QD, h->QD, 0, ncols, sink->st[4]));
@@ -546,13 +546,13 @@ int enqueue_gemv_d(bfp200_handle* h, int l, int ncols, bool pdl, int16_t* om, in
   return BFP200_OK;
 }
 
-int enqueue_layer_small(bfp200_handle* h, int l, int ncols, bool first_pdl) {
+int enqueue_layer_small(bfp200_handle* h, int l, int ncols, bool first_pdl, bool early_kv) {
   const bool pdl = h->pdl;
   mark(h, PK_MM_QKV);
   CKR(enqueue_gemv_qkv(h, l, ncols, pdl && first_pdl));
   mark(h, PK_ATTENTION);
   CK(launch_attention(h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), h->dims(), ncols, h->a_m.p, h->a_e.p, h->stream,
-                      pdl, h->pw_off.p, h->pw_data.p));
+                      pdl, h->pw_off.p, h->pw_data.p, early_kv));
   mark(h, PK_MM_O);
   CKR(enqueue_gemv_o(h, l, ncols, pdl, h->h1_m.p, h->h1_e.p));
   mark(h, PK_MM_GU);
@@ -588,13 +588,13 @@ int enqueue_head(bfp200_handle* h, int ncols) {
 // The embedding kernel is the first kernel after host copies of the column
 // descriptors (prefill) or after the non-PDL advance kernel (decode graph):
 // it is launched without programmatic dependent launch.
-int enqueue_forward(bfp200_handle* h, int ncols, bool head) {
+int enqueue_forward(bfp200_handle* h, int ncols, bool head, bool decode = false) {
   mark(h, PK_EMBED);
   CK(launch_embed(h->emb_m.p, h->emb_e.p, h->col_tok.p, h->D, ncols, h->h_m.p, h->h_e.p, h->stream, false));
   const bool small = small_path_ok(h, ncols);
   for (int l = 0; l < h->NL; ++l) {
-    if (small) CKR(enqueue_layer_small(h, l, ncols, /*first_pdl=*/true));
-    else CKR(enqueue_layer(h, l, ncols, nullptr));
+    if (small) CKR(enqueue_layer_small(h, l, ncols, /*first_pdl=*/true, decode));
+    else CKR(enqueue_layer(h, l, ncols, nullptr, true, decode));
   }
   if (head) CKR(enqueue_head(h, ncols));
   return BFP200_OK;
@@ -956,7 +956,7 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
         CK(cudaStreamSynchronize(h->stream));
         cudaGraph_t g;
         CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
-        int r = enqueue_forward(h, n_seq, true);
+        int r = enqueue_forward(h, n_seq, true, /*decode=*/true);
         advance_kernel<<<1, 256, 0, h->stream>>>(h->tok.p, h->cert.p, n_seq, n_gen, h->gen_out.p, h->col_tok.p,
                                                  h->col_pos.p, h->dec_step.p, h->uncert_dev.p);
         cudaError_t ce = cudaStreamEndCapture(h->stream, &g);

@@ -653,7 +653,8 @@ constexpr int ATT_VCHUNK = 256;   // V positions staged in shared memory per pas
 
 __global__ void __launch_bounds__(ATT_THREADS)
 attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
-                 double sqrt_hd, int16_t* am, int8_t* ae, const int* pw_off, const unsigned short* pw_data) {
+                 double sqrt_hd, int16_t* am, int8_t* ae, const int* pw_off, const unsigned short* pw_data,
+                 int early) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_qm[64];
   __shared__ int s_qe[4];
@@ -662,11 +663,8 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   __shared__ int s_lo[96], s_len[96];
   __shared__ double s_val[160];
   pdl_trigger();
-  pdl_wait();
   const int c = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int slot = cols.slot[c], pos = cols.pos[c];
-  const int T = pos + 1;
   const int grp = d.HQ / d.HKV;
   const int kvh = h / grp;
   const int HD = 64;
@@ -674,33 +672,63 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   const size_t sc_bytes = ((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15);
   uint4* vs = reinterpret_cast<uint4*>(smem + sc_bytes);                           // [VCHUNK][8]
   unsigned* ves = reinterpret_cast<unsigned*>(smem + sc_bytes + ATT_VCHUNK * 128);   // [VCHUNK]
-  if (tid < HD) s_qm[tid] = qr_m[(size_t)c * d.HQ * HD + h * HD + tid];
-  if (tid < 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h * 4 + tid];
-  __syncthreads();
+  uint4* ks = reinterpret_cast<uint4*>(smem + sc_bytes + ATT_VCHUNK * 132);          // [VCHUNK][8]
+  unsigned* kes = reinterpret_cast<unsigned*>(smem + sc_bytes + ATT_VCHUNK * 260);   // [VCHUNK]
+  // Rows 0..pos-1 of this head's K and V come from earlier launches.  In a
+  // decode step (early = 1) they are staged into shared memory before the
+  // dependency wait, overlapping the kernel that writes row pos.
+  if (!early) pdl_wait();
+  const int slot = cols.slot[c], pos = cols.pos[c];
+  const int T = pos + 1;
+  const int n0 = min(ATT_VCHUNK, T), nold = min(ATT_VCHUNK, pos);
   const size_t kbase = (((size_t)slot * d.NL + layer) * d.HKV + kvh) * d.MAX_CTX;
-  // the first V chunk streams into shared memory while the scores are formed
   {
-    const int n0 = min(ATT_VCHUNK, T);
+    const uint4* ksrc = reinterpret_cast<const uint4*>(kv.km + kbase * HD);
     const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + kbase * HD);
-    for (int i = tid; i < n0 * 8; i += ATT_THREADS) {
-      const unsigned dst = (unsigned)__cvta_generic_to_shared(vs + i);
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(vsrc + i) : "memory");
+    for (int i = tid; i < nold * 8; i += ATT_THREADS) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(ks + i)),
+                   "l"(ksrc + i) : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(vs + i)),
+                   "l"(vsrc + i) : "memory");
     }
-    const unsigned* esrc = reinterpret_cast<const unsigned*>(kv.ve + kbase * 4);
-    for (int i = tid; i < n0; i += ATT_THREADS) {
-      const unsigned dst = (unsigned)__cvta_generic_to_shared(ves + i);
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(dst), "l"(esrc + i) : "memory");
+    const unsigned* kesrc = reinterpret_cast<const unsigned*>(kv.ke + kbase * 4);
+    const unsigned* vesrc = reinterpret_cast<const unsigned*>(kv.ve + kbase * 4);
+    for (int i = tid; i < nold; i += ATT_THREADS) {
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"((unsigned)__cvta_generic_to_shared(kes + i)),
+                   "l"(kesrc + i) : "memory");
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"((unsigned)__cvta_generic_to_shared(ves + i)),
+                   "l"(vesrc + i) : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  // scores[t] = float(np.dot(q, k_t)) / math.sqrt(HD)   (:278), exact
+  if (early) pdl_wait();
+  // q of this head and row pos of K / V (written by the previous kernel)
+  if (tid < HD) s_qm[tid] = qr_m[(size_t)c * d.HQ * HD + h * HD + tid];
+  if (tid < 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h * 4 + tid];
+  if (pos < ATT_VCHUNK) {
+    if (tid < 8) ks[pos * 8 + tid] = reinterpret_cast<const uint4*>(kv.km + (kbase + pos) * HD)[tid];
+    else if (tid < 16) vs[pos * 8 + tid - 8] = reinterpret_cast<const uint4*>(kv.vm + (kbase + pos) * HD)[tid - 8];
+    else if (tid == 16) kes[pos] = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + pos) * 4);
+    else if (tid == 17) ves[pos] = *reinterpret_cast<const unsigned*>(kv.ve + (kbase + pos) * 4);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  // scores[t] = float(np.dot(q, k_t)) / math.sqrt(HD)   (:278), exact; rows
+  // beyond the first chunk are read from the arena
   double lmax = -INFINITY;
   for (int t = tid; t < T; t += ATT_THREADS) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
     uint4 kk[8];
-    #pragma unroll
-    for (int u = 0; u < 8; ++u) kk[u] = kr[u];
-    const unsigned ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
+    unsigned ke4;
+    if (t < n0) {
+      #pragma unroll
+      for (int u = 0; u < 8; ++u) kk[u] = ks[t * 8 + u];
+      ke4 = kes[t];
+    } else {
+      const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
+      #pragma unroll
+      for (int u = 0; u < 8; ++u) kk[u] = kr[u];
+      ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
+    }
     long long S[4];
     int E[4];
     #pragma unroll
@@ -744,9 +772,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   double acc = 0.0;
   for (int c0 = 0; c0 < T; c0 += ATT_VCHUNK) {
     const int n = min(ATT_VCHUNK, T - c0);
-    if (c0 == 0) {
-      asm volatile("cp.async.wait_all;" ::: "memory");
-    } else {
+    if (c0 > 0) {
       __syncthreads();
       const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + (kbase + c0) * HD);
       for (int i = tid; i < n * 8; i += ATT_THREADS) vs[i] = vsrc[i];
@@ -779,10 +805,10 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
 
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
                              int ncols, int16_t* am, int8_t* ae, cudaStream_t s, bool pdl, const int* pw_off,
-                             const unsigned short* pw_data) {
-  const size_t smem = (((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15)) + ATT_VCHUNK * 128 + ATT_VCHUNK * 4;
+                             const unsigned short* pw_data, bool early_kv) {
+  const size_t smem = (((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15)) + ATT_VCHUNK * 264;
   return launch_ex(attention_kernel, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
-                   cols, d, std::sqrt((double)d.HD), am, ae, pw_off, pw_data);
+                   cols, d, std::sqrt((double)d.HD), am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
 }
 
 // ---------------------------------------------------------------------------

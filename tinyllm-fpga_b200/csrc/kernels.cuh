@@ -158,10 +158,13 @@ cudaError_t launch_rope_kv(const int16_t* qkv_m, const int8_t* qkv_e, int16_t* q
                            int ncols, cudaStream_t s, bool pdl);
 // pw_off / pw_data: numpy pairwise-sum plans for lengths 1..MAX_CTX
 // (build_pw_plan), or nullptr for the generic single-lane tree walk.
+// early_kv: every column's K/V rows below its position were written by
+// earlier launches (a decode step), so they are read before the dependency
+// wait.
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
                              ColDesc cols, Dims d, int ncols, int16_t* am, int8_t* ae,
                              cudaStream_t s, bool pdl, const int* pw_off = nullptr,
-                             const unsigned short* pw_data = nullptr);
+                             const unsigned short* pw_data = nullptr, bool early_kv = false);
 cudaError_t launch_embed(const int16_t* emb_m, const int8_t* emb_e, const int* tokens, int D,
                          int ncols, int16_t* hm, int8_t* he, cudaStream_t s, bool pdl);
 cudaError_t launch_head_prep(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
