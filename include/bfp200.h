@@ -104,6 +104,11 @@ int bfp200_uncertified_steps(bfp200_handle* h, long long* count);
 /* Device time of the last generate call's phases, in milliseconds. */
 int bfp200_last_timing(bfp200_handle* h, double* prefill_ms, double* decode_ms);
 
+/* Number of kernels the last bfp200_generate launched on the device (prefill
+ * launches, plus one decode step's launches times n_gen, or the single
+ * persistent launch).  No reference counterpart: measurement support. */
+int bfp200_last_launches(bfp200_handle* h, long long* launches);
+
 /* Measurement: device time of one token's BFP matmuls (the 4 per layer of
  * every layer, production epilogues, `ncols` columns), replayed `reps` times
  * from a CUDA graph on the handle's stream between CUDA events.  Requires a

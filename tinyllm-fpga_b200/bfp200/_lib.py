@@ -47,6 +47,7 @@ SIGNATURES = {
     "bfp200_generate_multi": [_P, _I, _P, _P, _I, _I, _I, _P],
     "bfp200_uncertified_steps": [_P, C.POINTER(C.c_longlong)],
     "bfp200_last_timing": [_P, C.POINTER(_D), C.POINTER(_D)],
+    "bfp200_last_launches": [_P, C.POINTER(C.c_longlong)],
     "bfp200_tile_quantize": [_P, _P, _Z, _P, _P],
     "bfp200_tile_decode": [_P, _P, _P, _Z, _P],
     "bfp200_matvec": [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P],

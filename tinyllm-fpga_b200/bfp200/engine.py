@@ -99,6 +99,12 @@ class Decoder:
         check(_lib.lib().bfp200_last_timing(self._h, C.byref(a), C.byref(b)))
         return {"prefill_ms": a.value, "decode_ms": b.value}
 
+    def last_launches(self):
+        """Kernel launches of the last generate call (counted by the library)."""
+        n = C.c_longlong()
+        check(_lib.lib().bfp200_last_launches(self._h, C.byref(n)))
+        return n.value
+
     PROFILE_KINDS = ("embed", "rmsnorm", "mm_qkv", "rope_kv", "attention", "mm_o", "mm_gu", "mm_d", "head_prep",
                      "head_logits", "head_reduce")
 

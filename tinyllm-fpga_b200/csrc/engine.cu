@@ -288,6 +288,9 @@ struct bfp200_handle {
   int graph_cols = -1, graph_ngen = -1;
   long long uncert = 0;
   double t_prefill = 0.0, t_decode = 0.0;
+  long long launch_count = 0;       // kernel launches issued (mark); see bfp200_last_launches
+  long long graph_launches = 0;     // launches in one replay of the cached decode graph
+  long long last_launches = 0;      // kernel launches of the last generate call
   // per-kernel profiling (bfp200_profile_forward): an event before every launch
   std::vector<std::pair<int, cudaEvent_t>>* prof = nullptr;
 
@@ -362,7 +365,10 @@ int ensure_kv(bfp200_handle* h, int nslots) {
 enum ProfKind { PK_EMBED, PK_RMSNORM, PK_MM_QKV, PK_ROPE_KV, PK_ATTENTION, PK_MM_O, PK_MM_GU, PK_MM_D, PK_HEAD_PREP,
                 PK_HEAD_LOGITS, PK_HEAD_REDUCE, PK_COUNT };
 
+// Called before every kernel launch an enqueue_* function issues: counts the
+// launch, and with profiling on, records an event in front of it.
 void mark(bfp200_handle* h, int kind) {
+  ++h->launch_count;
   if (!h->prof) return;
   cudaEvent_t ev;
   cudaEventCreate(&ev);
@@ -910,16 +916,19 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
   cudaEvent_t ev0, ev1, ev2;
   cudaEventCreate(&ev0); cudaEventCreate(&ev1); cudaEventCreate(&ev2);
   CK(cudaEventRecord(ev0, h->stream));
+  h->launch_count = 0;
   for (int c0 = 0; c0 < ncp; c0 += h->cap) {
     const int nc = std::min(h->cap, ncp - c0);
     CK(cudaMemcpyAsync(h->col_slot.p, cs.data() + c0, nc * 4, cudaMemcpyHostToDevice, h->stream));
     CK(cudaMemcpyAsync(h->col_pos.p, cp.data() + c0, nc * 4, cudaMemcpyHostToDevice, h->stream));
     CK(cudaMemcpyAsync(h->col_tok.p, ct.data() + c0, nc * 4, cudaMemcpyHostToDevice, h->stream));
     CKR(enqueue_forward(h, nc, rtl));
-    if (rtl)
+    if (rtl) {
       scatter_tokens_kernel<<<(nc + 255) / 256, 256, 0, h->stream>>>(h->tok.p, h->cert.p, h->col_slot.p,
                                                                      h->col_pos.p, nc, h->cfg.NPROMPT_MAX,
                                                                      h->rtl_out.p, h->uncert_dev.p);
+      ++h->launch_count;
+    }
     CK(cudaStreamSynchronize(h->stream));   // host column arrays are reused by the next chunk
   }
   CK(cudaEventRecord(ev1, h->stream));
@@ -949,6 +958,7 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
       PersistArgs pa = persist_args(h, n_seq, n_gen);
       persistent_plan(pa, h->nsm, h->smem_optin);
       CK(launch_persistent_decode(pa, h->nsm, h->stream));
+      ++h->launch_count;
     } else {
       // one decode step captured once as a CUDA graph, replayed n_gen times
       if (!h->graph || h->graph_cols != n_seq || h->graph_ngen != n_gen) {
@@ -956,7 +966,10 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
         CK(cudaStreamSynchronize(h->stream));
         cudaGraph_t g;
         CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+        const long long before = h->launch_count;
         int r = enqueue_forward(h, n_seq, true, /*decode=*/true);
+        h->graph_launches = h->launch_count - before + 1;       // + the advance kernel
+        h->launch_count = before;
         advance_kernel<<<1, 256, 0, h->stream>>>(h->tok.p, h->cert.p, n_seq, n_gen, h->gen_out.p, h->col_tok.p,
                                                  h->col_pos.p, h->dec_step.p, h->uncert_dev.p);
         cudaError_t ce = cudaStreamEndCapture(h->stream, &g);
@@ -969,6 +982,7 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
         h->graph_ngen = n_gen;
       }
       for (int i = 0; i < n_gen; ++i) CK(cudaGraphLaunch(h->graph, h->stream));
+      h->launch_count += h->graph_launches * n_gen;
     }
   }
   CK(cudaEventRecord(ev2, h->stream));
@@ -983,6 +997,7 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
   cudaEventDestroy(ev0); cudaEventDestroy(ev1); cudaEventDestroy(ev2);
   h->t_prefill = ms1;
   h->t_decode = ms2;
+  h->last_launches = h->launch_count;
   h->uncert = unc;
   if (read_and_clear_error_flag(h->stream)) return fail(BFP200_ETIMEOUT, "a bounded device wait timed out");
   // ---- assemble: sim = prompt + generated; rtl = one argmax per step
@@ -1034,6 +1049,12 @@ int bfp200_generate_multi(bfp200_handle* const* hs, int n_dev, const int32_t* pr
 int bfp200_uncertified_steps(bfp200_handle* h, long long* count) {
   if (!h || !count) return fail(BFP200_EINVAL, "null argument");
   *count = h->uncert;
+  return BFP200_OK;
+}
+
+int bfp200_last_launches(bfp200_handle* h, long long* launches) {
+  if (!h || !launches) return fail(BFP200_EINVAL, "last_launches: null argument");
+  *launches = h->last_launches;
   return BFP200_OK;
 }
 
