@@ -252,6 +252,7 @@ struct bfp200_handle {
   bool use_clusters = true;   // K-split reduction through distributed shared memory
   bool use_small = true;      // 1..4 columns: the fused small-batch kernels (gemv.cu)
   bool use_persist = false;   // 1..4 columns: decode steps in one persistent kernel (persist.cu), opt-in
+  bool use_tc = true;         // >= 64 columns: matmuls on the tcgen05 tensor cores (tc.cu)
   int smem_optin = 0;
   // weights
   DBuf<uint8_t> wm_qkv, wm_o, wm_gu, wm_d;
@@ -283,6 +284,9 @@ struct bfp200_handle {
   DBuf<int> gen_out, dec_step, rtl_out;
   DBuf<long long> uncert_dev;
   DBuf<unsigned> psync;
+  // tensor-core records of the QKV, O, gate/up and down matrices, all layers
+  DBuf<uint8_t> tc_rec[4];
+  size_t tc_stride[4] = {0, 0, 0, 0};
   DBuf<unsigned> head_ctr;     // arrival counter of the single-launch head (left zeroed)
   cudaGraphExec_t graph = nullptr;
   int graph_cols = -1, graph_ngen = -1;
@@ -376,9 +380,49 @@ void mark(bfp200_handle* h, int kind) {
   h->prof->push_back({kind, ev});
 }
 
+// The tensor-core records of a handle matrix (one layer), found from its
+// DevMat pointer; nullptr for matrices the handle does not own.
+const uint8_t* tc_records_of(bfp200_handle* h, const DevMat& W) {
+  const DBuf<uint8_t>* wm[4] = {&h->wm_qkv, &h->wm_o, &h->wm_gu, &h->wm_d};
+  const int G[4] = {h->GQKV, h->GO, h->GGU, h->GD};
+  const int NT[4] = {h->NTD, h->QD / 16, h->NTD, h->NTF};
+  for (int m = 0; m < 4; ++m) {
+    if (!h->tc_rec[m].p || !wm[m]->p || W.G != G[m] || W.NT != NT[m]) continue;
+    const size_t stride = h->layer_stride_m(G[m], NT[m]);
+    if (W.wm >= wm[m]->p && W.wm < wm[m]->p + stride * h->NL) {
+      const size_t off = (size_t)(W.wm - wm[m]->p);
+      if (off % stride) return nullptr;
+      return h->tc_rec[m].p + h->tc_stride[m] * (off / stride);
+    }
+  }
+  return nullptr;
+}
+
+// >= 64 columns: the tcgen05 matmul (tc.cu)
+bool tc_path(bfp200_handle* h, const DevMat& W, int ncols, int epi) {
+  return h->use_tc && ncols >= 64 && tc_supported(W.NT, ncols) && !(epi == EPI_SWIGLU && W.G % 2);
+}
+
+int enqueue_tc(bfp200_handle* h, const uint8_t* rec, DevMat W, const int16_t* xm, const int8_t* xe, int x_ld,
+               int x_lde, int ncols, int epi, int16_t* om, int8_t* oe, int o_ld, int o_lde, const int16_t* rm,
+               const int8_t* re) {
+  TcArgs t;
+  t.rec = rec; t.we = W.we; t.rows = W.G * 16; t.NT = W.NT;
+  t.xm = xm; t.xe = xe; t.x_ld = x_ld; t.x_lde = x_lde; t.ncols = ncols;
+  t.mode = epi;
+  t.om = om; t.oe = oe; t.o_ld = o_ld; t.o_lde = o_lde; t.rm = rm; t.re = re;
+  t.err = error_flag_device_ptr();
+  CK(launch_tc_matmul(t, h->stream, h->pdl));
+  return BFP200_OK;
+}
+
 int enqueue_matmul(bfp200_handle* h, DevMat W, const int16_t* xm, const int8_t* xe, int x_ld, int x_lde,
                    int ncols, int epi, int16_t* om, int8_t* oe, int o_ld, int o_lde, const int16_t* rm,
                    const int8_t* re, long long* acc, unsigned* counters, int acc_ld) {
+  if (tc_path(h, W, ncols, epi)) {
+    if (const uint8_t* rec = tc_records_of(h, W))
+      return enqueue_tc(h, rec, W, xm, xe, x_ld, x_lde, ncols, epi, om, oe, o_ld, o_lde, rm, re);
+  }
   MatmulArgs a;
   a.W = W;
   a.xm = xm; a.xe = xe; a.x_ld = x_ld; a.x_lde = x_lde;
@@ -708,6 +752,7 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
   if (const char* e = std::getenv("BFP200_NO_CLUSTER")) h->use_clusters = !(e[0] == '1');
   if (const char* e = std::getenv("BFP200_NO_SMALL")) h->use_small = !(e[0] == '1');
   if (const char* e = std::getenv("BFP200_PERSIST")) h->use_persist = e[0] == '1';
+  if (const char* e = std::getenv("BFP200_NO_TC")) h->use_tc = !(e[0] == '1');
   h->smem_optin = (int)prop.sharedMemPerBlockOptin;
   cudaError_t ce = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
   if (ce != cudaSuccess) { delete h; return fail(BFP200_ECUDA, cudaGetErrorString(ce)); }
@@ -830,6 +875,22 @@ int bfp200_load_image(bfp200_handle* h, const void* img, size_t len) {
   CK(cudaMemcpyAsync(norms.data(), h->emb_norm.p, h->V * 8, cudaMemcpyDeviceToHost, h->stream));
   CK(cudaStreamSynchronize(h->stream));
   h->emb_norm_max = *std::max_element(norms.begin(), norms.end());
+  // tensor-core records for the batched path
+  {
+    const DBuf<uint8_t>* wm[4] = {&h->wm_qkv, &h->wm_o, &h->wm_gu, &h->wm_d};
+    const DBuf<int8_t>* we[4] = {&h->we_qkv, &h->we_o, &h->we_gu, &h->we_d};
+    const int G[4] = {h->GQKV, h->GO, h->GGU, h->GD};
+    const int NT[4] = {h->NTD, h->QD / 16, h->NTD, h->NTF};
+    for (int m = 0; m < 4; ++m) {
+      h->tc_stride[m] = tc_records_bytes(G[m] * 16, NT[m]);
+      CK(h->tc_rec[m].ensure(h->tc_stride[m] * h->NL));
+      for (int l = 0; l < h->NL; ++l) {
+        const DevMat W = h->mat(*wm[m], *we[m], G[m], NT[m], l);
+        CK(launch_tc_pack(W.wm, W.we, G[m] * 16, NT[m], h->tc_rec[m].p + h->tc_stride[m] * l, h->stream));
+      }
+    }
+    CK(cudaStreamSynchronize(h->stream));
+  }
   h->have_image = true;
   return BFP200_OK;
 }
@@ -1213,6 +1274,17 @@ int bfp200_matvec(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const
   CK(launch_pack_weights(dWm.p, dWe.p, D_out, NT, wm.p, we.p, 1, 0, h->stream));
   DevMat W;
   W.wm = wm.p; W.we = we.p; W.G = G; W.NT = NT;
+  if (tc_path(h, W, batch, EPI_STORE)) {
+    DBuf<uint8_t> rec;
+    CK(rec.ensure(tc_records_bytes(D_out, NT)));
+    CK(launch_tc_pack(wm.p, we.p, D_out, NT, rec.p, h->stream));
+    CKR(enqueue_tc(h, rec.p, W, dxm.p, dxe.p, D_in, NT, batch, EPI_STORE, dom.p, doe.p, D_out, G, nullptr, nullptr));
+    CK(cudaMemcpyAsync(out_m, dom.p, (size_t)batch * D_out * 2, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaMemcpyAsync(out_e, doe.p, (size_t)batch * G, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    if (read_and_clear_error_flag(h->stream)) return fail(BFP200_ETIMEOUT, "a bounded device wait timed out");
+    return BFP200_OK;
+  }
   const MMPlan p = plan_matmul(G, NT, batch, false, h->nsm);
   DBuf<long long> acc; DBuf<unsigned> cnt;
   if (p.ks > 1) {

@@ -86,6 +86,30 @@ struct GemvArgs {
   int8_t* qr_e = nullptr;
 };
 
+// Batched BFP matvec on the tcgen05 tensor cores (tc.cu), for >= 64 columns.
+// The weights are repacked once (launch_tc_pack) from DevMat into records of
+// 128 rows x one K tile; rows are padded to a multiple of 128.
+struct TcArgs {
+  const uint8_t* rec = nullptr;   // records of one matrix (one layer), tc_records_bytes(rows, NT) bytes
+  const int8_t* we = nullptr;     // the same matrix's DevMat tile exponents [G][NT][16]
+  int rows = 0, NT = 0;
+  const int16_t* xm = nullptr;    // input columns: column c at xm + c*x_ld, xe + c*x_lde
+  const int8_t* xe = nullptr;
+  int x_ld = 0, x_lde = 0;
+  int ncols = 0;
+  int mode = EPI_STORE;           // EPI_STORE / EPI_RESIDUAL / EPI_SWIGLU (rows interleave g/u groups)
+  int16_t* om = nullptr;
+  int8_t* oe = nullptr;
+  int o_ld = 0, o_lde = 0;
+  const int16_t* rm = nullptr;    // residual (EPI_RESIDUAL), output layout
+  const int8_t* re = nullptr;
+  int* err = nullptr;             // bounded-wait error flag
+};
+size_t tc_records_bytes(int rows, int NT);
+cudaError_t launch_tc_pack(const uint8_t* wm, const int8_t* we, int rows, int NT, uint8_t* rec, cudaStream_t s);
+bool tc_supported(int NT, int ncols);
+cudaError_t launch_tc_matmul(const TcArgs& a, cudaStream_t s, bool pdl);
+
 // Persistent small-batch decode (persist.cu): one cooperative launch runs
 // n_gen decode steps of 1..4 columns (embedding, all layers, head, token
 // feedback).  The weight matrices are in DevMat layout, one per layer,

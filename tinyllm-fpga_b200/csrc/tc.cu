@@ -1,0 +1,421 @@
+// tc.cu -- batched BFP matvec (>= 64 columns) on the tcgen05 tensor cores.
+//
+// matvec_hw_golden (gen_smollm_blockfp_full.py:214-233) needs, for every
+// output row r, column c and 16-element K tile t, the exact tile sum
+// S = sum_k W[r,k] x[c,k], floor-shifted by its own exponent gap before the
+// int64 accumulation.  The tensor cores form the tile sums; the CUDA cores
+// do the per-tile shift and accumulation.
+//
+// Limbs.  With W' = W - 128 = 256 Wh + Wl' (Wh = W >> 8, Wl' = (W & 255) - 128,
+// both signed 8-bit) and x' likewise,
+//   S = sum W'x' + 128 sum W + 128 sum x - 16 * 128^2
+//   sum W'x' = 65536 (Wh.xh) + 256 (Wh.xl' + Wl'.xh) + (Wl'.xl')
+// so every limb product is signed x signed.  One kind::i8 MMA per tile with
+// K = 32 (A = [Wl' | Wh]) produces the three limb sums side by side in N:
+// the B operand of all tiles is laid out once in shared memory as blocks of
+// Nc rows x 16 bytes  [0, xh_0, xl'_0, 0, xh_1, xl'_1, 0, ...]; tile t's
+// descriptor starts at block 3t with the K-chunk stride one block, so its
+// chunk 0 is [0; xh; xl'] and chunk 1 [xh; xl'; 0], and the N-blocks of D are
+// (Wh.xh, Wl'.xh + Wh.xl', Wl'.xl').  Every limb sum fits int32; they are
+// recombined in int64.
+//
+// Weights are repacked once into per-(128-row block, K tile) records
+//   [Wl' rows 128 x 16 B][Wh rows 128 x 16 B][cw int32 x 128][we int8 x 128]
+// with cw = 128 sum_k W - 16 * 128^2 (rows padded to a multiple of 128 are
+// zero weights).  Records stream through a shared-memory ring by TMA bulk
+// copies; D is double-buffered in tensor memory so tile t+1's MMA overlaps
+// tile t's epilogue.
+#include "bfp_device.cuh"
+#include "kernels.cuh"
+
+namespace bfp {
+
+namespace {
+
+constexpr int TC_THREADS = 256;
+constexpr int TC_M = 128;
+constexpr int TC_REC = 4736;            // bytes per (128-row block, K tile) record
+constexpr int TC_SA = 4;                // record ring stages
+constexpr long long TC_SPIN = 1LL << 20;
+
+__device__ __forceinline__ unsigned su32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void pdl_wait_tc() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger_tc() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ void mb_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(su32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mb_try(unsigned long long* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok) : "r"(su32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// bounded wait; returns false (and raises the error flag) when it gives up
+__device__ __forceinline__ bool mb_wait(unsigned long long* bar, unsigned parity, int* err) {
+  long long it = 0;
+  while (!mb_try(bar, parity)) {
+    if (++it > TC_SPIN) { atomicExch(err, 4); return false; }
+  }
+  return true;
+}
+
+__device__ __forceinline__ uint64_t smem_desc(const void* p, unsigned lbo, unsigned sbo) {
+  // K-major, no swizzle; start >> 4 [0,14), LBO >> 4 [16,30), SBO >> 4 [32,46),
+  // descriptor version 1 at [46,48), layout type 0 (none) at [61,64)
+  const uint64_t a = (su32(p) >> 4) & 0x3FFFu;
+  return a | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// kind::i8 instruction descriptor: D s32 [4,6)=2, A s8 [7,10)=1, B s8 [10,13)=1,
+// both K-major, N >> 3 at [17,23), M >> 4 at [24,29)
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n"
+      :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(z), "r"(z) : "memory");
+}
+__device__ __forceinline__ void tc_commit(unsigned long long* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(su32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 (or 8) consecutive 32-bit TMEM columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr) : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <int CPT>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[CPT]) {
+  if constexpr (CPT == 16) tmem_ld16(taddr, r);
+  else tmem_ld8(taddr, r);
+}
+
+// ---------------------------------------------------------------------------
+// repack: DevMat (planes [G][NT][2][16][16], exponents [G][NT][16]) -> records
+// ---------------------------------------------------------------------------
+__global__ void tc_pack_kernel(const uint8_t* wm, const int8_t* we, int rows, int NT, int gstride, int goff,
+                               uint8_t* rec) {
+  // block (b, t); thread = row within the 128-row block
+  const int b = blockIdx.x, t = blockIdx.y, r = threadIdx.x;
+  const int R = b * TC_M + r;
+  uint8_t* dst = rec + ((size_t)b * NT + t) * TC_REC;
+  uint4 hi = make_uint4(0, 0, 0, 0), lo = make_uint4(0, 0, 0, 0);
+  int8_t e = 0;
+  if (R < rows) {
+    const int g = (R / 16) * gstride + goff, ri = R % 16;
+    const uint4* src = reinterpret_cast<const uint4*>(wm + ((size_t)g * NT + t) * 512);
+    hi = src[ri];
+    lo = src[16 + ri];
+    e = we[((size_t)g * NT + t) * 16 + ri];
+  }
+  // W = 256 hi + lo; Wl' = lo - 128 = lo ^ 0x80 as a signed byte
+  int sw = 0;
+  const unsigned hw[4] = {hi.x, hi.y, hi.z, hi.w}, lw[4] = {lo.x, lo.y, lo.z, lo.w};
+  #pragma unroll
+  for (int q = 0; q < 4; ++q)
+    #pragma unroll
+    for (int k = 0; k < 4; ++k) sw += 256 * (int)(int8_t)(hw[q] >> (8 * k)) + (int)((lw[q] >> (8 * k)) & 0xFF);
+  const uint4 los = make_uint4(lo.x ^ 0x80808080u, lo.y ^ 0x80808080u, lo.z ^ 0x80808080u, lo.w ^ 0x80808080u);
+  reinterpret_cast<uint4*>(dst)[r] = los;                       // Wl' rows
+  reinterpret_cast<uint4*>(dst + 2048)[r] = hi;                 // Wh rows
+  reinterpret_cast<int*>(dst + 4096)[r] = 128 * sw - 16 * 128 * 128;
+  reinterpret_cast<int8_t*>(dst + 4608)[r] = e;
+}
+
+// ---------------------------------------------------------------------------
+// the matmul
+// ---------------------------------------------------------------------------
+struct TcLayout {
+  size_t bar, tptr, ring, z, xe, cx, total;
+};
+__host__ __device__ inline TcLayout tc_layout(int NT, int NCB) {
+  TcLayout L;
+  L.bar = 0;                                           // mbarriers: ring full [TC_SA], D full [2]
+  L.tptr = 64;                                         // TMEM base address
+  L.ring = 128;
+  L.z = L.ring + (size_t)TC_SA * TC_REC;
+  L.xe = L.z + (size_t)(3 * NT + 1) * NCB * 16;
+  L.cx = L.xe + (((size_t)NT * NCB + 15) & ~size_t(15));
+  L.total = L.cx + (size_t)NT * NCB * 4;
+  return L;
+}
+
+// NCB columns per CTA (16 or 32); warp w handles TMEM lanes 32 (w % 4) .. +31
+// (rows) and column half w / 4 (CPT = NCB / 2 columns per thread).
+template <int NCB, int MODE>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+tc_matmul_kernel(TcArgs a) {
+  constexpr int CPT = NCB / 2;
+  constexpr int N = 3 * NCB;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NT = a.NT;
+  const int blk = blockIdx.x, c0 = blockIdx.y * NCB;
+  const TcLayout L = tc_layout(NT, NCB);
+  unsigned long long* full = reinterpret_cast<unsigned long long*>(smem + L.bar);   // [TC_SA]
+  unsigned long long* dfull = full + TC_SA;                                          // [2]
+  uint32_t* tptr = reinterpret_cast<uint32_t*>(smem + L.tptr);
+  unsigned char* ring = smem + L.ring;
+  unsigned char* Z = smem + L.z;
+  int8_t* xe_s = reinterpret_cast<int8_t*>(smem + L.xe);     // [NT][NCB]
+  int* cx_s = reinterpret_cast<int*>(smem + L.cx);           // [NT][NCB]
+  const uint8_t* rec = a.rec + (size_t)blk * NT * TC_REC;
+  pdl_trigger_tc();
+  // ---- barriers and the first weight records: the weights do not depend on
+  // the previous kernel, so they stream before the wait
+  if (tid == 0) {
+    for (int s = 0; s < TC_SA; ++s) mb_init(&full[s], 1);
+    mb_init(&dfull[0], 1);
+    mb_init(&dfull[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int s = 0; s < TC_SA && s < NT; ++s) {
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&full[s])), "r"(TC_REC) : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   :: "r"(su32(ring + (size_t)s * TC_REC)), "l"(rec + (size_t)s * TC_REC), "r"(TC_REC),
+                      "r"(su32(&full[s])) : "memory");
+    }
+  }
+  pdl_wait_tc();
+  // tensor memory only after the wait: a CTA waiting on its predecessor holds
+  // none, so the predecessor's CTAs can always allocate theirs
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" :: "r"(su32(tptr)) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // ---- B operand of every tile, column exponents and sums (columns c0 .. c0+NCB-1)
+  for (int i = tid; i < NCB * 4; i += TC_THREADS) {           // the leading zero block (16 B units)
+    reinterpret_cast<uint4*>(Z)[i] = make_uint4(0, 0, 0, 0);
+  }
+  for (int i = tid; i < NT * NCB; i += TC_THREADS) {
+    const int t = i / NCB, c = i - t * NCB, col = c0 + c;
+    uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
+    int8_t e = -127;
+    if (col < a.ncols) {
+      const uint4* xp = reinterpret_cast<const uint4*>(a.xm + (size_t)col * a.x_ld + t * 16);
+      v0 = xp[0];
+      v1 = xp[1];
+      e = a.xe[(size_t)col * a.x_lde + t];
+    }
+    // x = 256 xh + lo: xh = odd bytes, xl' = even bytes ^ 0x80
+    const uint4 xh = make_uint4(__byte_perm(v0.x, v0.y, 0x7531), __byte_perm(v0.z, v0.w, 0x7531),
+                                __byte_perm(v1.x, v1.y, 0x7531), __byte_perm(v1.z, v1.w, 0x7531));
+    const uint4 xl = make_uint4(__byte_perm(v0.x, v0.y, 0x6420) ^ 0x80808080u, __byte_perm(v0.z, v0.w, 0x6420) ^ 0x80808080u,
+                                __byte_perm(v1.x, v1.y, 0x6420) ^ 0x80808080u, __byte_perm(v1.z, v1.w, 0x6420) ^ 0x80808080u);
+    uint4* zb = reinterpret_cast<uint4*>(Z + (size_t)(3 * t + 1) * NCB * 16);
+    zb[c] = xh;
+    zb[NCB + c] = xl;
+    zb[2 * NCB + c] = make_uint4(0, 0, 0, 0);
+    int sx = 0;
+    const unsigned w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    #pragma unroll
+    for (int k = 0; k < 8; ++k) sx += (int)(int16_t)(w[k] & 0xFFFF) + (int)(int16_t)(w[k] >> 16);
+    xe_s[i] = e;
+    cx_s[i] = 128 * sx;
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");     // B written by threads, read by the MMA
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tptr;
+  // ---- this thread: row (lane quarter) and its CPT columns
+  const int q = warp & 3, half = warp >> 2;
+  const int row = q * 32 + lane, R = blk * TC_M + row;
+  const int cb = half * CPT;
+  // max exponent per (row, column) over all tiles (:221-222)
+  int Mx[CPT];
+  #pragma unroll
+  for (int j = 0; j < CPT; ++j) Mx[j] = -100000;
+  {
+    const int g = R / 16, ri = R % 16;
+    for (int t = 0; t < NT; ++t) {
+      const int we = (R < a.rows) ? (int)a.we[((size_t)g * NT + t) * 16 + ri] : 0;
+      #pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const int e = we + (int)xe_s[t * NCB + cb + j];
+        Mx[j] = e > Mx[j] ? e : Mx[j];
+      }
+    }
+  }
+  long long acc[CPT];
+  #pragma unroll
+  for (int j = 0; j < CPT; ++j) acc[j] = 0;
+  const uint32_t idesc = idesc_i8(TC_M, N);
+  bool ok = true;
+  // MMA of tile 0
+  if (tid == 0) {
+    ok = mb_wait(&full[0], 0, a.err);
+    tc_fence_after();
+    tc_mma(tbase, smem_desc(ring, 2048, 128), smem_desc(Z, NCB * 16, 128), idesc);
+    tc_commit(&dfull[0]);
+  }
+  for (int t = 0; t < NT; ++t) {
+    const int b = t & 1, s = t % TC_SA;
+    // issue tile t+1 into the other D buffer (its previous reader, tile t-1,
+    // finished before the barrier that ended the last iteration)
+    if (tid == 0 && t + 1 < NT) {
+      const int s1 = (t + 1) % TC_SA;
+      ok = mb_wait(&full[s1], (unsigned)(((t + 1) / TC_SA) & 1), a.err) && ok;
+      tc_fence_after();
+      tc_mma(tbase + (uint32_t)((b ^ 1) * 128), smem_desc(ring + (size_t)s1 * TC_REC, 2048, 128),
+             smem_desc(Z + (size_t)3 * (t + 1) * NCB * 16, NCB * 16, 128), idesc);
+      tc_commit(&dfull[b ^ 1]);
+    }
+    // tile t: wait for its MMA, read the three limb sums
+    if (!mb_wait(&dfull[b], (unsigned)((t >> 1) & 1), a.err)) ok = false;
+    tc_fence_after();
+    uint32_t hh[CPT], cr[CPT], ll[CPT];
+    const uint32_t tq = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 128 + cb);
+    tmem_ld<CPT>(tq, hh);
+    tmem_ld<CPT>(tq + NCB, cr);
+    tmem_ld<CPT>(tq + 2 * NCB, ll);
+    tmem_wait_ld();
+    if (!mb_wait(&full[s], (unsigned)((t / TC_SA) & 1), a.err)) ok = false;   // complete already: orders the reads
+    const unsigned char* rs = ring + (size_t)s * TC_REC;
+    const int cw = reinterpret_cast<const int*>(rs + 4096)[row];
+    const int wer = reinterpret_cast<const int8_t*>(rs + 4608)[row];
+    // per-tile floor shift and int64 accumulation (:223-228)
+    #pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = cb + j;
+      const int sh = Mx[j] - wer - (int)xe_s[t * NCB + c];
+      const int lo = (int)ll[j] + cw + cx_s[t * NCB + c];
+      const long long S = ((long long)(int)hh[j] << 16) + ((long long)(int)cr[j] << 8) + (long long)lo;
+      acc[j] += (sh > ALIGN_MAX) ? 0LL : (S >> sh);
+    }
+    tc_fence_before();
+    __syncthreads();
+    // record stage s is free (MMA t done, every thread past its cw / we reads)
+    if (tid == 0 && t + TC_SA < NT) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&full[s])), "r"(TC_REC) : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   :: "r"(su32(ring + (size_t)s * TC_REC)), "l"(rec + (size_t)(t + TC_SA) * TC_REC), "r"(TC_REC),
+                      "r"(su32(&full[s])) : "memory");
+    }
+  }
+  // ---- epilogue: clip, scale (:229-232), quantize over 16-row output tiles (:233)
+  const bool row_ok = R < a.rows;
+  #pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int col = c0 + cb + j;
+    const bool valid = row_ok && col < a.ncols;
+    long long sacc = acc[j];
+    sacc = sacc > SAT_HI ? SAT_HI : (sacc < SAT_LO ? SAT_LO : sacc);
+    const double out_real = (double)sacc * pow2(Mx[j] - 30);
+    int qe;
+    int16_t qm = tile_quantize_16lanes(out_real, &qe);
+    const int cc = col < a.ncols ? col : 0;
+    if constexpr (MODE == EPI_STORE) {
+      if (valid) {
+        a.om[(size_t)cc * a.o_ld + R] = qm;
+        if ((R & 15) == 0) a.oe[(size_t)cc * a.o_lde + R / 16] = (int8_t)qe;
+      }
+    } else if constexpr (MODE == EPI_RESIDUAL) {
+      const double hv = valid ? bfp_decode(a.rm[(size_t)cc * a.o_ld + R], a.re[(size_t)cc * a.o_lde + R / 16]) : 0.0;
+      qm = tile_quantize_16lanes(__dadd_rn(hv, bfp_decode(qm, qe)), &qe);          // fpq(h + o)
+      if (valid) {
+        a.om[(size_t)cc * a.o_ld + R] = qm;
+        if ((R & 15) == 0) a.oe[(size_t)cc * a.o_lde + R / 16] = (int8_t)qe;
+      }
+    } else {   // EPI_SWIGLU: lanes 0-15 hold a gate group, lanes 16-31 its up group
+      // every lane runs the warp-wide quantizers; only the gate lanes' results are kept
+      const double mine = bfp_decode(qm, qe);
+      const double other = __shfl_xor_sync(0xffffffffu, mine, 16);
+      const bool is_g = (lane & 16) == 0;
+      const double sv = __ddiv_rn(mine, __dadd_rn(1.0, exp(-mine)));                  // silu_fp (:241-242)
+      int se;
+      const int16_t sm = tile_quantize_16lanes(sv, &se);
+      const double prod = is_g ? __dmul_rn(bfp_decode(sm, se), other) : 0.0;           // (:290)
+      int pe;
+      int16_t pm = tile_quantize_16lanes(prod, &pe);
+      const unsigned bal = __ballot_sync(0xffffffffu, is_g && valid && pm == (int16_t)-32768);
+      const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
+      pm = requant_mant(pm, has_min && pe < 127);                                     // (:291)
+      pe = requant_exp(pe, has_min);
+      const int ug = R / 32;                                                           // mlp group of the pair
+      if (is_g && valid) {
+        a.om[(size_t)cc * a.o_ld + ug * 16 + (lane & 15)] = pm;
+        if ((lane & 15) == 0) a.oe[(size_t)cc * a.o_lde + ug] = (int8_t)pe;
+      }
+    }
+  }
+  // ---- release tensor memory (all reads completed above)
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" :: "r"(tbase) : "memory");
+  }
+  (void)ok;
+}
+
+template <int NCB, int MODE>
+cudaError_t launch_tc_t(const TcArgs& a, cudaStream_t s, bool pdl) {
+  const size_t smem = tc_layout(a.NT, NCB).total;
+  cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<NCB, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.rows + TC_M - 1) / TC_M, (a.ncols + NCB - 1) / NCB);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<NCB, MODE>, a);
+}
+
+}  // namespace
+
+size_t tc_records_bytes(int rows, int NT) { return (size_t)((rows + TC_M - 1) / TC_M) * NT * TC_REC; }
+
+cudaError_t launch_tc_pack(const uint8_t* wm, const int8_t* we, int rows, int NT, uint8_t* rec, cudaStream_t s) {
+  dim3 grid((rows + TC_M - 1) / TC_M, NT);
+  tc_pack_kernel<<<grid, TC_M, 0, s>>>(wm, we, rows, NT, 1, 0, rec);
+  return cudaGetLastError();
+}
+
+bool tc_supported(int NT, int ncols) {
+  if (ncols < 1 || NT < 1) return false;
+  return tc_layout(NT, 32).total <= 200 * 1024 || tc_layout(NT, 16).total <= 200 * 1024;
+}
+
+cudaError_t launch_tc_matmul(const TcArgs& a, cudaStream_t s, bool pdl) {
+  // 32 columns per CTA when the grid still covers the SMs, else 16
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int nblk = (a.rows + TC_M - 1) / TC_M;
+  const bool wide = nblk * ((a.ncols + 31) / 32) >= nsm && tc_layout(a.NT, 32).total <= 200 * 1024;
+  if (!wide && tc_layout(a.NT, 16).total > 200 * 1024) return cudaErrorInvalidValue;
+  if (a.mode == EPI_SWIGLU && (a.rows % 32)) return cudaErrorInvalidValue;
+  switch (a.mode) {
+    case EPI_STORE: return wide ? launch_tc_t<32, EPI_STORE>(a, s, pdl) : launch_tc_t<16, EPI_STORE>(a, s, pdl);
+    case EPI_RESIDUAL:
+      return wide ? launch_tc_t<32, EPI_RESIDUAL>(a, s, pdl) : launch_tc_t<16, EPI_RESIDUAL>(a, s, pdl);
+    case EPI_SWIGLU: return wide ? launch_tc_t<32, EPI_SWIGLU>(a, s, pdl) : launch_tc_t<16, EPI_SWIGLU>(a, s, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace bfp
