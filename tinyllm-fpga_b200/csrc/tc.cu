@@ -32,7 +32,7 @@ namespace bfp {
 
 namespace {
 
-constexpr int TC_THREADS = 256;
+constexpr int TC_THREADS = 576;     // warp 0 TMA, warp 1 MMA, warps 2..17 epilogue
 constexpr int TC_M = 128;
 constexpr int TC_REC = 4736;            // bytes per (128-row block, K tile) record
 constexpr int TC_SA = 4;                // record ring stages
@@ -87,14 +87,7 @@ __device__ __forceinline__ void tc_commit(unsigned long long* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 16 (or 8) consecutive 32-bit TMEM columns of this warp's 32 lanes
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr) : "memory");
-}
+// consecutive 32-bit TMEM columns of this warp's 32 lanes
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -102,11 +95,21 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(taddr) : "memory");
+}
+
 template <int CPT>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[CPT]) {
-  if constexpr (CPT == 16) tmem_ld16(taddr, r);
-  else tmem_ld8(taddr, r);
+  if constexpr (CPT == 8) tmem_ld8(taddr, r);
+  else tmem_ld4(taddr, r);
 }
+
+// Per 128-row block: NT records, then the block's tile exponents row by row
+// ([128 rows][NTP] bytes, NTP = NT rounded up to 16) for the max-exponent pass.
+__host__ __device__ inline int tc_ntp(int NT) { return (NT + 15) & ~15; }
+__host__ __device__ inline size_t tc_block_bytes(int NT) { return (size_t)NT * TC_REC + (size_t)TC_M * tc_ntp(NT); }
 
 // ---------------------------------------------------------------------------
 // repack: DevMat (planes [G][NT][2][16][16], exponents [G][NT][16]) -> records
@@ -116,7 +119,8 @@ __global__ void tc_pack_kernel(const uint8_t* wm, const int8_t* we, int rows, in
   // block (b, t); thread = row within the 128-row block
   const int b = blockIdx.x, t = blockIdx.y, r = threadIdx.x;
   const int R = b * TC_M + r;
-  uint8_t* dst = rec + ((size_t)b * NT + t) * TC_REC;
+  uint8_t* blockp = rec + (size_t)b * tc_block_bytes(NT);
+  uint8_t* dst = blockp + (size_t)t * TC_REC;
   uint4 hi = make_uint4(0, 0, 0, 0), lo = make_uint4(0, 0, 0, 0);
   int8_t e = 0;
   if (R < rows) {
@@ -138,6 +142,7 @@ __global__ void tc_pack_kernel(const uint8_t* wm, const int8_t* we, int rows, in
   reinterpret_cast<uint4*>(dst + 2048)[r] = hi;                 // Wh rows
   reinterpret_cast<int*>(dst + 4096)[r] = 128 * sw - 16 * 128 * 128;
   reinterpret_cast<int8_t*>(dst + 4608)[r] = e;
+  reinterpret_cast<int8_t*>(blockp + (size_t)NT * TC_REC)[(size_t)r * tc_ntp(NT) + t] = e;
 }
 
 // ---------------------------------------------------------------------------
@@ -148,55 +153,63 @@ struct TcLayout {
 };
 __host__ __device__ inline TcLayout tc_layout(int NT, int NCB) {
   TcLayout L;
-  L.bar = 0;                                           // mbarriers: ring full [TC_SA], D full [2]
-  L.tptr = 64;                                         // TMEM base address
+  L.bar = 0;                                           // mbarriers: ring full / empty, D full / empty
+  L.tptr = 112;                                        // TMEM base address
   L.ring = 128;
   L.z = L.ring + (size_t)TC_SA * TC_REC;
   L.xe = L.z + (size_t)(3 * NT + 1) * NCB * 16;
-  L.cx = L.xe + (((size_t)NT * NCB + 15) & ~size_t(15));
+  L.cx = L.xe + (size_t)NT * NCB * 4;
   L.total = L.cx + (size_t)NT * NCB * 4;
   return L;
 }
 
-// NCB columns per CTA (16 or 32); warp w handles TMEM lanes 32 (w % 4) .. +31
-// (rows) and column half w / 4 (CPT = NCB / 2 columns per thread).
+// Warp roles: warp 0 streams the weight records (TMA), warp 1 issues the
+// MMAs, warps 2..17 are the epilogue: warp w reads TMEM lanes 32 (w % 4) ..
+// +31 (the rows) for column quarter (w - 2) / 4 (CPT = NCB / 4 columns per
+// thread).  Records pass through a ring of TC_SA stages (full: TMA bytes;
+// empty: the MMA's commit and one arrival per epilogue warp), D through
+// TC_NB tensor-memory buffers (full: MMA commit; empty: the epilogue warps).
+constexpr int TC_NB = 2;
+constexpr int TC_EPI_WARPS = 16;
+
 template <int NCB, int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 tc_matmul_kernel(TcArgs a) {
-  constexpr int CPT = NCB / 2;
+  constexpr int CPT = NCB / 4;
   constexpr int N = 3 * NCB;
   extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int NT = a.NT;
   const int blk = blockIdx.x, c0 = blockIdx.y * NCB;
   const TcLayout L = tc_layout(NT, NCB);
-  unsigned long long* full = reinterpret_cast<unsigned long long*>(smem + L.bar);   // [TC_SA]
-  unsigned long long* dfull = full + TC_SA;                                          // [2]
+  unsigned long long* rfull = reinterpret_cast<unsigned long long*>(smem + L.bar);   // [TC_SA]
+  unsigned long long* rempty = rfull + TC_SA;                                         // [TC_SA]
+  unsigned long long* dfull = rempty + TC_SA;                                         // [TC_NB]
+  unsigned long long* dempty = dfull + TC_NB;                                         // [TC_NB]
   uint32_t* tptr = reinterpret_cast<uint32_t*>(smem + L.tptr);
   unsigned char* ring = smem + L.ring;
   unsigned char* Z = smem + L.z;
-  int8_t* xe_s = reinterpret_cast<int8_t*>(smem + L.xe);     // [NT][NCB]
+  int* xe_s = reinterpret_cast<int*>(smem + L.xe);           // [NT][NCB]
   int* cx_s = reinterpret_cast<int*>(smem + L.cx);           // [NT][NCB]
-  const uint8_t* rec = a.rec + (size_t)blk * NT * TC_REC;
+  const uint8_t* rec = a.rec + (size_t)blk * tc_block_bytes(NT);
   pdl_trigger_tc();
   // ---- barriers and the first weight records: the weights do not depend on
   // the previous kernel, so they stream before the wait
   if (tid == 0) {
-    for (int s = 0; s < TC_SA; ++s) mb_init(&full[s], 1);
-    mb_init(&dfull[0], 1);
-    mb_init(&dfull[1], 1);
+    for (int s = 0; s < TC_SA; ++s) { mb_init(&rfull[s], 1); mb_init(&rempty[s], 1 + TC_EPI_WARPS); }
+    for (int b = 0; b < TC_NB; ++b) { mb_init(&dfull[b], 1); mb_init(&dempty[b], TC_EPI_WARPS); }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int s = 0; s < TC_SA && s < NT; ++s) {
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&full[s])), "r"(TC_REC) : "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&rfull[s])), "r"(TC_REC) : "memory");
       asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                    :: "r"(su32(ring + (size_t)s * TC_REC)), "l"(rec + (size_t)s * TC_REC), "r"(TC_REC),
-                      "r"(su32(&full[s])) : "memory");
+                      "r"(su32(&rfull[s])) : "memory");
     }
   }
   pdl_wait_tc();
   // tensor memory only after the wait: a CTA waiting on its predecessor holds
   // none, so the predecessor's CTAs can always allocate theirs
-  if (warp == 0) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" :: "r"(su32(tptr)) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -204,166 +217,209 @@ tc_matmul_kernel(TcArgs a) {
   for (int i = tid; i < NCB * 4; i += TC_THREADS) {           // the leading zero block (16 B units)
     reinterpret_cast<uint4*>(Z)[i] = make_uint4(0, 0, 0, 0);
   }
-  for (int i = tid; i < NT * NCB; i += TC_THREADS) {
-    const int t = i / NCB, c = i - t * NCB, col = c0 + c;
-    uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
-    int8_t e = -127;
-    if (col < a.ncols) {
-      const uint4* xp = reinterpret_cast<const uint4*>(a.xm + (size_t)col * a.x_ld + t * 16);
-      v0 = xp[0];
-      v1 = xp[1];
-      e = a.xe[(size_t)col * a.x_lde + t];
-    }
-    // x = 256 xh + lo: xh = odd bytes, xl' = even bytes ^ 0x80
-    const uint4 xh = make_uint4(__byte_perm(v0.x, v0.y, 0x7531), __byte_perm(v0.z, v0.w, 0x7531),
-                                __byte_perm(v1.x, v1.y, 0x7531), __byte_perm(v1.z, v1.w, 0x7531));
-    const uint4 xl = make_uint4(__byte_perm(v0.x, v0.y, 0x6420) ^ 0x80808080u, __byte_perm(v0.z, v0.w, 0x6420) ^ 0x80808080u,
-                                __byte_perm(v1.x, v1.y, 0x6420) ^ 0x80808080u, __byte_perm(v1.z, v1.w, 0x6420) ^ 0x80808080u);
-    uint4* zb = reinterpret_cast<uint4*>(Z + (size_t)(3 * t + 1) * NCB * 16);
-    zb[c] = xh;
-    zb[NCB + c] = xl;
-    zb[2 * NCB + c] = make_uint4(0, 0, 0, 0);
-    int sx = 0;
-    const unsigned w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  constexpr int ZB = 4;                                      // items in flight per thread
+  for (int i0 = tid; i0 < NT * NCB; i0 += ZB * TC_THREADS) {
+    uint4 v[ZB][2];
+    int8_t ev[ZB];
     #pragma unroll
-    for (int k = 0; k < 8; ++k) sx += (int)(int16_t)(w[k] & 0xFFFF) + (int)(int16_t)(w[k] >> 16);
-    xe_s[i] = e;
-    cx_s[i] = 128 * sx;
+    for (int u = 0; u < ZB; ++u) {
+      const int i = i0 + u * TC_THREADS, t = i / NCB, c = i - t * NCB, col = c0 + c;
+      v[u][0] = v[u][1] = make_uint4(0, 0, 0, 0);
+      ev[u] = -127;
+      if (i < NT * NCB && col < a.ncols) {
+        const uint4* xp = reinterpret_cast<const uint4*>(a.xm + (size_t)col * a.x_ld + t * 16);
+        v[u][0] = xp[0];
+        v[u][1] = xp[1];
+        ev[u] = a.xe[(size_t)col * a.x_lde + t];
+      }
+    }
+    #pragma unroll
+    for (int u = 0; u < ZB; ++u) {
+      const int i = i0 + u * TC_THREADS, t = i / NCB, c = i - t * NCB;
+      if (i >= NT * NCB) break;
+      const uint4 v0 = v[u][0], v1 = v[u][1];
+      // x = 256 xh + lo: xh = odd bytes, xl' = even bytes ^ 0x80
+      const uint4 xh = make_uint4(__byte_perm(v0.x, v0.y, 0x7531), __byte_perm(v0.z, v0.w, 0x7531),
+                                  __byte_perm(v1.x, v1.y, 0x7531), __byte_perm(v1.z, v1.w, 0x7531));
+      const uint4 xl = make_uint4(__byte_perm(v0.x, v0.y, 0x6420) ^ 0x80808080u, __byte_perm(v0.z, v0.w, 0x6420) ^ 0x80808080u,
+                                  __byte_perm(v1.x, v1.y, 0x6420) ^ 0x80808080u, __byte_perm(v1.z, v1.w, 0x6420) ^ 0x80808080u);
+      uint4* zb = reinterpret_cast<uint4*>(Z + (size_t)(3 * t + 1) * NCB * 16);
+      zb[c] = xh;
+      zb[NCB + c] = xl;
+      zb[2 * NCB + c] = make_uint4(0, 0, 0, 0);
+      int sx = 0;
+      const unsigned w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      #pragma unroll
+      for (int k = 0; k < 8; ++k) sx += (int)(int16_t)(w[k] & 0xFFFF) + (int)(int16_t)(w[k] >> 16);
+      xe_s[i] = (int)ev[u];
+      cx_s[i] = 128 * sx;
+    }
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");     // B written by threads, read by the MMA
+  tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tptr;
-  // ---- this thread: row (lane quarter) and its CPT columns
-  const int q = warp & 3, half = warp >> 2;
-  const int row = q * 32 + lane, R = blk * TC_M + row;
-  const int cb = half * CPT;
-  // max exponent per (row, column) over all tiles (:221-222)
-  int Mx[CPT];
-  #pragma unroll
-  for (int j = 0; j < CPT; ++j) Mx[j] = -100000;
-  {
-    const int g = R / 16, ri = R % 16;
-    for (int t = 0; t < NT; ++t) {
-      const int we = (R < a.rows) ? (int)a.we[((size_t)g * NT + t) * 16 + ri] : 0;
-      #pragma unroll
-      for (int j = 0; j < CPT; ++j) {
-        const int e = we + (int)xe_s[t * NCB + cb + j];
-        Mx[j] = e > Mx[j] ? e : Mx[j];
+  const uint32_t idesc = idesc_i8(TC_M, N);
+
+  if (warp == 0) {
+    // ---- producer: refill a ring stage once its MMA and epilogue reads are done
+    if (lane == 0) {
+      for (int t = TC_SA; t < NT; ++t) {
+        const int s = t % TC_SA;
+        mb_wait(&rempty[s], (unsigned)(((t / TC_SA) - 1) & 1), a.err);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&rfull[s])), "r"(TC_REC) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     :: "r"(su32(ring + (size_t)s * TC_REC)), "l"(rec + (size_t)t * TC_REC), "r"(TC_REC),
+                        "r"(su32(&rfull[s])) : "memory");
       }
     }
-  }
-  long long acc[CPT];
-  #pragma unroll
-  for (int j = 0; j < CPT; ++j) acc[j] = 0;
-  const uint32_t idesc = idesc_i8(TC_M, N);
-  bool ok = true;
-  // MMA of tile 0
-  if (tid == 0) {
-    ok = mb_wait(&full[0], 0, a.err);
-    tc_fence_after();
-    tc_mma(tbase, smem_desc(ring, 2048, 128), smem_desc(Z, NCB * 16, 128), idesc);
-    tc_commit(&dfull[0]);
-  }
-  for (int t = 0; t < NT; ++t) {
-    const int b = t & 1, s = t % TC_SA;
-    // issue tile t+1 into the other D buffer (its previous reader, tile t-1,
-    // finished before the barrier that ended the last iteration)
-    if (tid == 0 && t + 1 < NT) {
-      const int s1 = (t + 1) % TC_SA;
-      ok = mb_wait(&full[s1], (unsigned)(((t + 1) / TC_SA) & 1), a.err) && ok;
-      tc_fence_after();
-      tc_mma(tbase + (uint32_t)((b ^ 1) * 128), smem_desc(ring + (size_t)s1 * TC_REC, 2048, 128),
-             smem_desc(Z + (size_t)3 * (t + 1) * NCB * 16, NCB * 16, 128), idesc);
-      tc_commit(&dfull[b ^ 1]);
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      for (int t = 0; t < NT; ++t) {
+        const int s = t % TC_SA, b = t % TC_NB;
+        mb_wait(&rfull[s], (unsigned)((t / TC_SA) & 1), a.err);
+        if (t >= TC_NB) mb_wait(&dempty[b], (unsigned)(((t / TC_NB) - 1) & 1), a.err);
+        tc_fence_after();
+        tc_mma(tbase + (uint32_t)(b * 128), smem_desc(ring + (size_t)s * TC_REC, 2048, 128),
+               smem_desc(Z + (size_t)3 * t * NCB * 16, NCB * 16, 128), idesc);
+        tc_commit(&dfull[b]);
+        tc_commit(&rempty[s]);
+      }
     }
-    // tile t: wait for its MMA, read the three limb sums
-    if (!mb_wait(&dfull[b], (unsigned)((t >> 1) & 1), a.err)) ok = false;
-    tc_fence_after();
-    uint32_t hh[CPT], cr[CPT], ll[CPT];
-    const uint32_t tq = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 128 + cb);
-    tmem_ld<CPT>(tq, hh);
-    tmem_ld<CPT>(tq + NCB, cr);
-    tmem_ld<CPT>(tq + 2 * NCB, ll);
-    tmem_wait_ld();
-    if (!mb_wait(&full[s], (unsigned)((t / TC_SA) & 1), a.err)) ok = false;   // complete already: orders the reads
-    const unsigned char* rs = ring + (size_t)s * TC_REC;
-    const int cw = reinterpret_cast<const int*>(rs + 4096)[row];
-    const int wer = reinterpret_cast<const int8_t*>(rs + 4608)[row];
-    // per-tile floor shift and int64 accumulation (:223-228)
+  } else {
+    // ---- epilogue warps
+    const int q = warp & 3, quarter = (warp - 2) >> 2;
+    const int row = q * 32 + lane, R = blk * TC_M + row;
+    const int cb = quarter * CPT;
+    // max exponent per (row, column) over all tiles (:221-222); the row's tile
+    // exponents come from the block's exponent table, 16 at a time
+    int Mx[CPT];
+    #pragma unroll
+    for (int j = 0; j < CPT; ++j) Mx[j] = -100000;
+    {
+      const int NTP = tc_ntp(NT);
+      const uint4* wrow = reinterpret_cast<const uint4*>(rec + (size_t)NT * TC_REC + (size_t)row * NTP);
+      for (int t0 = 0; t0 < NT; t0 += 16) {
+        const uint4 w16 = wrow[t0 / 16];
+        const unsigned ww[4] = {w16.x, w16.y, w16.z, w16.w};
+        #pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int t = t0 + k;
+          if (t < NT) {
+            const int we = (int)(int8_t)(ww[k >> 2] >> (8 * (k & 3)));
+            #pragma unroll
+            for (int j = 0; j < CPT; j += 4) {
+              const int4 e4 = *reinterpret_cast<const int4*>(xe_s + t * NCB + cb + j);
+              const int ev4[4] = {e4.x, e4.y, e4.z, e4.w};
+              #pragma unroll
+              for (int q2 = 0; q2 < 4; ++q2) {
+                const int e = we + ev4[q2];
+                Mx[j + q2] = e > Mx[j + q2] ? e : Mx[j + q2];
+              }
+            }
+          }
+        }
+      }
+    }
+    long long acc[CPT];
+    #pragma unroll
+    for (int j = 0; j < CPT; ++j) acc[j] = 0;
+    for (int t = 0; t < NT; ++t) {
+      const int s = t % TC_SA, b = t % TC_NB;
+      // the three limb sums of tile t
+      mb_wait(&dfull[b], (unsigned)((t / TC_NB) & 1), a.err);
+      tc_fence_after();
+      uint32_t hh[CPT], cr[CPT], ll[CPT];
+      const uint32_t tq = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 128 + cb);
+      tmem_ld<CPT>(tq, hh);
+      tmem_ld<CPT>(tq + NCB, cr);
+      tmem_ld<CPT>(tq + 2 * NCB, ll);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(su32(&dempty[b])) : "memory");
+      // the row's correction and exponent of tile t (complete: orders the reads)
+      mb_wait(&rfull[s], (unsigned)((t / TC_SA) & 1), a.err);
+      const unsigned char* rs = ring + (size_t)s * TC_REC;
+      const int cw = reinterpret_cast<const int*>(rs + 4096)[row];
+      const int wer = reinterpret_cast<const int8_t*>(rs + 4608)[row];
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(su32(&rempty[s])) : "memory");
+      // per-tile floor shift and int64 accumulation (:223-228).  S = 65536 hh +
+      // 256 cr + lo is formed as ((256 hh + cr) * 256 + lo): 256 hh + cr fits int32.
+      #pragma unroll
+      for (int j = 0; j < CPT; j += 4) {
+        const int4 e4 = *reinterpret_cast<const int4*>(xe_s + t * NCB + cb + j);
+        const int4 x4 = *reinterpret_cast<const int4*>(cx_s + t * NCB + cb + j);
+        const int ev4[4] = {e4.x, e4.y, e4.z, e4.w}, cv4[4] = {x4.x, x4.y, x4.z, x4.w};
+        #pragma unroll
+        for (int q2 = 0; q2 < 4; ++q2) {
+          const int jj = j + q2;
+          const int sh = Mx[jj] - wer - ev4[q2];
+          const int lo = (int)ll[jj] + cw + cv4[q2];
+          const int u = (int)hh[jj] * 256 + (int)cr[jj];
+          const long long S = (long long)u * 256 + (long long)lo;
+          if (sh <= ALIGN_MAX) acc[jj] += S >> sh;
+        }
+      }
+    }
+    // ---- epilogue: clip, scale (:229-232), quantize over 16-row output tiles (:233)
+    const bool row_ok = R < a.rows;
     #pragma unroll
     for (int j = 0; j < CPT; ++j) {
-      const int c = cb + j;
-      const int sh = Mx[j] - wer - (int)xe_s[t * NCB + c];
-      const int lo = (int)ll[j] + cw + cx_s[t * NCB + c];
-      const long long S = ((long long)(int)hh[j] << 16) + ((long long)(int)cr[j] << 8) + (long long)lo;
-      acc[j] += (sh > ALIGN_MAX) ? 0LL : (S >> sh);
-    }
-    tc_fence_before();
-    __syncthreads();
-    // record stage s is free (MMA t done, every thread past its cw / we reads)
-    if (tid == 0 && t + TC_SA < NT) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&full[s])), "r"(TC_REC) : "memory");
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                   :: "r"(su32(ring + (size_t)s * TC_REC)), "l"(rec + (size_t)(t + TC_SA) * TC_REC), "r"(TC_REC),
-                      "r"(su32(&full[s])) : "memory");
-    }
-  }
-  // ---- epilogue: clip, scale (:229-232), quantize over 16-row output tiles (:233)
-  const bool row_ok = R < a.rows;
-  #pragma unroll
-  for (int j = 0; j < CPT; ++j) {
-    const int col = c0 + cb + j;
-    const bool valid = row_ok && col < a.ncols;
-    long long sacc = acc[j];
-    sacc = sacc > SAT_HI ? SAT_HI : (sacc < SAT_LO ? SAT_LO : sacc);
-    const double out_real = (double)sacc * pow2(Mx[j] - 30);
-    int qe;
-    int16_t qm = tile_quantize_16lanes(out_real, &qe);
-    const int cc = col < a.ncols ? col : 0;
-    if constexpr (MODE == EPI_STORE) {
-      if (valid) {
-        a.om[(size_t)cc * a.o_ld + R] = qm;
-        if ((R & 15) == 0) a.oe[(size_t)cc * a.o_lde + R / 16] = (int8_t)qe;
-      }
-    } else if constexpr (MODE == EPI_RESIDUAL) {
-      const double hv = valid ? bfp_decode(a.rm[(size_t)cc * a.o_ld + R], a.re[(size_t)cc * a.o_lde + R / 16]) : 0.0;
-      qm = tile_quantize_16lanes(__dadd_rn(hv, bfp_decode(qm, qe)), &qe);          // fpq(h + o)
-      if (valid) {
-        a.om[(size_t)cc * a.o_ld + R] = qm;
-        if ((R & 15) == 0) a.oe[(size_t)cc * a.o_lde + R / 16] = (int8_t)qe;
-      }
-    } else {   // EPI_SWIGLU: lanes 0-15 hold a gate group, lanes 16-31 its up group
-      // every lane runs the warp-wide quantizers; only the gate lanes' results are kept
-      const double mine = bfp_decode(qm, qe);
-      const double other = __shfl_xor_sync(0xffffffffu, mine, 16);
-      const bool is_g = (lane & 16) == 0;
-      const double sv = __ddiv_rn(mine, __dadd_rn(1.0, exp(-mine)));                  // silu_fp (:241-242)
-      int se;
-      const int16_t sm = tile_quantize_16lanes(sv, &se);
-      const double prod = is_g ? __dmul_rn(bfp_decode(sm, se), other) : 0.0;           // (:290)
-      int pe;
-      int16_t pm = tile_quantize_16lanes(prod, &pe);
-      const unsigned bal = __ballot_sync(0xffffffffu, is_g && valid && pm == (int16_t)-32768);
-      const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
-      pm = requant_mant(pm, has_min && pe < 127);                                     // (:291)
-      pe = requant_exp(pe, has_min);
-      const int ug = R / 32;                                                           // mlp group of the pair
-      if (is_g && valid) {
-        a.om[(size_t)cc * a.o_ld + ug * 16 + (lane & 15)] = pm;
-        if ((lane & 15) == 0) a.oe[(size_t)cc * a.o_lde + ug] = (int8_t)pe;
+      const int col = c0 + cb + j;
+      const bool valid = row_ok && col < a.ncols;
+      long long sacc = acc[j];
+      sacc = sacc > SAT_HI ? SAT_HI : (sacc < SAT_LO ? SAT_LO : sacc);
+      const double out_real = (double)sacc * pow2(Mx[j] - 30);
+      int qe;
+      int16_t qm = tile_quantize_16lanes(out_real, &qe);
+      const int cc = col < a.ncols ? col : 0;
+      if constexpr (MODE == EPI_STORE) {
+        if (valid) {
+          a.om[(size_t)cc * a.o_ld + R] = qm;
+          if ((R & 15) == 0) a.oe[(size_t)cc * a.o_lde + R / 16] = (int8_t)qe;
+        }
+      } else if constexpr (MODE == EPI_RESIDUAL) {
+        const double hv = valid ? bfp_decode(a.rm[(size_t)cc * a.o_ld + R], a.re[(size_t)cc * a.o_lde + R / 16]) : 0.0;
+        qm = tile_quantize_16lanes(__dadd_rn(hv, bfp_decode(qm, qe)), &qe);          // fpq(h + o)
+        if (valid) {
+          a.om[(size_t)cc * a.o_ld + R] = qm;
+          if ((R & 15) == 0) a.oe[(size_t)cc * a.o_lde + R / 16] = (int8_t)qe;
+        }
+      } else {   // EPI_SWIGLU: lanes 0-15 hold a gate group, lanes 16-31 its up group
+        // every lane runs the warp-wide quantizers; only the gate lanes' results are kept
+        const double mine = bfp_decode(qm, qe);
+        const double other = __shfl_xor_sync(0xffffffffu, mine, 16);
+        const bool is_g = (lane & 16) == 0;
+        const double sv = __ddiv_rn(mine, __dadd_rn(1.0, exp(-mine)));                  // silu_fp (:241-242)
+        int se;
+        const int16_t sm = tile_quantize_16lanes(sv, &se);
+        const double prod = is_g ? __dmul_rn(bfp_decode(sm, se), other) : 0.0;           // (:290)
+        int pe;
+        int16_t pm = tile_quantize_16lanes(prod, &pe);
+        const unsigned bal = __ballot_sync(0xffffffffu, is_g && valid && pm == (int16_t)-32768);
+        const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
+        pm = requant_mant(pm, has_min && pe < 127);                                     // (:291)
+        pe = requant_exp(pe, has_min);
+        const int ug = R / 32;                                                           // mlp group of the pair
+        if (is_g && valid) {
+          a.om[(size_t)cc * a.o_ld + ug * 16 + (lane & 15)] = pm;
+          if ((lane & 15) == 0) a.oe[(size_t)cc * a.o_lde + ug] = (int8_t)pe;
+        }
       }
     }
   }
-  // ---- release tensor memory (all reads completed above)
+  // ---- release tensor memory (every MMA waited for, every load completed)
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" :: "r"(tbase) : "memory");
   }
-  (void)ok;
 }
 
 template <int NCB, int MODE>
@@ -387,7 +443,7 @@ cudaError_t launch_tc_t(const TcArgs& a, cudaStream_t s, bool pdl) {
 
 }  // namespace
 
-size_t tc_records_bytes(int rows, int NT) { return (size_t)((rows + TC_M - 1) / TC_M) * NT * TC_REC; }
+size_t tc_records_bytes(int rows, int NT) { return (size_t)((rows + TC_M - 1) / TC_M) * tc_block_bytes(NT); }
 
 cudaError_t launch_tc_pack(const uint8_t* wm, const int8_t* we, int rows, int NT, uint8_t* rec, cudaStream_t s) {
   dim3 grid((rows + TC_M - 1) / TC_M, NT);
