@@ -169,7 +169,9 @@ def run_ours(args, world, rank, local):
     prompts2, ngen2 = synth.config_prompts(2)
     ngen2 = args.n_gen
     prompts3, ngen3 = synth.config_prompts(3)
-    lo, hi = rank * len(prompts3) // world, (rank + 1) * len(prompts3) // world
+    # contiguous blocks balanced by total steps (bfp200.dist), one per rank
+    from bfp200 import dist as bd
+    lo, hi = bd.partition_sequences([len(p) for p in prompts3], ngen3, world)[rank]
     part3 = prompts3[lo:hi]
 
     # ---- cfg2 (bs1): device time of each generate (events on the library's stream)
@@ -251,7 +253,7 @@ def run_ours(args, world, rank, local):
         "roofline": roof,
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 48 * 4 + 4,
                 "d2h_bytes_per_step": (48 + ngen2) * 4 + 8},
-        "gpu_launches": launches,
+        "gpu_launches": int(sum_over_ranks(launches, world)),
         "bs256": bs256,
         "kernel_profile_ms": profile,
         "uncertified_steps": uncert,

@@ -14,6 +14,8 @@ pack     quantize_W (GPU), byte-exact DDR3 image packing
 synth    seeded synthetic model + benchmark prompts
 ops      op-level GPU functions (tile_quantize, matvec, rmsnorm_fp, ...)
 engine   Decoder (one GPU) and generate_multi (sequence-parallel, no collectives)
+dist     one process per GPU: step-balanced sequence partition, token gather,
+         sharded-head argmax exchange (torch.distributed)
 sim      drop-in facade with the reference module's names
 """
 from ._lib import BfpError

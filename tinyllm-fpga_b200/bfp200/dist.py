@@ -1,0 +1,106 @@
+"""Multi-process (one process per GPU) decode over torch.distributed.
+
+Independent sequences shard naturally: every rank holds a full replica of
+the image and decodes a contiguous block of the sequences, with no
+collective on the data path.  Blocks are balanced by total steps (prompt
+length + n_gen), the rule bfp200_generate_multi uses inside one process.
+The ranks meet only to gather the token streams at the end.
+
+For single-stream latency the head can be split by vocabulary rows across
+ranks; each rank reduces its rows to (max logit, lowest index, runner-up)
+and the ranks combine those with one all-gather of 24 bytes per rank
+(`combine_argmax`).  The combination keeps the lowest index on ties, so the
+result is the argmax of the whole vocabulary (np.argmax semantics,
+gen_smollm_blockfp_full.py:439-440).
+"""
+from __future__ import annotations
+
+import bisect
+
+import numpy as np
+
+
+def partition_sequences(prompt_lens, n_gen, world):
+    """Contiguous blocks [lo, hi) of the sequences for `world` ranks,
+    balanced by total steps (prompt length + n_gen)."""
+    n = len(prompt_lens)
+    cum = [0]
+    for L in prompt_lens:
+        cum.append(cum[-1] + int(L) + int(n_gen))
+    bounds = [0]
+    for d in range(1, world):
+        target = cum[n] * d // world
+        b = bisect.bisect_left(cum, target)
+        bounds.append(max(b, bounds[-1]))
+    bounds.append(n)
+    return [(bounds[r], bounds[r + 1]) for r in range(world)]
+
+
+def _gather_objects(obj, world, group=None):
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, obj, group=group)
+    return out
+
+
+def generate_distributed(decoder, prompts, n_gen, feed_mode="sim", group=None):
+    """Decodes this rank's block of `prompts` on its decoder and returns the
+    token streams of all sequences (on every rank), in input order.
+
+    `decoder` is anything with generate(prompts, n_gen, feed_mode) -> list
+    of token lists (a bfp200.Decoder on the rank's GPU)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    blocks = partition_sequences([len(p) for p in prompts], n_gen, world)
+    lo, hi = blocks[rank]
+    mine = decoder.generate(prompts[lo:hi], n_gen, feed_mode=feed_mode) if hi > lo else []
+    parts = _gather_objects((lo, hi, mine), world, group)
+    out = [None] * len(prompts)
+    for lo_r, hi_r, toks in parts:
+        out[lo_r:hi_r] = toks
+    return out
+
+
+def _better(v, i, bv, bi):
+    """(v, i) beats (bv, bi): larger logit, or equal logit with a lower index."""
+    return v > bv or (v == bv and i < bi)
+
+
+def reduce_argmax(parts):
+    """Combines (best value, best index, runner-up value) triples of disjoint
+    vocabulary shards into the global triple (lowest index on ties)."""
+    best, bidx, sec = -np.inf, np.iinfo(np.int64).max, -np.inf
+    for v, i, s in parts:
+        v, i, s = float(v), int(i), float(s)
+        if _better(v, i, best, bidx):
+            sec = max(sec, best)
+            best, bidx = v, i
+        else:
+            sec = max(sec, v)
+        sec = max(sec, s)
+    return best, bidx, sec
+
+
+def combine_argmax(value, index, second, group=None):
+    """All-gathers every rank's shard triple (24 bytes) and returns the
+    global (value, index, runner-up) on every rank.  Works on the nccl
+    backend (CUDA tensors) and on gloo (CPU)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) \
+        if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    mine = torch.tensor([float(value), float(index), float(second)], dtype=torch.float64, device=dev)
+    allv = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allv, mine, group=group)
+    parts = [(t[0].item(), int(t[1].item()), t[2].item()) for t in allv]
+    return reduce_argmax(parts)
+
+
+def shard_rows(vocab, world, rank):
+    """Contiguous vocabulary rows [lo, hi) of `rank` for the sharded head."""
+    return rank * vocab // world, (rank + 1) * vocab // world
+
+
+__all__ = ["partition_sequences", "generate_distributed", "reduce_argmax", "combine_argmax", "shard_rows"]
