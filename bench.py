@@ -165,7 +165,6 @@ def run_ours(args, world, rank, local):
     build_s = time.time() - t0
     dec = Decoder(cfg2, device=local)
     dec.load_image(img)
-    del img
     prompts2, ngen2 = synth.config_prompts(2)
     ngen2 = args.n_gen
     prompts3, ngen3 = synth.config_prompts(3)
@@ -207,7 +206,8 @@ def run_ours(args, world, rank, local):
     # for one token's 120 launches (4 per layer) is measured with events on
     # the library stream by replaying the decode-step matmuls.
     wbytes, hbytes = weight_bytes_per_token(cfg2)
-    mm = matmul_timing(dec, ncols=1, reps=args.mm_reps)
+    mm_ms, mm_n = dec.time_matmuls(1, args.mm_reps)
+    mm = {"ms_per_token": mm_ms, "launches": mm_n}
     achieved_gbs = wbytes / (mm["ms_per_token"] / 1e3) / 1e9
     peak = pk["hbm_gbs"]
     roof = {"kernel": "gemv_kernel (fused QKV / O / gate-up / down matvecs, bs1)", "bound": "hbm", "achieved": round(achieved_gbs, 1),
@@ -235,10 +235,25 @@ def run_ours(args, world, rank, local):
         bs256 = {"value": round(len(prompts3) * ngen3 / (b_step / 1e3), 1), "unit": "tok/s",
                  "ms_per_step": round(b_step, 3), "sequences": len(prompts3), "n_gen": ngen3,
                  "scaling": "strong", "uncertified_steps": dec.uncertified_steps()}
+        if part3:
+            bs256["roofline"] = batched_roofline(dec, len(part3), max(1, args.mm_reps // 5), pk, pk_kind)
 
     profile = {"bs1_pos176": dec.profile_forward(1, 176)}
-    if not args.no_bs256:
+    if not args.no_bs256 and part3:
         profile["bs256_pos100"] = dec.profile_forward(len(part3), 100)
+    sharded = None
+    if world > 1:
+        sharded = sharded_head_run(dec, prompts2, ngen2, args, world, decode_tok_ms)
+    dec.close()
+    cfg5 = None
+    if not args.no_cfg5:
+        # cfg5: leaf ops and attention at batch 64, KV length 2048 (serialised
+        # per-kernel times of one forward pass at position 2047)
+        d5 = Decoder(BfpConfig(MAX_CTX=2048, max_seqs=64), device=local)
+        d5.load_image(img)
+        cfg5 = {"batch": 64, "pos": 2047, "kernel_ms": d5.profile_forward(64, 2047)}
+        d5.close()
+    del img
     res = {
         "metric": "BFP decode tok/s (bs1, cfg2)", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
@@ -256,24 +271,54 @@ def run_ours(args, world, rank, local):
         "gpu_launches": int(sum_over_ranks(launches, world)),
         "bs256": bs256,
         "kernel_profile_ms": profile,
+        "cfg5": cfg5,
+        "sharded_head": sharded,
         "uncertified_steps": uncert,
         "image_build_s": round(build_s, 1),
         "clocks": clk.summary(),
     }
     if rank == 0 and not args.no_cpu:
         res["cpu_baseline"] = cpu_baseline(args)
-    dec.close()
     return res
 
 
-def matmul_timing(dec, ncols, reps):
-    import ctypes as C
-    from bfp200 import _lib
-    L = _lib.lib()
-    ms = C.c_double()
-    n = C.c_int()
-    _lib.check(L.bfp200_time_matmuls(dec.handle, ncols, reps, C.byref(ms), C.byref(n)))
-    return {"ms_per_token": ms.value, "launches": n.value}
+def sharded_head_run(dec, prompts, n_gen, args, world, replica_tok_ms):
+    """cfg5's single-stream mode: the cfg2 stream decoded by all ranks with
+    the head split by vocabulary rows and the argmax exchanged by NCCL inside
+    the library's decode graph.  Device time per generated token, max over
+    ranks, next to the unsharded (replica) time."""
+    from bfp200.dist import shard_head_distributed
+    shard_head_distributed(dec)
+    for _ in range(max(1, args.warmup // 2)):
+        dec.generate(prompts, n_gen)
+    ms = []
+    for _ in range(max(1, args.steps // 2)):
+        dec.generate(prompts, n_gen)
+        ms.append(dec.last_timing()["decode_ms"] / n_gen)
+    dec.shard_head(None, 1, 0)
+    tok_ms = max_over_ranks(statistics.mean(ms), world)
+    return {"ranks": world, "decode_us_per_token": round(tok_ms * 1e3, 2),
+            "replica_decode_us_per_token": round(replica_tok_ms * 1e3, 2),
+            "vocab_rows_per_rank": 49152 // world, "exchange": "NCCL all-gather of 32 B per rank per step"}
+
+
+LAYER_MACS = 106_168_320      # int16 MACs of one token's 4 x 30 layer matvecs (head excluded)
+
+
+def batched_roofline(dec, ncols, reps, pk, pk_kind):
+    """The batched matvecs of one decode step at this rank's column count:
+    tcgen05 kind::i8 (>= 64 columns) or the dp2a kernel.  Algorithmic work =
+    the int16 MACs, counted as 4 int8 limb MACs each (2 ops per MAC), against
+    the int8 dense peak taken as twice the measured bf16 GEMM rate (the
+    nominal int8 : bf16 ratio of B200)."""
+    ms, n = dec.time_matmuls(ncols, reps)
+    tops = LAYER_MACS * ncols * 4 * 2 / (ms / 1e3) / 1e12
+    peak = 2 * pk["bf16_tflops"]
+    return {"kernel": "tc_matmul_kernel (tcgen05 kind::i8 limbs)" if ncols >= 64 else "bfp_matmul_kernel (dp2a)",
+            "bound": "tensor", "achieved": round(tops, 2), "peak": round(peak, 1), "unit": "TOPS (int8)",
+            "frac": round(tops / peak, 5), "traffic": None, "peak_kind": f"2 x bf16 ({pk_kind})",
+            "ncols": ncols, "ms_per_step": round(ms, 4), "launches_per_step": n,
+            "int16_macs_per_s": round(LAYER_MACS * ncols / (ms / 1e3) / 1e12, 3)}
 
 
 def cpu_baseline(args):
@@ -367,6 +412,7 @@ def main():
     ap.add_argument("--no-bs256", action="store_true", help="skip the bs256 measurement (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--mm-reps", type=int, default=50, help="graph replays for the matmul roofline timing")
+    ap.add_argument("--no-cfg5", action="store_true", help="skip the batch-64 / KV-2048 kernel profile")
     args = ap.parse_args()
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))

@@ -96,6 +96,37 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
 int bfp200_generate_multi(bfp200_handle* const* hs, int n_dev, const int32_t* prompt_ids, const int32_t* prompt_lens,
                           int n_seq, int n_gen, int feed_mode, int32_t* out_tokens);
 
+/* Vocabulary-sharded head (single-stream latency over several GPUs).  Every
+ * rank runs all layers on the same sequences; rank r scans embedding rows
+ * [r V / n, (r+1) V / n) and the ranks exchange one (max logit, lowest index,
+ * runner-up, ||hn||) record per sequence with an NCCL all-gather on the
+ * handle's stream (captured in the decode graph), then every rank combines
+ * them into the argmax of the whole vocabulary (np.argmax semantics,
+ * gen_smollm_blockfp_full.py:439-440: lowest index on ties).  NCCL is loaded
+ * at run time (libnccl.so.2 already in the process, else $BFP200_NCCL_LIB,
+ * else the loader's search path); NVLS is left off unless NCCL_NVLS_ENABLE
+ * is set.  A sharded handle's generate must be called on every rank with the
+ * same arguments; its waits give up after $BFP200_NCCL_TIMEOUT_S seconds
+ * (default 120), abort the communicator and return BFP200_ETIMEOUT.
+ * Replaces: nothing in the reference (single FPGA, unsharded head :437-440). */
+#define BFP200_NCCL_ID_BYTES 128
+/* A fresh NCCL unique id (rank 0 makes it, every rank passes it to
+ * bfp200_head_shard). */
+int bfp200_nccl_unique_id(uint8_t* id);
+/* Joins rank `rank` of an `nranks`-rank vocabulary-sharded head (blocks until
+ * every rank has joined).  id == NULL with nranks == 1 leaves sharding; a
+ * one-rank group (id given, nranks == 1) runs the sharded head path over the
+ * whole vocabulary. */
+int bfp200_head_shard(bfp200_handle* h, const uint8_t* id, int nranks, int rank);
+/* One process, n_dev handles on distinct devices: shards the head over all
+ * of them (rank = position in hs). */
+int bfp200_head_shard_group(bfp200_handle* const* hs, int n_dev);
+/* Runs bfp200_generate on every handle of a sharded group concurrently (one
+ * host thread each) and returns rank 0's tokens after checking that every
+ * rank produced the same ones. */
+int bfp200_generate_sharded(bfp200_handle* const* hs, int n_dev, const int32_t* prompt_ids,
+                            const int32_t* prompt_lens, int n_seq, int n_gen, int feed_mode, int32_t* out_tokens);
+
 /* Number of head argmax decisions of the last generate call whose fp64
  * margin did not certify agreement with every summation order (0 means the
  * token stream is independent of the reference's BLAS). */

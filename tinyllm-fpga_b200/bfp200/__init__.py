@@ -13,13 +13,15 @@ image    DDR3 region map, .hex ROM files, cfg.svh, token files
 pack     quantize_W (GPU), byte-exact DDR3 image packing
 synth    seeded synthetic model + benchmark prompts
 ops      op-level GPU functions (tile_quantize, matvec, rmsnorm_fp, ...)
-engine   Decoder (one GPU) and generate_multi (sequence-parallel, no collectives)
+engine   Decoder (one GPU), generate_multi (sequence-parallel, no collectives),
+         shard_group / generate_sharded (vocabulary-sharded head, NCCL)
 dist     one process per GPU: step-balanced sequence partition, token gather,
          sharded-head argmax exchange (torch.distributed)
 sim      drop-in facade with the reference module's names
 """
 from ._lib import BfpError
 from .config import BfpConfig, SMOLLM2_135M
-from .engine import Decoder, generate_multi
+from .engine import Decoder, generate_multi, generate_sharded, nccl_unique_id, shard_group
 
-__all__ = ["BfpError", "BfpConfig", "SMOLLM2_135M", "Decoder", "generate_multi"]
+__all__ = ["BfpError", "BfpConfig", "SMOLLM2_135M", "Decoder", "generate_multi", "generate_sharded",
+           "nccl_unique_id", "shard_group"]

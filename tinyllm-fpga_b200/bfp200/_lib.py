@@ -62,7 +62,29 @@ SIGNATURES = {
     "bfp200_time_matmuls": [_P, _I, _I, C.POINTER(_D), C.POINTER(_I)],
     "bfp200_profile_forward": [_P, _I, _I, _P, _P],
     "bfp200_matvec_noalloc": [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P],
+    "bfp200_nccl_unique_id": [_P],
+    "bfp200_head_shard": [_P, _P, _I, _I],
+    "bfp200_head_shard_group": [_P, _I],
+    "bfp200_generate_sharded": [_P, _I, _P, _P, _I, _I, _I, _P],
 }
+NCCL_ID_BYTES = 128
+
+
+def _nccl_hint():
+    """Points the library's run-time NCCL loader at the NCCL that torch
+    ships (nvidia-nccl wheel) unless the caller chose one."""
+    if "BFP200_NCCL_LIB" in os.environ:
+        return
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return
+    for d in (spec.submodule_search_locations or []) if spec else []:
+        cand = os.path.join(d, "lib", "libnccl.so.2")
+        if os.path.exists(cand):
+            os.environ["BFP200_NCCL_LIB"] = cand
+            return
 
 _lib = None
 
@@ -73,6 +95,7 @@ def lib():
     if _lib is None:
         if not os.path.exists(LIB_PATH):
             raise BfpError(ENODEV, f"{LIB_PATH} not built (run bfp200.build.build())")
+        _nccl_hint()
         L = C.CDLL(LIB_PATH)
         for name, args in SIGNATURES.items():
             f = getattr(L, name)

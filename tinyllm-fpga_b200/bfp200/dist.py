@@ -99,8 +99,26 @@ def combine_argmax(value, index, second, group=None):
 
 
 def shard_rows(vocab, world, rank):
-    """Contiguous vocabulary rows [lo, hi) of `rank` for the sharded head."""
+    """Contiguous vocabulary rows [lo, hi) of `rank` for the sharded head
+    (the split libbfp200's sharded head uses)."""
     return rank * vocab // world, (rank + 1) * vocab // world
 
 
-__all__ = ["partition_sequences", "generate_distributed", "reduce_argmax", "combine_argmax", "shard_rows"]
+def shard_head_distributed(decoder, group=None):
+    """Joins this rank's decoder to a vocabulary-sharded head over the
+    process group: rank 0 makes the NCCL id, the group broadcasts it, every
+    rank joins the library's own communicator.  Afterwards every rank calls
+    decoder.generate() with the same prompts and gets the same tokens; the
+    argmax exchange runs inside the library's decode graph (one all-gather
+    of 32 bytes per sequence and rank per step)."""
+    import torch.distributed as dist
+    from .engine import nccl_unique_id
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    box = [nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    decoder.shard_head(box[0], world, rank)
+
+
+__all__ = ["partition_sequences", "generate_distributed", "reduce_argmax", "combine_argmax", "shard_rows",
+           "shard_head_distributed"]

@@ -116,6 +116,27 @@ class Decoder:
         check(_lib.lib().bfp200_profile_forward(self._h, int(ncols), int(pos), ptr(ms), ptr(n)))
         return {k: (round(float(a), 4), int(b)) for k, a, b in zip(self.PROFILE_KINDS, ms, n)}
 
+    def shard_head(self, uid, nranks, rank):
+        """Joins rank `rank` of an `nranks`-way vocabulary-sharded head
+        (every rank passes the same `uid` from nccl_unique_id(); blocks until
+        all ranks joined).  uid=None leaves sharding; a one-rank group runs
+        the sharded head path over the whole vocabulary.  Afterwards
+        generate() must be called on every rank with the same arguments."""
+        if uid is None:
+            check(_lib.lib().bfp200_head_shard(self._h, None, 1, 0))
+            return
+        buf = np.frombuffer(bytes(uid), np.uint8).copy()
+        assert buf.size == _lib.NCCL_ID_BYTES, "NCCL unique id must be 128 bytes"
+        check(_lib.lib().bfp200_head_shard(self._h, ptr(buf), int(nranks), int(rank)))
+
+    def time_matmuls(self, ncols, reps=20):
+        """Device time (ms) of one decode step's matvecs (4 per layer, all
+        layers) at ncols columns, replayed from a CUDA graph `reps` times
+        between events; returns (ms per step, launches per step)."""
+        ms, n = C.c_double(), C.c_int()
+        check(_lib.lib().bfp200_time_matmuls(self._h, int(ncols), int(reps), C.byref(ms), C.byref(n)))
+        return ms.value, n.value
+
     # -- one layer (fwd_layer, :261-293) ----------------------------------------
     def stage_dims(self):
         d = np.empty(_lib.NSTAGES, np.int32)
@@ -159,15 +180,16 @@ class Decoder:
         return res, per
 
 
-def generate_multi(decoders, prompts, n_gen, feed_mode="sim"):
-    """Sequences split into contiguous blocks over the decoders (one per GPU),
-    run concurrently, no collectives (bfp200_generate_multi)."""
-    hs = (C.c_void_p * len(decoders))(*[d.handle.value for d in decoders])
+def _handles(decoders):
+    return (C.c_void_p * len(decoders))(*[d.handle.value for d in decoders])
+
+
+def _run_many(fn, decoders, prompts, n_gen, feed_mode):
     lens = arr([len(p) for p in prompts], np.int32)
     ids = arr(np.concatenate([np.asarray(p, dtype=np.int64) for p in prompts]), np.int32)
     out = np.empty(int(lens.sum()) + len(prompts) * n_gen, np.int32)
-    check(_lib.lib().bfp200_generate_multi(C.cast(hs, C.c_void_p), len(decoders), ptr(ids), ptr(lens), len(prompts),
-                                           int(n_gen), FEED_MODES[feed_mode], ptr(out)))
+    check(fn(C.cast(_handles(decoders), C.c_void_p), len(decoders), ptr(ids), ptr(lens), len(prompts), int(n_gen),
+             FEED_MODES[feed_mode], ptr(out)))
     res, o = [], 0
     for L in lens:
         res.append(out[o:o + L + n_gen].tolist())
@@ -175,4 +197,30 @@ def generate_multi(decoders, prompts, n_gen, feed_mode="sim"):
     return res
 
 
-__all__ = ["Decoder", "generate_multi", "ROM_KINDS"]
+def generate_multi(decoders, prompts, n_gen, feed_mode="sim"):
+    """Sequences split into contiguous blocks over the decoders (one per GPU),
+    run concurrently, no collectives (bfp200_generate_multi)."""
+    return _run_many(_lib.lib().bfp200_generate_multi, decoders, prompts, n_gen, feed_mode)
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id for Decoder.shard_head (made by one rank)."""
+    buf = np.zeros(_lib.NCCL_ID_BYTES, np.uint8)
+    check(_lib.lib().bfp200_nccl_unique_id(ptr(buf)))
+    return buf.tobytes()
+
+
+def shard_group(decoders):
+    """Shards the head's vocabulary over decoders on distinct GPUs of this
+    process (rank = position in the list; one NCCL communicator)."""
+    check(_lib.lib().bfp200_head_shard_group(C.cast(_handles(decoders), C.c_void_p), len(decoders)))
+
+
+def generate_sharded(decoders, prompts, n_gen, feed_mode="sim"):
+    """Every decoder of a sharded group decodes all `prompts` (single-stream
+    latency: the layers run redundantly, the head is split by vocabulary
+    rows and the argmax exchanged by NCCL); returns the common tokens."""
+    return _run_many(_lib.lib().bfp200_generate_sharded, decoders, prompts, n_gen, feed_mode)
+
+
+__all__ = ["Decoder", "generate_multi", "generate_sharded", "shard_group", "nccl_unique_id", "ROM_KINDS"]

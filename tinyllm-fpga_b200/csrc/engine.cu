@@ -10,9 +10,14 @@
 #include "bfp_device.cuh"
 #include "kernels.cuh"
 
+#include <dlfcn.h>
+
 #include <algorithm>
+#include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <numeric>
 #include <string>
 #include <thread>
@@ -241,6 +246,62 @@ __global__ void scatter_tokens_kernel(const int* tok, const int* cert, const int
 
 int bfp200_set_error(int code, const std::string& msg) { return fail(code, msg); }
 
+// ---------------------------------------------------------------------------
+// NCCL, loaded at run time: only the vocabulary-sharded head uses it, so the
+// library itself does not depend on libnccl.  The types are NCCL's C ABI
+// (ncclUniqueId: 128 bytes by value; results and data types: C enums).
+// ---------------------------------------------------------------------------
+struct NcclUid { char internal[BFP200_NCCL_ID_BYTES]; };
+typedef struct ncclComm* NcclComm;
+constexpr int NCCL_OK = 0, NCCL_IN_PROGRESS = 7, NCCL_F64 = 8;
+
+struct NcclApi {
+  int (*get_unique_id)(NcclUid*) = nullptr;
+  int (*comm_init_rank)(NcclComm*, int, NcclUid, int) = nullptr;
+  int (*comm_init_all)(NcclComm*, int, const int*) = nullptr;
+  int (*all_gather)(const void*, void*, size_t, int, NcclComm, cudaStream_t) = nullptr;
+  int (*comm_destroy)(NcclComm) = nullptr;
+  int (*comm_abort)(NcclComm) = nullptr;
+  int (*async_error)(NcclComm, int*) = nullptr;
+  const char* (*error_string)(int) = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    // the copy already in the process (e.g. torch's), else $BFP200_NCCL_LIB,
+    // else whatever the loader finds
+    void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!lib)
+      if (const char* p = std::getenv("BFP200_NCCL_LIB")) lib = dlopen(p, RTLD_NOW | RTLD_GLOBAL);
+    if (!lib) lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!lib) return;
+    auto sym = [&](const char* n) { return dlsym(lib, n); };
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
+    api.comm_init_all = reinterpret_cast<decltype(api.comm_init_all)>(sym("ncclCommInitAll"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+    api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
+    api.async_error = reinterpret_cast<decltype(api.async_error)>(sym("ncclCommGetAsyncError"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_init_all && api.all_gather && api.comm_destroy &&
+             api.comm_abort && api.async_error && api.error_string;
+  });
+  return api;
+}
+
+std::string nccl_err(int r) {
+  const NcclApi& a = nccl();
+  return a.error_string ? std::string(a.error_string(r)) : "NCCL error " + std::to_string(r);
+}
+
+// small exchanges gain nothing from NVLink SHARP; keep the multicast objects
+// unbound unless the caller asked for them
+void nccl_env_defaults() { setenv("NCCL_NVLS_ENABLE", "0", /*overwrite=*/0); }
+
 struct bfp200_handle {
   bfp200_cfg cfg{};
   int device = 0;
@@ -288,6 +349,11 @@ struct bfp200_handle {
   DBuf<uint8_t> tc_rec[4];
   size_t tc_stride[4] = {0, 0, 0, 0};
   DBuf<unsigned> head_ctr;     // arrival counter of the single-launch head (left zeroed)
+  // vocabulary-sharded head: this rank scans rows [v_lo, v_hi) and exchanges
+  // one record per column with the other ranks (xsend -> xrecv, all-gather)
+  NcclComm comm = nullptr;
+  int shard_n = 1, shard_rank = 0, v_lo = 0, v_hi = 0;
+  DBuf<double> xsend, xrecv;
   cudaGraphExec_t graph = nullptr;
   int graph_cols = -1, graph_ngen = -1;
   long long uncert = 0;
@@ -299,7 +365,8 @@ struct bfp200_handle {
   std::vector<std::pair<int, cudaEvent_t>>* prof = nullptr;
 
   ~bfp200_handle() {
-    if (graph) cudaGraphExecDestroy(graph);
+    if (graph) cudaGraphExecDestroy(graph);       // before the communicator its NCCL node uses
+    if (comm) nccl().comm_destroy(comm);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -351,6 +418,7 @@ int ensure_cols(bfp200_handle* h, int ncols) {
   CK(h->tok.ensure(cap)); CK(h->cert.ensure(cap));
   CK(h->col_slot.ensure(cap)); CK(h->col_pos.ensure(cap)); CK(h->col_kvpos.ensure(cap)); CK(h->col_tok.ensure(cap));
   CK(h->head_ctr.ensure(1));
+  if (h->comm) { CK(h->xsend.ensure((size_t)cap * 4)); CK(h->xrecv.ensure((size_t)h->shard_n * cap * 4)); }
   h->cap = cap;
   if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; h->graph_cols = -1; }
   return BFP200_OK;
@@ -612,8 +680,39 @@ int enqueue_layer_small(bfp200_handle* h, int l, int ncols, bool first_pdl, bool
   return BFP200_OK;
 }
 
+// Vocabulary-sharded head: this rank's rows give one (best, index,
+// runner-up, ||hn||) record per column, the ranks all-gather the records and
+// every rank combines them into the token (lowest index on ties).
+int enqueue_head_sharded(bfp200_handle* h, int ncols) {
+  cudaStream_t s = h->stream;
+  const int NT = h->D / 16, nv = h->v_hi - h->v_lo;
+  const int16_t* em = h->emb_m.p + (size_t)h->v_lo * h->D;
+  const int8_t* ee = h->emb_e.p + (size_t)h->v_lo * NT;
+  mark(h, PK_HEAD_LOGITS);
+  if (h->use_small && head_small_supported(ncols, h->D)) {
+    CK(launch_head_small(h->h_m.p, h->h_e.p, h->nw.p, h->cfg.eps, em, ee, nv, h->D, ncols, h->emb_norm_max,
+                         h->part_val.p, h->part_idx.p, h->part_sec.p, h->head_ctr.p, h->tok.p, h->cert.p, s, h->pdl,
+                         h->v_lo, h->xsend.p));
+  } else {
+    CK(launch_head_prep(h->h_m.p, h->h_e.p, h->nw.p, h->cfg.eps, h->D, ncols, h->hn.p, h->hn_norm.p, s, h->pdl));
+    ++h->launch_count;
+    int nrb = 0;
+    CK(launch_head_logits(em, ee, nv, h->D, h->hn.p, ncols, h->part_val.p, h->part_idx.p, h->part_sec.p, &nrb, s,
+                          h->pdl));
+    ++h->launch_count;
+    CK(launch_head_reduce(h->part_val.p, h->part_idx.p, h->part_sec.p, nrb, h->hn_norm.p, h->emb_norm_max, h->D,
+                          ncols, h->tok.p, h->cert.p, s, h->pdl, h->v_lo, h->xsend.p));
+  }
+  const int r = nccl().all_gather(h->xsend.p, h->xrecv.p, (size_t)ncols * 4, NCCL_F64, h->comm, s);
+  if (r != NCCL_OK && r != NCCL_IN_PROGRESS) return fail(BFP200_ECUDA, "ncclAllGather: " + nccl_err(r));
+  mark(h, PK_HEAD_REDUCE);
+  CK(launch_head_combine(h->xrecv.p, h->shard_n, ncols, h->emb_norm_max, h->D, h->V, h->tok.p, h->cert.p, s));
+  return BFP200_OK;
+}
+
 int enqueue_head(bfp200_handle* h, int ncols) {
   cudaStream_t s = h->stream;
+  if (h->comm) return enqueue_head_sharded(h, ncols);
   if (h->use_small && head_small_supported(ncols, h->D)) {
     // one launch: hn, logits, certified argmax (last CTA); head_ctr is
     // allocated by ensure_cols, outside any stream capture
@@ -678,6 +777,54 @@ bool persist_ok(bfp200_handle* h, int ncols) {
   if (!h->use_persist || ncols < 1 || ncols > 4) return false;
   PersistArgs a = persist_args(h, ncols, 1);
   return a.err != nullptr && persistent_plan(a, h->nsm, h->smem_optin);
+}
+
+// Leaves any sharding (destroys the decode graph first: it holds the
+// communicator's all-gather) and joins `comm` as rank `rank` of `n`.
+int set_shard(bfp200_handle* h, NcclComm comm, int n, int rank) {
+  CK(cudaSetDevice(h->device));
+  cudaStreamSynchronize(h->stream);
+  if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; h->graph_cols = -1; }
+  if (h->comm) { nccl().comm_destroy(h->comm); h->comm = nullptr; }
+  h->comm = comm;
+  h->shard_n = comm ? n : 1;
+  h->shard_rank = comm ? rank : 0;
+  h->v_lo = (int)((long long)h->shard_rank * h->V / h->shard_n);
+  h->v_hi = (int)((long long)(h->shard_rank + 1) * h->V / h->shard_n);
+  if (comm && h->cap > 0) {
+    CK(h->xsend.ensure((size_t)h->cap * 4));
+    CK(h->xrecv.ensure((size_t)h->shard_n * h->cap * 4));
+  }
+  return BFP200_OK;
+}
+
+// Waits for the handle's stream.  With a sharded head the wait is bounded:
+// a rank that never joins the exchange (or an NCCL error) aborts the
+// communicator, which ends the waiting NCCL kernel, and the handle leaves
+// sharding.
+int sync_stream(bfp200_handle* h) {
+  if (!h->comm) { CK(cudaStreamSynchronize(h->stream)); return BFP200_OK; }
+  double limit_s = 120.0;
+  if (const char* e = std::getenv("BFP200_NCCL_TIMEOUT_S")) limit_s = std::max(0.1, std::atof(e));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(h->stream);
+    if (e == cudaSuccess) return BFP200_OK;
+    if (e != cudaErrorNotReady) return fail(BFP200_ECUDA, std::string("CUDA: ") + cudaGetErrorString(e));
+    int ae = NCCL_OK;
+    nccl().async_error(h->comm, &ae);
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if ((ae != NCCL_OK && ae != NCCL_IN_PROGRESS) || el > limit_s) {
+      nccl().comm_abort(h->comm);
+      h->comm = nullptr;
+      cudaStreamSynchronize(h->stream);
+      set_shard(h, nullptr, 1, 0);
+      return fail(BFP200_ETIMEOUT, ae != NCCL_OK && ae != NCCL_IN_PROGRESS
+                                       ? "sharded head: NCCL error " + nccl_err(ae)
+                                       : "sharded head: the exchange did not complete (a rank is missing)");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
 }
 
 int check_cfg(const bfp200_cfg& c) {
@@ -745,6 +892,7 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
   h->nsm = prop.multiProcessorCount;
   h->D = cfg->D; h->HQ = cfg->H_Q; h->HKV = cfg->H_KV; h->HD = cfg->HD; h->FFN = cfg->FFN; h->NL = cfg->NL;
   h->V = cfg->VOCAB; h->MAXC = cfg->MAX_CTX;
+  h->v_lo = 0; h->v_hi = h->V;
   h->NTD = h->D / 16; h->NTF = h->FFN / 16; h->KVD = h->HKV * h->HD; h->QD = h->HQ * h->HD;
   h->RQKV = h->QD + 2 * h->KVD;
   h->GQKV = h->RQKV / 16; h->GO = h->D / 16; h->GGU = 2 * h->FFN / 16; h->GD = h->D / 16;
@@ -990,14 +1138,14 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
                                                                      h->rtl_out.p, h->uncert_dev.p);
       ++h->launch_count;
     }
-    CK(cudaStreamSynchronize(h->stream));   // host column arrays are reused by the next chunk
+    CKR(sync_stream(h));   // host column arrays are reused by the next chunk
   }
   CK(cudaEventRecord(ev1, h->stream));
   std::vector<int32_t> rtl_host;
   if (rtl) {
     rtl_host.resize((size_t)n_seq * h->cfg.NPROMPT_MAX);
     CK(cudaMemcpyAsync(rtl_host.data(), h->rtl_out.p, rtl_host.size() * 4, cudaMemcpyDeviceToHost, h->stream));
-    CK(cudaStreamSynchronize(h->stream));
+    CKR(sync_stream(h));
   }
   // ---- decode: column s = sequence s at position len_s, fed its last token
   std::vector<int> dslot(n_seq), dpos(n_seq), dtok(n_seq);
@@ -1024,7 +1172,7 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
       // one decode step captured once as a CUDA graph, replayed n_gen times
       if (!h->graph || h->graph_cols != n_seq || h->graph_ngen != n_gen) {
         if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; }
-        CK(cudaStreamSynchronize(h->stream));
+        CKR(sync_stream(h));
         cudaGraph_t g;
         CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
         const long long before = h->launch_count;
@@ -1051,7 +1199,7 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
   if (n_gen > 0) CK(cudaMemcpyAsync(gen.data(), h->gen_out.p, gen.size() * 4, cudaMemcpyDeviceToHost, h->stream));
   long long unc = 0;
   CK(cudaMemcpyAsync(&unc, h->uncert_dev.p, 8, cudaMemcpyDeviceToHost, h->stream));
-  CK(cudaStreamSynchronize(h->stream));
+  CKR(sync_stream(h));
   float ms1 = 0, ms2 = 0;
   cudaEventElapsedTime(&ms1, ev0, ev1);
   cudaEventElapsedTime(&ms2, ev1, ev2);
@@ -1107,6 +1255,90 @@ int bfp200_generate_multi(bfp200_handle* const* hs, int n_dev, const int32_t* pr
   return BFP200_OK;
 }
 
+int bfp200_nccl_unique_id(uint8_t* id) {
+  if (!id) return fail(BFP200_EINVAL, "nccl_unique_id: null argument");
+  const NcclApi& a = nccl();
+  if (!a.ok) return fail(BFP200_ENODEV, "NCCL (libnccl.so.2) could not be loaded");
+  NcclUid u;
+  const int r = a.get_unique_id(&u);
+  if (r != NCCL_OK) return fail(BFP200_ECUDA, "ncclGetUniqueId: " + nccl_err(r));
+  std::memcpy(id, u.internal, BFP200_NCCL_ID_BYTES);
+  return BFP200_OK;
+}
+
+int bfp200_head_shard(bfp200_handle* h, const uint8_t* id, int nranks, int rank) {
+  if (!h || nranks < 1 || rank < 0 || rank >= nranks) return fail(BFP200_EINVAL, "head_shard: bad arguments");
+  if (!id) {
+    if (nranks == 1) return set_shard(h, nullptr, 1, 0);
+    return fail(BFP200_EINVAL, "head_shard: null id");
+  }
+  if (nranks > h->V) return fail(BFP200_EINVAL, "head_shard: more ranks than vocabulary rows");
+  const NcclApi& a = nccl();
+  if (!a.ok) return fail(BFP200_ENODEV, "NCCL (libnccl.so.2) could not be loaded");
+  CK(cudaSetDevice(h->device));
+  nccl_env_defaults();
+  NcclUid u;
+  std::memcpy(u.internal, id, BFP200_NCCL_ID_BYTES);
+  NcclComm c = nullptr;
+  const int r = a.comm_init_rank(&c, nranks, u, rank);
+  if (r != NCCL_OK) return fail(BFP200_ECUDA, "ncclCommInitRank: " + nccl_err(r));
+  return set_shard(h, c, nranks, rank);
+}
+
+int bfp200_head_shard_group(bfp200_handle* const* hs, int n_dev) {
+  if (!hs || n_dev < 1) return fail(BFP200_EINVAL, "head_shard_group: bad arguments");
+  std::vector<int> devs(n_dev);
+  for (int d = 0; d < n_dev; ++d) {
+    if (!hs[d]) return fail(BFP200_EINVAL, "head_shard_group: null handle");
+    devs[d] = hs[d]->device;
+    for (int e = 0; e < d; ++e)
+      if (devs[e] == devs[d]) return fail(BFP200_EINVAL, "head_shard_group: two handles on one device");
+  }
+  if (n_dev == 1) return set_shard(hs[0], nullptr, 1, 0);
+  const NcclApi& a = nccl();
+  if (!a.ok) return fail(BFP200_ENODEV, "NCCL (libnccl.so.2) could not be loaded");
+  for (int d = 0; d < n_dev; ++d) CKR(set_shard(hs[d], nullptr, 1, 0));
+  nccl_env_defaults();
+  std::vector<NcclComm> comms(n_dev, nullptr);
+  const int r = a.comm_init_all(comms.data(), n_dev, devs.data());
+  if (r != NCCL_OK) return fail(BFP200_ECUDA, "ncclCommInitAll: " + nccl_err(r));
+  for (int d = 0; d < n_dev; ++d) CKR(set_shard(hs[d], comms[d], n_dev, d));
+  return BFP200_OK;
+}
+
+int bfp200_generate_sharded(bfp200_handle* const* hs, int n_dev, const int32_t* prompt_ids,
+                            const int32_t* prompt_lens, int n_seq, int n_gen, int feed_mode, int32_t* out_tokens) {
+  if (!hs || n_dev < 1 || !out_tokens || n_gen < 0) return fail(BFP200_EINVAL, "generate_sharded: bad arguments");
+  for (int d = 0; d < n_dev; ++d) {
+    if (!hs[d]) return fail(BFP200_EINVAL, "generate_sharded: null handle");
+    if (n_dev > 1 && (!hs[d]->comm || hs[d]->shard_n != n_dev || hs[d]->shard_rank != d))
+      return fail(BFP200_ESTATE, "generate_sharded: handles are not one sharded group in rank order");
+  }
+  size_t n_out = 0;
+  if (prompt_ids) {
+    if (!prompt_lens || n_seq <= 0) return fail(BFP200_EINVAL, "generate_sharded: bad prompt arguments");
+    for (int i = 0; i < n_seq; ++i) n_out += (size_t)std::max(0, prompt_lens[i]) + n_gen;
+  } else {
+    n_out = hs[0]->rom_prompt.size() + n_gen;
+  }
+  std::vector<std::vector<int32_t>> outs(n_dev, std::vector<int32_t>(n_out, 0));
+  std::vector<int> rc(n_dev, BFP200_OK);
+  std::vector<std::string> errs(n_dev);
+  std::vector<std::thread> th;
+  for (int d = 0; d < n_dev; ++d)
+    th.emplace_back([&, d] {
+      rc[d] = bfp200_generate(hs[d], prompt_ids, prompt_lens, n_seq, n_gen, feed_mode, outs[d].data());
+      if (rc[d] != BFP200_OK) errs[d] = g_err;
+    });
+  for (auto& t : th) t.join();
+  for (int d = 0; d < n_dev; ++d)
+    if (rc[d] != BFP200_OK) return fail(rc[d], "rank " + std::to_string(d) + ": " + errs[d]);
+  for (int d = 1; d < n_dev; ++d)
+    if (outs[d] != outs[0]) return fail(BFP200_ESTATE, "generate_sharded: ranks disagree on the tokens");
+  std::copy(outs[0].begin(), outs[0].end(), out_tokens);
+  return BFP200_OK;
+}
+
 int bfp200_uncertified_steps(bfp200_handle* h, long long* count) {
   if (!h || !count) return fail(BFP200_EINVAL, "null argument");
   *count = h->uncert;
@@ -1130,6 +1362,7 @@ int bfp200_profile_forward(bfp200_handle* h, int ncols, int pos, double* ms_by_k
   if (!h || ncols <= 0 || !ms_by_kind) return fail(BFP200_EINVAL, "profile_forward: bad arguments");
   if (!h->have_image) return fail(BFP200_ESTATE, "profile_forward before load_image");
   if (ncols > h->cfg.max_seqs || pos < 0 || pos >= h->MAXC) return fail(BFP200_EINVAL, "profile_forward: ncols/pos");
+  if (h->comm) return fail(BFP200_ESTATE, "profile_forward: not on a handle with a sharded head");
   CK(cudaSetDevice(h->device));
   CKR(ensure_kv(h, ncols));
   CKR(ensure_cols(h, ncols));

@@ -837,6 +837,25 @@ cudaError_t launch_embed(const int16_t* emb_m, const int8_t* emb_e, const int* t
 // certificate that any summation order (the reference's BLAS) picks the
 // same index.
 // ---------------------------------------------------------------------------
+// Margin above which the fp64 argmax is the same for every summation order:
+// |fl(dot) - dot| <= gamma_D ||hn|| ||e_v|| (any order), so two orders differ
+// by at most twice that per logit, four times between two logits.
+__device__ __forceinline__ double head_margin(int D, double hn_norm, double emb_norm_max) {
+  const double u = 1.1102230246251565e-16;
+  const double gam = (D + 2) * u / (1.0 - (D + 2) * u);
+  return 4.0 * gam * hn_norm * emb_norm_max * (1.0 + 1e-6);
+}
+
+// One vocabulary shard's result for one column: index -1 when the shard had
+// no finite logit (every row NaN) or no rows.
+__device__ __forceinline__ void store_shard_triple(double* x, double best, int bi, int v_base, double sec,
+                                                   double hn_norm) {
+  x[0] = best;
+  x[1] = bi == 0x7fffffff ? -1.0 : (double)(bi + v_base);
+  x[2] = sec;
+  x[3] = hn_norm;
+}
+
 __global__ void __launch_bounds__(NORM_THREADS)
 head_prep_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, double eps, int D, int ncols, double* hn,
                  double* hn_norm) {
@@ -1072,7 +1091,8 @@ cudaError_t launch_head_logits(const int16_t* emb_m, const int8_t* emb_e, int VO
 }
 
 __global__ void head_reduce_kernel(const double* part_val, const int* part_idx, const double* part_second, int nrb,
-                                   const double* hn_norm, double emb_norm_max, int D, int* tok_out, int* cert_out) {
+                                   const double* hn_norm, double emb_norm_max, int D, int* tok_out, int* cert_out,
+                                   int v_base, double* xout) {
   pdl_trigger();
   pdl_wait();
   const int c = blockIdx.x;
@@ -1095,15 +1115,44 @@ __global__ void head_reduce_kernel(const double* part_val, const int* part_idx, 
     else sec = fmax(sec, ob);
     sec = fmax(sec, os);
   }
-  if (lane == 0) {
+  if (lane == 0 && xout) {
+    // vocabulary shard: (best, global index, runner-up, ||hn||) for the exchange
+    store_shard_triple(xout + 4 * c, best, bi, v_base, sec, hn_norm[c]);
+  } else if (lane == 0) {
     // |fl(dot) - dot| <= gamma_D * sum|a_i b_i| <= gamma_D * ||hn|| * ||e_v|| for
     // every summation order; two orders differ by at most twice that per logit.
-    const double u = 1.1102230246251565e-16;
-    const double gam = (D + 2) * u / (1.0 - (D + 2) * u);
-    const double margin = 4.0 * gam * hn_norm[c] * emb_norm_max * (1.0 + 1e-6);
     tok_out[c] = bi;
-    cert_out[c] = (best - sec) > margin ? 1 : 0;
+    cert_out[c] = (best - sec) > head_margin(D, hn_norm[c], emb_norm_max) ? 1 : 0;
   }
+}
+
+// Combines the vocabulary shards' (best, index, runner-up, ||hn||) records of
+// every column, gathered rank-major ([rank][column][4]), into the argmax of
+// the whole vocabulary (lowest index on ties) and its certificate.
+__global__ void head_combine_kernel(const double* g, int nranks, int ncols, double emb_norm_max, int D, int VOCAB,
+                                    int* tok_out, int* cert_out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= ncols) return;
+  double best = -INFINITY, sec = -INFINITY;
+  long long bi = 0x7fffffffffffLL;
+  for (int r = 0; r < nranks; ++r) {
+    const double* x = g + ((size_t)r * ncols + c) * 4;
+    const double v = x[0], s2 = x[2];
+    const long long xi = x[1] < 0.0 ? 0x7fffffffffffLL : (long long)x[1];
+    if (v > best || (v == best && xi < bi)) { sec = fmax(sec, best); best = v; bi = xi; }
+    else sec = fmax(sec, v);
+    sec = fmax(sec, s2);
+  }
+  const bool ok = bi >= 0 && bi < VOCAB;
+  tok_out[c] = ok ? (int)bi : 0;
+  cert_out[c] = (ok && (best - sec) > head_margin(D, g[(size_t)c * 4 + 3], emb_norm_max)) ? 1 : 0;
+}
+
+cudaError_t launch_head_combine(const double* gathered, int nranks, int ncols, double emb_norm_max, int D, int VOCAB,
+                                int* tok_out, int* cert_out, cudaStream_t s) {
+  head_combine_kernel<<<(ncols + 127) / 128, 128, 0, s>>>(gathered, nranks, ncols, emb_norm_max, D, VOCAB, tok_out,
+                                                           cert_out);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
@@ -1124,7 +1173,8 @@ template <int NC>
 __global__ void __launch_bounds__(256)
 head_small_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, double eps, const int16_t* emb_m,
                   const int8_t* emb_e, int VOCAB, int D, int ncols, double emb_norm_max, double* part_val,
-                  int* part_idx, double* part_second, unsigned* done_ctr, int* tok_out, int* cert_out) {
+                  int* part_idx, double* part_second, unsigned* done_ctr, int* tok_out, int* cert_out, int v_base,
+                  double* xout) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_lo[96], s_len[96];
   __shared__ double s_val[96];
@@ -1271,14 +1321,13 @@ head_small_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, dou
       else s2 = fmax(s2, ob);
       s2 = fmax(s2, os);
     }
-    if (lane == 0) {
-      // |fl(dot) - dot| <= gamma_D ||hn|| ||e_v|| for every summation order
-      const double u = 1.1102230246251565e-16;
-      const double gam = (D + 2) * u / (1.0 - (D + 2) * u);
-      const double margin = 4.0 * gam * (sqrt(ss) * (1.0 + 1e-12)) * emb_norm_max * (1.0 + 1e-6);
+    const double hnn = sqrt(ss) * (1.0 + 1e-12);
+    if (lane == 0 && xout) {
+      store_shard_triple(xout + 4 * c, b, bi, v_base, s2, hnn);     // vocabulary shard: for the exchange
+    } else if (lane == 0) {
       const bool ok = bi >= 0 && bi < VOCAB;              // no index: every logit was NaN
       tok_out[c] = ok ? bi : 0;
-      cert_out[c] = (ok && (b - s2) > margin) ? 1 : 0;
+      cert_out[c] = (ok && (b - s2) > head_margin(D, hnn, emb_norm_max)) ? 1 : 0;
     }
   }
   if (tid == 0) *done_ctr = 0u;                          // ready for the next launch
@@ -1294,7 +1343,8 @@ size_t head_small_smem(int ncols, int D) {
 cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
                               const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, int ncols,
                               double emb_norm_max, double* part_val, int* part_idx, double* part_second,
-                              unsigned* done_ctr, int* tok_out, int* cert_out, cudaStream_t s, bool pdl) {
+                              unsigned* done_ctr, int* tok_out, int* cert_out, cudaStream_t s, bool pdl,
+                              int v_base, double* xout) {
   if (!head_small_supported(ncols, D)) return cudaErrorInvalidValue;
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
@@ -1302,16 +1352,18 @@ cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double*
   const size_t smem = head_small_smem(ncols, D);
   if (ncols <= 1)
     return launch_ex(head_small_kernel<1>, dim3(nsm), dim3(256), smem, s, pdl, hm, he, norm_w, eps, emb_m, emb_e,
-                     VOCAB, D, ncols, emb_norm_max, part_val, part_idx, part_second, done_ctr, tok_out, cert_out);
+                     VOCAB, D, ncols, emb_norm_max, part_val, part_idx, part_second, done_ctr, tok_out, cert_out,
+                     v_base, xout);
   return launch_ex(head_small_kernel<4>, dim3(nsm), dim3(256), smem, s, pdl, hm, he, norm_w, eps, emb_m, emb_e,
-                   VOCAB, D, ncols, emb_norm_max, part_val, part_idx, part_second, done_ctr, tok_out, cert_out);
+                   VOCAB, D, ncols, emb_norm_max, part_val, part_idx, part_second, done_ctr, tok_out, cert_out,
+                   v_base, xout);
 }
 
 cudaError_t launch_head_reduce(const double* part_val, const int* part_idx, const double* part_second,
                                int n_rowblocks, const double* hn_norm, double emb_norm_max, int D, int ncols,
-                               int* tok_out, int* cert_out, cudaStream_t s, bool pdl) {
+                               int* tok_out, int* cert_out, cudaStream_t s, bool pdl, int v_base, double* xout) {
   return launch_ex(head_reduce_kernel, dim3(ncols), dim3(32), 0, s, pdl, part_val, part_idx, part_second,
-                   n_rowblocks, hn_norm, emb_norm_max, D, tok_out, cert_out);
+                   n_rowblocks, hn_norm, emb_norm_max, D, tok_out, cert_out, v_base, xout);
 }
 
 // ---------------------------------------------------------------------------

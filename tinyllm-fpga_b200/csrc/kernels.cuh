@@ -201,7 +201,14 @@ cudaError_t launch_head_logits(const int16_t* emb_m, const int8_t* emb_e, int VO
 // error bound of any summation order).
 cudaError_t launch_head_reduce(const double* part_val, const int* part_idx, const double* part_second,
                                int n_rowblocks, const double* hn_norm, double emb_norm_max, int D,
-                               int ncols, int* tok_out, int* cert_out, cudaStream_t s, bool pdl);
+                               int ncols, int* tok_out, int* cert_out, cudaStream_t s, bool pdl,
+                               int v_base = 0, double* xout = nullptr);
+// Vocabulary sharding: with xout set, the head kernels write, per column,
+// (best, global index = local + v_base, runner-up, ||hn||) to xout[4 c ..]
+// instead of the token; head_combine reduces the records of all shards
+// (rank-major [rank][column][4]) to the token and its certificate.
+cudaError_t launch_head_combine(const double* gathered, int nranks, int ncols, double emb_norm_max, int D,
+                                int VOCAB, int* tok_out, int* cert_out, cudaStream_t s);
 
 // Head of 1..4 columns in one launch: hn, fp64 logits, and (last CTA) the
 // certified argmax.  done_ctr: a zeroed word, left zeroed on return.
@@ -209,7 +216,8 @@ bool head_small_supported(int ncols, int D);
 cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
                               const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, int ncols,
                               double emb_norm_max, double* part_val, int* part_idx, double* part_second,
-                              unsigned* done_ctr, int* tok_out, int* cert_out, cudaStream_t s, bool pdl);
+                              unsigned* done_ctr, int* tok_out, int* cert_out, cudaStream_t s, bool pdl,
+                              int v_base = 0, double* xout = nullptr);
 
 // Standalone ops (the reference's module-level functions).
 cudaError_t launch_tile_quantize(const double* v, long long ntiles, int16_t* m, int8_t* e, cudaStream_t s);
