@@ -90,6 +90,19 @@ int bfp200_load_rom(bfp200_handle* h, int kind, const uint16_t* entries, size_t 
 int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq, int n_gen,
                     int feed_mode, int32_t* out_tokens);
 
+/* Replaces: the sampling head of the hardware emulator
+ * (sim_rtl_fp_hw.py:204-216: TEMP / TOPK / SEED): scaled = logits / T, the
+ * TOPK largest kept (TOPK 0 = all), p = softmax with numpy's pairwise sum,
+ * token = np.random.choice(p) (cdf = sequential cumsum, searchsorted of one
+ * random_sample).  Sequence s draws from np.random.seed(seed + s)'s stream
+ * (sequence 0 = the reference's SEED); like the reference, one draw is made
+ * and discarded at the last prompt position.  Feed rule "sim".  Among
+ * logits equal to the TOPK-th largest the lowest ids are kept.  temperature
+ * <= 0 is greedy decoding.  A draw whose u lies within the head's fp64
+ * error bound of a cdf step is counted by bfp200_uncertified_steps. */
+int bfp200_generate_sampled(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq,
+                            int n_gen, double temperature, int top_k, uint32_t seed, int32_t* out_tokens);
+
 /* Same as bfp200_generate, with the sequences split into contiguous blocks
  * over n_dev handles (one per GPU), run concurrently with no collectives.
  * Replaces: nothing in the reference (single FPGA, single stream). */

@@ -323,6 +323,46 @@ def head_logits(h, norm_w_q, embed, eps=1e-5):
     return h_normed @ embed.T
 
 
+def sample_token(logits, T, topk, rng):
+    """sim_rtl_fp_hw.py:206-216: temperature / top-k sampling of one token
+    with the legacy numpy generator `rng` (np.random.RandomState)."""
+    if not T > 0:
+        return int(np.argmax(logits))
+    scaled = logits / T
+    if topk > 0:
+        idx = np.argsort(scaled)[-topk:]
+        mask = np.full_like(scaled, -np.inf)
+        mask[idx] = scaled[idx]
+        scaled = mask
+    scaled -= scaled.max()
+    p = np.exp(scaled)
+    p = p / p.sum()
+    return int(rng.choice(len(p), p=p))
+
+
+def generate_sampled(model, ids, n_gen, T, topk, seed, max_ctx=None, cfg: Cfg = Cfg()):
+    """The sampling driver loop of sim_rtl_fp_hw.py:196-219 on this model:
+    np.random.seed(SEED) stream, a token drawn at every step >= len(ids)-1
+    (the first one discarded, as in the greedy loop :437-443), feed rule
+    'sim'.  Returns prompt + n_gen ids."""
+    rng = np.random.RandomState(seed)
+    ids = [int(t) for t in ids]
+    n_steps = len(ids) + n_gen
+    kv = new_kv(cfg, n_steps if max_ctx is None else max_ctx)
+    generated = list(ids)
+    for step in range(n_steps):
+        tid = ids[step] if step < len(ids) else generated[-1]
+        h = model.embed_q(tid)
+        cs = rope_cos_sin(step, cfg.HD, cfg.rope_base)
+        for li in range(cfg.NL):
+            h = fwd_layer(h, model.layers[li], pos=step, kv=kv[li], kv_pos=step, cfg=cfg, cs=cs)
+        if step >= len(ids) - 1:
+            nid = sample_token(head_logits(h, model.norm_w_q, model.embed, cfg.eps), T, topk, rng)
+            if step >= len(ids):
+                generated.append(nid)
+    return generated
+
+
 def generate(model, ids, n_gen, max_ctx=None, feed_mode="sim", cfg: Cfg = Cfg(), trace=None):
     """gen_smollm_blockfp_full.py:425-449 (feed_mode='sim', default) or the
     RTL feed rule of autoregress_bfp_top.sv:358-384 (feed_mode='rtl').

@@ -89,6 +89,22 @@ class Decoder:
             o += L + n_gen
         return res
 
+    def generate_sampled(self, prompts, n_gen, temperature, top_k=0, seed=1):
+        """Temperature / top-k sampling like the reference emulator
+        (sim_rtl_fp_hw.py:204-216, env TEMP / TOPK / SEED): sequence s uses
+        np.random.seed(seed + s)'s stream.  temperature <= 0 is greedy.
+        Returns prompt + n_gen ids per sequence."""
+        lens = arr([len(p) for p in prompts], np.int32)
+        ids = arr(np.concatenate([np.asarray(p, dtype=np.int64) for p in prompts]), np.int32)
+        out = np.empty(int(lens.sum()) + len(prompts) * n_gen, np.int32)
+        check(_lib.lib().bfp200_generate_sampled(self._h, ptr(ids), ptr(lens), len(prompts), int(n_gen),
+                                                 float(temperature), int(top_k), int(seed) & 0xFFFFFFFF, ptr(out)))
+        res, o = [], 0
+        for L in lens:
+            res.append(out[o:o + L + n_gen].tolist())
+            o += L + n_gen
+        return res
+
     def uncertified_steps(self) -> int:
         n = C.c_longlong()
         check(_lib.lib().bfp200_uncertified_steps(self._h, C.byref(n)))

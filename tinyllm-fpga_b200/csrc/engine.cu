@@ -14,6 +14,8 @@
 
 #include <algorithm>
 #include <chrono>
+#include <map>
+#include <tuple>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -349,13 +351,24 @@ struct bfp200_handle {
   DBuf<uint8_t> tc_rec[4];
   size_t tc_stride[4] = {0, 0, 0, 0};
   DBuf<unsigned> head_ctr;     // arrival counter of the single-launch head (left zeroed)
+  // tensor-core matmul configuration (columns per CTA, K split) per
+  // (rows, K tiles, columns, epilogue), chosen by timing the candidates
+  std::map<std::tuple<int, int, int, int>, std::pair<int, int>> tc_cfg;
   // vocabulary-sharded head: this rank scans rows [v_lo, v_hi) and exchanges
   // one record per column with the other ranks (xsend -> xrecv, all-gather)
   NcclComm comm = nullptr;
   int shard_n = 1, shard_rank = 0, v_lo = 0, v_hi = 0;
   DBuf<double> xsend, xrecv;
+  // sampling (bfp200_generate_sampled): full logits, scratch, uniforms, and
+  // numpy's pairwise-sum plan for the vocabulary length
+  DBuf<double> s_logits, s_work, s_cdf, s_uni;
+  DBuf<int> s_incl;
+  DBuf<unsigned short> v_plan;
+  int v_plan_leaves = 0;
   cudaGraphExec_t graph = nullptr;
   int graph_cols = -1, graph_ngen = -1;
+  double graph_temp = 0.0;        // sampling parameters the cached graph was captured with (0: greedy)
+  int graph_topk = 0;
   long long uncert = 0;
   double t_prefill = 0.0, t_decode = 0.0;
   long long launch_count = 0;       // kernel launches issued (mark); see bfp200_last_launches
@@ -471,6 +484,39 @@ bool tc_path(bfp200_handle* h, const DevMat& W, int ncols, int epi) {
   return h->use_tc && ncols >= 64 && tc_supported(W.NT, ncols) && !(epi == EPI_SWIGLU && W.G % 2);
 }
 
+// Times every valid (columns per CTA, K split) candidate of one matmul call
+// on its own arguments (the call only reads its inputs and writes its
+// outputs, so repeating it is harmless) and keeps the fastest.
+int tc_tune(bfp200_handle* h, TcArgs t, const std::tuple<int, int, int, int>& key) {
+  static const int KS[] = {1, 2, 3, 4, 6, 8};
+  cudaEvent_t e0, e1;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  float best = -1.f;
+  std::pair<int, int> pick{0, 0};
+  for (int ncb : {16, 32})
+    for (int ks : KS) {
+      if (!tc_config_valid(t.NT, ncb, ks)) continue;
+      t.ncb = ncb;
+      t.ks = ks;
+      if (launch_tc_matmul(t, h->stream, false) != cudaSuccess) { cudaGetLastError(); continue; }
+      cudaEventRecord(e0, h->stream);
+      bool ok = true;
+      for (int r = 0; r < 2 && ok; ++r) ok = launch_tc_matmul(t, h->stream, false) == cudaSuccess;
+      cudaEventRecord(e1, h->stream);
+      h->launch_count += 3;
+      if (!ok) { cudaGetLastError(); continue; }
+      if (cudaEventSynchronize(e1) != cudaSuccess) { cudaGetLastError(); continue; }
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, e0, e1);
+      if (best < 0.f || ms < best) { best = ms; pick = {ncb, ks}; }
+    }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  h->tc_cfg[key] = pick;                 // {0, 0}: the built-in choice
+  return BFP200_OK;
+}
+
 int enqueue_tc(bfp200_handle* h, const uint8_t* rec, DevMat W, const int16_t* xm, const int8_t* xe, int x_ld,
                int x_lde, int ncols, int epi, int16_t* om, int8_t* oe, int o_ld, int o_lde, const int16_t* rm,
                const int8_t* re) {
@@ -480,6 +526,17 @@ int enqueue_tc(bfp200_handle* h, const uint8_t* rec, DevMat W, const int16_t* xm
   t.mode = epi;
   t.om = om; t.oe = oe; t.o_ld = o_ld; t.o_lde = o_lde; t.rm = rm; t.re = re;
   t.err = error_flag_device_ptr();
+  const auto key = std::make_tuple(t.rows, t.NT, ncols, epi);
+  auto it = h->tc_cfg.find(key);
+  if (it == h->tc_cfg.end()) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(h->stream, &st);
+    if (st == cudaStreamCaptureStatusNone) {        // (inside a capture: the built-in choice)
+      CKR(tc_tune(h, t, key));
+      it = h->tc_cfg.find(key);
+    }
+  }
+  if (it != h->tc_cfg.end()) { t.ncb = it->second.first; t.ks = it->second.second; }
   CK(launch_tc_matmul(t, h->stream, h->pdl));
   return BFP200_OK;
 }
@@ -731,6 +788,53 @@ int enqueue_head(bfp200_handle* h, int ncols) {
   mark(h, PK_HEAD_REDUCE);
   CK(launch_head_reduce(h->part_val.p, h->part_idx.p, h->part_sec.p, nrb, h->hn_norm.p, h->emb_norm_max, h->D, ncols,
                         h->tok.p, h->cert.p, s, h->pdl));
+  return BFP200_OK;
+}
+
+// The four matmuls of layer l at ncols columns on the handle's scratch
+// activations (measurement, and choosing tensor-core configurations before
+// a graph capture): their outputs are overwritten by any later forward.
+int enqueue_layer_matmuls(bfp200_handle* h, int l, int ncols) {
+  long long* acc = h->acc.p;
+  unsigned* cnt = h->counters.p;
+  const int accld = h->cap;
+  CKR(enqueue_matmul(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
+                     EPI_STORE, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->RQKV / 16, nullptr, nullptr, acc, cnt, accld));
+  CKR(enqueue_matmul(h, h->mat(h->wm_o, h->we_o, h->GO, h->QD / 16, l), h->a_m.p, h->a_e.p, h->QD, h->QD / 16,
+                     ncols, EPI_RESIDUAL, h->h1_m.p, h->h1_e.p, h->D, h->NTD, h->h_m.p, h->h_e.p, acc, cnt, accld));
+  CKR(enqueue_matmul(h, h->mat(h->wm_gu, h->we_gu, h->GGU, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
+                     EPI_SWIGLU, h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF, nullptr, nullptr, acc, cnt, accld));
+  CKR(enqueue_matmul(h, h->mat(h->wm_d, h->we_d, h->GD, h->NTF, l), h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF, ncols,
+                     EPI_RESIDUAL, h->dbg_m.p, h->dbg_e.p, h->D, h->NTD, h->h1_m.p, h->h1_e.p, acc, cnt, accld));
+  return BFP200_OK;
+}
+
+struct Sampling {
+  double temperature = 0.0;
+  int top_k = 0;
+  uint32_t seed = 0;
+};
+
+// Sampled head: hn, the full fp64 logits of every column, then one sampling
+// CTA per column (uniforms indexed by the device step counter).
+int enqueue_sample_head(bfp200_handle* h, int ncols, const Sampling& smp, int u_ld) {
+  cudaStream_t s = h->stream;
+  mark(h, PK_HEAD_PREP);
+  CK(launch_head_prep(h->h_m.p, h->h_e.p, h->nw.p, h->cfg.eps, h->D, ncols, h->hn.p, h->hn_norm.p, s, h->pdl));
+  int nrb = 0;
+  mark(h, PK_HEAD_LOGITS);
+  CK(launch_head_logits(h->emb_m.p, h->emb_e.p, h->V, h->D, h->hn.p, ncols, h->part_val.p, h->part_idx.p,
+                        h->part_sec.p, &nrb, s, h->pdl, h->s_logits.p));
+  SampleArgs a;
+  a.logits = h->s_logits.p; a.ld = h->V; a.V = h->V; a.D = h->D;
+  a.temperature = smp.temperature; a.top_k = smp.top_k;
+  a.work = h->s_work.p; a.cdf = h->s_cdf.p; a.incl = h->s_incl.p;
+  a.plan = h->v_plan.p;
+  a.uniforms = h->s_uni.p; a.u_ld = u_ld; a.step = h->dec_step.p;
+  a.hn_norm = h->hn_norm.p; a.emb_norm_max = h->emb_norm_max;
+  a.tok = h->tok.p; a.cert = h->cert.p;
+  mark(h, PK_HEAD_REDUCE);
+  CK(launch_sample(a, ncols, h->v_plan_leaves, s));
   return BFP200_OK;
 }
 
@@ -1081,9 +1185,29 @@ int bfp200_load_rom(bfp200_handle* h, int kind, const uint16_t* entries, size_t 
   return BFP200_OK;
 }
 
+static int generate_impl(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq,
+                         int n_gen, int feed_mode, int32_t* out_tokens, const Sampling* smp);
+
 int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq, int n_gen,
                     int feed_mode, int32_t* out_tokens) {
+  return generate_impl(h, prompt_ids, prompt_lens, n_seq, n_gen, feed_mode, out_tokens, nullptr);
+}
+
+int bfp200_generate_sampled(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq,
+                            int n_gen, double temperature, int top_k, uint32_t seed, int32_t* out_tokens) {
+  if (!(temperature > 0.0)) return generate_impl(h, prompt_ids, prompt_lens, n_seq, n_gen, 0, out_tokens, nullptr);
+  if (!std::isfinite(temperature) || top_k < 0) return fail(BFP200_EINVAL, "generate_sampled: bad temperature / top_k");
+  Sampling smp;
+  smp.temperature = temperature;
+  smp.top_k = top_k;
+  smp.seed = seed;
+  return generate_impl(h, prompt_ids, prompt_lens, n_seq, n_gen, 0, out_tokens, &smp);
+}
+
+static int generate_impl(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq,
+                         int n_gen, int feed_mode, int32_t* out_tokens, const Sampling* smp) {
   if (!h || !out_tokens) return fail(BFP200_EINVAL, "generate: null argument");
+  if (smp && h->comm) return fail(BFP200_EINVAL, "sampling is not available with a sharded head");
   if (!h->have_image) return fail(BFP200_ESTATE, "generate before load_image");
   if (feed_mode != 0 && feed_mode != 1) return fail(BFP200_EINVAL, "feed_mode must be 0 (sim) or 1 (rtl)");
   if (n_gen < 0) return fail(BFP200_EINVAL, "n_gen < 0");
@@ -1154,6 +1278,25 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
     dpos[s] = lens[s];
     dtok[s] = rtl ? rtl_host[(size_t)s * h->cfg.NPROMPT_MAX + lens[s] - 1] : ids[off[s] + lens[s] - 1];
   }
+  const int u_ld = n_gen + 1;
+  if (n_gen > 0 && smp) {
+    // one uniform per sampled step; index 0 is the draw the reference makes
+    // (and discards) at the last prompt position
+    const size_t nv = (size_t)n_seq * h->V;
+    CK(h->s_logits.ensure(nv)); CK(h->s_work.ensure(nv)); CK(h->s_cdf.ensure(nv)); CK(h->s_incl.ensure(nv));
+    CK(h->s_uni.ensure((size_t)n_seq * u_ld));
+    if (!h->v_plan_leaves) {
+      std::vector<unsigned short> plan;
+      build_pw_plan_one(h->V, plan);
+      CK(h->v_plan.ensure(plan.size()));
+      CK(cudaMemcpyAsync(h->v_plan.p, plan.data(), plan.size() * 2, cudaMemcpyHostToDevice, h->stream));
+      h->v_plan_leaves = plan[0];
+    }
+    std::vector<double> uni((size_t)n_seq * u_ld);
+    for (int s = 0; s < n_seq; ++s) mt19937_uniforms(smp->seed + (uint32_t)s, u_ld, uni.data() + (size_t)s * u_ld);
+    CK(cudaMemcpyAsync(h->s_uni.p, uni.data(), uni.size() * 8, cudaMemcpyHostToDevice, h->stream));
+    CKR(sync_stream(h));
+  }
   if (n_gen > 0) {
     CK(h->gen_out.ensure((size_t)n_seq * n_gen));
     CK(h->dec_step.ensure(1));
@@ -1161,7 +1304,7 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
     CK(cudaMemcpyAsync(h->col_pos.p, dpos.data(), n_seq * 4, cudaMemcpyHostToDevice, h->stream));
     CK(cudaMemcpyAsync(h->col_tok.p, dtok.data(), n_seq * 4, cudaMemcpyHostToDevice, h->stream));
     CK(cudaMemsetAsync(h->dec_step.p, 0, 4, h->stream));
-    if (persist_ok(h, n_seq)) {
+    if (!smp && persist_ok(h, n_seq)) {
       CK(h->psync.ensure(PERSIST_SYNC_WORDS));
       CK(cudaMemsetAsync(h->psync.p, 0, PERSIST_SYNC_WORDS * sizeof(unsigned), h->stream));
       PersistArgs pa = persist_args(h, n_seq, n_gen);
@@ -1170,13 +1313,22 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
       ++h->launch_count;
     } else {
       // one decode step captured once as a CUDA graph, replayed n_gen times
-      if (!h->graph || h->graph_cols != n_seq || h->graph_ngen != n_gen) {
+      const double temp = smp ? smp->temperature : 0.0;
+      const int topk = smp ? smp->top_k : 0;
+      if (!h->graph || h->graph_cols != n_seq || h->graph_ngen != n_gen || h->graph_temp != temp ||
+          h->graph_topk != topk) {
         if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; }
+        if (!small_path_ok(h, n_seq) && h->use_tc && n_seq >= 64) {
+          // tensor-core configurations are chosen by timing, which a capture
+          // cannot do: run the layer shapes once first (scratch outputs only)
+          CKR(enqueue_layer_matmuls(h, 0, n_seq));
+        }
         CKR(sync_stream(h));
         cudaGraph_t g;
         CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
         const long long before = h->launch_count;
-        int r = enqueue_forward(h, n_seq, true, /*decode=*/true);
+        int r = enqueue_forward(h, n_seq, smp == nullptr, /*decode=*/true);
+        if (r == BFP200_OK && smp) r = enqueue_sample_head(h, n_seq, *smp, u_ld);
         h->graph_launches = h->launch_count - before + 1;       // + the advance kernel
         h->launch_count = before;
         advance_kernel<<<1, 256, 0, h->stream>>>(h->tok.p, h->cert.p, n_seq, n_gen, h->gen_out.p, h->col_tok.p,
@@ -1189,6 +1341,8 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
         CK(ce);
         h->graph_cols = n_seq;
         h->graph_ngen = n_gen;
+        h->graph_temp = temp;
+        h->graph_topk = topk;
       }
       for (int i = 0; i < n_gen; ++i) CK(cudaGraphLaunch(h->graph, h->stream));
       h->launch_count += h->graph_launches * n_gen;
@@ -1403,9 +1557,6 @@ int bfp200_time_matmuls(bfp200_handle* h, int ncols, int reps, double* ms_per_to
   if (!h->have_image) return fail(BFP200_ESTATE, "time_matmuls before load_image");
   CK(cudaSetDevice(h->device));
   CKR(ensure_cols(h, ncols));
-  long long* acc = h->acc.p;
-  unsigned* cnt = h->counters.p;
-  const int accld = h->cap;
   const bool small = small_path_ok(h, ncols);
   auto body = [&]() -> int {
     for (int l = 0; l < h->NL && small; ++l) {
@@ -1414,21 +1565,13 @@ int bfp200_time_matmuls(bfp200_handle* h, int ncols, int reps, double* ms_per_to
       CKR(enqueue_gemv_gu(h, l, ncols, h->pdl));
       CKR(enqueue_gemv_d(h, l, ncols, h->pdl, h->dbg_m.p, h->dbg_e.p));
     }
-    for (int l = 0; l < h->NL && !small; ++l) {
-      CKR(enqueue_matmul(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD,
-                         ncols, EPI_STORE, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->RQKV / 16, nullptr, nullptr, acc, cnt,
-                         accld));
-      CKR(enqueue_matmul(h, h->mat(h->wm_o, h->we_o, h->GO, h->QD / 16, l), h->a_m.p, h->a_e.p, h->QD, h->QD / 16,
-                         ncols, EPI_RESIDUAL, h->h1_m.p, h->h1_e.p, h->D, h->NTD, h->h_m.p, h->h_e.p, acc, cnt,
-                         accld));
-      CKR(enqueue_matmul(h, h->mat(h->wm_gu, h->we_gu, h->GGU, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
-                         EPI_SWIGLU, h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF, nullptr, nullptr, acc, cnt, accld));
-      CKR(enqueue_matmul(h, h->mat(h->wm_d, h->we_d, h->GD, h->NTF, l), h->mlp_m.p, h->mlp_e.p, h->FFN, h->NTF,
-                         ncols, EPI_RESIDUAL, h->dbg_m.p, h->dbg_e.p, h->D, h->NTD, h->h1_m.p, h->h1_e.p, acc, cnt,
-                         accld));
-    }
+    for (int l = 0; l < h->NL && !small; ++l) CKR(enqueue_layer_matmuls(h, l, ncols));
     return BFP200_OK;
   };
+  if (!small) {                       // choose the tensor-core configurations outside the capture
+    CKR(enqueue_layer_matmuls(h, 0, ncols));
+    CK(cudaStreamSynchronize(h->stream));
+  }
   CK(cudaStreamSynchronize(h->stream));
   cudaGraph_t g;
   CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));

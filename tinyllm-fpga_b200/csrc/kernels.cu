@@ -713,41 +713,59 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
-  // scores[t] = float(np.dot(q, k_t)) / math.sqrt(HD)   (:278), exact; rows
-  // beyond the first chunk are read from the arena
+  // scores[t] = float(np.dot(q, k_t)) / math.sqrt(HD)   (:278), exact.  Four
+  // lanes per position, one 16-element tile each (a 64-bit multiply-add per
+  // product); the quad's four tile sums are combined exactly.  Rows beyond
+  // the first chunk are read from the arena.  Dividing by a power of two
+  // equals multiplying by its exact reciprocal (both round the same real).
+  const bool pow2_hd = (__double_as_longlong(sqrt_hd) & 0x000FFFFFFFFFFFFFLL) == 0;
+  const double inv_hd = 1.0 / sqrt_hd;
   double lmax = -INFINITY;
-  for (int t = tid; t < T; t += ATT_THREADS) {
-    uint4 kk[8];
-    unsigned ke4;
-    if (t < n0) {
-      #pragma unroll
-      for (int u = 0; u < 8; ++u) kk[u] = ks[t * 8 + u];
-      ke4 = kes[t];
-    } else {
-      const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
-      #pragma unroll
-      for (int u = 0; u < 8; ++u) kk[u] = kr[u];
-      ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
-    }
-    long long S[4];
-    int E[4];
-    #pragma unroll
-    for (int jt = 0; jt < 4; ++jt) {
-      const unsigned w[8] = {kk[2 * jt].x, kk[2 * jt].y, kk[2 * jt].z, kk[2 * jt].w,
-                             kk[2 * jt + 1].x, kk[2 * jt + 1].y, kk[2 * jt + 1].z, kk[2 * jt + 1].w};
-      long long sacc = 0;
-      #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int lo = (int)(int16_t)(w[u] & 0xFFFF), hi = (int)(int16_t)(w[u] >> 16);
-        sacc += (long long)(s_qm[jt * 16 + 2 * u] * lo) + (long long)(s_qm[jt * 16 + 2 * u + 1] * hi);
+  {
+    const int jt = tid & 3, qb = lane & ~3;
+    const int* qp = s_qm + jt * 16;
+    for (int t0 = 0; t0 < T; t0 += ATT_THREADS / 4) {
+      const int t = t0 + (tid >> 2);
+      long long S = 0;
+      int E = 0;
+      if (t < T) {
+        uint4 k0, k1;
+        unsigned ke4;
+        if (t < n0) {
+          k0 = ks[t * 8 + 2 * jt];
+          k1 = ks[t * 8 + 2 * jt + 1];
+          ke4 = kes[t];
+        } else {
+          const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
+          k0 = kr[2 * jt];
+          k1 = kr[2 * jt + 1];
+          ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
+        }
+        const unsigned w[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          S += (long long)qp[2 * u] * (int)(int16_t)(w[u] & 0xFFFF);
+          S += (long long)qp[2 * u + 1] * (int)(int16_t)(w[u] >> 16);
+        }
+        E = s_qe[jt] + (int)(int8_t)(ke4 >> (8 * jt));
       }
-      S[jt] = sacc;
-      E[jt] = s_qe[jt] + (int)(int8_t)(ke4 >> (8 * jt));
+      long long S4[4];
+      int E4[4];
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        S4[j] = __shfl_sync(0xffffffffu, S, qb + j);
+        E4[j] = __shfl_sync(0xffffffffu, E, qb + j);
+      }
+      if (t < T && jt == 0) {
+        const double dot = exact_tile_dot4(S4, E4);
+        const double v = pow2_hd ? __dmul_rn(dot, inv_hd) : __ddiv_rn(dot, sqrt_hd);
+        sc[t] = v;
+        lmax = v > lmax ? v : lmax;
+      }
     }
-    const double v = __ddiv_rn(exact_tile_dot4(S, E), sqrt_hd);
-    sc[t] = v;
-    lmax = v > lmax ? v : lmax;
   }
+  // (the max reduction's barrier below orders these sc[] writes before the
+  // exp pass, which reads them with a different thread mapping)
   // softmax_fp (:245-247): e = exp(x - max); e / e.sum()
   for (int off = 16; off; off >>= 1) {
     const double o = __shfl_xor_sync(0xffffffffu, lmax, off);
@@ -893,89 +911,155 @@ cudaError_t launch_head_prep(const int16_t* hm, const int8_t* he, const double* 
                    D, ncols, hn, hn_norm);
 }
 
-template <int RT, int CT, int TR, int TC>
+// Batched head on the fp64 tensor cores (mma.sync m8n8k4 .f64, IEEE
+// round-to-nearest per operation, so the logits obey the same any-order
+// error bound the certificate assumes).  CTA tile: 128 vocabulary rows x 64
+// columns; 8 warps as 4 (rows) x 2 (columns), each 32 x 32 = 4 x 4 m8n8
+// tiles.  K advances one BFP tile (16) at a time: the CTA decodes its rows'
+// mantissas into shared memory (exact, k-major) and stages hn k-major, double
+// buffered, with the next tile's global loads in flight during the MMAs.
+// Rows of a k plane are padded by 8 doubles so a fragment load (4 k x 8 rows)
+// touches every bank exactly twice.  Output per (column, row block): best,
+// lowest index of the best, runner-up.
+constexpr int HD_RT = 128, HD_CT = 64, HD_PAD = 8;
+constexpr int HD_ES = HD_RT + HD_PAD, HD_HS = HD_CT + HD_PAD;
+
+size_t head_dmma_smem() { return (size_t)2 * 16 * (HD_ES + HD_HS) * sizeof(double); }
+
+__device__ __forceinline__ void dmma_m8n8k4(double (&d)[2], double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+               : "+d"(d[0]), "+d"(d[1]) : "d"(a), "d"(b));
+}
+
 __global__ void __launch_bounds__(256)
-head_logits_kernel(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, const double* hn, int ncols,
-                   double* part_val, int* part_idx, double* part_second) {
-  static_assert((RT / TR) * (CT / TC) == 256, "thread tiling");
-  __shared__ double Es[16][RT + 1];
-  __shared__ double Hs[16][CT + 1];
-  __shared__ double s_val[RT / TR][CT];
-  __shared__ int s_idx[RT / TR][CT];
-  __shared__ double s_sec[RT / TR][CT];
+head_dmma_kernel(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, const double* hn, int ncols,
+                 double* part_val, int* part_idx, double* part_second, double* logits_out) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  double* Es = reinterpret_cast<double*>(smem);            // [2][16][HD_ES]
+  double* Hs = Es + 2 * 16 * HD_ES;                        // [2][16][HD_HS]
+  __shared__ double r_val[4][HD_CT], r_sec[4][HD_CT];
+  __shared__ int r_idx[4][HD_CT];
   pdl_trigger();
-  const int tid = threadIdx.x;
-  const int tx = tid % (CT / TC), ty = tid / (CT / TC);
-  const int v0 = blockIdx.x * RT, c0 = blockIdx.y * CT;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wr = warp & 3, wc = warp >> 2;
+  const int v0 = blockIdx.x * HD_RT, c0 = blockIdx.y * HD_CT;
   const int NT = D / 16;
-  double acc[TR][TC];
-  #pragma unroll
-  for (int a = 0; a < TR; ++a)
+  // staging roles: E row er / half eh (8 mantissas); H column hc, k quarter hq
+  const int er = tid >> 1, eh = tid & 1, ev = v0 + er;
+  const int hc = tid >> 2, hq = (tid & 3) * 4;
+  const bool e_ok = ev < VOCAB, h_ok = c0 + hc < ncols;
+  uint4 em = make_uint4(0, 0, 0, 0);
+  int ee = 0;
+  double hv[4] = {0.0, 0.0, 0.0, 0.0};
+  auto load_e = [&](int t) {
+    if (e_ok) {
+      em = *reinterpret_cast<const uint4*>(emb_m + (size_t)ev * D + t * 16 + eh * 8);
+      ee = emb_e[(size_t)ev * NT + t];
+    }
+  };
+  auto load_h = [&](int t) {
+    if (h_ok) {
+      const double2* hp = reinterpret_cast<const double2*>(hn + (size_t)(c0 + hc) * D + t * 16 + hq);
+      const double2 x0 = hp[0], x1 = hp[1];
+      hv[0] = x0.x; hv[1] = x0.y; hv[2] = x1.x; hv[3] = x1.y;
+    }
+  };
+  auto store = [&](int buf) {
+    double* E = Es + buf * 16 * HD_ES;
+    double* H = Hs + buf * 16 * HD_HS;
+    const double sc = pow2(ee - 15);
+    const unsigned w[4] = {em.x, em.y, em.z, em.w};
     #pragma unroll
-    for (int b = 0; b < TC; ++b) acc[a][b] = 0.0;
+    for (int q = 0; q < 8; ++q)
+      E[(eh * 8 + q) * HD_ES + er] = (double)(int)(int16_t)((w[q >> 1] >> (16 * (q & 1))) & 0xFFFF) * sc;
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) H[(hq + q) * HD_HS + hc] = hv[q];
+  };
+  double acc[4][4][2];
+  #pragma unroll
+  for (int i = 0; i < 4; ++i)
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+  load_e(0);                       // the embedding does not depend on the previous kernel
   pdl_wait();
-  for (int t = 0; t < NT; ++t) {
-    for (int o = tid; o < RT * 16; o += 256) {
-      const int r = o / 16, k = o % 16;
-      const int v = v0 + r;
-      double val = 0.0;
-      if (v < VOCAB) val = bfp_decode(emb_m[(size_t)v * D + t * 16 + k], emb_e[(size_t)v * NT + t]);
-      Es[k][r] = val;
-    }
-    for (int o = tid; o < CT * 16; o += 256) {
-      const int cc = o / 16, k = o % 16;
-      Hs[k][cc] = (c0 + cc < ncols) ? hn[(size_t)(c0 + cc) * D + t * 16 + k] : 0.0;
-    }
-    __syncthreads();
-    #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      double av[TR], bv[TC];
-      #pragma unroll
-      for (int a = 0; a < TR; ++a) av[a] = Es[k][ty * TR + a];
-      #pragma unroll
-      for (int b = 0; b < TC; ++b) bv[b] = Hs[k][tx * TC + b];
-      #pragma unroll
-      for (int a = 0; a < TR; ++a)
-        #pragma unroll
-        for (int b = 0; b < TC; ++b) acc[a][b] = fma(av[a], bv[b], acc[a][b]);
-    }
-    __syncthreads();
-  }
-  // per thread: best / runner-up among its TR rows, per column
-  #pragma unroll
-  for (int b = 0; b < TC; ++b) {
-    double best = -INFINITY, sec = -INFINITY;
-    int bi = 0x7fffffff;
-    #pragma unroll
-    for (int a = 0; a < TR; ++a) {
-      const int v = v0 + ty * TR + a;
-      if (v >= VOCAB) continue;
-      const double x = acc[a][b];
-      if (x > best) { sec = best; best = x; bi = v; }
-      else if (x > sec) sec = x;
-    }
-    s_val[ty][tx * TC + b] = best;
-    s_idx[ty][tx * TC + b] = bi;
-    s_sec[ty][tx * TC + b] = sec;
-  }
+  load_h(0);
+  store(0);
   __syncthreads();
-  for (int cc = tid; cc < CT; cc += 256) {
-    if (c0 + cc >= ncols) continue;
+  for (int t = 0; t < NT; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < NT) { load_e(t + 1); load_h(t + 1); }
+    const double* E = Es + buf * 16 * HD_ES + wr * 32 + (lane >> 2);
+    const double* H = Hs + buf * 16 * HD_HS + wc * 32 + (lane >> 2);
+    #pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const int k = ks * 4 + (lane & 3);
+      double a[4], b[4];
+      #pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = E[k * HD_ES + i * 8];
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = H[k * HD_HS + j * 8];
+      #pragma unroll
+      for (int i = 0; i < 4; ++i)
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) dmma_m8n8k4(acc[i][j], a[i], b[j]);
+    }
+    if (t + 1 < NT) store(buf ^ 1);
+    __syncthreads();
+  }
+  if (logits_out) {
+    #pragma unroll
+    for (int i = 0; i < 4; ++i)
+      #pragma unroll
+      for (int j = 0; j < 4; ++j)
+        #pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int v = v0 + wr * 32 + i * 8 + (lane >> 2), col = c0 + wc * 32 + j * 8 + (lane & 3) * 2 + e;
+          if (v < VOCAB && col < ncols) logits_out[(size_t)col * VOCAB + v] = acc[i][j][e];
+        }
+  }
+  // best / runner-up per column over this warp's 32 rows: own 4 rows, then
+  // the 8 lanes that share lane & 3 (rows lane >> 2)
+  #pragma unroll
+  for (int j = 0; j < 4; ++j)
+    #pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      double best = -INFINITY, sec = -INFINITY;
+      int bi = 0x7fffffff;
+      #pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int v = v0 + wr * 32 + i * 8 + (lane >> 2);
+        const double x = acc[i][j][e];
+        if (v < VOCAB) {
+          if (x > best) { sec = best; best = x; bi = v; }
+          else if (x > sec) sec = x;
+        }
+      }
+      #pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        const double ob = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        const double os = __shfl_xor_sync(0xffffffffu, sec, off);
+        if (ob > best || (ob == best && oi < bi)) { sec = fmax(sec, best); best = ob; bi = oi; }
+        else sec = fmax(sec, ob);
+        sec = fmax(sec, os);
+      }
+      if (lane < 4) {
+        const int cc = wc * 32 + j * 8 + lane * 2 + e;
+        r_val[wr][cc] = best; r_idx[wr][cc] = bi; r_sec[wr][cc] = sec;
+      }
+    }
+  __syncthreads();
+  if (tid < HD_CT && c0 + tid < ncols) {
     double best = -INFINITY, sec = -INFINITY;
     int bi = 0x7fffffff;
-    for (int y = 0; y < RT / TR; ++y) {   // ascending row order: ties keep the lowest index
-      const double x = s_val[y][cc];
-      const int xi = s_idx[y][cc];
-      const double xs = s_sec[y][cc];
-      if (x > best || (x == best && xi < bi)) {
-        sec = fmax(sec, best);
-        best = x; bi = xi;
-      } else {
-        sec = fmax(sec, x);
-      }
-      sec = fmax(sec, xs);
+    for (int y = 0; y < 4; ++y) {                          // ascending rows: ties keep the lowest index
+      const double x = r_val[y][tid];
+      const int xi = r_idx[y][tid];
+      if (x > best || (x == best && xi < bi)) { sec = fmax(sec, best); best = x; bi = xi; }
+      else sec = fmax(sec, x);
+      sec = fmax(sec, r_sec[y][tid]);
     }
-    const size_t o = (size_t)(c0 + cc) * gridDim.x + blockIdx.x;
+    const size_t o = (size_t)(c0 + tid) * gridDim.x + blockIdx.x;
     part_val[o] = best; part_idx[o] = bi; part_second[o] = sec;
   }
 }
@@ -986,7 +1070,7 @@ head_logits_kernel(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, 
 template <int NC>
 __global__ void __launch_bounds__(256)
 head_gemv_kernel(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, const double* hn, int ncols,
-                 double* part_val, int* part_idx, double* part_second) {
+                 double* part_val, int* part_idx, double* part_second, double* logits_out) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double w_best[8][NC], w_sec[8][NC];
   __shared__ int w_idx[8][NC];
@@ -1045,6 +1129,7 @@ head_gemv_kernel(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, co
         #pragma unroll
         for (int off = 16; off; off >>= 1) acc[cc] += __shfl_xor_sync(0xffffffffu, acc[cc], off);
         const double x = acc[cc];
+        if (logits_out && lane == 0 && cc < ncols) logits_out[(size_t)cc * VOCAB + vr[q]] = x;
         if (x > best[cc]) { sec[cc] = best[cc]; best[cc] = x; bidx[cc] = vr[q]; }
         else if (x > sec[cc]) sec[cc] = x;
       }
@@ -1071,7 +1156,7 @@ head_gemv_kernel(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, co
 
 cudaError_t launch_head_logits(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, const double* hn,
                                int ncols, double* part_val, int* part_idx, double* part_second, int* n_rowblocks,
-                               cudaStream_t s, bool pdl) {
+                               cudaStream_t s, bool pdl, double* logits_out) {
   if (ncols <= 4 && D % 8 == 0 && D <= 768) {
     int dev = 0, nsm = 148;
     cudaGetDevice(&dev);
@@ -1080,14 +1165,14 @@ cudaError_t launch_head_logits(const int16_t* emb_m, const int8_t* emb_e, int VO
     const size_t smem = (size_t)(ncols <= 1 ? 1 : 4) * D * 8;
     if (ncols <= 1)
       return launch_ex(head_gemv_kernel<1>, dim3(*n_rowblocks), dim3(256), smem, s, pdl, emb_m, emb_e, VOCAB, D, hn,
-                       ncols, part_val, part_idx, part_second);
+                       ncols, part_val, part_idx, part_second, logits_out);
     return launch_ex(head_gemv_kernel<4>, dim3(*n_rowblocks), dim3(256), smem, s, pdl, emb_m, emb_e, VOCAB, D, hn,
-                     ncols, part_val, part_idx, part_second);
+                     ncols, part_val, part_idx, part_second, logits_out);
   }
-  constexpr int RT = 64, CT = 64;
-  *n_rowblocks = (VOCAB + RT - 1) / RT;
-  return launch_ex(head_logits_kernel<RT, CT, 4, 4>, dim3(*n_rowblocks, (ncols + CT - 1) / CT), dim3(256), 0, s,
-                   pdl, emb_m, emb_e, VOCAB, D, hn, ncols, part_val, part_idx, part_second);
+  if (D % 16) return cudaErrorInvalidValue;
+  *n_rowblocks = (VOCAB + HD_RT - 1) / HD_RT;
+  return launch_ex(head_dmma_kernel, dim3(*n_rowblocks, (ncols + HD_CT - 1) / HD_CT), dim3(256), head_dmma_smem(),
+                   s, pdl, emb_m, emb_e, VOCAB, D, hn, ncols, part_val, part_idx, part_second, logits_out);
 }
 
 __global__ void head_reduce_kernel(const double* part_val, const int* part_idx, const double* part_second, int nrb,
@@ -1655,6 +1740,7 @@ cudaError_t init_kernel_attributes() {
   set((const void*)head_gemv_kernel<4>);
   set((const void*)head_small_kernel<1>);
   set((const void*)head_small_kernel<4>);
+  set((const void*)head_dmma_kernel);
   const cudaError_t g = init_gemv_attributes();
   return e != cudaSuccess ? e : g;
 }

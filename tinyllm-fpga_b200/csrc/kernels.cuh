@@ -104,11 +104,13 @@ struct TcArgs {
   const int16_t* rm = nullptr;    // residual (EPI_RESIDUAL), output layout
   const int8_t* re = nullptr;
   int* err = nullptr;             // bounded-wait error flag
+  int ncb = 0, ks = 0;            // columns per CTA (16 / 32) and K split (1..8); 0: built-in choice
 };
 size_t tc_records_bytes(int rows, int NT);
 cudaError_t launch_tc_pack(const uint8_t* wm, const int8_t* we, int rows, int NT, uint8_t* rec, cudaStream_t s);
 bool tc_supported(int NT, int ncols);
 cudaError_t launch_tc_matmul(const TcArgs& a, cudaStream_t s, bool pdl);
+bool tc_config_valid(int NT, int ncb, int ks);
 
 // Persistent small-batch decode (persist.cu): one cooperative launch runs
 // n_gen decode steps of 1..4 columns (embedding, all layers, head, token
@@ -195,7 +197,8 @@ cudaError_t launch_head_prep(const int16_t* hm, const int8_t* he, const double* 
                              int D, int ncols, double* hn, double* hn_norm, cudaStream_t s, bool pdl);
 cudaError_t launch_head_logits(const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D,
                                const double* hn, int ncols, double* part_val, int* part_idx,
-                               double* part_second, int* n_rowblocks, cudaStream_t s, bool pdl);
+                               double* part_second, int* n_rowblocks, cudaStream_t s, bool pdl,
+                               double* logits_out = nullptr);   // optional [ncols][VOCAB] logits
 // Reduces per-row-block partials to the argmax; writes tok_out[c] and the
 // certification flag (1 = the margin to the runner-up exceeds the fp64 dot
 // error bound of any summation order).
@@ -212,6 +215,31 @@ cudaError_t launch_head_combine(const double* gathered, int nranks, int ncols, d
 
 // Head of 1..4 columns in one launch: hn, fp64 logits, and (last CTA) the
 // certified argmax.  done_ctr: a zeroed word, left zeroed on return.
+// Temperature / top-k sampling (sample.cu): one CTA per column reads the
+// column's fp64 logits, the uniform of decode step *step + 1 and writes the
+// token and its certificate.  work / cdf: [ncols][ld] doubles, incl:
+// [ncols][ld] ints of scratch; plan: numpy's pairwise-sum plan for VOCAB.
+struct SampleArgs {
+  const double* logits = nullptr;
+  int ld = 0, V = 0, D = 0;
+  double temperature = 1.0;
+  int top_k = 0;
+  double* work = nullptr;
+  double* cdf = nullptr;
+  int* incl = nullptr;
+  const unsigned short* plan = nullptr;
+  const double* uniforms = nullptr;   // [ncols][u_ld]
+  int u_ld = 0;
+  const int* step = nullptr;
+  const double* hn_norm = nullptr;
+  double emb_norm_max = 0.0;
+  int* tok = nullptr;
+  int* cert = nullptr;
+};
+cudaError_t launch_sample(const SampleArgs& a, int ncols, int plan_leaves, cudaStream_t s);
+// n uniforms of numpy's legacy generator after np.random.seed(seed)
+void mt19937_uniforms(uint32_t seed, int n, double* out);
+
 bool head_small_supported(int ncols, int D);
 cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
                               const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, int ncols,

@@ -148,19 +148,40 @@ __global__ void tc_pack_kernel(const uint8_t* wm, const int8_t* we, int rows, in
 // ---------------------------------------------------------------------------
 // the matmul
 // ---------------------------------------------------------------------------
+// Shared memory of one CTA that owns ntl of the NT K tiles (split K: the
+// CTAs of a cluster share the tiles; every CTA keeps all NT column exponents
+// for the max-exponent pass, and a 128 x NCB int64 block for the reduction).
 struct TcLayout {
-  size_t bar, tptr, ring, z, xe, cx, total;
+  size_t bar, tptr, ring, z, xe, cx, red, total;
 };
-__host__ __device__ inline TcLayout tc_layout(int NT, int NCB) {
+__host__ __device__ inline TcLayout tc_layout(int NT, int NCB, int ntl, bool split) {
   TcLayout L;
   L.bar = 0;                                           // mbarriers: ring full / empty, D full / empty
   L.tptr = 112;                                        // TMEM base address
   L.ring = 128;
   L.z = L.ring + (size_t)TC_SA * TC_REC;
-  L.xe = L.z + (size_t)(3 * NT + 1) * NCB * 16;
+  L.xe = L.z + (size_t)(3 * ntl + 1) * NCB * 16;
   L.cx = L.xe + (size_t)NT * NCB * 4;
-  L.total = L.cx + (size_t)NT * NCB * 4;
+  L.red = L.cx + (size_t)ntl * NCB * 4;
+  L.red = (L.red + 15) & ~(size_t)15;
+  L.total = L.red + (split ? (size_t)TC_M * NCB * 8 : 0);
   return L;
+}
+
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ long long ld_peer_s64(const long long* p, unsigned rank) {
+  unsigned remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(su32(p)), "r"(rank));
+  long long v;
+  asm volatile("ld.shared::cluster.s64 %0, [%1];" : "=l"(v) : "r"(remote) : "memory");
+  return v;
 }
 
 // Warp roles: warp 0 streams the weight records (TMA), warp 1 issues the
@@ -169,6 +190,10 @@ __host__ __device__ inline TcLayout tc_layout(int NT, int NCB) {
 // thread).  Records pass through a ring of TC_SA stages (full: TMA bytes;
 // empty: the MMA's commit and one arrival per epilogue warp), D through
 // TC_NB tensor-memory buffers (full: MMA commit; empty: the epilogue warps).
+// Split K: gridDim.z CTAs form a cluster over the K tiles of one output
+// block; each computes the full max exponent, accumulates its own tiles,
+// and cluster rank 0 adds the others' int64 sums through distributed shared
+// memory (integer addition: exact in any order) before the epilogue.
 constexpr int TC_NB = 2;
 constexpr int TC_EPI_WARPS = 16;
 
@@ -181,7 +206,10 @@ tc_matmul_kernel(TcArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int NT = a.NT;
   const int blk = blockIdx.x, c0 = blockIdx.y * NCB;
-  const TcLayout L = tc_layout(NT, NCB);
+  const int ks = gridDim.z;
+  const int kr = ks > 1 ? (int)cluster_rank() : 0;
+  const int t_lo = kr * NT / ks, t_hi = (kr + 1) * NT / ks, ntl = t_hi - t_lo;
+  const TcLayout L = tc_layout(NT, NCB, (NT + ks - 1) / ks, ks > 1);
   unsigned long long* rfull = reinterpret_cast<unsigned long long*>(smem + L.bar);   // [TC_SA]
   unsigned long long* rempty = rfull + TC_SA;                                         // [TC_SA]
   unsigned long long* dfull = rempty + TC_SA;                                         // [TC_NB]
@@ -190,8 +218,10 @@ tc_matmul_kernel(TcArgs a) {
   unsigned char* ring = smem + L.ring;
   unsigned char* Z = smem + L.z;
   int* xe_s = reinterpret_cast<int*>(smem + L.xe);           // [NT][NCB]
-  int* cx_s = reinterpret_cast<int*>(smem + L.cx);           // [NT][NCB]
+  int* cx_s = reinterpret_cast<int*>(smem + L.cx);           // [ntl][NCB]
+  long long* red = reinterpret_cast<long long*>(smem + L.red); // [NCB][128] (split K)
   const uint8_t* rec = a.rec + (size_t)blk * tc_block_bytes(NT);
+  const uint8_t* rec_k = rec + (size_t)t_lo * TC_REC;         // this CTA's first K tile
   pdl_trigger_tc();
   // ---- barriers and the first weight records: the weights do not depend on
   // the previous kernel, so they stream before the wait
@@ -199,10 +229,10 @@ tc_matmul_kernel(TcArgs a) {
     for (int s = 0; s < TC_SA; ++s) { mb_init(&rfull[s], 1); mb_init(&rempty[s], 1 + TC_EPI_WARPS); }
     for (int b = 0; b < TC_NB; ++b) { mb_init(&dfull[b], 1); mb_init(&dempty[b], TC_EPI_WARPS); }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int s = 0; s < TC_SA && s < NT; ++s) {
+    for (int s = 0; s < TC_SA && s < ntl; ++s) {
       asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&rfull[s])), "r"(TC_REC) : "memory");
       asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                   :: "r"(su32(ring + (size_t)s * TC_REC)), "l"(rec + (size_t)s * TC_REC), "r"(TC_REC),
+                   :: "r"(su32(ring + (size_t)s * TC_REC)), "l"(rec_k + (size_t)s * TC_REC), "r"(TC_REC),
                       "r"(su32(&rfull[s])) : "memory");
     }
   }
@@ -214,7 +244,7 @@ tc_matmul_kernel(TcArgs a) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   // ---- B operand of every tile, column exponents and sums (columns c0 .. c0+NCB-1)
-  for (int i = tid; i < NCB * 4; i += TC_THREADS) {           // the leading zero block (16 B units)
+  for (int i = tid; i < NCB; i += TC_THREADS) {               // the leading zero block (NCB x 16 B)
     reinterpret_cast<uint4*>(Z)[i] = make_uint4(0, 0, 0, 0);
   }
   constexpr int ZB = 4;                                      // items in flight per thread
@@ -227,9 +257,11 @@ tc_matmul_kernel(TcArgs a) {
       v[u][0] = v[u][1] = make_uint4(0, 0, 0, 0);
       ev[u] = -127;
       if (i < NT * NCB && col < a.ncols) {
-        const uint4* xp = reinterpret_cast<const uint4*>(a.xm + (size_t)col * a.x_ld + t * 16);
-        v[u][0] = xp[0];
-        v[u][1] = xp[1];
+        if (t >= t_lo && t < t_hi) {
+          const uint4* xp = reinterpret_cast<const uint4*>(a.xm + (size_t)col * a.x_ld + t * 16);
+          v[u][0] = xp[0];
+          v[u][1] = xp[1];
+        }
         ev[u] = a.xe[(size_t)col * a.x_lde + t];
       }
     }
@@ -237,13 +269,16 @@ tc_matmul_kernel(TcArgs a) {
     for (int u = 0; u < ZB; ++u) {
       const int i = i0 + u * TC_THREADS, t = i / NCB, c = i - t * NCB;
       if (i >= NT * NCB) break;
+      xe_s[i] = (int)ev[u];
+      if (t < t_lo || t >= t_hi) continue;
+      const int lt = t - t_lo;
       const uint4 v0 = v[u][0], v1 = v[u][1];
       // x = 256 xh + lo: xh = odd bytes, xl' = even bytes ^ 0x80
       const uint4 xh = make_uint4(__byte_perm(v0.x, v0.y, 0x7531), __byte_perm(v0.z, v0.w, 0x7531),
                                   __byte_perm(v1.x, v1.y, 0x7531), __byte_perm(v1.z, v1.w, 0x7531));
       const uint4 xl = make_uint4(__byte_perm(v0.x, v0.y, 0x6420) ^ 0x80808080u, __byte_perm(v0.z, v0.w, 0x6420) ^ 0x80808080u,
                                   __byte_perm(v1.x, v1.y, 0x6420) ^ 0x80808080u, __byte_perm(v1.z, v1.w, 0x6420) ^ 0x80808080u);
-      uint4* zb = reinterpret_cast<uint4*>(Z + (size_t)(3 * t + 1) * NCB * 16);
+      uint4* zb = reinterpret_cast<uint4*>(Z + (size_t)(3 * lt + 1) * NCB * 16);
       zb[c] = xh;
       zb[NCB + c] = xl;
       zb[2 * NCB + c] = make_uint4(0, 0, 0, 0);
@@ -251,8 +286,7 @@ tc_matmul_kernel(TcArgs a) {
       const unsigned w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
       #pragma unroll
       for (int k = 0; k < 8; ++k) sx += (int)(int16_t)(w[k] & 0xFFFF) + (int)(int16_t)(w[k] >> 16);
-      xe_s[i] = (int)ev[u];
-      cx_s[i] = 128 * sx;
+      cx_s[lt * NCB + c] = 128 * sx;
     }
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");     // B written by threads, read by the MMA
@@ -261,24 +295,29 @@ tc_matmul_kernel(TcArgs a) {
   tc_fence_after();
   const uint32_t tbase = *tptr;
   const uint32_t idesc = idesc_i8(TC_M, N);
+  // per epilogue thread: max exponent and int64 sum of (row, column cb + j)
+  int Mx[CPT];
+  long long acc[CPT];
+  #pragma unroll
+  for (int j = 0; j < CPT; ++j) { Mx[j] = 0; acc[j] = 0; }
 
   if (warp == 0) {
     // ---- producer: refill a ring stage once its MMA and epilogue reads are done
     if (lane == 0) {
-      for (int t = TC_SA; t < NT; ++t) {
+      for (int t = TC_SA; t < ntl; ++t) {
         const int s = t % TC_SA;
         mb_wait(&rempty[s], (unsigned)(((t / TC_SA) - 1) & 1), a.err);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&rfull[s])), "r"(TC_REC) : "memory");
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                     :: "r"(su32(ring + (size_t)s * TC_REC)), "l"(rec + (size_t)t * TC_REC), "r"(TC_REC),
+                     :: "r"(su32(ring + (size_t)s * TC_REC)), "l"(rec_k + (size_t)t * TC_REC), "r"(TC_REC),
                         "r"(su32(&rfull[s])) : "memory");
       }
     }
   } else if (warp == 1) {
     // ---- MMA issuer
     if (lane == 0) {
-      for (int t = 0; t < NT; ++t) {
+      for (int t = 0; t < ntl; ++t) {
         const int s = t % TC_SA, b = t % TC_NB;
         mb_wait(&rfull[s], (unsigned)((t / TC_SA) & 1), a.err);
         if (t >= TC_NB) mb_wait(&dempty[b], (unsigned)(((t / TC_NB) - 1) & 1), a.err);
@@ -292,11 +331,10 @@ tc_matmul_kernel(TcArgs a) {
   } else {
     // ---- epilogue warps
     const int q = warp & 3, quarter = (warp - 2) >> 2;
-    const int row = q * 32 + lane, R = blk * TC_M + row;
+    const int row = q * 32 + lane;
     const int cb = quarter * CPT;
     // max exponent per (row, column) over all tiles (:221-222); the row's tile
     // exponents come from the block's exponent table, 16 at a time
-    int Mx[CPT];
     #pragma unroll
     for (int j = 0; j < CPT; ++j) Mx[j] = -100000;
     {
@@ -324,11 +362,10 @@ tc_matmul_kernel(TcArgs a) {
         }
       }
     }
-    long long acc[CPT];
     #pragma unroll
     for (int j = 0; j < CPT; ++j) acc[j] = 0;
-    for (int t = 0; t < NT; ++t) {
-      const int s = t % TC_SA, b = t % TC_NB;
+    for (int t = 0; t < ntl; ++t) {
+      const int s = t % TC_SA, b = t % TC_NB, tg = t_lo + t;
       // the three limb sums of tile t
       mb_wait(&dfull[b], (unsigned)((t / TC_NB) & 1), a.err);
       tc_fence_after();
@@ -352,7 +389,7 @@ tc_matmul_kernel(TcArgs a) {
       // 256 cr + lo is formed as ((256 hh + cr) * 256 + lo): 256 hh + cr fits int32.
       #pragma unroll
       for (int j = 0; j < CPT; j += 4) {
-        const int4 e4 = *reinterpret_cast<const int4*>(xe_s + t * NCB + cb + j);
+        const int4 e4 = *reinterpret_cast<const int4*>(xe_s + tg * NCB + cb + j);
         const int4 x4 = *reinterpret_cast<const int4*>(cx_s + t * NCB + cb + j);
         const int ev4[4] = {e4.x, e4.y, e4.z, e4.w}, cv4[4] = {x4.x, x4.y, x4.z, x4.w};
         #pragma unroll
@@ -366,6 +403,27 @@ tc_matmul_kernel(TcArgs a) {
         }
       }
     }
+    if (ks > 1) {
+      #pragma unroll
+      for (int j = 0; j < CPT; ++j) red[(cb + j) * TC_M + row] = acc[j];
+    }
+  }
+  // ---- split K: cluster rank 0 adds the other CTAs' sums (DSMEM); the
+  // second barrier keeps every CTA's shared memory alive until it is read
+  if (ks > 1) {
+    cluster_sync_all();
+    if (kr == 0 && warp >= 2) {
+      const int q = warp & 3, quarter = (warp - 2) >> 2, row = q * 32 + lane, cb = quarter * CPT;
+      for (int r = 1; r < ks; ++r)
+        #pragma unroll
+        for (int j = 0; j < CPT; ++j) acc[j] += ld_peer_s64(red + (cb + j) * TC_M + row, (unsigned)r);
+    }
+    cluster_sync_all();
+  }
+  if (warp >= 2 && kr == 0) {
+    const int q = warp & 3, quarter = (warp - 2) >> 2;
+    const int row = q * 32 + lane, R = blk * TC_M + row;
+    const int cb = quarter * CPT;
     // ---- epilogue: clip, scale (:229-232), quantize over 16-row output tiles (:233)
     const bool row_ok = R < a.rows;
     #pragma unroll
@@ -423,22 +481,50 @@ tc_matmul_kernel(TcArgs a) {
 }
 
 template <int NCB, int MODE>
-cudaError_t launch_tc_t(const TcArgs& a, cudaStream_t s, bool pdl) {
-  const size_t smem = tc_layout(a.NT, NCB).total;
+cudaError_t launch_tc_t(const TcArgs& a, int ks, cudaStream_t s, bool pdl) {
+  const size_t smem = tc_layout(a.NT, NCB, (a.NT + ks - 1) / ks, ks > 1).total;
   cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<NCB, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
+  if (ks > 1) {
+    e = cudaFuncSetAttribute(tc_matmul_kernel<NCB, MODE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    if (e != cudaSuccess) return e;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.rows + TC_M - 1) / TC_M, (a.ncols + NCB - 1) / NCB);
+  cfg.gridDim = dim3((a.rows + TC_M - 1) / TC_M, (a.ncols + NCB - 1) / NCB, ks);
   cfg.blockDim = dim3(TC_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (ks > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = ks;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<NCB, MODE>, a);
+}
+
+bool tc_config_fits(int NT, int ncb, int ks) {
+  return (ncb == 16 || ncb == 32) && ks >= 1 && ks <= 8 && ks <= NT &&
+         tc_layout(NT, ncb, (NT + ks - 1) / ks, ks > 1).total <= 200 * 1024;
+}
+
+// Without a tuned configuration: no K split; 32 columns per CTA when that
+// grid still covers the SMs, else 16.
+void tc_default_config(int rows, int NT, int ncols, int nsm, int* ncb, int* ks) {
+  const int nblk = (rows + TC_M - 1) / TC_M;
+  *ks = 1;
+  *ncb = (nblk * ((ncols + 31) / 32) >= nsm && tc_config_fits(NT, 32, 1)) ? 32 : 16;
 }
 
 }  // namespace
@@ -453,23 +539,27 @@ cudaError_t launch_tc_pack(const uint8_t* wm, const int8_t* we, int rows, int NT
 
 bool tc_supported(int NT, int ncols) {
   if (ncols < 1 || NT < 1) return false;
-  return tc_layout(NT, 32).total <= 200 * 1024 || tc_layout(NT, 16).total <= 200 * 1024;
+  return tc_config_fits(NT, 16, 1) || tc_config_fits(NT, 16, 8);
 }
 
+bool tc_config_valid(int NT, int ncb, int ks) { return tc_config_fits(NT, ncb, ks); }
+
 cudaError_t launch_tc_matmul(const TcArgs& a, cudaStream_t s, bool pdl) {
-  // 32 columns per CTA when the grid still covers the SMs, else 16
-  int dev = 0, nsm = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  const int nblk = (a.rows + TC_M - 1) / TC_M;
-  const bool wide = nblk * ((a.ncols + 31) / 32) >= nsm && tc_layout(a.NT, 32).total <= 200 * 1024;
-  if (!wide && tc_layout(a.NT, 16).total > 200 * 1024) return cudaErrorInvalidValue;
+  int ncb = a.ncb, ks = a.ks;
+  if (ncb == 0 || ks == 0) {
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    tc_default_config(a.rows, a.NT, a.ncols, nsm, &ncb, &ks);
+  }
+  if (!tc_config_fits(a.NT, ncb, ks)) return cudaErrorInvalidValue;
   if (a.mode == EPI_SWIGLU && (a.rows % 32)) return cudaErrorInvalidValue;
+  const bool w = ncb == 32;
   switch (a.mode) {
-    case EPI_STORE: return wide ? launch_tc_t<32, EPI_STORE>(a, s, pdl) : launch_tc_t<16, EPI_STORE>(a, s, pdl);
+    case EPI_STORE: return w ? launch_tc_t<32, EPI_STORE>(a, ks, s, pdl) : launch_tc_t<16, EPI_STORE>(a, ks, s, pdl);
     case EPI_RESIDUAL:
-      return wide ? launch_tc_t<32, EPI_RESIDUAL>(a, s, pdl) : launch_tc_t<16, EPI_RESIDUAL>(a, s, pdl);
-    case EPI_SWIGLU: return wide ? launch_tc_t<32, EPI_SWIGLU>(a, s, pdl) : launch_tc_t<16, EPI_SWIGLU>(a, s, pdl);
+      return w ? launch_tc_t<32, EPI_RESIDUAL>(a, ks, s, pdl) : launch_tc_t<16, EPI_RESIDUAL>(a, ks, s, pdl);
+    case EPI_SWIGLU: return w ? launch_tc_t<32, EPI_SWIGLU>(a, ks, s, pdl) : launch_tc_t<16, EPI_SWIGLU>(a, ks, s, pdl);
   }
   return cudaErrorInvalidValue;
 }
