@@ -140,6 +140,37 @@ int bfp200_head_shard_group(bfp200_handle* const* hs, int n_dev);
 int bfp200_generate_sharded(bfp200_handle* const* hs, int n_dev, const int32_t* prompt_ids,
                             const int32_t* prompt_lens, int n_seq, int n_gen, int feed_mode, int32_t* out_tokens);
 
+/* Fixed-point ("rtl-exact") leaf ops: the integer arithmetic of the FPGA
+ * modules, as pinned by the reference's per-op golden generators
+ * (rtl/vc707/host/gen_*_bfp_golden.py).  Host buffers; tiles of 16
+ * elements; vectors are contiguous ([vec][D] mantissas, [vec][D/16] tile
+ * exponents).  The ROMs are the caller's (as the RTL's $readmemh files):
+ * exp_lut = exp_lut.hex (1024 x Q1.15), silu_lut = silu_lut.hex (65536 x
+ * int16), turns_q31 = rope_freq_turns.svh (HD/2 x Q0.31).
+ * Replaces: matvec_bfp_engine.sv via gen_matvec_bfp_golden.py:49-104 -- a
+ * running-alignment 48-bit accumulation, one exponent per OUTPUT element
+ * (y_e has D_out entries per column); W_m is [D_out][D_in/16][16]. */
+int bfp200_rtl_matvec(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m, const int8_t* W_e,
+                      int D_out, int D_in, int batch, int16_t* y_m, int8_t* y_e);
+/* Replaces: rmsnorm_bfp.sv via gen_rmsnorm_bfp_golden.py:43-144 (Newton-Raphson
+ * 1/sqrt from a seed table, Q12.12). */
+int bfp200_rtl_rmsnorm(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* g_m, const int8_t* g_e,
+                       int D, int nvec, int16_t* y_m, int8_t* y_e);
+/* Replaces: rope_bfp.sv via gen_rope_bfp_golden.py:25-124 (CORDIC sin/cos);
+ * y_e has one exponent per ELEMENT ([vec][HD]). */
+int bfp200_rtl_rope(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int32_t* pos, int nvec, int HD,
+                    const uint32_t* turns_q31, int16_t* y_m, int8_t* y_e);
+/* Replaces: softmax_bfp.sv via gen_softmax_bfp_golden.py:34-83; one shared
+ * exponent per vector in and out (x_e, y_e: nvec entries). */
+int bfp200_rtl_softmax(bfp200_handle* h, const int16_t* x_m, const int32_t* x_e, int n, int nvec,
+                       const uint16_t* exp_lut, int16_t* y_m, int32_t* y_e);
+/* Replaces: swiglu_bfp.sv via gen_swiglu_bfp_golden.py:45-77; n elements. */
+int bfp200_rtl_swiglu(bfp200_handle* h, const int16_t* gate_m, const int8_t* gate_e, const int16_t* up_m,
+                      const int8_t* up_e, size_t n, const int16_t* silu_lut, int16_t* y_m, int8_t* y_e);
+/* Replaces: the residual adder via gen_residual_bfp_golden.py:20-45. */
+int bfp200_rtl_residual(bfp200_handle* h, const int16_t* a_m, const int8_t* a_e, const int16_t* b_m,
+                        const int8_t* b_e, size_t n, int16_t* y_m, int8_t* y_e);
+
 /* Number of head argmax decisions of the last generate call whose fp64
  * margin did not certify agreement with every summation order (0 means the
  * token stream is independent of the reference's BLAS). */

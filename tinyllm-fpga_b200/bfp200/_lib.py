@@ -63,6 +63,12 @@ SIGNATURES = {
     "bfp200_profile_forward": [_P, _I, _I, _P, _P],
     "bfp200_matvec_noalloc": [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P],
     "bfp200_generate_sampled": [_P, _P, _P, _I, _I, _D, _I, C.c_uint32, _P],
+    "bfp200_rtl_matvec": [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P],
+    "bfp200_rtl_rmsnorm": [_P, _P, _P, _P, _P, _I, _I, _P, _P],
+    "bfp200_rtl_rope": [_P, _P, _P, _P, _I, _I, _P, _P, _P],
+    "bfp200_rtl_softmax": [_P, _P, _P, _I, _I, _P, _P, _P],
+    "bfp200_rtl_swiglu": [_P, _P, _P, _P, _P, _Z, _P, _P, _P],
+    "bfp200_rtl_residual": [_P, _P, _P, _P, _P, _Z, _P, _P],
     "bfp200_nccl_unique_id": [_P],
     "bfp200_head_shard": [_P, _P, _I, _I],
     "bfp200_head_shard_group": [_P, _I],

@@ -931,6 +931,19 @@ int sync_stream(bfp200_handle* h) {
   }
 }
 
+// host <-> device staging of the op-level entry points
+template <typename T>
+int upload(DBuf<T>& d, const T* host, size_t n, cudaStream_t s) {
+  CK(d.ensure(n ? n : 1));
+  if (n) CK(cudaMemcpyAsync(d.p, host, n * sizeof(T), cudaMemcpyHostToDevice, s));
+  return BFP200_OK;
+}
+template <typename T>
+int download(T* host, const DBuf<T>& d, size_t n, cudaStream_t s) {
+  if (n) CK(cudaMemcpyAsync(host, d.p, n * sizeof(T), cudaMemcpyDeviceToHost, s));
+  return BFP200_OK;
+}
+
 int check_cfg(const bfp200_cfg& c) {
   if (c.D <= 0 || c.D % 16 || c.FFN <= 0 || c.FFN % 16 || c.H_Q <= 0 || c.H_KV <= 0 || c.H_Q % c.H_KV ||
       c.HD != 64 || c.H_Q * c.HD != c.D || c.NL <= 0 || c.VOCAB <= 0 || c.VOCAB % 16 || c.MAX_CTX <= 0 ||
@@ -1757,6 +1770,118 @@ int bfp200_rope_fp(bfp200_handle* h, const double* x, const int32_t* pos, int nv
   CK(cudaMemcpyAsync(dcs.p, cs.data(), cs.size() * 8, cudaMemcpyHostToDevice, h->stream));
   CK(launch_rope_fp(dx.p, dcs.p, HD, nvec, dout.p, h->stream));
   CK(cudaMemcpyAsync(out, dout.p, (size_t)nvec * HD * 8, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+// ---------------------------------------------------------------------------
+// fixed-point ("rtl-exact") leaf ops: host buffers in and out
+// ---------------------------------------------------------------------------
+
+int bfp200_rtl_matvec(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m, const int8_t* W_e,
+                      int D_out, int D_in, int batch, int16_t* y_m, int8_t* y_e) {
+  if (!h || !x_m || !x_e || !W_m || !W_e || !y_m || !y_e || D_out <= 0 || D_in <= 0 || D_in % 16 ||
+      D_in / 16 > 96 || batch <= 0)
+    return fail(BFP200_EINVAL, "rtl_matvec: bad arguments (D_in a multiple of 16, at most 1536)");
+  CK(cudaSetDevice(h->device));
+  const int NT = D_in / 16;
+  DBuf<int16_t> xm, wm, ym;
+  DBuf<int8_t> xe, we, ye;
+  CKR(upload(xm, x_m, (size_t)batch * D_in, h->stream)); CKR(upload(xe, x_e, (size_t)batch * NT, h->stream));
+  CKR(upload(wm, W_m, (size_t)D_out * D_in, h->stream)); CKR(upload(we, W_e, (size_t)D_out * NT, h->stream));
+  CK(ym.ensure((size_t)batch * D_out)); CK(ye.ensure((size_t)batch * D_out));
+  CK(launch_rtl_matvec(xm.p, xe.p, wm.p, we.p, D_out, NT, batch, ym.p, ye.p, h->stream));
+  CKR(download(y_m, ym, (size_t)batch * D_out, h->stream)); CKR(download(y_e, ye, (size_t)batch * D_out, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_rtl_rmsnorm(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* g_m, const int8_t* g_e,
+                       int D, int nvec, int16_t* y_m, int8_t* y_e) {
+  if (!h || !x_m || !x_e || !g_m || !g_e || !y_m || !y_e || D <= 0 || D % 16 || D / 16 > 96 || nvec <= 0)
+    return fail(BFP200_EINVAL, "rtl_rmsnorm: bad arguments (D a multiple of 16, at most 1536)");
+  CK(cudaSetDevice(h->device));
+  const size_t n = (size_t)nvec * D, nt = n / 16;
+  DBuf<int16_t> xm, gm, ym;
+  DBuf<int8_t> xe, ge, ye;
+  CKR(upload(xm, x_m, n, h->stream)); CKR(upload(xe, x_e, nt, h->stream));
+  CKR(upload(gm, g_m, n, h->stream)); CKR(upload(ge, g_e, nt, h->stream));
+  CK(ym.ensure(n)); CK(ye.ensure(nt));
+  CK(launch_rtl_rmsnorm(xm.p, xe.p, gm.p, ge.p, D, nvec, ym.p, ye.p, h->stream));
+  CKR(download(y_m, ym, n, h->stream)); CKR(download(y_e, ye, nt, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_rtl_rope(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int32_t* pos, int nvec, int HD,
+                    const uint32_t* turns_q31, int16_t* y_m, int8_t* y_e) {
+  if (!h || !x_m || !x_e || !pos || !turns_q31 || !y_m || !y_e || nvec <= 0 || HD <= 0 || HD % 32)
+    return fail(BFP200_EINVAL, "rtl_rope: bad arguments (HD a multiple of 32)");
+  for (int i = 0; i < nvec; ++i)
+    if (pos[i] < 0 || pos[i] >= (1 << 20)) return fail(BFP200_EINVAL, "rtl_rope: position outside 0 .. 2^20-1");
+  CK(cudaSetDevice(h->device));
+  const size_t n = (size_t)nvec * HD;
+  DBuf<int16_t> xm, ym;
+  DBuf<int8_t> xe, ye;
+  DBuf<int> dp;
+  DBuf<unsigned> dt;
+  CKR(upload(xm, x_m, n, h->stream)); CKR(upload(xe, x_e, n / 16, h->stream));
+  CKR(upload(dp, (const int*)pos, (size_t)nvec, h->stream));
+  CKR(upload(dt, (const unsigned*)turns_q31, (size_t)HD / 2, h->stream));
+  CK(ym.ensure(n)); CK(ye.ensure(n));
+  CK(launch_rtl_rope(xm.p, xe.p, dp.p, dt.p, HD, nvec, ym.p, ye.p, h->stream));
+  CKR(download(y_m, ym, n, h->stream)); CKR(download(y_e, ye, n, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_rtl_softmax(bfp200_handle* h, const int16_t* x_m, const int32_t* x_e, int n, int nvec,
+                       const uint16_t* exp_lut, int16_t* y_m, int32_t* y_e) {
+  if (!h || !x_m || !x_e || !exp_lut || !y_m || !y_e || n <= 0 || n > 65536 || nvec <= 0)
+    return fail(BFP200_EINVAL, "rtl_softmax: bad arguments (1 <= n <= 65536)");
+  CK(cudaSetDevice(h->device));
+  const size_t nn = (size_t)nvec * n;
+  DBuf<int16_t> xm, ym;
+  DBuf<int> xe, ye;
+  DBuf<uint16_t> lut;
+  CKR(upload(xm, x_m, nn, h->stream)); CKR(upload(xe, (const int*)x_e, (size_t)nvec, h->stream));
+  CKR(upload(lut, exp_lut, 1024, h->stream));
+  CK(ym.ensure(nn)); CK(ye.ensure((size_t)nvec));
+  CK(launch_rtl_softmax(xm.p, xe.p, n, nvec, lut.p, ym.p, ye.p, h->stream));
+  CKR(download(y_m, ym, nn, h->stream)); CKR(download((int*)y_e, ye, (size_t)nvec, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_rtl_swiglu(bfp200_handle* h, const int16_t* gate_m, const int8_t* gate_e, const int16_t* up_m,
+                      const int8_t* up_e, size_t n, const int16_t* silu_lut, int16_t* y_m, int8_t* y_e) {
+  if (!h || !gate_m || !gate_e || !up_m || !up_e || !silu_lut || !y_m || !y_e || n == 0 || n % 16)
+    return fail(BFP200_EINVAL, "rtl_swiglu: bad arguments (n a multiple of 16)");
+  CK(cudaSetDevice(h->device));
+  DBuf<int16_t> gm, um, ym, lut;
+  DBuf<int8_t> ge, ue, ye;
+  CKR(upload(gm, gate_m, n, h->stream)); CKR(upload(ge, gate_e, n / 16, h->stream));
+  CKR(upload(um, up_m, n, h->stream)); CKR(upload(ue, up_e, n / 16, h->stream));
+  CKR(upload(lut, silu_lut, 65536, h->stream));
+  CK(ym.ensure(n)); CK(ye.ensure(n / 16));
+  CK(launch_rtl_swiglu(gm.p, ge.p, um.p, ue.p, (long long)(n / 16), lut.p, ym.p, ye.p, h->stream));
+  CKR(download(y_m, ym, n, h->stream)); CKR(download(y_e, ye, n / 16, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return BFP200_OK;
+}
+
+int bfp200_rtl_residual(bfp200_handle* h, const int16_t* a_m, const int8_t* a_e, const int16_t* b_m,
+                        const int8_t* b_e, size_t n, int16_t* y_m, int8_t* y_e) {
+  if (!h || !a_m || !a_e || !b_m || !b_e || !y_m || !y_e || n == 0 || n % 16)
+    return fail(BFP200_EINVAL, "rtl_residual: bad arguments (n a multiple of 16)");
+  CK(cudaSetDevice(h->device));
+  DBuf<int16_t> am, bm, ym;
+  DBuf<int8_t> ae, be, ye;
+  CKR(upload(am, a_m, n, h->stream)); CKR(upload(ae, a_e, n / 16, h->stream));
+  CKR(upload(bm, b_m, n, h->stream)); CKR(upload(be, b_e, n / 16, h->stream));
+  CK(ym.ensure(n)); CK(ye.ensure(n / 16));
+  CK(launch_rtl_residual(am.p, ae.p, bm.p, be.p, (long long)(n / 16), ym.p, ye.p, h->stream));
+  CKR(download(y_m, ym, n, h->stream)); CKR(download(y_e, ye, n / 16, h->stream));
   CK(cudaStreamSynchronize(h->stream));
   return BFP200_OK;
 }

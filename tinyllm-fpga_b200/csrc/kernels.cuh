@@ -240,6 +240,24 @@ cudaError_t launch_sample(const SampleArgs& a, int ncols, int plan_leaves, cudaS
 // n uniforms of numpy's legacy generator after np.random.seed(seed)
 void mt19937_uniforms(uint32_t seed, int n, double* out);
 
+// Fixed-point ("rtl-exact") leaf ops of the FPGA modules (rtl.cu), batched;
+// device pointers.  Layouts: tile-major mantissas [vec][D], tile exponents
+// [vec][D/16]; matvec W [R][NT][16] + [R][NT], outputs [batch][R] with one
+// exponent per element; rope exponents out [vec][HD] (per element); softmax
+// one exponent per vector.
+cudaError_t launch_rtl_matvec(const int16_t* xm, const int8_t* xe, const int16_t* wm, const int8_t* we, int R,
+                              int NT, int batch, int16_t* ym, int8_t* ye, cudaStream_t s);
+cudaError_t launch_rtl_rmsnorm(const int16_t* xm, const int8_t* xe, const int16_t* gm, const int8_t* ge, int D,
+                               int nvec, int16_t* ym, int8_t* ye, cudaStream_t s);
+cudaError_t launch_rtl_rope(const int16_t* xm, const int8_t* xe, const int* pos, const unsigned* turns, int HD,
+                            int nvec, int16_t* ym, int8_t* ye, cudaStream_t s);
+cudaError_t launch_rtl_softmax(const int16_t* xm, const int* xe, int n, int nvec, const uint16_t* lut, int16_t* ym,
+                               int* ye, cudaStream_t s);
+cudaError_t launch_rtl_swiglu(const int16_t* gm, const int8_t* ge, const int16_t* um, const int8_t* ue,
+                              long long ntiles, const int16_t* lut, int16_t* ym, int8_t* ye, cudaStream_t s);
+cudaError_t launch_rtl_residual(const int16_t* am, const int8_t* ae, const int16_t* bm, const int8_t* be,
+                                long long ntiles, int16_t* ym, int8_t* ye, cudaStream_t s);
+
 bool head_small_supported(int ncols, int D);
 cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
                               const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, int ncols,
