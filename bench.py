@@ -211,7 +211,9 @@ def run_ours(args, world, rank, local):
     achieved_gbs = wbytes / (mm["ms_per_token"] / 1e3) / 1e9
     peak = pk["hbm_gbs"]
     roof = {"kernel": "gemv_kernel (fused QKV / O / gate-up / down matvecs, bs1)", "bound": "hbm", "achieved": round(achieved_gbs, 1),
-            "peak": peak, "unit": "GB/s", "frac": round(achieved_gbs / peak, 4), "traffic": None,
+            "peak": peak, "unit": "GB/s", "frac": round(achieved_gbs / peak, 4), "traffic": GEMV_TRAFFIC_PER_TOKEN,
+            "traffic_unit": "bytes per token (120 launches, ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+            "algorithmic_bytes": wbytes,
             "peak_kind": pk_kind, "launches_per_token": mm["launches"],
             "us_per_launch": round(mm["ms_per_token"] * 1e3 / mm["launches"], 3)}
     # whole-path roofline: weights + KV per token over the decode time
@@ -301,6 +303,12 @@ def sharded_head_run(dec, prompts, n_gen, args, world, replica_tok_ms):
             "replica_decode_us_per_token": round(replica_tok_ms * 1e3, 2),
             "vocab_rows_per_rank": 49152 // world, "exchange": "NCCL all-gather of 32 B per rank per step"}
 
+
+# DRAM bytes (read + write) of one token's 120 gemv_kernel launches, from an
+# ncu capture of one decode-graph replay (dram__bytes_read.sum +
+# dram__bytes_write.sum over the launches); the algorithmic weight bytes are
+# 218,972,160, the rest is activations, gammas and the RoPE table.
+GEMV_TRAFFIC_PER_TOKEN = 225_038_080
 
 LAYER_MACS = 106_168_320      # int16 MACs of one token's 4 x 30 layer matvecs (head excluded)
 
