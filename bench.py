@@ -256,6 +256,7 @@ def run_ours(args, world, rank, local):
         cfg5 = {"batch": 64, "pos": 2047, "kernel_ms": d5.profile_forward(64, 2047)}
         d5.close()
     del img
+    cfg4 = None if args.no_cfg4 else cfg4_sweep(args.cfg4_batches)
     res = {
         "metric": "BFP decode tok/s (bs1, cfg2)", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
@@ -274,6 +275,7 @@ def run_ours(args, world, rank, local):
         "bs256": bs256,
         "kernel_profile_ms": profile,
         "cfg5": cfg5,
+        "cfg4": cfg4,
         "sharded_head": sharded,
         "uncertified_steps": uncert,
         "image_build_s": round(build_s, 1),
@@ -282,6 +284,32 @@ def run_ours(args, world, rank, local):
     if rank == 0 and not args.no_cpu:
         res["cpu_baseline"] = cpu_baseline(args)
     return res
+
+
+CFG4_SHAPES = ((576, 576), (192, 576), (1536, 576), (576, 1536), (49152, 576))
+
+
+def cfg4_sweep(batches):
+    """configs[3] (cfg4): the isolated BFP matvec over the model's weight
+    shapes (D_out x D_in), mantissas uniform int16, tile exponents uniform in
+    [-20, 4], inputs tile_quantize(N(0,1)), seed 4; device time per call
+    (bfp200_matvec_timed, weights and inputs resident, 10 repetitions) and
+    the rate it implies (weight GB/s, int16 MAC/s)."""
+    from bfp200 import ops
+    rng = np.random.default_rng(4)
+    out = {}
+    for dout, din in CFG4_SHAPES:
+        nt = din // 16
+        W_m = rng.integers(-32768, 32768, size=(dout, nt, 16), dtype=np.int64).astype(np.int16)
+        W_e = rng.integers(-20, 5, size=(dout, nt)).astype(np.int8)
+        row = {}
+        for b in batches:
+            xm, xe = ops.tile_quantize(rng.standard_normal(b * din))
+            _, _, ms = ops.matvec_timed(xm.reshape(b, nt, 16), xe.reshape(b, nt), W_m, W_e, reps=10)
+            row[str(b)] = {"us": round(ms * 1e3, 2), "weight_gbs": round(dout * din * 2.0625 / (ms / 1e3) / 1e9, 1),
+                           "tmacs": round(dout * din * b / (ms / 1e3) / 1e12, 3)}
+        out[f"{dout}x{din}"] = row
+    return out
 
 
 def sharded_head_run(dec, prompts, n_gen, args, world, replica_tok_ms):
@@ -421,6 +449,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--mm-reps", type=int, default=50, help="graph replays for the matmul roofline timing")
     ap.add_argument("--no-cfg5", action="store_true", help="skip the batch-64 / KV-2048 kernel profile")
+    ap.add_argument("--no-cfg4", action="store_true", help="skip the matvec shape x batch sweep")
+    ap.add_argument("--cfg4-batches", type=lambda s: [int(x) for x in s.split(",")], default=[1, 8, 64, 256, 1024],
+                    help="batch sizes of the matvec sweep")
     args = ap.parse_args()
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))

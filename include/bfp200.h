@@ -140,6 +140,13 @@ int bfp200_head_shard_group(bfp200_handle* const* hs, int n_dev);
 int bfp200_generate_sharded(bfp200_handle* const* hs, int n_dev, const int32_t* prompt_ids,
                             const int32_t* prompt_lens, int n_seq, int n_gen, int feed_mode, int32_t* out_tokens);
 
+/* Measurement: bfp200_matvec whose device time (the matvec launch alone,
+ * after one untimed call) is averaged over `reps` back-to-back repetitions;
+ * outputs as bfp200_matvec.  No reference counterpart (cfg4 sweep timing). */
+int bfp200_matvec_timed(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m,
+                        const int8_t* W_e, int D_out, int D_in, int batch, int reps, int16_t* out_m, int8_t* out_e,
+                        double* ms_per_call);
+
 /* Fixed-point ("rtl-exact") leaf ops: the integer arithmetic of the FPGA
  * modules, as pinned by the reference's per-op golden generators
  * (rtl/vc707/host/gen_*_bfp_golden.py).  Host buffers; tiles of 16

@@ -81,6 +81,23 @@ def matvec(X_m, X_e, W_m, W_e):
     return om, oe
 
 
+def matvec_timed(X_m, X_e, W_m, W_e, reps=20):
+    """matvec plus its device time: (m, e, ms per call averaged over `reps`
+    back-to-back launches after one untimed call)."""
+    W_m = arr(W_m, np.int16)
+    W_e = arr(W_e, np.int8)
+    D_out, NT = W_e.shape
+    X_m = arr(X_m, np.int16).reshape(-1, NT * TILE)
+    B = X_m.shape[0]
+    X_e = arr(X_e, np.int8).reshape(B, NT)
+    om = np.empty((B, D_out), np.int16)
+    oe = np.empty((B, D_out // TILE), np.int8)
+    ms = _lib.C.c_double()
+    check(_lib.lib().bfp200_matvec_timed(context(), ptr(X_m), ptr(X_e), ptr(W_m), ptr(W_e), D_out, NT * TILE, B,
+                                         int(reps), ptr(om), ptr(oe), _lib.C.byref(ms)))
+    return om, oe, ms.value
+
+
 def matvec_hw_golden(x_m, x_e, W_m, W_e):
     """Drop-in for the reference's matvec_hw_golden: one column, returns the
     float64 vector fp_quantize_vec(out_real)."""

@@ -235,6 +235,38 @@ __device__ __forceinline__ double np_pw_leaf(const double* a, int n) {
   return res;
 }
 
+// np_pw_leaf by 8 cooperating lanes (lane & 7 = accumulator j, the group
+// aligned to 8 lanes, all 32 lanes executing): each lane runs numpy's
+// accumulator j sequentially, the groups combine
+// ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) by xor shuffles (lower lane = left
+// operand), and lane 0 of the group adds the tail.  Same operations in the
+// same order as np_pw_leaf; the result is valid on lane 0 of each group.
+__device__ __forceinline__ double np_pw_leaf_8lanes(const double* a, int n) {
+  const int j = threadIdx.x & 7;
+  double v = 0.0;
+  if (n >= 8) {
+    const int lim = n - (n % 8);
+    v = a[j];
+    for (int i = 8 + j; i < lim; i += 8) v = __dadd_rn(v, a[i]);
+  }
+  double o = __shfl_xor_sync(0xffffffffu, v, 1);
+  if ((j & 1) == 0) v = __dadd_rn(v, o);
+  o = __shfl_xor_sync(0xffffffffu, v, 2);
+  if ((j & 3) == 0) v = __dadd_rn(v, o);
+  o = __shfl_xor_sync(0xffffffffu, v, 4);
+  if (j == 0) {
+    if (n < 8) {
+      double res = 0.0;
+      for (int i = 0; i < n; ++i) res = __dadd_rn(res, a[i]);
+      v = res;
+    } else {
+      v = __dadd_rn(v, o);
+      for (int i = n - (n % 8); i < n; ++i) v = __dadd_rn(v, a[i]);
+    }
+  }
+  return v;
+}
+
 // Enumerates the leaves of the pairwise tree of size n in order, writing
 // (start, len) pairs; returns the count.  Single thread.
 __device__ __forceinline__ int np_pw_leaves(int n, int* lo_out, int* len_out, int max_leaves) {
@@ -356,9 +388,11 @@ __device__ __forceinline__ double np_sum_warp_plan(const double* a, int n, const
   const unsigned short* starts = plan + 2;
   const unsigned short* lvl = starts + L;
   const unsigned short* ops = lvl + H;
-  for (int k = lane; k < L; k += 32) {
-    const int s0 = starts[k], e0 = (k + 1 < L) ? starts[k + 1] : n;
-    sval[k] = np_pw_leaf(a + s0, e0 - s0);
+  for (int k0 = 0; k0 < L; k0 += 4) {                 // four leaves at a time, 8 lanes each
+    const int k = k0 + (lane >> 3);
+    const int s0 = k < L ? starts[k] : 0, e0 = k < L ? ((k + 1 < L) ? starts[k + 1] : n) : 0;
+    const double v = np_pw_leaf_8lanes(a + s0, e0 - s0);
+    if (k < L && (lane & 7) == 0) sval[k] = v;
   }
   __syncwarp();
   int base = 0;
@@ -383,15 +417,18 @@ __device__ __forceinline__ double np_sum_warp_plan(const double* a, int n, const
 static __device__ __noinline__ double np_sum_warp_generic(const double* a, int n, int* s_lo, int* s_len, double* s_val) {
   const int lane = threadIdx.x & 31;
   if (n <= 128) {
-    double r = 0.0;
-    if (lane == 0) r = __dadd_rn(0.0, np_pw_leaf(a, n));
-    return __shfl_sync(0xffffffffu, r, 0);
+    const double r = np_pw_leaf_8lanes(a, n);
+    return __dadd_rn(0.0, __shfl_sync(0xffffffffu, r, 0));
   }
   int nl = 0;
   if (lane == 0) nl = np_pw_leaves(n, s_lo, s_len, 64);
   nl = __shfl_sync(0xffffffffu, nl, 0);
   __syncwarp();
-  for (int i = lane; i < nl; i += 32) s_val[i] = np_pw_leaf(a + s_lo[i], s_len[i]);
+  for (int i0 = 0; i0 < nl; i0 += 4) {               // four leaves at a time, 8 lanes each
+    const int i = i0 + (lane >> 3);
+    const double v = np_pw_leaf_8lanes(a + (i < nl ? s_lo[i] : 0), i < nl ? s_len[i] : 0);
+    if (i < nl && (lane & 7) == 0) s_val[i] = v;
+  }
   __syncwarp();
   double r = 0.0;
   if (lane == 0) r = __dadd_rn(0.0, np_pw_combine(n, s_val));

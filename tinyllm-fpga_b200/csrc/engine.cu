@@ -379,7 +379,7 @@ struct bfp200_handle {
 
   ~bfp200_handle() {
     if (graph) cudaGraphExecDestroy(graph);       // before the communicator its NCCL node uses
-    if (comm) nccl().comm_destroy(comm);
+    if (comm) nccl().comm_abort(comm);            // local teardown: never waits on other ranks
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -889,7 +889,9 @@ int set_shard(bfp200_handle* h, NcclComm comm, int n, int rank) {
   CK(cudaSetDevice(h->device));
   cudaStreamSynchronize(h->stream);
   if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; h->graph_cols = -1; }
-  if (h->comm) { nccl().comm_destroy(h->comm); h->comm = nullptr; }
+  // local teardown (ncclCommAbort frees the communicator without waiting on
+  // the other ranks; every exchange of this handle has completed or timed out)
+  if (h->comm) { nccl().comm_abort(h->comm); h->comm = nullptr; }
   h->comm = comm;
   h->shard_n = comm ? n : 1;
   h->shard_rank = comm ? rank : 0;
@@ -1644,8 +1646,25 @@ int bfp200_tile_decode(bfp200_handle* h, const int16_t* m, const int8_t* e, size
   return BFP200_OK;
 }
 
+static int matvec_impl(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m,
+                       const int8_t* W_e, int D_out, int D_in, int batch, int16_t* out_m, int8_t* out_e, int reps,
+                       double* ms_per_call);
+
 int bfp200_matvec(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m, const int8_t* W_e,
                   int D_out, int D_in, int batch, int16_t* out_m, int8_t* out_e) {
+  return matvec_impl(h, x_m, x_e, W_m, W_e, D_out, D_in, batch, out_m, out_e, 0, nullptr);
+}
+
+int bfp200_matvec_timed(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m,
+                        const int8_t* W_e, int D_out, int D_in, int batch, int reps, int16_t* out_m, int8_t* out_e,
+                        double* ms_per_call) {
+  if (reps <= 0 || !ms_per_call) return fail(BFP200_EINVAL, "matvec_timed: reps >= 1 and an output required");
+  return matvec_impl(h, x_m, x_e, W_m, W_e, D_out, D_in, batch, out_m, out_e, reps, ms_per_call);
+}
+
+static int matvec_impl(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m,
+                       const int8_t* W_e, int D_out, int D_in, int batch, int16_t* out_m, int8_t* out_e, int reps,
+                       double* ms_per_call) {
   if (!h || !x_m || !x_e || !W_m || !W_e || !out_m || !out_e || D_out <= 0 || D_in <= 0 || D_out % 16 ||
       D_in % 16 || batch <= 0)
     return fail(BFP200_EINVAL, "matvec: bad arguments (D_out, D_in multiples of 16, batch >= 1)");
@@ -1663,25 +1682,42 @@ int bfp200_matvec(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const
   CK(launch_pack_weights(dWm.p, dWe.p, D_out, NT, wm.p, we.p, 1, 0, h->stream));
   DevMat W;
   W.wm = wm.p; W.we = we.p; W.G = G; W.NT = NT;
-  if (tc_path(h, W, batch, EPI_STORE)) {
-    DBuf<uint8_t> rec;
+  DBuf<uint8_t> rec;
+  DBuf<long long> acc; DBuf<unsigned> cnt;
+  const bool tc = tc_path(h, W, batch, EPI_STORE);
+  if (tc) {
     CK(rec.ensure(tc_records_bytes(D_out, NT)));
     CK(launch_tc_pack(wm.p, we.p, D_out, NT, rec.p, h->stream));
-    CKR(enqueue_tc(h, rec.p, W, dxm.p, dxe.p, D_in, NT, batch, EPI_STORE, dom.p, doe.p, D_out, G, nullptr, nullptr));
-    CK(cudaMemcpyAsync(out_m, dom.p, (size_t)batch * D_out * 2, cudaMemcpyDeviceToHost, h->stream));
-    CK(cudaMemcpyAsync(out_e, doe.p, (size_t)batch * G, cudaMemcpyDeviceToHost, h->stream));
-    CK(cudaStreamSynchronize(h->stream));
-    if (read_and_clear_error_flag(h->stream)) return fail(BFP200_ETIMEOUT, "a bounded device wait timed out");
-    return BFP200_OK;
+  } else {
+    const MMPlan p = plan_matmul(G, NT, batch, false, h->nsm);
+    if (p.ks > 1) {
+      CK(acc.ensure((size_t)D_out * batch));
+      CK(cnt.ensure((size_t)G * ((batch + p.bn - 1) / p.bn)));
+    }
   }
-  const MMPlan p = plan_matmul(G, NT, batch, false, h->nsm);
-  DBuf<long long> acc; DBuf<unsigned> cnt;
-  if (p.ks > 1) {
-    CK(acc.ensure((size_t)D_out * batch));
-    CK(cnt.ensure((size_t)G * ((batch + p.bn - 1) / p.bn)));
+  // the matvec only reads its inputs and writes its outputs: repeating it
+  // (timing) leaves the same result
+  auto run = [&]() -> int {
+    if (tc) return enqueue_tc(h, rec.p, W, dxm.p, dxe.p, D_in, NT, batch, EPI_STORE, dom.p, doe.p, D_out, G, nullptr,
+                              nullptr);
+    return enqueue_matmul(h, W, dxm.p, dxe.p, D_in, NT, batch, EPI_STORE, dom.p, doe.p, D_out, G, nullptr, nullptr,
+                          acc.p, cnt.p, batch);
+  };
+  CKR(run());
+  if (reps > 0) {
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0)); CK(cudaEventCreate(&e1));
+    int r = BFP200_OK;
+    CK(cudaEventRecord(e0, h->stream));
+    for (int i = 0; i < reps && r == BFP200_OK; ++i) r = run();
+    CK(cudaEventRecord(e1, h->stream));
+    CK(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0); cudaEventDestroy(e1);
+    if (r != BFP200_OK) return r;
+    *ms_per_call = ms / reps;
   }
-  CKR(enqueue_matmul(h, W, dxm.p, dxe.p, D_in, NT, batch, EPI_STORE, dom.p, doe.p, D_out, G, nullptr, nullptr, acc.p,
-                     cnt.p, batch));
   CK(cudaMemcpyAsync(out_m, dom.p, (size_t)batch * D_out * 2, cudaMemcpyDeviceToHost, h->stream));
   CK(cudaMemcpyAsync(out_e, doe.p, (size_t)batch * G, cudaMemcpyDeviceToHost, h->stream));
   CK(cudaStreamSynchronize(h->stream));

@@ -650,18 +650,25 @@ cudaError_t launch_rope_kv(const int16_t* qkv_m, const int8_t* qkv_e, int16_t* q
 // ---------------------------------------------------------------------------
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_VCHUNK = 256;   // V positions staged in shared memory per pass
+constexpr int ATT_PLAN_MAX = 512; // pairwise-sum plan entries kept in shared memory (3 L + H)
 
+// LANES4: scores with four lanes per position (many columns: more positions in
+// flight per CTA); otherwise one position per thread (1..4 columns: the
+// shortest code and chain).  Separate instantiations keep each variant's
+// executed code small -- at one column the kernel's code is fetched cold on
+// every layer.
+template <bool LANES4>
 __global__ void __launch_bounds__(ATT_THREADS)
 attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
-                 double sqrt_hd, int16_t* am, int8_t* ae, const int* pw_off, const unsigned short* pw_data,
-                 int early) {
+                 double sqrt_hd, double inv_hd, int16_t* am, int8_t* ae, const int* pw_off,
+                 const unsigned short* pw_data, int early) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_qm[64];
   __shared__ int s_qe[4];
   __shared__ double s_red[ATT_THREADS / 32];
   __shared__ double s_bcast;
-  __shared__ int s_lo[96], s_len[96];
   __shared__ double s_val[160];
+  __shared__ unsigned short s_plan[ATT_PLAN_MAX];
   pdl_trigger();
   const int c = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -701,6 +708,19 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
+  // numpy's pairwise-sum plan for this length (host-built table, constant
+  // for the whole run) into shared memory, also before the wait
+  const unsigned short* plan;
+  {
+    const unsigned short* gp = pw_data + pw_off[T];
+    const int np = 3 * (int)gp[0] + (int)gp[1];
+    if (np <= ATT_PLAN_MAX) {
+      for (int i = tid; i < np; i += ATT_THREADS) s_plan[i] = gp[i];
+      plan = s_plan;
+    } else {
+      plan = gp;
+    }
+  }
   if (early) pdl_wait();
   // q of this head and row pos of K / V (written by the previous kernel)
   if (tid < HD) s_qm[tid] = qr_m[(size_t)c * d.HQ * HD + h * HD + tid];
@@ -718,10 +738,43 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   // product); the quad's four tile sums are combined exactly.  Rows beyond
   // the first chunk are read from the arena.  Dividing by a power of two
   // equals multiplying by its exact reciprocal (both round the same real).
-  const bool pow2_hd = (__double_as_longlong(sqrt_hd) & 0x000FFFFFFFFFFFFFLL) == 0;
-  const double inv_hd = 1.0 / sqrt_hd;
+  const bool pow2_hd = inv_hd != 0.0;               // inv_hd: exact 1/sqrt(HD) when that is a power of two
   double lmax = -INFINITY;
-  {
+  if (!LANES4) {
+    for (int t = tid; t < T; t += ATT_THREADS) {
+      uint4 kk[8];
+      unsigned ke4;
+      if (t < n0) {
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) kk[u] = ks[t * 8 + u];
+        ke4 = kes[t];
+      } else {
+        const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) kk[u] = kr[u];
+        ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
+      }
+      long long S[4];
+      int E[4];
+      #pragma unroll
+      for (int jt = 0; jt < 4; ++jt) {
+        const unsigned w[8] = {kk[2 * jt].x, kk[2 * jt].y, kk[2 * jt].z, kk[2 * jt].w,
+                               kk[2 * jt + 1].x, kk[2 * jt + 1].y, kk[2 * jt + 1].z, kk[2 * jt + 1].w};
+        long long sacc = 0;
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          sacc += (long long)s_qm[jt * 16 + 2 * u] * (int)(int16_t)(w[u] & 0xFFFF);
+          sacc += (long long)s_qm[jt * 16 + 2 * u + 1] * (int)(int16_t)(w[u] >> 16);
+        }
+        S[jt] = sacc;
+        E[jt] = s_qe[jt] + (int)(int8_t)(ke4 >> (8 * jt));
+      }
+      const double dot = exact_tile_dot4(S, E);
+      const double v = pow2_hd ? __dmul_rn(dot, inv_hd) : __ddiv_rn(dot, sqrt_hd);
+      sc[t] = v;
+      lmax = v > lmax ? v : lmax;
+    }
+  } else {
     const int jt = tid & 3, qb = lane & ~3;
     const int* qp = s_qm + jt * 16;
     for (int t0 = 0; t0 < T; t0 += ATT_THREADS / 4) {
@@ -778,8 +831,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   for (int t = tid; t < T; t += ATT_THREADS) sc[t] = exp(__dsub_rn(sc[t], mx));
   __syncthreads();
   if (warp == 0) {
-    const double S = pw_off ? np_sum_warp_plan(sc, T, pw_data + pw_off[T], s_val)
-                            : np_sum_warp(sc, T, s_lo, s_len, s_val);
+    const double S = np_sum_warp_plan(sc, T, plan, s_val);
     if (lane == 0) s_bcast = S;
   }
   __syncthreads();
@@ -825,8 +877,15 @@ cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv
                              int ncols, int16_t* am, int8_t* ae, cudaStream_t s, bool pdl, const int* pw_off,
                              const unsigned short* pw_data, bool early_kv) {
   const size_t smem = (((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15)) + ATT_VCHUNK * 264;
-  return launch_ex(attention_kernel, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
-                   cols, d, std::sqrt((double)d.HD), am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
+  if (!pw_off || !pw_data) return cudaErrorInvalidValue;      // the pairwise-sum plans are required
+  const double sq = std::sqrt((double)d.HD);
+  int ex = 0;
+  const double inv = std::frexp(sq, &ex) == 0.5 ? std::ldexp(1.0, 1 - ex) : 0.0;   // 1/sq, exact, or 0
+  if (ncols <= 4)
+    return launch_ex(attention_kernel<false>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv,
+                     layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
+  return launch_ex(attention_kernel<true>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
+                   cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
 }
 
 // ---------------------------------------------------------------------------
@@ -1731,7 +1790,8 @@ cudaError_t init_kernel_attributes() {
   set((const void*)bfp_matmul_kernel<2, true>);
   set((const void*)rmsnorm_quant_kernel);
   set((const void*)head_prep_kernel);
-  set((const void*)attention_kernel);
+  set((const void*)attention_kernel<false>);
+  set((const void*)attention_kernel<true>);
   set((const void*)rmsnorm_fp_kernel);
   set((const void*)softmax_fp_kernel);
   set((const void*)np_sum_kernel);

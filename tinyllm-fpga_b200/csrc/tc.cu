@@ -424,49 +424,75 @@ tc_matmul_kernel(TcArgs a) {
     const int q = warp & 3, quarter = (warp - 2) >> 2;
     const int row = q * 32 + lane, R = blk * TC_M + row;
     const int cb = quarter * CPT;
-    // ---- epilogue: clip, scale (:229-232), quantize over 16-row output tiles (:233)
+    // ---- epilogue: clip, scale (:229-232), quantize over 16-row output tiles
+    // (:233); the CPT columns' quantizations are interleaved (independent
+    // warp-wide reductions)
     const bool row_ok = R < a.rows;
+    double v[CPT];
+    int16_t qm[CPT];
+    int qe[CPT];
     #pragma unroll
     for (int j = 0; j < CPT; ++j) {
-      const int col = c0 + cb + j;
-      const bool valid = row_ok && col < a.ncols;
       long long sacc = acc[j];
       sacc = sacc > SAT_HI ? SAT_HI : (sacc < SAT_LO ? SAT_LO : sacc);
-      const double out_real = (double)sacc * pow2(Mx[j] - 30);
-      int qe;
-      int16_t qm = tile_quantize_16lanes(out_real, &qe);
-      const int cc = col < a.ncols ? col : 0;
-      if constexpr (MODE == EPI_STORE) {
-        if (valid) {
-          a.om[(size_t)cc * a.o_ld + R] = qm;
-          if ((R & 15) == 0) a.oe[(size_t)cc * a.o_lde + R / 16] = (int8_t)qe;
+      v[j] = (double)sacc * pow2(Mx[j] - 30);
+    }
+    tile_quantize_16lanes_n<CPT>(v, qm, qe);
+    if constexpr (MODE == EPI_STORE) {
+      #pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const int col = c0 + cb + j;
+        if (row_ok && col < a.ncols) {
+          a.om[(size_t)col * a.o_ld + R] = qm[j];
+          if ((R & 15) == 0) a.oe[(size_t)col * a.o_lde + R / 16] = (int8_t)qe[j];
         }
-      } else if constexpr (MODE == EPI_RESIDUAL) {
-        const double hv = valid ? bfp_decode(a.rm[(size_t)cc * a.o_ld + R], a.re[(size_t)cc * a.o_lde + R / 16]) : 0.0;
-        qm = tile_quantize_16lanes(__dadd_rn(hv, bfp_decode(qm, qe)), &qe);          // fpq(h + o)
-        if (valid) {
-          a.om[(size_t)cc * a.o_ld + R] = qm;
-          if ((R & 15) == 0) a.oe[(size_t)cc * a.o_lde + R / 16] = (int8_t)qe;
+      }
+    } else if constexpr (MODE == EPI_RESIDUAL) {
+      #pragma unroll
+      for (int j = 0; j < CPT; ++j) {                                                  // fpq(h + o)
+        const int col = c0 + cb + j;
+        const bool valid = row_ok && col < a.ncols;
+        const double hv = valid ? bfp_decode(a.rm[(size_t)col * a.o_ld + R], a.re[(size_t)col * a.o_lde + R / 16])
+                                : 0.0;
+        v[j] = __dadd_rn(hv, bfp_decode(qm[j], qe[j]));
+      }
+      tile_quantize_16lanes_n<CPT>(v, qm, qe);
+      #pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const int col = c0 + cb + j;
+        if (row_ok && col < a.ncols) {
+          a.om[(size_t)col * a.o_ld + R] = qm[j];
+          if ((R & 15) == 0) a.oe[(size_t)col * a.o_lde + R / 16] = (int8_t)qe[j];
         }
-      } else {   // EPI_SWIGLU: lanes 0-15 hold a gate group, lanes 16-31 its up group
-        // every lane runs the warp-wide quantizers; only the gate lanes' results are kept
-        const double mine = bfp_decode(qm, qe);
-        const double other = __shfl_xor_sync(0xffffffffu, mine, 16);
-        const bool is_g = (lane & 16) == 0;
-        const double sv = __ddiv_rn(mine, __dadd_rn(1.0, exp(-mine)));                  // silu_fp (:241-242)
-        int se;
-        const int16_t sm = tile_quantize_16lanes(sv, &se);
-        const double prod = is_g ? __dmul_rn(bfp_decode(sm, se), other) : 0.0;           // (:290)
-        int pe;
-        int16_t pm = tile_quantize_16lanes(prod, &pe);
+      }
+    } else {   // EPI_SWIGLU: lanes 0-15 hold a gate group, lanes 16-31 its up group
+      // every lane runs the warp-wide quantizers; only the gate lanes' results are kept
+      const bool is_g = (lane & 16) == 0;
+      double other[CPT];
+      #pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const double mine = bfp_decode(qm[j], qe[j]);
+        other[j] = __shfl_xor_sync(0xffffffffu, mine, 16);
+        v[j] = __ddiv_rn(mine, __dadd_rn(1.0, exp(-mine)));                             // silu_fp (:241-242)
+      }
+      tile_quantize_16lanes_n<CPT>(v, qm, qe);
+      #pragma unroll
+      for (int j = 0; j < CPT; ++j) v[j] = is_g ? __dmul_rn(bfp_decode(qm[j], qe[j]), other[j]) : 0.0;   // (:290)
+      tile_quantize_16lanes_n<CPT>(v, qm, qe);
+      const int ug = R / 32;                                                             // mlp group of the pair
+      #pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const int col = c0 + cb + j;
+        const bool valid = row_ok && col < a.ncols;
+        int16_t pm = qm[j];
+        int pe = qe[j];
         const unsigned bal = __ballot_sync(0xffffffffu, is_g && valid && pm == (int16_t)-32768);
         const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
         pm = requant_mant(pm, has_min && pe < 127);                                     // (:291)
         pe = requant_exp(pe, has_min);
-        const int ug = R / 32;                                                           // mlp group of the pair
         if (is_g && valid) {
-          a.om[(size_t)cc * a.o_ld + ug * 16 + (lane & 15)] = pm;
-          if ((lane & 15) == 0) a.oe[(size_t)cc * a.o_lde + ug] = (int8_t)pe;
+          a.om[(size_t)col * a.o_ld + ug * 16 + (lane & 15)] = pm;
+          if ((lane & 15) == 0) a.oe[(size_t)col * a.o_lde + ug] = (int8_t)pe;
         }
       }
     }
