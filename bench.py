@@ -118,6 +118,7 @@ def dist_init():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ["BFP200_DEVICE"] = str(local)       # the op-level helpers' device (bfp200.ops)
     if world > 1:
         import datetime
         import torch
@@ -139,7 +140,7 @@ def max_over_ranks(x, world):
         return x
     import torch
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -149,7 +150,7 @@ def sum_over_ranks(x, world):
         return x
     import torch
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
 
@@ -248,7 +249,7 @@ def run_ours(args, world, rank, local):
         sharded = sharded_head_run(dec, prompts2, ngen2, args, world, decode_tok_ms)
     dec.close()
     cfg5 = None
-    if not args.no_cfg5:
+    if not args.no_cfg5 and rank == 0:                  # per-GPU kernel profile: rank 0
         # cfg5: leaf ops and attention at batch 64, KV length 2048 (serialised
         # per-kernel times of one forward pass at position 2047)
         d5 = Decoder(BfpConfig(MAX_CTX=2048, max_seqs=64), device=local)
@@ -256,7 +257,7 @@ def run_ours(args, world, rank, local):
         cfg5 = {"batch": 64, "pos": 2047, "kernel_ms": d5.profile_forward(64, 2047)}
         d5.close()
     del img
-    cfg4 = None if args.no_cfg4 else cfg4_sweep(args.cfg4_batches)
+    cfg4 = None if (args.no_cfg4 or rank != 0) else cfg4_sweep(args.cfg4_batches)   # per-GPU: rank 0
     res = {
         "metric": "BFP decode tok/s (bs1, cfg2)", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,

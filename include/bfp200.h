@@ -118,7 +118,10 @@ int bfp200_generate_multi(bfp200_handle* const* hs, int n_dev, const int32_t* pr
  * gen_smollm_blockfp_full.py:439-440: lowest index on ties).  NCCL is loaded
  * at run time (libnccl.so.2 already in the process, else $BFP200_NCCL_LIB,
  * else the loader's search path); NVLS is left off unless NCCL_NVLS_ENABLE
- * is set.  A sharded handle's generate must be called on every rank with the
+ * is set, and peers connect at communicator creation unless
+ * NCCL_RUNTIME_CONNECT is set (the first exchange then never blocks the host
+ * inside a graph capture).  Joining a group makes one exchange.  A sharded
+ * handle's generate must be called on every rank with the
  * same arguments; its waits give up after $BFP200_NCCL_TIMEOUT_S seconds
  * (default 120), abort the communicator and return BFP200_ETIMEOUT.
  * Replaces: nothing in the reference (single FPGA, unsharded head :437-440). */

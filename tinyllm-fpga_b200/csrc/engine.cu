@@ -248,6 +248,21 @@ __global__ void scatter_tokens_kernel(const int* tok, const int* cert, const int
 
 int bfp200_set_error(int code, const std::string& msg) { return fail(code, msg); }
 
+// Makes a handle's device current for one entry point and restores the
+// caller's device afterwards (callers such as torch keep their own notion of
+// the current device).
+struct DeviceGuard {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    err = cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
 // ---------------------------------------------------------------------------
 // NCCL, loaded at run time: only the vocabulary-sharded head uses it, so the
 // library itself does not depend on libnccl.  The types are NCCL's C ABI
@@ -266,6 +281,8 @@ struct NcclApi {
   int (*comm_abort)(NcclComm) = nullptr;
   int (*async_error)(NcclComm, int*) = nullptr;
   const char* (*error_string)(int) = nullptr;
+  int (*group_start)() = nullptr;
+  int (*group_end)() = nullptr;
   bool ok = false;
 };
 
@@ -289,8 +306,10 @@ const NcclApi& nccl() {
     api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
     api.async_error = reinterpret_cast<decltype(api.async_error)>(sym("ncclCommGetAsyncError"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+    api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
+    api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
     api.ok = api.get_unique_id && api.comm_init_rank && api.comm_init_all && api.all_gather && api.comm_destroy &&
-             api.comm_abort && api.async_error && api.error_string;
+             api.comm_abort && api.async_error && api.error_string && api.group_start && api.group_end;
   });
   return api;
 }
@@ -300,9 +319,15 @@ std::string nccl_err(int r) {
   return a.error_string ? std::string(a.error_string(r)) : "NCCL error " + std::to_string(r);
 }
 
-// small exchanges gain nothing from NVLink SHARP; keep the multicast objects
-// unbound unless the caller asked for them
-void nccl_env_defaults() { setenv("NCCL_NVLS_ENABLE", "0", /*overwrite=*/0); }
+// Small exchanges gain nothing from NVLink SHARP: keep the multicast objects
+// unbound.  Connect every peer at communicator creation (NCCL otherwise
+// connects on the first collective, a host-side exchange that would block an
+// exchange captured in a graph, or wait forever for a rank that never comes).
+// Caller settings win.
+void nccl_env_defaults() {
+  setenv("NCCL_NVLS_ENABLE", "0", /*overwrite=*/0);
+  setenv("NCCL_RUNTIME_CONNECT", "0", /*overwrite=*/0);
+}
 
 struct bfp200_handle {
   bfp200_cfg cfg{};
@@ -358,7 +383,7 @@ struct bfp200_handle {
   // one record per column with the other ranks (xsend -> xrecv, all-gather)
   NcclComm comm = nullptr;
   int shard_n = 1, shard_rank = 0, v_lo = 0, v_hi = 0;
-  DBuf<double> xsend, xrecv;
+  DBuf<double> xsend, xrecv, xwarm;
   // sampling (bfp200_generate_sampled): full logits, scratch, uniforms, and
   // numpy's pairwise-sum plan for the vocabulary length
   DBuf<double> s_logits, s_work, s_cdf, s_uni;
@@ -886,7 +911,8 @@ bool persist_ok(bfp200_handle* h, int ncols) {
 // Leaves any sharding (destroys the decode graph first: it holds the
 // communicator's all-gather) and joins `comm` as rank `rank` of `n`.
 int set_shard(bfp200_handle* h, NcclComm comm, int n, int rank) {
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   cudaStreamSynchronize(h->stream);
   if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; h->graph_cols = -1; }
   // local teardown (ncclCommAbort frees the communicator without waiting on
@@ -901,6 +927,16 @@ int set_shard(bfp200_handle* h, NcclComm comm, int n, int rank) {
     CK(h->xsend.ensure((size_t)h->cap * 4));
     CK(h->xrecv.ensure((size_t)h->shard_n * h->cap * 4));
   }
+  if (comm) CK(h->xwarm.ensure((size_t)(h->shard_n + 1) * 4));
+  return BFP200_OK;
+}
+
+// One all-gather on a freshly joined communicator (every rank makes it at
+// the same point), outside any graph capture, waited for with the bounded
+// poll: the exchange path is exercised once before decode graphs hold it.
+int enqueue_warm_exchange(bfp200_handle* h) {
+  const int r = nccl().all_gather(h->xwarm.p, h->xwarm.p + 4, 4, NCCL_F64, h->comm, h->stream);
+  if (r != NCCL_OK && r != NCCL_IN_PROGRESS) return fail(BFP200_ECUDA, "ncclAllGather: " + nccl_err(r));
   return BFP200_OK;
 }
 
@@ -1003,7 +1039,8 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
   CK(cudaGetDeviceProperties(&prop, device));
   if (prop.major != 10) return fail(BFP200_ENODEV, "libbfp200 is built for sm_100a (B200); device is sm_" +
                                                        std::to_string(prop.major) + std::to_string(prop.minor));
-  CK(cudaSetDevice(device));
+  DeviceGuard dguard(device);
+  CK(dguard.err);
   CK(init_kernel_attributes());
   auto* h = new bfp200_handle();
   h->cfg = *cfg;
@@ -1052,7 +1089,7 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
 
 int bfp200_close(bfp200_handle* h) {
   if (!h) return BFP200_OK;
-  cudaSetDevice(h->device);
+  DeviceGuard dguard(h->device);
   cudaStreamSynchronize(h->stream);
   delete h;
   return BFP200_OK;
@@ -1077,7 +1114,8 @@ static int upload_gammas(bfp200_handle* h) {
 
 int bfp200_load_image(bfp200_handle* h, const void* img, size_t len) {
   if (!h || !img) return fail(BFP200_EINVAL, "load_image: null argument");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   const auto rs = image_regions(h->cfg);
   const size_t total = find_region(rs, "END")->off;
   if (len != total)
@@ -1164,7 +1202,8 @@ int bfp200_load_image(bfp200_handle* h, const void* img, size_t len) {
 
 int bfp200_load_rom(bfp200_handle* h, int kind, const uint16_t* entries, size_t n) {
   if (!h || (!entries && n)) return fail(BFP200_EINVAL, "load_rom: null argument");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   const size_t nld = (size_t)h->NL * h->D, nlt = (size_t)h->NL * h->NTD;
   auto put16 = [&](std::vector<int16_t>& v, size_t want) -> int {
     if (n != want) return fail(BFP200_EIMAGE, "load_rom kind " + std::to_string(kind) + ": " + std::to_string(n) +
@@ -1244,7 +1283,8 @@ static int generate_impl(bfp200_handle* h, const int32_t* prompt_ids, const int3
   }
   for (int32_t t : ids)
     if (t < 0 || t >= h->V) return fail(BFP200_EINVAL, "token id outside the vocabulary");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   CKR(ensure_kv(h, n_seq));
   // ---- prefill: every prompt position, position-major
   const int PREFILL_CHUNK = 1024;
@@ -1444,14 +1484,17 @@ int bfp200_head_shard(bfp200_handle* h, const uint8_t* id, int nranks, int rank)
   if (nranks > h->V) return fail(BFP200_EINVAL, "head_shard: more ranks than vocabulary rows");
   const NcclApi& a = nccl();
   if (!a.ok) return fail(BFP200_ENODEV, "NCCL (libnccl.so.2) could not be loaded");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   nccl_env_defaults();
   NcclUid u;
   std::memcpy(u.internal, id, BFP200_NCCL_ID_BYTES);
   NcclComm c = nullptr;
   const int r = a.comm_init_rank(&c, nranks, u, rank);
   if (r != NCCL_OK) return fail(BFP200_ECUDA, "ncclCommInitRank: " + nccl_err(r));
-  return set_shard(h, c, nranks, rank);
+  CKR(set_shard(h, c, nranks, rank));
+  CKR(enqueue_warm_exchange(h));
+  return sync_stream(h);
 }
 
 int bfp200_head_shard_group(bfp200_handle* const* hs, int n_dev) {
@@ -1466,12 +1509,26 @@ int bfp200_head_shard_group(bfp200_handle* const* hs, int n_dev) {
   if (n_dev == 1) return set_shard(hs[0], nullptr, 1, 0);
   const NcclApi& a = nccl();
   if (!a.ok) return fail(BFP200_ENODEV, "NCCL (libnccl.so.2) could not be loaded");
+  DeviceGuard dguard(hs[0]->device);
   for (int d = 0; d < n_dev; ++d) CKR(set_shard(hs[d], nullptr, 1, 0));
   nccl_env_defaults();
   std::vector<NcclComm> comms(n_dev, nullptr);
   const int r = a.comm_init_all(comms.data(), n_dev, devs.data());
   if (r != NCCL_OK) return fail(BFP200_ECUDA, "ncclCommInitAll: " + nccl_err(r));
   for (int d = 0; d < n_dev; ++d) CKR(set_shard(hs[d], comms[d], n_dev, d));
+  // one thread drives every device here: the warm exchange is one NCCL group
+  int rg = a.group_start();
+  for (int d = 0; d < n_dev && rg == NCCL_OK; ++d) {
+    cudaSetDevice(hs[d]->device);
+    if (enqueue_warm_exchange(hs[d]) != BFP200_OK) rg = -1;
+  }
+  const int re = a.group_end();
+  if (rg != NCCL_OK || (re != NCCL_OK && re != NCCL_IN_PROGRESS))
+    return fail(BFP200_ECUDA, "warm exchange of the sharded head failed");
+  for (int d = 0; d < n_dev; ++d) {
+    DeviceGuard g(hs[d]->device);
+    CKR(sync_stream(hs[d]));
+  }
   return BFP200_OK;
 }
 
@@ -1532,7 +1589,8 @@ int bfp200_profile_forward(bfp200_handle* h, int ncols, int pos, double* ms_by_k
   if (!h->have_image) return fail(BFP200_ESTATE, "profile_forward before load_image");
   if (ncols > h->cfg.max_seqs || pos < 0 || pos >= h->MAXC) return fail(BFP200_EINVAL, "profile_forward: ncols/pos");
   if (h->comm) return fail(BFP200_ESTATE, "profile_forward: not on a handle with a sharded head");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   CKR(ensure_kv(h, ncols));
   CKR(ensure_cols(h, ncols));
   std::vector<int> slots(ncols), poss(ncols, pos), toks(ncols, 0);
@@ -1570,7 +1628,8 @@ int bfp200_profile_forward(bfp200_handle* h, int ncols, int pos, double* ms_by_k
 int bfp200_time_matmuls(bfp200_handle* h, int ncols, int reps, double* ms_per_token, int* launches_per_token) {
   if (!h || ncols <= 0 || reps <= 0 || !ms_per_token) return fail(BFP200_EINVAL, "time_matmuls: bad arguments");
   if (!h->have_image) return fail(BFP200_ESTATE, "time_matmuls before load_image");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   CKR(ensure_cols(h, ncols));
   const bool small = small_path_ok(h, ncols);
   auto body = [&]() -> int {
@@ -1621,7 +1680,8 @@ int bfp200_time_matmuls(bfp200_handle* h, int ncols, int reps, double* ms_per_to
 int bfp200_tile_quantize(bfp200_handle* h, const double* v, size_t n, int16_t* m, int8_t* e) {
   if (!h || (n && (!v || !m || !e)) || n % 16) return fail(BFP200_EINVAL, "tile_quantize: bad arguments");
   if (!n) return BFP200_OK;
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   DBuf<double> dv; DBuf<int16_t> dm; DBuf<int8_t> de;
   CK(dv.ensure(n)); CK(dm.ensure(n)); CK(de.ensure(n / 16));
   CK(cudaMemcpyAsync(dv.p, v, n * 8, cudaMemcpyHostToDevice, h->stream));
@@ -1635,7 +1695,8 @@ int bfp200_tile_quantize(bfp200_handle* h, const double* v, size_t n, int16_t* m
 int bfp200_tile_decode(bfp200_handle* h, const int16_t* m, const int8_t* e, size_t n, double* v) {
   if (!h || (n && (!v || !m || !e)) || n % 16) return fail(BFP200_EINVAL, "tile_decode: bad arguments");
   if (!n) return BFP200_OK;
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   DBuf<double> dv; DBuf<int16_t> dm; DBuf<int8_t> de;
   CK(dv.ensure(n)); CK(dm.ensure(n)); CK(de.ensure(n / 16));
   CK(cudaMemcpyAsync(dm.p, m, n * 2, cudaMemcpyHostToDevice, h->stream));
@@ -1668,7 +1729,8 @@ static int matvec_impl(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, 
   if (!h || !x_m || !x_e || !W_m || !W_e || !out_m || !out_e || D_out <= 0 || D_in <= 0 || D_out % 16 ||
       D_in % 16 || batch <= 0)
     return fail(BFP200_EINVAL, "matvec: bad arguments (D_out, D_in multiples of 16, batch >= 1)");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   const int NT = D_in / 16, G = D_out / 16;
   DBuf<int16_t> dWm, dxm, dom; DBuf<int8_t> dWe, dxe, doe; DBuf<uint8_t> wm; DBuf<int8_t> we;
   CK(dWm.ensure((size_t)D_out * D_in)); CK(dWe.ensure((size_t)D_out * NT));
@@ -1729,7 +1791,8 @@ int bfp200_rmsnorm_fp(bfp200_handle* h, const double* x, const double* gamma, in
                       double* out) {
   if (!h || !x || !gamma || !out || n <= 0 || n % 16 || ncols <= 0 || n > 8192)
     return fail(BFP200_EINVAL, "rmsnorm_fp: bad arguments");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   DBuf<double> dx, dg, dout;
   CK(dx.ensure((size_t)n * ncols)); CK(dg.ensure(n)); CK(dout.ensure((size_t)n * ncols));
   CK(cudaMemcpyAsync(dx.p, x, (size_t)n * ncols * 8, cudaMemcpyHostToDevice, h->stream));
@@ -1743,7 +1806,8 @@ int bfp200_rmsnorm_fp(bfp200_handle* h, const double* x, const double* gamma, in
 int bfp200_silu_fp(bfp200_handle* h, const double* x, size_t n, double* out) {
   if (!h || (n && (!x || !out)) || n % 16) return fail(BFP200_EINVAL, "silu_fp: bad arguments");
   if (!n) return BFP200_OK;
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   DBuf<double> dx, dout;
   CK(dx.ensure(n)); CK(dout.ensure(n));
   CK(cudaMemcpyAsync(dx.p, x, n * 8, cudaMemcpyHostToDevice, h->stream));
@@ -1755,7 +1819,8 @@ int bfp200_silu_fp(bfp200_handle* h, const double* x, size_t n, double* out) {
 
 int bfp200_softmax_fp(bfp200_handle* h, const double* x, int n, int ncols, double* out) {
   if (!h || !x || !out || n <= 0 || ncols <= 0 || n > 4096) return fail(BFP200_EINVAL, "softmax_fp: bad arguments");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   DBuf<double> dx, dout;
   CK(dx.ensure((size_t)n * ncols)); CK(dout.ensure((size_t)n * ncols));
   CK(cudaMemcpyAsync(dx.p, x, (size_t)n * ncols * 8, cudaMemcpyHostToDevice, h->stream));
@@ -1767,7 +1832,8 @@ int bfp200_softmax_fp(bfp200_handle* h, const double* x, int n, int ncols, doubl
 
 int bfp200_pairwise_sum(bfp200_handle* h, const double* x, int n, int ncols, double* out) {
   if (!h || !x || !out || n <= 0 || ncols <= 0 || n > 3072) return fail(BFP200_EINVAL, "pairwise_sum: bad arguments");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   DBuf<double> dx, dout;
   CK(dx.ensure((size_t)n * ncols)); CK(dout.ensure(ncols));
   CK(cudaMemcpyAsync(dx.p, x, (size_t)n * ncols * 8, cudaMemcpyHostToDevice, h->stream));
@@ -1786,7 +1852,8 @@ int bfp200_pairwise_sum(bfp200_handle* h, const double* x, int n, int ncols, dou
 
 int bfp200_rope_fp(bfp200_handle* h, const double* x, const int32_t* pos, int nvec, int HD, double base, double* out) {
   if (!h || !x || !pos || !out || nvec <= 0 || HD <= 0 || HD % 32) return fail(BFP200_EINVAL, "rope_fp: bad arguments");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   std::vector<double> cs((size_t)nvec * HD);
   for (int i = 0; i < nvec; ++i) {
     if (pos[i] < 0) return fail(BFP200_EINVAL, "rope_fp: negative position");
@@ -1819,7 +1886,8 @@ int bfp200_rtl_matvec(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, c
   if (!h || !x_m || !x_e || !W_m || !W_e || !y_m || !y_e || D_out <= 0 || D_in <= 0 || D_in % 16 ||
       D_in / 16 > 96 || batch <= 0)
     return fail(BFP200_EINVAL, "rtl_matvec: bad arguments (D_in a multiple of 16, at most 1536)");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   const int NT = D_in / 16;
   DBuf<int16_t> xm, wm, ym;
   DBuf<int8_t> xe, we, ye;
@@ -1836,7 +1904,8 @@ int bfp200_rtl_rmsnorm(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, 
                        int D, int nvec, int16_t* y_m, int8_t* y_e) {
   if (!h || !x_m || !x_e || !g_m || !g_e || !y_m || !y_e || D <= 0 || D % 16 || D / 16 > 96 || nvec <= 0)
     return fail(BFP200_EINVAL, "rtl_rmsnorm: bad arguments (D a multiple of 16, at most 1536)");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   const size_t n = (size_t)nvec * D, nt = n / 16;
   DBuf<int16_t> xm, gm, ym;
   DBuf<int8_t> xe, ge, ye;
@@ -1855,7 +1924,8 @@ int bfp200_rtl_rope(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, con
     return fail(BFP200_EINVAL, "rtl_rope: bad arguments (HD a multiple of 32)");
   for (int i = 0; i < nvec; ++i)
     if (pos[i] < 0 || pos[i] >= (1 << 20)) return fail(BFP200_EINVAL, "rtl_rope: position outside 0 .. 2^20-1");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   const size_t n = (size_t)nvec * HD;
   DBuf<int16_t> xm, ym;
   DBuf<int8_t> xe, ye;
@@ -1875,7 +1945,8 @@ int bfp200_rtl_softmax(bfp200_handle* h, const int16_t* x_m, const int32_t* x_e,
                        const uint16_t* exp_lut, int16_t* y_m, int32_t* y_e) {
   if (!h || !x_m || !x_e || !exp_lut || !y_m || !y_e || n <= 0 || n > 65536 || nvec <= 0)
     return fail(BFP200_EINVAL, "rtl_softmax: bad arguments (1 <= n <= 65536)");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   const size_t nn = (size_t)nvec * n;
   DBuf<int16_t> xm, ym;
   DBuf<int> xe, ye;
@@ -1893,7 +1964,8 @@ int bfp200_rtl_swiglu(bfp200_handle* h, const int16_t* gate_m, const int8_t* gat
                       const int8_t* up_e, size_t n, const int16_t* silu_lut, int16_t* y_m, int8_t* y_e) {
   if (!h || !gate_m || !gate_e || !up_m || !up_e || !silu_lut || !y_m || !y_e || n == 0 || n % 16)
     return fail(BFP200_EINVAL, "rtl_swiglu: bad arguments (n a multiple of 16)");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   DBuf<int16_t> gm, um, ym, lut;
   DBuf<int8_t> ge, ue, ye;
   CKR(upload(gm, gate_m, n, h->stream)); CKR(upload(ge, gate_e, n / 16, h->stream));
@@ -1910,7 +1982,8 @@ int bfp200_rtl_residual(bfp200_handle* h, const int16_t* a_m, const int8_t* a_e,
                         const int8_t* b_e, size_t n, int16_t* y_m, int8_t* y_e) {
   if (!h || !a_m || !a_e || !b_m || !b_e || !y_m || !y_e || n == 0 || n % 16)
     return fail(BFP200_EINVAL, "rtl_residual: bad arguments (n a multiple of 16)");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   DBuf<int16_t> am, bm, ym;
   DBuf<int8_t> ae, be, ye;
   CKR(upload(am, a_m, n, h->stream)); CKR(upload(ae, a_e, n / 16, h->stream));
@@ -1940,7 +2013,8 @@ int bfp200_fwd_layer(bfp200_handle* h, int layer, const double* h_in, const int3
     if (pos[c] < 0 || pos[c] >= h->MAXC || kv_pos[c] < 0 || kv_pos[c] >= h->MAXC || kv_pos[c] >= max_ctx ||
         pos[c] != kv_pos[c])
       return fail(BFP200_EINVAL, "fwd_layer: positions must satisfy pos == kv_pos < min(MAX_CTX, max_ctx)");
-  CK(cudaSetDevice(h->device));
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
   CKR(ensure_kv(h, ncols));
   CKR(ensure_cols(h, ncols));
   const int D = h->D, HKV = h->HKV, HD = h->HD;

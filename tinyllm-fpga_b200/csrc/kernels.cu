@@ -649,7 +649,10 @@ cudaError_t launch_rope_kv(const int16_t* qkv_m, const int8_t* qkv_e, int16_t* q
 // accumulation attn += sm[t] * v[t], fpq, then tile_quantize for the O matvec.
 // ---------------------------------------------------------------------------
 constexpr int ATT_THREADS = 256;
-constexpr int ATT_VCHUNK = 256;   // V positions staged in shared memory per pass
+// K / V positions staged in shared memory per pass: 256 at 1-4 columns (one
+// pass for the usual contexts), 128 batched (half the shared memory, so four
+// CTAs fit an SM and more sequential accumulations run side by side)
+__host__ __device__ constexpr int att_vchunk(bool lanes4) { return lanes4 ? 128 : 256; }
 constexpr int ATT_PLAN_MAX = 512; // pairwise-sum plan entries kept in shared memory (3 L + H)
 
 // LANES4: scores with four lanes per position (many columns: more positions in
@@ -675,6 +678,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   const int grp = d.HQ / d.HKV;
   const int kvh = h / grp;
   const int HD = 64;
+  constexpr int ATT_VCHUNK = att_vchunk(LANES4);
   double* sc = reinterpret_cast<double*>(smem);                                     // [MAX_CTX]
   const size_t sc_bytes = ((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15);
   uint4* vs = reinterpret_cast<uint4*>(smem + sc_bytes);                           // [VCHUNK][8]
@@ -876,12 +880,13 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
                              int ncols, int16_t* am, int8_t* ae, cudaStream_t s, bool pdl, const int* pw_off,
                              const unsigned short* pw_data, bool early_kv) {
-  const size_t smem = (((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15)) + ATT_VCHUNK * 264;
+  const bool lanes4 = ncols > 4;
+  const size_t smem = (((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15)) + (size_t)att_vchunk(lanes4) * 264;
   if (!pw_off || !pw_data) return cudaErrorInvalidValue;      // the pairwise-sum plans are required
   const double sq = std::sqrt((double)d.HD);
   int ex = 0;
   const double inv = std::frexp(sq, &ex) == 0.5 ? std::ldexp(1.0, 1 - ex) : 0.0;   // 1/sq, exact, or 0
-  if (ncols <= 4)
+  if (!lanes4)
     return launch_ex(attention_kernel<false>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv,
                      layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
   return launch_ex(attention_kernel<true>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
