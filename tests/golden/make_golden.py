@@ -3,8 +3,8 @@
 own simulator functions (jrrk2/tinyllm-fpga rtl/vc707/host/
 gen_smollm_blockfp_full.py and gen_smollm_blockfp_ddr.py).
 
-This script needs a checkout of the reference (REF_ROOT, default
-/root/reference) plus torch and transformers, which the reference imports at
+This script needs a checkout of the reference (environment variable
+REF_ROOT) plus torch and transformers, which the reference imports at
 module level.  It is run once, in a container that has the reference, and its
 outputs are committed; the tests never need the reference itself.
 
@@ -30,7 +30,7 @@ sys.path.insert(0, HERE)
 from oracle import synth  # noqa: E402  (input data: the seeded synthetic model)
 import inputs  # noqa: E402  (seeded input generators shared with the tests)
 
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+REF_ROOT = os.environ["REF_ROOT"]          # the reference checkout
 
 
 def load_ref(name, max_ctx=64):

@@ -11,8 +11,8 @@ they read their LUTs from ./generated and write their own small vectors
 there -- and its golden_* function is then called on further seeded inputs.
 The RoPE frequency table is written in the generator's .svh format by the
 formula of rtl/vc707/sim/gen_rope_freq_table.py (that script writes into its
-own source tree).  Run once where the reference exists; the tests only read
-the .npz.
+own source tree).  Run once where the reference exists (REF_ROOT = its
+checkout); the tests only read the .npz.
 
 Usage:  python tests/golden/make_rtl_golden.py
 """
@@ -28,7 +28,7 @@ import tempfile
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+REF_ROOT = os.environ["REF_ROOT"]          # the reference checkout
 HOST = os.path.join(REF_ROOT, "rtl/vc707/host")
 SIM = os.path.join(REF_ROOT, "rtl/vc707/sim")
 TILE = 16
