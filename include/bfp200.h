@@ -122,8 +122,10 @@ int bfp200_generate_multi(bfp200_handle* const* hs, int n_dev, const int32_t* pr
  * NCCL_RUNTIME_CONNECT is set (the first exchange then never blocks the host
  * inside a graph capture).  Joining a group makes one exchange.  A sharded
  * handle's generate must be called on every rank with the
- * same arguments; its waits give up after $BFP200_NCCL_TIMEOUT_S seconds
- * (default 120), abort the communicator and return BFP200_ETIMEOUT.
+ * same arguments; its final wait polls with a limit of
+ * $BFP200_NCCL_TIMEOUT_S seconds (default 120), after which it aborts the
+ * communicator (ncclCommAbort) and returns BFP200_ETIMEOUT once the abort
+ * has ended the exchange.
  * Replaces: nothing in the reference (single FPGA, unsharded head :437-440). */
 #define BFP200_NCCL_ID_BYTES 128
 /* A fresh NCCL unique id (rank 0 makes it, every rank passes it to
