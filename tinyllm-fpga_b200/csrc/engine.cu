@@ -376,6 +376,7 @@ struct bfp200_handle {
   DBuf<uint8_t> tc_rec[4];
   size_t tc_stride[4] = {0, 0, 0, 0};
   DBuf<unsigned> head_ctr;     // arrival counter of the single-launch head (left zeroed)
+  HeadAdvance head_adv;        // set while a decode graph is captured: the head does the token feedback
   // tensor-core matmul configuration (columns per CTA, K split) per
   // (rows, K tiles, columns, epilogue), chosen by timing the candidates
   std::map<std::tuple<int, int, int, int>, std::pair<int, int>> tc_cfg;
@@ -801,7 +802,7 @@ int enqueue_head(bfp200_handle* h, int ncols) {
     mark(h, PK_HEAD_LOGITS);
     CK(launch_head_small(h->h_m.p, h->h_e.p, h->nw.p, h->cfg.eps, h->emb_m.p, h->emb_e.p, h->V, h->D, ncols,
                          h->emb_norm_max, h->part_val.p, h->part_idx.p, h->part_sec.p, h->head_ctr.p, h->tok.p,
-                         h->cert.p, s, h->pdl));
+                         h->cert.p, s, h->pdl, 0, nullptr, h->head_adv));
     return BFP200_OK;
   }
   mark(h, PK_HEAD_PREP);
@@ -1382,12 +1383,21 @@ static int generate_impl(bfp200_handle* h, const int32_t* prompt_ids, const int3
         cudaGraph_t g;
         CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
         const long long before = h->launch_count;
+        // 1..4 columns, greedy, unsharded: the single-launch head also feeds
+        // the token back (no separate advance kernel)
+        const bool fused_adv = !smp && !h->comm && h->use_small && head_small_supported(n_seq, h->D);
+        if (fused_adv) {
+          h->head_adv.gen_out = h->gen_out.p; h->head_adv.col_tok = h->col_tok.p; h->head_adv.col_pos = h->col_pos.p;
+          h->head_adv.step = h->dec_step.p; h->head_adv.uncert = h->uncert_dev.p; h->head_adv.n_gen = n_gen;
+        }
         int r = enqueue_forward(h, n_seq, smp == nullptr, /*decode=*/true);
+        h->head_adv = HeadAdvance();
         if (r == BFP200_OK && smp) r = enqueue_sample_head(h, n_seq, *smp, u_ld);
-        h->graph_launches = h->launch_count - before + 1;       // + the advance kernel
+        h->graph_launches = h->launch_count - before + (fused_adv ? 0 : 1);   // + the advance kernel
         h->launch_count = before;
-        advance_kernel<<<1, 256, 0, h->stream>>>(h->tok.p, h->cert.p, n_seq, n_gen, h->gen_out.p, h->col_tok.p,
-                                                 h->col_pos.p, h->dec_step.p, h->uncert_dev.p);
+        if (!fused_adv)
+          advance_kernel<<<1, 256, 0, h->stream>>>(h->tok.p, h->cert.p, n_seq, n_gen, h->gen_out.p, h->col_tok.p,
+                                                   h->col_pos.p, h->dec_step.p, h->uncert_dev.p);
         cudaError_t ce = cudaStreamEndCapture(h->stream, &g);
         if (r != BFP200_OK) { if (ce == cudaSuccess) cudaGraphDestroy(g); return r; }
         CK(ce);

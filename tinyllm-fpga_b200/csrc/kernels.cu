@@ -1323,7 +1323,7 @@ __global__ void __launch_bounds__(256)
 head_small_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, double eps, const int16_t* emb_m,
                   const int8_t* emb_e, int VOCAB, int D, int ncols, double emb_norm_max, double* part_val,
                   int* part_idx, double* part_second, unsigned* done_ctr, int* tok_out, int* cert_out, int v_base,
-                  double* xout) {
+                  double* xout, HeadAdvance adv) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_lo[96], s_len[96];
   __shared__ double s_val[96];
@@ -1382,6 +1382,18 @@ head_small_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, dou
   int bidx[NC];
   #pragma unroll
   for (int c = 0; c < NC; ++c) { best[c] = -INFINITY; sec[c] = -INFINITY; bidx[c] = 0x7fffffff; }
+  // one column: this lane's 24 hn values (its 8-element chunks of the row,
+  // the same for every row) live in registers; each chunk's 8 mantissa
+  // products are summed first and scaled by the chunk's power of two once
+  // (exact scaling), so an element costs a conversion and an FMA.  Every
+  // logit keeps at most D + 2 roundings per term -- the certificate's bound.
+  double hreg[3][8];
+  if constexpr (NC == 1) {
+    #pragma unroll
+    for (int j = 0; j < 3; ++j)
+      #pragma unroll
+      for (int t = 0; t < 8; ++t) hreg[j][t] = 32 * j < NU ? hnT[j * 256 + t * 32 + lane] : 0.0;   // hnT holds HS
+  }
   for (int v0 = gw; v0 < VOCAB; v0 += HS_RF * nw) {
     double acc[HS_RF][NC];
     #pragma unroll
@@ -1396,11 +1408,19 @@ head_small_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, dou
       for (int q = 0; q < HS_RF; ++q) {
         const double scl = pow2(ex[q][j] - 15);
         const unsigned ww[4] = {w[q][j].x, w[q][j].y, w[q][j].z, w[q][j].w};
-        #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const double ev = (double)(int)(int16_t)((ww[t >> 1] >> (16 * (t & 1))) & 0xFFFF) * scl;
+        if constexpr (NC == 1) {
+          double part = 0.0;
           #pragma unroll
-          for (int c = 0; c < NC; ++c) acc[q][c] = fma(ev, hp[c * HS + t * 32], acc[q][c]);
+          for (int t = 0; t < 8; ++t)
+            part = fma((double)(int)(int16_t)((ww[t >> 1] >> (16 * (t & 1))) & 0xFFFF), hreg[j][t], part);
+          acc[q][0] = fma(part, scl, acc[q][0]);
+        } else {
+          #pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const double ev = (double)(int)(int16_t)((ww[t >> 1] >> (16 * (t & 1))) & 0xFFFF) * scl;
+            #pragma unroll
+            for (int c = 0; c < NC; ++c) acc[q][c] = fma(ev, hp[c * HS + t * 32], acc[q][c]);
+          }
         }
       }
     }
@@ -1479,6 +1499,22 @@ head_small_kernel(const int16_t* hm, const int8_t* he, const double* norm_w, dou
       cert_out[c] = (ok && (b - s2) > head_margin(D, hnn, emb_norm_max)) ? 1 : 0;
     }
   }
+  if (adv.gen_out && !xout) {                           // the step's token feedback
+    __syncthreads();
+    if (tid == 0) {
+      const int step = *adv.step;
+      long long bad = 0;
+      for (int c = 0; c < ncols; ++c) {
+        const int t = tok_out[c];
+        if (step < adv.n_gen) adv.gen_out[(size_t)c * adv.n_gen + step] = t;
+        adv.col_tok[c] = t;
+        adv.col_pos[c] += 1;
+        bad += cert_out[c] ? 0 : 1;
+      }
+      if (bad) *adv.uncert += bad;
+      *adv.step = step + 1;
+    }
+  }
   if (tid == 0) *done_ctr = 0u;                          // ready for the next launch
 }
 
@@ -1493,7 +1529,7 @@ cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double*
                               const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, int ncols,
                               double emb_norm_max, double* part_val, int* part_idx, double* part_second,
                               unsigned* done_ctr, int* tok_out, int* cert_out, cudaStream_t s, bool pdl,
-                              int v_base, double* xout) {
+                              int v_base, double* xout, HeadAdvance adv) {
   if (!head_small_supported(ncols, D)) return cudaErrorInvalidValue;
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
@@ -1502,10 +1538,10 @@ cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double*
   if (ncols <= 1)
     return launch_ex(head_small_kernel<1>, dim3(nsm), dim3(256), smem, s, pdl, hm, he, norm_w, eps, emb_m, emb_e,
                      VOCAB, D, ncols, emb_norm_max, part_val, part_idx, part_second, done_ctr, tok_out, cert_out,
-                     v_base, xout);
+                     v_base, xout, adv);
   return launch_ex(head_small_kernel<4>, dim3(nsm), dim3(256), smem, s, pdl, hm, he, norm_w, eps, emb_m, emb_e,
                    VOCAB, D, ncols, emb_norm_max, part_val, part_idx, part_second, done_ctr, tok_out, cert_out,
-                   v_base, xout);
+                   v_base, xout, adv);
 }
 
 cudaError_t launch_head_reduce(const double* part_val, const int* part_idx, const double* part_second,

@@ -259,11 +259,23 @@ cudaError_t launch_rtl_residual(const int16_t* am, const int8_t* ae, const int16
                                 long long ntiles, int16_t* ym, int8_t* ye, cudaStream_t s);
 
 bool head_small_supported(int ncols, int D);
+// The decode step's token feedback, done by the single-launch head's last CTA
+// instead of a separate kernel: gen_out[c][*step] = token (step < n_gen),
+// col_tok[c] = token, col_pos[c] += 1, uncertified decisions added to
+// *uncert, *step += 1.  gen_out == nullptr: no feedback.
+struct HeadAdvance {
+  int* gen_out = nullptr;
+  int* col_tok = nullptr;
+  int* col_pos = nullptr;
+  int* step = nullptr;
+  long long* uncert = nullptr;
+  int n_gen = 0;
+};
 cudaError_t launch_head_small(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
                               const int16_t* emb_m, const int8_t* emb_e, int VOCAB, int D, int ncols,
                               double emb_norm_max, double* part_val, int* part_idx, double* part_second,
                               unsigned* done_ctr, int* tok_out, int* cert_out, cudaStream_t s, bool pdl,
-                              int v_base = 0, double* xout = nullptr);
+                              int v_base = 0, double* xout = nullptr, HeadAdvance adv = HeadAdvance());
 
 // Standalone ops (the reference's module-level functions).
 cudaError_t launch_tile_quantize(const double* v, long long ntiles, int16_t* m, int8_t* e, cudaStream_t s);
