@@ -102,6 +102,9 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
  * error bound of a cdf step is counted by bfp200_uncertified_steps. */
 int bfp200_generate_sampled(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq,
                             int n_gen, double temperature, int top_k, uint32_t seed, int32_t* out_tokens);
+/* The uniforms the sampled decode draws for one sequence: the first n values
+ * of np.random.seed(seed); np.random.random_sample() (host only, no device). */
+int bfp200_sample_uniforms(uint32_t seed, int n, double* out);
 
 /* Same as bfp200_generate, with the sequences split into contiguous blocks
  * over n_dev handles (one per GPU), run concurrently with no collectives.

@@ -63,6 +63,7 @@ SIGNATURES = {
     "bfp200_profile_forward": [_P, _I, _I, _P, _P],
     "bfp200_matvec_noalloc": [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P],
     "bfp200_generate_sampled": [_P, _P, _P, _I, _I, _D, _I, C.c_uint32, _P],
+    "bfp200_sample_uniforms": [C.c_uint32, _I, _P],
     "bfp200_matvec_timed": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, C.POINTER(_D)],
     "bfp200_rtl_matvec": [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P],
     "bfp200_rtl_rmsnorm": [_P, _P, _P, _P, _P, _I, _I, _P, _P],

@@ -1248,6 +1248,12 @@ int bfp200_generate(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* 
   return generate_impl(h, prompt_ids, prompt_lens, n_seq, n_gen, feed_mode, out_tokens, nullptr);
 }
 
+int bfp200_sample_uniforms(uint32_t seed, int n, double* out) {
+  if (n < 0 || (n > 0 && !out)) return fail(BFP200_EINVAL, "sample_uniforms: bad arguments");
+  mt19937_uniforms(seed, n, out);
+  return BFP200_OK;
+}
+
 int bfp200_generate_sampled(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq,
                             int n_gen, double temperature, int top_k, uint32_t seed, int32_t* out_tokens) {
   if (!(temperature > 0.0)) return generate_impl(h, prompt_ids, prompt_lens, n_seq, n_gen, 0, out_tokens, nullptr);
