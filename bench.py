@@ -13,6 +13,14 @@ does not shard, so N GPUs run N independent streams -- weak scaling).
 The same line carries ``bs256``: configs[2] = "cfg3", 256 ragged sequences
 x 128 tokens, sequences split over the ranks with no collectives.
 
+Further keys: ``roofline`` (the bs1 gemv kernels against the measured HBM copy
+bandwidth, with their measured DRAM traffic), ``bs256.roofline`` (the batched
+tensor-core matvecs), ``cfg5`` (per-kernel times at batch 64 / KV 2047, rank
+0), ``cfg4`` (the isolated matvec over the model's weight shapes x batch 1 ..
+1024, rank 0), ``cpu_baseline`` (the oracle port on one host core, rank 0) and,
+with ``--sharded-head`` at N > 1, ``sharded_head`` (single-stream decode with
+the vocabulary-sharded head).
+
 ``--impl reference`` times the reference algorithm on the host cores (the
 numpy restatement under oracle/, since the reference is Python that cannot
 be installed on the GPU box) with the same metric and unit.
@@ -245,7 +253,7 @@ def run_ours(args, world, rank, local):
     if not args.no_bs256 and part3:
         profile["bs256_pos100"] = dec.profile_forward(len(part3), 100)
     sharded = None
-    if world > 1:
+    if world > 1 and args.sharded_head:
         sharded = sharded_head_run(dec, prompts2, ngen2, args, world, decode_tok_ms)
     dec.close()
     cfg5 = None
@@ -451,6 +459,8 @@ def main():
     ap.add_argument("--mm-reps", type=int, default=50, help="graph replays for the matmul roofline timing")
     ap.add_argument("--no-cfg5", action="store_true", help="skip the batch-64 / KV-2048 kernel profile")
     ap.add_argument("--no-cfg4", action="store_true", help="skip the matvec shape x batch sweep")
+    ap.add_argument("--sharded-head", action="store_true",
+                    help="with N > 1 GPUs, also time the single-stream decode with the vocabulary-sharded head")
     ap.add_argument("--cfg4-batches", type=lambda s: [int(x) for x in s.split(",")], default=[1, 8, 64, 256, 1024],
                     help="batch sizes of the matvec sweep")
     args = ap.parse_args()
