@@ -245,9 +245,17 @@ __device__ __forceinline__ double np_pw_leaf_8lanes(const double* a, int n) {
   const int j = threadIdx.x & 7;
   double v = 0.0;
   if (n >= 8) {
-    const int lim = n - (n % 8);
-    v = a[j];
-    for (int i = 8 + j; i < lim; i += 8) v = __dadd_rn(v, a[i]);
+    // the tree's leaves hold at most 128 elements: up to 16 per accumulator,
+    // all loaded before the addition chain starts
+    const int cnt = n >> 3;
+    double x[16];
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = i < cnt ? a[8 * i + j] : 0.0;
+    v = x[0];
+    #pragma unroll
+    for (int i = 1; i < 16; ++i)
+      if (i < cnt) v = __dadd_rn(v, x[i]);
+    for (int i = 128 + j; i < 8 * cnt; i += 8) v = __dadd_rn(v, a[i]);   // longer runs (not a tree leaf)
   }
   double o = __shfl_xor_sync(0xffffffffu, v, 1);
   if ((j & 1) == 0) v = __dadd_rn(v, o);

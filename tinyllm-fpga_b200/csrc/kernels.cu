@@ -654,6 +654,10 @@ constexpr int ATT_THREADS = 256;
 // CTAs fit an SM and more sequential accumulations run side by side)
 __host__ __device__ constexpr int att_vchunk(bool lanes4) { return lanes4 ? 128 : 256; }
 constexpr int ATT_PLAN_MAX = 512; // pairwise-sum plan entries kept in shared memory (3 L + H)
+// Staged K rows are 8 chunks of 16 B; chunk u of position t is stored at slot
+// u ^ (t & 7), so the 8 threads of a shared-memory phase (8 positions, or 2
+// positions x 4 tiles batched) hit 8 different bank groups instead of one.
+__device__ __forceinline__ int att_kswz(int i) { return (i & ~7) | ((i ^ (i >> 3)) & 7); }
 
 // LANES4: scores with four lanes per position (many columns: more positions in
 // flight per CTA); otherwise one position per thread (1..4 columns: the
@@ -697,7 +701,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
     const uint4* ksrc = reinterpret_cast<const uint4*>(kv.km + kbase * HD);
     const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + kbase * HD);
     for (int i = tid; i < nold * 8; i += ATT_THREADS) {
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(ks + i)),
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(ks + att_kswz(i))),
                    "l"(ksrc + i) : "memory");
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(vs + i)),
                    "l"(vsrc + i) : "memory");
@@ -730,7 +734,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   if (tid < HD) s_qm[tid] = qr_m[(size_t)c * d.HQ * HD + h * HD + tid];
   if (tid < 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h * 4 + tid];
   if (pos < ATT_VCHUNK) {
-    if (tid < 8) ks[pos * 8 + tid] = reinterpret_cast<const uint4*>(kv.km + (kbase + pos) * HD)[tid];
+    if (tid < 8) ks[att_kswz(pos * 8 + tid)] = reinterpret_cast<const uint4*>(kv.km + (kbase + pos) * HD)[tid];
     else if (tid < 16) vs[pos * 8 + tid - 8] = reinterpret_cast<const uint4*>(kv.vm + (kbase + pos) * HD)[tid - 8];
     else if (tid == 16) kes[pos] = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + pos) * 4);
     else if (tid == 17) ves[pos] = *reinterpret_cast<const unsigned*>(kv.ve + (kbase + pos) * 4);
@@ -750,7 +754,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
       unsigned ke4;
       if (t < n0) {
         #pragma unroll
-        for (int u = 0; u < 8; ++u) kk[u] = ks[t * 8 + u];
+        for (int u = 0; u < 8; ++u) kk[u] = ks[t * 8 + (u ^ (t & 7))];
         ke4 = kes[t];
       } else {
         const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
@@ -789,8 +793,8 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
         uint4 k0, k1;
         unsigned ke4;
         if (t < n0) {
-          k0 = ks[t * 8 + 2 * jt];
-          k1 = ks[t * 8 + 2 * jt + 1];
+          k0 = ks[t * 8 + ((2 * jt) ^ (t & 7))];
+          k1 = ks[t * 8 + ((2 * jt + 1) ^ (t & 7))];
           ke4 = kes[t];
         } else {
           const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
