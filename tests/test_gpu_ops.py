@@ -78,6 +78,29 @@ def test_matvec_sweep(ops, shape):
         assert np.array_equal(Y[cols], ref), key
 
 
+@pytest.mark.parametrize("shape", [(576, 576), (576, 1536)])
+def test_matvec_batched_shift_paths(ops, shape):
+    """Batched (tensor-core) matvec with model-like exponent spreads, where
+    every per-tile shift is small, and with outlier tiles that push some
+    shifts past 16: both shift paths of the epilogue against the oracle."""
+    D_out, D_in = shape
+    rng = np.random.default_rng([9, D_out, D_in])
+    NT = D_in // 16
+    W_m = rng.integers(-32768, 32768, size=(D_out, NT, 16)).astype(np.int16)
+    W_e = rng.integers(-3, 1, size=(D_out, NT)).astype(np.int8)
+    B = 256
+    X_m, X_e = inputs.sweep_x(D_in, B, D_out)
+    cols = np.linspace(0, B - 1, 12).astype(int)
+    om, oe = ops.matvec(X_m, X_e, W_m, W_e)
+    Y = ops.tile_decode(om.reshape(-1), oe.reshape(-1)).reshape(B, D_out)
+    assert np.array_equal(Y[cols], O.matvec_cols(X_m[cols], X_e[cols], W_m, W_e))
+    X_e2 = X_e.copy()
+    X_e2[::3, NT // 2] += 20                    # outlier tiles: shifts of 17..30 elsewhere
+    om, oe = ops.matvec(X_m, X_e2, W_m, W_e)
+    Y = ops.tile_decode(om.reshape(-1), oe.reshape(-1)).reshape(B, D_out)
+    assert np.array_equal(Y[cols], O.matvec_cols(X_m[cols], X_e2[cols], W_m, W_e))
+
+
 @pytest.mark.parametrize("name", ["shift_mask", "saturate", "mixed", "zero_x"])
 def test_matvec_edges(ops, name):
     z = np.load(golden_path(f"matvec_edge_{name}.npz"))

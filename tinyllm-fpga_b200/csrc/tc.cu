@@ -84,6 +84,12 @@ __device__ __forceinline__ void tc_commit(unsigned long long* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                :: "r"(su32(bar)) : "memory");
 }
+// d = a * b + c with a 64-bit product and sum (one wide integer multiply-add)
+__device__ __forceinline__ long long mad_wide_s32(int a, int b, long long c) {
+  long long d;
+  asm("mad.wide.s32 %0, %1, %2, %3;" : "=l"(d) : "r"(a), "r"(b), "l"(c));
+  return d;
+}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -152,7 +158,7 @@ __global__ void tc_pack_kernel(const uint8_t* wm, const int8_t* we, int rows, in
 // CTAs of a cluster share the tiles; every CTA keeps all NT column exponents
 // for the max-exponent pass, and a 128 x NCB int64 block for the reduction).
 struct TcLayout {
-  size_t bar, tptr, ring, z, xe, cx, red, total;
+  size_t bar, tptr, ring, z, xe, cx, emin, red, total;
 };
 __host__ __device__ inline TcLayout tc_layout(int NT, int NCB, int ntl, bool split) {
   TcLayout L;
@@ -162,7 +168,8 @@ __host__ __device__ inline TcLayout tc_layout(int NT, int NCB, int ntl, bool spl
   L.z = L.ring + (size_t)TC_SA * TC_REC;
   L.xe = L.z + (size_t)(3 * ntl + 1) * NCB * 16;
   L.cx = L.xe + (size_t)NT * NCB * 4;
-  L.red = L.cx + (size_t)ntl * NCB * 4;
+  L.emin = L.cx + (size_t)ntl * NCB * 4;
+  L.red = L.emin + (size_t)NT * 4 * 4;
   L.red = (L.red + 15) & ~(size_t)15;
   L.total = L.red + (split ? (size_t)TC_M * NCB * 8 : 0);
   return L;
@@ -219,6 +226,7 @@ tc_matmul_kernel(TcArgs a) {
   unsigned char* Z = smem + L.z;
   int* xe_s = reinterpret_cast<int*>(smem + L.xe);           // [NT][NCB]
   int* cx_s = reinterpret_cast<int*>(smem + L.cx);           // [ntl][NCB]
+  int* emin_s = reinterpret_cast<int*>(smem + L.emin);       // [NT][4]: min column exponent per column quarter
   long long* red = reinterpret_cast<long long*>(smem + L.red); // [NCB][128] (split K)
   const uint8_t* rec = a.rec + (size_t)blk * tc_block_bytes(NT);
   const uint8_t* rec_k = rec + (size_t)t_lo * TC_REC;         // this CTA's first K tile
@@ -337,6 +345,14 @@ tc_matmul_kernel(TcArgs a) {
     // exponents come from the block's exponent table, 16 at a time
     #pragma unroll
     for (int j = 0; j < CPT; ++j) Mx[j] = -100000;
+    if (q == 0) {
+      for (int t = lane; t < NT; t += 32) {
+        int mn = xe_s[t * NCB + cb];
+        #pragma unroll
+        for (int j = 1; j < CPT; ++j) mn = min(mn, xe_s[t * NCB + cb + j]);
+        emin_s[t * 4 + quarter] = mn;
+      }
+    }
     {
       const int NTP = tc_ntp(NT);
       const uint4* wrow = reinterpret_cast<const uint4*>(rec + (size_t)NT * TC_REC + (size_t)row * NTP);
@@ -353,15 +369,16 @@ tc_matmul_kernel(TcArgs a) {
               const int4 e4 = *reinterpret_cast<const int4*>(xe_s + t * NCB + cb + j);
               const int ev4[4] = {e4.x, e4.y, e4.z, e4.w};
               #pragma unroll
-              for (int q2 = 0; q2 < 4; ++q2) {
-                const int e = we + ev4[q2];
-                Mx[j + q2] = e > Mx[j + q2] ? e : Mx[j + q2];
-              }
+              for (int q2 = 0; q2 < 4; ++q2) Mx[j + q2] = __viaddmax_s32(we, ev4[q2], Mx[j + q2]);
             }
           }
         }
       }
     }
+    int MxMax = Mx[0];
+    #pragma unroll
+    for (int j = 1; j < CPT; ++j) MxMax = max(MxMax, Mx[j]);
+    asm volatile("bar.sync 1, %0;" :: "r"(TC_EPI_WARPS * 32) : "memory");     // emin_s complete
     #pragma unroll
     for (int j = 0; j < CPT; ++j) acc[j] = 0;
     for (int t = 0; t < ntl; ++t) {
@@ -385,8 +402,29 @@ tc_matmul_kernel(TcArgs a) {
       const int wer = reinterpret_cast<const int8_t*>(rs + 4608)[row];
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(su32(&rempty[s])) : "memory");
-      // per-tile floor shift and int64 accumulation (:223-228).  S = 65536 hh +
-      // 256 cr + lo is formed as ((256 hh + cr) * 256 + lo): 256 hh + cr fits int32.
+      // per-tile floor shift and int64 accumulation (:223-228).  S = 65536 hh + w
+      // with w = 256 cr + lo (|w| < 2^29).  When every shift of this warp's
+      // pairs is at most 16 (a bound from the row's largest max exponent and
+      // the quarter's smallest column exponent), floor(S / 2^sh) =
+      // hh * 2^(16-sh) + (w >> sh) exactly: two 32 x 32 -> 64-bit multiply-adds.
+      const int shb = MxMax - wer - emin_s[tg * 4 + quarter];
+      if (__all_sync(0xffffffffu, shb <= 16)) {
+        #pragma unroll
+        for (int j = 0; j < CPT; j += 4) {
+          const int4 e4 = *reinterpret_cast<const int4*>(xe_s + tg * NCB + cb + j);
+          const int4 x4 = *reinterpret_cast<const int4*>(cx_s + t * NCB + cb + j);
+          const int ev4[4] = {e4.x, e4.y, e4.z, e4.w}, cv4[4] = {x4.x, x4.y, x4.z, x4.w};
+          #pragma unroll
+          for (int q2 = 0; q2 < 4; ++q2) {
+            const int jj = j + q2;
+            const int sh = Mx[jj] - wer - ev4[q2];
+            const int w = (int)cr[jj] * 256 + ((int)ll[jj] + cw + cv4[q2]);
+            acc[jj] = mad_wide_s32(w >> sh, 1, mad_wide_s32((int)hh[jj], 0x10000 >> sh, acc[jj]));
+          }
+        }
+        continue;
+      }
+      // general shifts: S = ((256 hh + cr) * 256 + lo) in 64 bits (256 hh + cr fits int32)
       #pragma unroll
       for (int j = 0; j < CPT; j += 4) {
         const int4 e4 = *reinterpret_cast<const int4*>(xe_s + tg * NCB + cb + j);
