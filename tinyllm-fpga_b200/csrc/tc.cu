@@ -158,19 +158,20 @@ __global__ void tc_pack_kernel(const uint8_t* wm, const int8_t* we, int rows, in
 // CTAs of a cluster share the tiles; every CTA keeps all NT column exponents
 // for the max-exponent pass, and a 128 x NCB int64 block for the reduction).
 struct TcLayout {
-  size_t bar, tptr, ring, z, xe, cx, emin, red, total;
+  size_t bar, tptr, ring, z, xe, xe16, cx, emin, wex, red, total;
 };
 __host__ __device__ inline TcLayout tc_layout(int NT, int NCB, int ntl, bool split) {
   TcLayout L;
-  L.bar = 0;                                           // mbarriers: ring full / empty, D full / empty
+  L.bar = 0;                                           // mbarriers: ring full / empty, D full / empty, exponents
   L.tptr = 112;                                        // TMEM base address
   L.ring = 128;
   L.z = L.ring + (size_t)TC_SA * TC_REC;
   L.xe = L.z + (size_t)(3 * ntl + 1) * NCB * 16;
-  L.cx = L.xe + (size_t)NT * NCB * 4;
+  L.xe16 = L.xe + (size_t)NT * NCB * 4;
+  L.cx = L.xe16 + (size_t)NT * NCB * 2;
   L.emin = L.cx + (size_t)ntl * NCB * 4;
-  L.red = L.emin + (size_t)NT * 4 * 4;
-  L.red = (L.red + 15) & ~(size_t)15;
+  L.wex = (L.emin + (size_t)NT * 4 * 4 + 15) & ~(size_t)15;
+  L.red = L.wex + (size_t)TC_M * tc_ntp(NT);
   L.total = L.red + (split ? (size_t)TC_M * NCB * 8 : 0);
   return L;
 }
@@ -221,13 +222,16 @@ tc_matmul_kernel(TcArgs a) {
   unsigned long long* rempty = rfull + TC_SA;                                         // [TC_SA]
   unsigned long long* dfull = rempty + TC_SA;                                         // [TC_NB]
   unsigned long long* dempty = dfull + TC_NB;                                         // [TC_NB]
+  unsigned long long* wbar = dempty + TC_NB;                                          // the exponent table
   uint32_t* tptr = reinterpret_cast<uint32_t*>(smem + L.tptr);
   unsigned char* ring = smem + L.ring;
   unsigned char* Z = smem + L.z;
   int* xe_s = reinterpret_cast<int*>(smem + L.xe);           // [NT][NCB]
+  int16_t* xe16_s = reinterpret_cast<int16_t*>(smem + L.xe16); // [NT][NCB], the same exponents as 16-bit lanes
   int* cx_s = reinterpret_cast<int*>(smem + L.cx);           // [ntl][NCB]
   int* emin_s = reinterpret_cast<int*>(smem + L.emin);       // [NT][4]: min column exponent per column quarter
   long long* red = reinterpret_cast<long long*>(smem + L.red); // [NCB][128] (split K)
+  const unsigned char* wex_s = smem + L.wex;                  // [128][NTP] tile exponents of the block's rows
   const uint8_t* rec = a.rec + (size_t)blk * tc_block_bytes(NT);
   const uint8_t* rec_k = rec + (size_t)t_lo * TC_REC;         // this CTA's first K tile
   pdl_trigger_tc();
@@ -236,7 +240,14 @@ tc_matmul_kernel(TcArgs a) {
   if (tid == 0) {
     for (int s = 0; s < TC_SA; ++s) { mb_init(&rfull[s], 1); mb_init(&rempty[s], 1 + TC_EPI_WARPS); }
     for (int b = 0; b < TC_NB; ++b) { mb_init(&dfull[b], 1); mb_init(&dempty[b], TC_EPI_WARPS); }
+    mb_init(wbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    {
+      const unsigned wbytes = (unsigned)(TC_M * tc_ntp(NT));
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(wbar)), "r"(wbytes) : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   :: "r"(su32(wex_s)), "l"(rec + (size_t)NT * TC_REC), "r"(wbytes), "r"(su32(wbar)) : "memory");
+    }
     for (int s = 0; s < TC_SA && s < ntl; ++s) {
       asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&rfull[s])), "r"(TC_REC) : "memory");
       asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -278,6 +289,7 @@ tc_matmul_kernel(TcArgs a) {
       const int i = i0 + u * TC_THREADS, t = i / NCB, c = i - t * NCB;
       if (i >= NT * NCB) break;
       xe_s[i] = (int)ev[u];
+      xe16_s[i] = (int16_t)ev[u];
       if (t < t_lo || t >= t_hi) continue;
       const int lt = t - t_lo;
       const uint4 v0 = v[u][0], v1 = v[u][1];
@@ -306,8 +318,9 @@ tc_matmul_kernel(TcArgs a) {
   // per epilogue thread: max exponent and int64 sum of (row, column cb + j)
   int Mx[CPT];
   long long acc[CPT];
+  int resid[CPT];                 // EPI_RESIDUAL: h mantissa (low 16 bits) and tile exponent (above)
   #pragma unroll
-  for (int j = 0; j < CPT; ++j) { Mx[j] = 0; acc[j] = 0; }
+  for (int j = 0; j < CPT; ++j) { Mx[j] = 0; acc[j] = 0; resid[j] = 0; }
 
   if (warp == 0) {
     // ---- producer: refill a ring stage once its MMA and epilogue reads are done
@@ -354,8 +367,14 @@ tc_matmul_kernel(TcArgs a) {
       }
     }
     {
+      // two (row, column) pairs per instruction: exponent sums fit 16 bits
+      // (|we + ex| <= 254), so max(we + ex, M) runs on packed 16-bit lanes
       const int NTP = tc_ntp(NT);
-      const uint4* wrow = reinterpret_cast<const uint4*>(rec + (size_t)NT * TC_REC + (size_t)row * NTP);
+      mb_wait(wbar, 0u, a.err);                              // the table, copied before the dependency wait
+      const uint4* wrow = reinterpret_cast<const uint4*>(wex_s + (size_t)row * NTP);
+      unsigned m2[CPT / 2];
+      #pragma unroll
+      for (int k = 0; k < CPT / 2; ++k) m2[k] = 0x8AD08AD0u;            // -30000 in both lanes
       for (int t0 = 0; t0 < NT; t0 += 16) {
         const uint4 w16 = wrow[t0 / 16];
         const unsigned ww[4] = {w16.x, w16.y, w16.z, w16.w};
@@ -363,21 +382,44 @@ tc_matmul_kernel(TcArgs a) {
         for (int k = 0; k < 16; ++k) {
           const int t = t0 + k;
           if (t < NT) {
-            const int we = (int)(int8_t)(ww[k >> 2] >> (8 * (k & 3)));
-            #pragma unroll
-            for (int j = 0; j < CPT; j += 4) {
-              const int4 e4 = *reinterpret_cast<const int4*>(xe_s + t * NCB + cb + j);
-              const int ev4[4] = {e4.x, e4.y, e4.z, e4.w};
-              #pragma unroll
-              for (int q2 = 0; q2 < 4; ++q2) Mx[j + q2] = __viaddmax_s32(we, ev4[q2], Mx[j + q2]);
+            const unsigned we2 = (unsigned)(uint16_t)(int16_t)(int8_t)(ww[k >> 2] >> (8 * (k & 3))) * 0x10001u;
+            const int16_t* xr = xe16_s + t * NCB + cb;
+            if constexpr (CPT == 8) {
+              const uint4 x8 = *reinterpret_cast<const uint4*>(xr);
+              m2[0] = __viaddmax_s16x2(we2, x8.x, m2[0]);
+              m2[1] = __viaddmax_s16x2(we2, x8.y, m2[1]);
+              m2[2] = __viaddmax_s16x2(we2, x8.z, m2[2]);
+              m2[3] = __viaddmax_s16x2(we2, x8.w, m2[3]);
+            } else {
+              const uint2 x4 = *reinterpret_cast<const uint2*>(xr);
+              m2[0] = __viaddmax_s16x2(we2, x4.x, m2[0]);
+              m2[1] = __viaddmax_s16x2(we2, x4.y, m2[1]);
             }
           }
         }
+      }
+      #pragma unroll
+      for (int k = 0; k < CPT / 2; ++k) {
+        Mx[2 * k] = (int)(int16_t)(m2[k] & 0xFFFFu);
+        Mx[2 * k + 1] = (int)(int16_t)(m2[k] >> 16);
       }
     }
     int MxMax = Mx[0];
     #pragma unroll
     for (int j = 1; j < CPT; ++j) MxMax = max(MxMax, Mx[j]);
+    if constexpr (MODE == EPI_RESIDUAL) {
+      // the residual input, loaded now so its latency hides behind the tiles
+      const int R = blk * TC_M + row;
+      if (kr == 0 && R < a.rows) {
+        #pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+          const int col = c0 + cb + j;
+          if (col < a.ncols)
+            resid[j] = (int)((unsigned)(uint16_t)a.rm[(size_t)col * a.o_ld + R] |
+                             ((unsigned)(int)a.re[(size_t)col * a.o_lde + R / 16] << 16));
+        }
+      }
+    }
     asm volatile("bar.sync 1, %0;" :: "r"(TC_EPI_WARPS * 32) : "memory");     // emin_s complete
     #pragma unroll
     for (int j = 0; j < CPT; ++j) acc[j] = 0;
@@ -490,8 +532,7 @@ tc_matmul_kernel(TcArgs a) {
       for (int j = 0; j < CPT; ++j) {                                                  // fpq(h + o)
         const int col = c0 + cb + j;
         const bool valid = row_ok && col < a.ncols;
-        const double hv = valid ? bfp_decode(a.rm[(size_t)col * a.o_ld + R], a.re[(size_t)col * a.o_lde + R / 16])
-                                : 0.0;
+        const double hv = valid ? bfp_decode((int16_t)(resid[j] & 0xFFFF), resid[j] >> 16) : 0.0;
         v[j] = __dadd_rn(hv, bfp_decode(qm[j], qe[j]));
       }
       tile_quantize_16lanes_n<CPT>(v, qm, qe);
@@ -580,7 +621,7 @@ cudaError_t launch_tc_t(const TcArgs& a, int ks, cudaStream_t s, bool pdl) {
 
 bool tc_config_fits(int NT, int ncb, int ks) {
   return (ncb == 16 || ncb == 32) && ks >= 1 && ks <= 8 && ks <= NT &&
-         tc_layout(NT, ncb, (NT + ks - 1) / ks, ks > 1).total <= 200 * 1024;
+         tc_layout(NT, ncb, (NT + ks - 1) / ks, ks > 1).total <= 227 * 1024;
 }
 
 // Without a tuned configuration: no K split; 32 columns per CTA when that
