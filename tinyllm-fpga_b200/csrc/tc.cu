@@ -20,11 +20,19 @@
 // recombined in int64.
 //
 // Weights are repacked once into per-(128-row block, K tile) records
-//   [Wl' rows 128 x 16 B][Wh rows 128 x 16 B][cw int32 x 128][we int8 x 128]
-// with cw = 128 sum_k W - 16 * 128^2 (rows padded to a multiple of 128 are
-// zero weights).  Records stream through a shared-memory ring by TMA bulk
-// copies; D is double-buffered in tensor memory so tile t+1's MMA overlaps
-// tile t's epilogue.
+//   [Wl' rows 128 x 16 B][Wh rows 128 x 16 B]
+// followed by per-block tables of the rows' corrections cw = 128 sum_k W -
+// 16 * 128^2 and tile exponents (rows padded to a multiple of 128 are zero
+// weights).  Records stream through a shared-memory ring by TMA bulk copies;
+// the tables are bulk-copied once per CTA before the dependency wait.  D
+// cycles through four tensor-memory buffers so the MMAs of the next tiles
+// overlap the epilogue of this one.
+//
+// Per (row, column, tile) the epilogue needs S >> sh with sh = (max exponent
+// of the row and column) - (tile exponent).  The max exponents come first
+// (two pairs per instruction on packed 16-bit lanes); then every tile costs
+// two wide multiply-adds when its shifts are at most 16, the general 64-bit
+// shift otherwise.
 #include "bfp_device.cuh"
 #include "kernels.cuh"
 
@@ -34,7 +42,7 @@ namespace {
 
 constexpr int TC_THREADS = 576;     // warp 0 TMA, warp 1 MMA, warps 2..17 epilogue
 constexpr int TC_M = 128;
-constexpr int TC_REC = 4736;            // bytes per (128-row block, K tile) record
+constexpr int TC_REC = 4096;            // bytes per (128-row block, K tile) record: Wl' and Wh rows
 constexpr int TC_SA = 4;                // record ring stages
 constexpr long long TC_SPIN = 1LL << 20;
 
@@ -112,10 +120,16 @@ __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[CPT]) {
   else tmem_ld4(taddr, r);
 }
 
-// Per 128-row block: NT records, then the block's tile exponents row by row
-// ([128 rows][NTP] bytes, NTP = NT rounded up to 16) for the max-exponent pass.
+// Per 128-row block: NT records, the rows' limb corrections tile by tile
+// ([NT][128] int32), their tile exponents tile by tile ([NT][128] int8) and
+// row by row ([128 rows][NTP] bytes, NTP = NT rounded up to 16: the
+// max-exponent pass).  The tables are copied into shared memory once per
+// CTA; only the records stream through the ring.
 __host__ __device__ inline int tc_ntp(int NT) { return (NT + 15) & ~15; }
-__host__ __device__ inline size_t tc_block_bytes(int NT) { return (size_t)NT * TC_REC + (size_t)TC_M * tc_ntp(NT); }
+__host__ __device__ inline size_t tc_cw_off(int NT) { return (size_t)NT * TC_REC; }
+__host__ __device__ inline size_t tc_wt_off(int NT) { return (size_t)NT * (TC_REC + TC_M * 4); }
+__host__ __device__ inline size_t tc_we_off(int NT) { return (size_t)NT * (TC_REC + TC_M * 5); }
+__host__ __device__ inline size_t tc_block_bytes(int NT) { return tc_we_off(NT) + (size_t)TC_M * tc_ntp(NT); }
 
 // ---------------------------------------------------------------------------
 // repack: DevMat (planes [G][NT][2][16][16], exponents [G][NT][16]) -> records
@@ -146,9 +160,9 @@ __global__ void tc_pack_kernel(const uint8_t* wm, const int8_t* we, int rows, in
   const uint4 los = make_uint4(lo.x ^ 0x80808080u, lo.y ^ 0x80808080u, lo.z ^ 0x80808080u, lo.w ^ 0x80808080u);
   reinterpret_cast<uint4*>(dst)[r] = los;                       // Wl' rows
   reinterpret_cast<uint4*>(dst + 2048)[r] = hi;                 // Wh rows
-  reinterpret_cast<int*>(dst + 4096)[r] = 128 * sw - 16 * 128 * 128;
-  reinterpret_cast<int8_t*>(dst + 4608)[r] = e;
-  reinterpret_cast<int8_t*>(blockp + (size_t)NT * TC_REC)[(size_t)r * tc_ntp(NT) + t] = e;
+  reinterpret_cast<int*>(blockp + tc_cw_off(NT))[(size_t)t * TC_M + r] = 128 * sw - 16 * 128 * 128;
+  reinterpret_cast<int8_t*>(blockp + tc_wt_off(NT))[(size_t)t * TC_M + r] = e;
+  reinterpret_cast<int8_t*>(blockp + tc_we_off(NT))[(size_t)r * tc_ntp(NT) + t] = e;
 }
 
 // ---------------------------------------------------------------------------
@@ -158,20 +172,22 @@ __global__ void tc_pack_kernel(const uint8_t* wm, const int8_t* we, int rows, in
 // CTAs of a cluster share the tiles; every CTA keeps all NT column exponents
 // for the max-exponent pass, and a 128 x NCB int64 block for the reduction).
 struct TcLayout {
-  size_t bar, tptr, ring, z, xe, xe16, cx, emin, wex, red, total;
+  size_t bar, tptr, ring, z, xe, xe16, cx, emin, wex, cwt, wet, red, total;
 };
 __host__ __device__ inline TcLayout tc_layout(int NT, int NCB, int ntl, bool split) {
   TcLayout L;
   L.bar = 0;                                           // mbarriers: ring full / empty, D full / empty, exponents
-  L.tptr = 112;                                        // TMEM base address
-  L.ring = 128;
+  L.tptr = 192;                                        // TMEM base address
+  L.ring = 256;
   L.z = L.ring + (size_t)TC_SA * TC_REC;
   L.xe = L.z + (size_t)(3 * ntl + 1) * NCB * 16;
   L.xe16 = L.xe + (size_t)NT * NCB * 4;
   L.cx = L.xe16 + (size_t)NT * NCB * 2;
   L.emin = L.cx + (size_t)ntl * NCB * 4;
   L.wex = (L.emin + (size_t)NT * 4 * 4 + 15) & ~(size_t)15;
-  L.red = L.wex + (size_t)TC_M * tc_ntp(NT);
+  L.cwt = L.wex + (size_t)TC_M * tc_ntp(NT);
+  L.wet = L.cwt + (size_t)ntl * TC_M * 4;
+  L.red = (L.wet + (size_t)ntl * TC_M + 15) & ~(size_t)15;
   L.total = L.red + (split ? (size_t)TC_M * NCB * 8 : 0);
   return L;
 }
@@ -196,13 +212,15 @@ __device__ __forceinline__ long long ld_peer_s64(const long long* p, unsigned ra
 // MMAs, warps 2..17 are the epilogue: warp w reads TMEM lanes 32 (w % 4) ..
 // +31 (the rows) for column quarter (w - 2) / 4 (CPT = NCB / 4 columns per
 // thread).  Records pass through a ring of TC_SA stages (full: TMA bytes;
-// empty: the MMA's commit and one arrival per epilogue warp), D through
-// TC_NB tensor-memory buffers (full: MMA commit; empty: the epilogue warps).
+// empty: the MMA's commit), D through TC_NB tensor-memory buffers of 128
+// columns (full: MMA commit; empty: the epilogue warps).  512 columns is the
+// whole of an SM's tensor memory: one CTA fits an SM (registers), and the
+// next kernel's CTAs allocate only after their dependency wait.
 // Split K: gridDim.z CTAs form a cluster over the K tiles of one output
 // block; each computes the full max exponent, accumulates its own tiles,
 // and cluster rank 0 adds the others' int64 sums through distributed shared
 // memory (integer addition: exact in any order) before the epilogue.
-constexpr int TC_NB = 2;
+constexpr int TC_NB = 4;
 constexpr int TC_EPI_WARPS = 16;
 
 template <int NCB, int MODE>
@@ -232,21 +250,31 @@ tc_matmul_kernel(TcArgs a) {
   int* emin_s = reinterpret_cast<int*>(smem + L.emin);       // [NT][4]: min column exponent per column quarter
   long long* red = reinterpret_cast<long long*>(smem + L.red); // [NCB][128] (split K)
   const unsigned char* wex_s = smem + L.wex;                  // [128][NTP] tile exponents of the block's rows
+  const int* cw_s = reinterpret_cast<const int*>(smem + L.cwt); // [ntl][128] limb corrections of this CTA's tiles
+  const int8_t* wt_s = reinterpret_cast<const int8_t*>(smem + L.wet); // [ntl][128] their tile exponents
   const uint8_t* rec = a.rec + (size_t)blk * tc_block_bytes(NT);
   const uint8_t* rec_k = rec + (size_t)t_lo * TC_REC;         // this CTA's first K tile
   pdl_trigger_tc();
   // ---- barriers and the first weight records: the weights do not depend on
   // the previous kernel, so they stream before the wait
   if (tid == 0) {
-    for (int s = 0; s < TC_SA; ++s) { mb_init(&rfull[s], 1); mb_init(&rempty[s], 1 + TC_EPI_WARPS); }
+    for (int s = 0; s < TC_SA; ++s) { mb_init(&rfull[s], 1); mb_init(&rempty[s], 1); }
     for (int b = 0; b < TC_NB; ++b) { mb_init(&dfull[b], 1); mb_init(&dempty[b], TC_EPI_WARPS); }
     mb_init(wbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     {
-      const unsigned wbytes = (unsigned)(TC_M * tc_ntp(NT));
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(wbar)), "r"(wbytes) : "memory");
+      const unsigned wbytes = (unsigned)(TC_M * tc_ntp(NT)), cbytes = (unsigned)(ntl * TC_M * 4),
+                     tbytes = (unsigned)(ntl * TC_M);
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(wbar)), "r"(wbytes + cbytes + tbytes)
+                   : "memory");
       asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                   :: "r"(su32(wex_s)), "l"(rec + (size_t)NT * TC_REC), "r"(wbytes), "r"(su32(wbar)) : "memory");
+                   :: "r"(su32(wt_s)), "l"(rec + tc_wt_off(NT) + (size_t)t_lo * TC_M), "r"(tbytes), "r"(su32(wbar))
+                   : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   :: "r"(su32(wex_s)), "l"(rec + tc_we_off(NT)), "r"(wbytes), "r"(su32(wbar)) : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   :: "r"(su32(cw_s)), "l"(rec + tc_cw_off(NT) + (size_t)t_lo * TC_M * 4), "r"(cbytes), "r"(su32(wbar))
+                   : "memory");
     }
     for (int s = 0; s < TC_SA && s < ntl; ++s) {
       asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(su32(&rfull[s])), "r"(TC_REC) : "memory");
@@ -259,7 +287,7 @@ tc_matmul_kernel(TcArgs a) {
   // tensor memory only after the wait: a CTA waiting on its predecessor holds
   // none, so the predecessor's CTAs can always allocate theirs
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" :: "r"(su32(tptr)) : "memory");
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" :: "r"(su32(tptr)) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   // ---- B operand of every tile, column exponents and sums (columns c0 .. c0+NCB-1)
@@ -372,36 +400,48 @@ tc_matmul_kernel(TcArgs a) {
       const int NTP = tc_ntp(NT);
       mb_wait(wbar, 0u, a.err);                              // the table, copied before the dependency wait
       const uint4* wrow = reinterpret_cast<const uint4*>(wex_s + (size_t)row * NTP);
-      unsigned m2[CPT / 2];
+      // four independent chains (tile t in chain t % 4), merged at the end
+      unsigned m2[4][CPT / 2];
       #pragma unroll
-      for (int k = 0; k < CPT / 2; ++k) m2[k] = 0x8AD08AD0u;            // -30000 in both lanes
-      for (int t0 = 0; t0 < NT; t0 += 16) {
+      for (int c = 0; c < 4; ++c)
+        #pragma unroll
+        for (int k = 0; k < CPT / 2; ++k) m2[c][k] = 0x8AD08AD0u;       // -30000 in both lanes
+      auto step = [&](int t, unsigned wbyte, unsigned (&m)[CPT / 2]) {
+        const unsigned we2 = (unsigned)(uint16_t)(int16_t)(int8_t)wbyte * 0x10001u;
+        const int16_t* xr = xe16_s + t * NCB + cb;
+        if constexpr (CPT == 8) {
+          const uint4 x8 = *reinterpret_cast<const uint4*>(xr);
+          m[0] = __viaddmax_s16x2(we2, x8.x, m[0]);
+          m[1] = __viaddmax_s16x2(we2, x8.y, m[1]);
+          m[2] = __viaddmax_s16x2(we2, x8.z, m[2]);
+          m[3] = __viaddmax_s16x2(we2, x8.w, m[3]);
+        } else {
+          const uint2 x4 = *reinterpret_cast<const uint2*>(xr);
+          m[0] = __viaddmax_s16x2(we2, x4.x, m[0]);
+          m[1] = __viaddmax_s16x2(we2, x4.y, m[1]);
+        }
+      };
+      int t0 = 0;
+      for (; t0 + 16 <= NT; t0 += 16) {                     // whole groups of 16 tiles: no guards
         const uint4 w16 = wrow[t0 / 16];
         const unsigned ww[4] = {w16.x, w16.y, w16.z, w16.w};
         #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const int t = t0 + k;
-          if (t < NT) {
-            const unsigned we2 = (unsigned)(uint16_t)(int16_t)(int8_t)(ww[k >> 2] >> (8 * (k & 3))) * 0x10001u;
-            const int16_t* xr = xe16_s + t * NCB + cb;
-            if constexpr (CPT == 8) {
-              const uint4 x8 = *reinterpret_cast<const uint4*>(xr);
-              m2[0] = __viaddmax_s16x2(we2, x8.x, m2[0]);
-              m2[1] = __viaddmax_s16x2(we2, x8.y, m2[1]);
-              m2[2] = __viaddmax_s16x2(we2, x8.z, m2[2]);
-              m2[3] = __viaddmax_s16x2(we2, x8.w, m2[3]);
-            } else {
-              const uint2 x4 = *reinterpret_cast<const uint2*>(xr);
-              m2[0] = __viaddmax_s16x2(we2, x4.x, m2[0]);
-              m2[1] = __viaddmax_s16x2(we2, x4.y, m2[1]);
-            }
-          }
-        }
+        for (int k = 0; k < 16; ++k) step(t0 + k, ww[k >> 2] >> (8 * (k & 3)), m2[k & 3]);
+      }
+      if (t0 < NT) {
+        const uint4 w16 = wrow[t0 / 16];
+        const unsigned ww[4] = {w16.x, w16.y, w16.z, w16.w};
+        #pragma unroll
+        for (int k = 0; k < 16; ++k)
+          if (t0 + k < NT) step(t0 + k, ww[k >> 2] >> (8 * (k & 3)), m2[k & 3]);
       }
       #pragma unroll
+      for (int k = 0; k < CPT / 2; ++k)
+        m2[0][k] = __vmaxs2(__vmaxs2(m2[0][k], m2[1][k]), __vmaxs2(m2[2][k], m2[3][k]));
+      #pragma unroll
       for (int k = 0; k < CPT / 2; ++k) {
-        Mx[2 * k] = (int)(int16_t)(m2[k] & 0xFFFFu);
-        Mx[2 * k + 1] = (int)(int16_t)(m2[k] >> 16);
+        Mx[2 * k] = (int)(int16_t)(m2[0][k] & 0xFFFFu);
+        Mx[2 * k + 1] = (int)(int16_t)(m2[0][k] >> 16);
       }
     }
     int MxMax = Mx[0];
@@ -424,7 +464,7 @@ tc_matmul_kernel(TcArgs a) {
     #pragma unroll
     for (int j = 0; j < CPT; ++j) acc[j] = 0;
     for (int t = 0; t < ntl; ++t) {
-      const int s = t % TC_SA, b = t % TC_NB, tg = t_lo + t;
+      const int b = t % TC_NB, tg = t_lo + t;
       // the three limb sums of tile t
       mb_wait(&dfull[b], (unsigned)((t / TC_NB) & 1), a.err);
       tc_fence_after();
@@ -437,13 +477,9 @@ tc_matmul_kernel(TcArgs a) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(su32(&dempty[b])) : "memory");
-      // the row's correction and exponent of tile t (complete: orders the reads)
-      mb_wait(&rfull[s], (unsigned)((t / TC_SA) & 1), a.err);
-      const unsigned char* rs = ring + (size_t)s * TC_REC;
-      const int cw = reinterpret_cast<const int*>(rs + 4096)[row];
-      const int wer = reinterpret_cast<const int8_t*>(rs + 4608)[row];
-      __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(su32(&rempty[s])) : "memory");
+      // the row's correction and exponent of tile t (tables in shared memory)
+      const int cw = cw_s[t * TC_M + row];
+      const int wer = (int)wt_s[t * TC_M + row];
       // per-tile floor shift and int64 accumulation (:223-228).  S = 65536 hh + w
       // with w = 256 cr + lo (|w| < 2^29).  When every shift of this warp's
       // pairs is at most 16 (a bound from the row's largest max exponent and
@@ -581,7 +617,7 @@ tc_matmul_kernel(TcArgs a) {
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" :: "r"(tbase) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" :: "r"(tbase) : "memory");
   }
 }
 
