@@ -881,6 +881,198 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   }
 }
 
+// Batched GQA attention with one CTA per (column, KV head): the grp query
+// heads that share a KV head use one staged copy of its K / V rows, and their
+// grp x 64 sequential accumulations run side by side (a thread per head and
+// dimension).  Per head: the same operations in the same order as
+// attention_kernel (scores four lanes per position, softmax_fp with numpy's
+// pairwise sum, sm[t] * v[t] accumulated sequentially in t).  Needs grp * 64
+// <= ATT_THREADS.
+constexpr int ATT_MAXG = ATT_THREADS / 64;
+__host__ __device__ inline size_t att_group_sc_stride(int max_ctx) { return ((size_t)max_ctx + 1) & ~size_t(1); }
+
+__global__ void __launch_bounds__(ATT_THREADS)
+attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
+                       double sqrt_hd, double inv_hd, int16_t* am, int8_t* ae, const int* pw_off,
+                       const unsigned short* pw_data, int early) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int HD = 64;
+  constexpr int VCH = att_vchunk(true);
+  __shared__ int s_qm[ATT_MAXG * HD];
+  __shared__ int s_qe[ATT_MAXG * 4];
+  __shared__ double s_red[ATT_THREADS / 32][ATT_MAXG];
+  __shared__ double s_mx[ATT_MAXG], s_sum[ATT_MAXG];
+  __shared__ double s_val[ATT_MAXG][160];
+  __shared__ unsigned short s_plan[ATT_PLAN_MAX];
+  pdl_trigger();
+  const int c = blockIdx.x, kvh = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = d.HQ / d.HKV, h0 = kvh * grp;
+  const size_t scs = att_group_sc_stride(d.MAX_CTX);
+  double* sc = reinterpret_cast<double*>(smem);                                     // [grp][scs]
+  const size_t sc_bytes = ((size_t)grp * scs * 8 + 15) & ~size_t(15);
+  uint4* vs = reinterpret_cast<uint4*>(smem + sc_bytes);                           // [VCH][8]
+  unsigned* ves = reinterpret_cast<unsigned*>(smem + sc_bytes + VCH * 128);        // [VCH]
+  uint4* ks = reinterpret_cast<uint4*>(smem + sc_bytes + VCH * 132);               // [VCH][8], swizzled
+  unsigned* kes = reinterpret_cast<unsigned*>(smem + sc_bytes + VCH * 260);        // [VCH]
+  if (!early) pdl_wait();
+  const int slot = cols.slot[c], pos = cols.pos[c];
+  const int T = pos + 1;
+  const int n0 = min(VCH, T), nold = min(VCH, pos);
+  const size_t kbase = (((size_t)slot * d.NL + layer) * d.HKV + kvh) * d.MAX_CTX;
+  {
+    const uint4* ksrc = reinterpret_cast<const uint4*>(kv.km + kbase * HD);
+    const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + kbase * HD);
+    for (int i = tid; i < nold * 8; i += ATT_THREADS) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(ks + att_kswz(i))),
+                   "l"(ksrc + i) : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(vs + i)),
+                   "l"(vsrc + i) : "memory");
+    }
+    const unsigned* kesrc = reinterpret_cast<const unsigned*>(kv.ke + kbase * 4);
+    const unsigned* vesrc = reinterpret_cast<const unsigned*>(kv.ve + kbase * 4);
+    for (int i = tid; i < nold; i += ATT_THREADS) {
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"((unsigned)__cvta_generic_to_shared(kes + i)),
+                   "l"(kesrc + i) : "memory");
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"((unsigned)__cvta_generic_to_shared(ves + i)),
+                   "l"(vesrc + i) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  const unsigned short* plan;
+  {
+    const unsigned short* gp = pw_data + pw_off[T];
+    const int np = 3 * (int)gp[0] + (int)gp[1];
+    if (np <= ATT_PLAN_MAX) {
+      for (int i = tid; i < np; i += ATT_THREADS) s_plan[i] = gp[i];
+      plan = s_plan;
+    } else {
+      plan = gp;
+    }
+  }
+  if (early) pdl_wait();
+  for (int i = tid; i < grp * HD; i += ATT_THREADS) s_qm[i] = qr_m[(size_t)c * d.HQ * HD + (size_t)h0 * HD + i];
+  if (tid < grp * 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h0 * 4 + tid];
+  if (pos < VCH) {
+    if (tid < 8) ks[att_kswz(pos * 8 + tid)] = reinterpret_cast<const uint4*>(kv.km + (kbase + pos) * HD)[tid];
+    else if (tid < 16) vs[pos * 8 + tid - 8] = reinterpret_cast<const uint4*>(kv.vm + (kbase + pos) * HD)[tid - 8];
+    else if (tid == 16) kes[pos] = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + pos) * 4);
+    else if (tid == 17) ves[pos] = *reinterpret_cast<const unsigned*>(kv.ve + (kbase + pos) * 4);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  // scores (:278), four lanes per (head, position), one 16-element tile each
+  const bool pow2_hd = inv_hd != 0.0;
+  const int jt = tid & 3, qb = lane & ~3;
+  for (int h = 0; h < grp; ++h) {
+    const int* qp = s_qm + h * HD + jt * 16;
+    double lmax = -INFINITY;
+    for (int t0 = 0; t0 < T; t0 += ATT_THREADS / 4) {
+      const int t = t0 + (tid >> 2);
+      long long S = 0;
+      int E = 0;
+      if (t < T) {
+        uint4 k0, k1;
+        unsigned ke4;
+        if (t < n0) {
+          k0 = ks[t * 8 + ((2 * jt) ^ (t & 7))];
+          k1 = ks[t * 8 + ((2 * jt + 1) ^ (t & 7))];
+          ke4 = kes[t];
+        } else {
+          const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
+          k0 = kr[2 * jt];
+          k1 = kr[2 * jt + 1];
+          ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
+        }
+        const unsigned w[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          S += (long long)qp[2 * u] * (int)(int16_t)(w[u] & 0xFFFF);
+          S += (long long)qp[2 * u + 1] * (int)(int16_t)(w[u] >> 16);
+        }
+        E = s_qe[h * 4 + jt] + (int)(int8_t)(ke4 >> (8 * jt));
+      }
+      long long S4[4];
+      int E4[4];
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        S4[j] = __shfl_sync(0xffffffffu, S, qb + j);
+        E4[j] = __shfl_sync(0xffffffffu, E, qb + j);
+      }
+      if (t < T && jt == 0) {
+        const double dot = exact_tile_dot4(S4, E4);
+        const double v = pow2_hd ? __dmul_rn(dot, inv_hd) : __ddiv_rn(dot, sqrt_hd);
+        sc[h * scs + t] = v;
+        lmax = v > lmax ? v : lmax;
+      }
+    }
+    for (int off = 16; off; off >>= 1) {
+      const double o = __shfl_xor_sync(0xffffffffu, lmax, off);
+      lmax = o > lmax ? o : lmax;
+    }
+    if (lane == 0) s_red[warp][h] = lmax;
+  }
+  __syncthreads();
+  if (tid < grp) {
+    double mx = s_red[0][tid];
+    for (int w = 1; w < ATT_THREADS / 32; ++w) mx = s_red[w][tid] > mx ? s_red[w][tid] : mx;
+    s_mx[tid] = mx;
+  }
+  __syncthreads();
+  // softmax_fp (:245-247) per head
+  for (int i = tid; i < grp * T; i += ATT_THREADS) {
+    const int h = i / T, t = i - h * T;
+    sc[h * scs + t] = exp(__dsub_rn(sc[h * scs + t], s_mx[h]));
+  }
+  __syncthreads();
+  if (warp < grp) {
+    const double S = np_sum_warp_plan(sc + warp * scs, T, plan, s_val[warp]);
+    if (lane == 0) s_sum[warp] = S;
+  }
+  __syncthreads();
+  for (int i = tid; i < grp * T; i += ATT_THREADS) {
+    const int h = i / T, t = i - h * T;
+    sc[h * scs + t] = __ddiv_rn(sc[h * scs + t], s_sum[h]);
+  }
+  // attn[h] += sm[t] * v[t], sequential in t (:280-281), one thread per (head, dimension)
+  const int hh = tid / HD, dim = tid % HD;
+  const bool acc_thread = hh < grp;
+  const double* smh = sc + (size_t)(acc_thread ? hh : 0) * scs;
+  double acc = 0.0;
+  for (int c0 = 0; c0 < T; c0 += VCH) {
+    const int n = min(VCH, T - c0);
+    if (c0 > 0) {
+      __syncthreads();
+      const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + (kbase + c0) * HD);
+      for (int i = tid; i < n * 8; i += ATT_THREADS) vs[i] = vsrc[i];
+      const unsigned* esrc = reinterpret_cast<const unsigned*>(kv.ve + (kbase + c0) * 4);
+      for (int i = tid; i < n; i += ATT_THREADS) ves[i] = esrc[i];
+    }
+    __syncthreads();
+    if (acc_thread) {
+      const int16_t* vrow = reinterpret_cast<const int16_t*>(vs) + dim;
+      const int sh = 8 * (dim >> 4);
+      #pragma unroll 8
+      for (int t = 0; t < n; ++t) {
+        const int e = (int)(int8_t)(ves[t] >> sh);
+        const double vv = bfp_decode(vrow[(size_t)t * HD], e);
+        acc = __dadd_rn(acc, __dmul_rn(smh[c0 + t], vv));
+      }
+    }
+  }
+  if (acc_thread) {                      // whole warps: grp * 64 threads
+    int e;
+    int16_t m = tile_quantize_16lanes(acc, &e);             // fpq(attn)   (:282)
+    const unsigned bal = __ballot_sync(0xffffffffu, m == (int16_t)-32768);
+    const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
+    m = requant_mant(m, has_min && e < 127);               // tile_quantize(attn) (:283)
+    e = requant_exp(e, has_min);
+    const size_t hq = (size_t)c * d.HQ + h0 + hh;
+    am[hq * HD + dim] = m;
+    if ((dim & 15) == 0) ae[hq * 4 + dim / 16] = (int8_t)e;
+  }
+}
+
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
                              int ncols, int16_t* am, int8_t* ae, cudaStream_t s, bool pdl, const int* pw_off,
                              const unsigned short* pw_data, bool early_kv) {
@@ -893,6 +1085,20 @@ cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv
   if (!lanes4)
     return launch_ex(attention_kernel<false>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv,
                      layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
+  // per KV head when that still gives every SM at least two CTAs
+  static int nsm = 0;
+  if (nsm == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      nsm = 148;
+  }
+  const int grp = d.HQ / d.HKV;
+  if (d.HD == 64 && grp * d.HKV == d.HQ && grp * 64 <= ATT_THREADS && (long long)ncols * d.HKV >= 2LL * nsm) {
+    const size_t gsm = (((size_t)grp * att_group_sc_stride(d.MAX_CTX) * 8 + 15) & ~size_t(15)) +
+                       (size_t)att_vchunk(true) * 264;
+    return launch_ex(attention_group_kernel, dim3(ncols, d.HKV), dim3(ATT_THREADS), gsm, s, pdl, qr_m, qr_e, kv,
+                     layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
+  }
   return launch_ex(attention_kernel<true>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
                    cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
 }
@@ -1837,6 +2043,7 @@ cudaError_t init_kernel_attributes() {
   set((const void*)head_prep_kernel);
   set((const void*)attention_kernel<false>);
   set((const void*)attention_kernel<true>);
+  set((const void*)attention_group_kernel);
   set((const void*)rmsnorm_fp_kernel);
   set((const void*)softmax_fp_kernel);
   set((const void*)np_sum_kernel);
