@@ -18,6 +18,7 @@
 #include <tuple>
 #include <cmath>
 #include <cstdlib>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <numeric>
@@ -540,6 +541,9 @@ int tc_tune(bfp200_handle* h, TcArgs t, const std::tuple<int, int, int, int>& ke
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   h->tc_cfg[key] = pick;                 // {0, 0}: the built-in choice
+  if (const char* lg = std::getenv("BFP200_TC_LOG"); lg && *lg && *lg != '0')
+    std::fprintf(stderr, "bfp200: tensor-core matmul %d x %d at %d columns (epilogue %d): %d columns per CTA, K split %d, "
+                 "%.1f us\n", t.rows, t.NT * 16, t.ncols, t.mode, pick.first, pick.second, best * 1e3f / 2.f);
   return BFP200_OK;
 }
 
