@@ -386,12 +386,18 @@ tc_matmul_kernel(TcArgs a) {
     // exponents come from the block's exponent table, 16 at a time
     #pragma unroll
     for (int j = 0; j < CPT; ++j) Mx[j] = -100000;
-    if (q == 0) {
+    if (q == 0) {                   // smallest column exponent of the quarter, per tile (one vector load each)
       for (int t = lane; t < NT; t += 32) {
-        int mn = xe_s[t * NCB + cb];
-        #pragma unroll
-        for (int j = 1; j < CPT; ++j) mn = min(mn, xe_s[t * NCB + cb + j]);
-        emin_s[t * 4 + quarter] = mn;
+        const int16_t* xr = xe16_s + t * NCB + cb;
+        unsigned m;
+        if constexpr (CPT == 8) {
+          const uint4 x8 = *reinterpret_cast<const uint4*>(xr);
+          m = __vmins2(__vmins2(x8.x, x8.y), __vmins2(x8.z, x8.w));
+        } else {
+          const uint2 x4 = *reinterpret_cast<const uint2*>(xr);
+          m = __vmins2(x4.x, x4.y);
+        }
+        emin_s[t * 4 + quarter] = min((int)(int16_t)(m & 0xFFFFu), (int)(int16_t)(m >> 16));
       }
     }
     {
