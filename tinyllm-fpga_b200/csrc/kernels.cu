@@ -1086,12 +1086,9 @@ cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv
     return launch_ex(attention_kernel<false>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv,
                      layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
   // per KV head when that still gives every SM at least two CTAs
-  static int nsm = 0;
-  if (nsm == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      nsm = 148;
-  }
+  int dev = 0, nsm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return cudaErrorInvalidDevice;
   const int grp = d.HQ / d.HKV;
   if (d.HD == 64 && grp * d.HKV == d.HQ && grp * 64 <= ATT_THREADS && (long long)ncols * d.HKV >= 2LL * nsm) {
     const size_t gsm = (((size_t)grp * att_group_sc_stride(d.MAX_CTX) * 8 + 15) & ~size_t(15)) +
