@@ -13,13 +13,16 @@ does not shard, so N GPUs run N independent streams -- weak scaling).
 The same line carries ``bs256``: configs[2] = "cfg3", 256 ragged sequences
 x 128 tokens, sequences split over the ranks with no collectives.
 
-Further keys: ``roofline`` (the bs1 gemv kernels against the measured HBM copy
-bandwidth, with their measured DRAM traffic), ``bs256.roofline`` (the batched
-tensor-core matvecs), ``cfg5`` (per-kernel times at batch 64 / KV 2047, rank
-0), ``cfg4`` (the isolated matvec over the model's weight shapes x batch 1 ..
-1024, rank 0), ``cpu_baseline`` (the oracle port on one host core, rank 0) and,
-with ``--sharded-head`` at N > 1, ``sharded_head`` (single-stream decode with
-the vocabulary-sharded head).
+Further keys of the final line: ``roofline`` (the bs1 matvec kernels against
+the measured HBM copy bandwidth), ``path_roofline_frac`` (weight + KV bytes
+per token over the decode time), ``bs256`` (tok/s, ms per step, and the
+batched tensor-core matvecs' roofline), ``cpu_baseline`` (the oracle port on
+all usable host cores, rank 0 at N = 1) and, at N > 1, ``sharded_head``
+(single-stream decode with the vocabulary-sharded head; ``--no-sharded-head``
+skips it).  The bulky sections -- ``cfg5`` (per-kernel times at batch 64 / KV
+2047), ``cfg4`` (the isolated matvec over the model's weight shapes x batch
+1 .. 1024) and ``kernel_profile_ms`` -- go on a preceding line
+``{"detail": ...}``, so the last line stays short.
 
 ``--impl reference`` times the reference algorithm on the host cores (the
 numpy restatement under oracle/, since the reference is Python that cannot
@@ -168,6 +171,9 @@ def run_ours(args, world, rank, local):
     from bfp200 import BfpConfig, Decoder, synth, _lib
 
     pk, pk_kind = peaks()
+    # the CPU baseline runs first, before this process touches the GPU, so its
+    # worker pool can fork (rank 0 at N = 1 only)
+    cpu = cpu_baselines(args) if (rank == 0 and world == 1 and not args.no_cpu) else None
     cfg2 = BfpConfig(MAX_CTX=48 + 256, max_seqs=256)
     t0 = time.time()
     img = synth.synthetic_image(BfpConfig(), seed=0)
@@ -219,7 +225,7 @@ def run_ours(args, world, rank, local):
     mm = {"ms_per_token": mm_ms, "launches": mm_n}
     achieved_gbs = wbytes / (mm["ms_per_token"] / 1e3) / 1e9
     peak = pk["hbm_gbs"]
-    roof = {"kernel": "gemv_kernel (fused QKV / O / gate-up / down matvecs, bs1)", "bound": "hbm", "achieved": round(achieved_gbs, 1),
+    roof = {"kernel": "bfp_gemv_small_kernel (fused QKV / O / gate-up / down matvecs, bs1)", "bound": "hbm", "achieved": round(achieved_gbs, 1),
             "peak": peak, "unit": "GB/s", "frac": round(achieved_gbs / peak, 4), "traffic": GEMV_TRAFFIC_PER_TOKEN,
             "traffic_unit": "bytes per token (120 launches, ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "algorithmic_bytes": wbytes,
@@ -243,7 +249,8 @@ def run_ours(args, world, rank, local):
             b_ms.append(t["prefill_ms"] + t["decode_ms"])
         barrier(world)
         b_step = max_over_ranks(statistics.mean(b_ms), world)
-        bs256 = {"value": round(len(prompts3) * ngen3 / (b_step / 1e3), 1), "unit": "tok/s",
+        bs256 = {"metric": "BFP decode tok/s (bs256, cfg3)",
+                 "value": round(len(prompts3) * ngen3 / (b_step / 1e3), 1), "unit": "tok/s",
                  "ms_per_step": round(b_step, 3), "sequences": len(prompts3), "n_gen": ngen3,
                  "scaling": "strong", "uncertified_steps": dec.uncertified_steps()}
         if part3:
@@ -253,7 +260,7 @@ def run_ours(args, world, rank, local):
     if not args.no_bs256 and part3:
         profile["bs256_pos100"] = dec.profile_forward(len(part3), 100)
     sharded = None
-    if world > 1 and args.sharded_head:
+    if world > 1 and not args.no_sharded_head:
         sharded = sharded_head_run(dec, prompts2, ngen2, args, world, decode_tok_ms)
     dec.close()
     cfg5 = None
@@ -282,17 +289,17 @@ def run_ours(args, world, rank, local):
                 "d2h_bytes_per_step": (48 + ngen2) * 4 + 8},
         "gpu_launches": int(sum_over_ranks(launches, world)),
         "bs256": bs256,
-        "kernel_profile_ms": profile,
-        "cfg5": cfg5,
-        "cfg4": cfg4,
         "sharded_head": sharded,
         "uncertified_steps": uncert,
         "image_build_s": round(build_s, 1),
         "clocks": clk.summary(),
     }
-    if rank == 0 and not args.no_cpu:
-        res["cpu_baseline"] = cpu_baseline(args)
-    return res
+    if cpu is not None:
+        res["cpu_baseline"] = cpu["cfg2"]
+        if bs256 is not None:
+            bs256["cpu_baseline"] = cpu["cfg3"]
+    detail = {"kernel_profile_ms": profile, "cfg5": cfg5, "cfg4": cfg4}
+    return res, detail
 
 
 CFG4_SHAPES = ((576, 576), (192, 576), (1536, 576), (576, 1536), (49152, 576))
@@ -341,7 +348,7 @@ def sharded_head_run(dec, prompts, n_gen, args, world, replica_tok_ms):
             "vocab_rows_per_rank": 49152 // world, "exchange": "NCCL all-gather of 32 B per rank per step"}
 
 
-# DRAM bytes (read + write) of one token's 120 gemv_kernel launches, from an
+# DRAM bytes (read + write) of one token's 120 bfp_gemv_small_kernel launches, from an
 # ncu capture of one decode-graph replay (dram__bytes_read.sum +
 # dram__bytes_write.sum over the launches); the algorithmic weight bytes are
 # 218,972,160, the rest is activations, gammas and the RoPE table.
@@ -366,59 +373,42 @@ def batched_roofline(dec, ncols, reps, pk, pk_kind):
             "int16_macs_per_s": round(LAYER_MACS * ncols / (ms / 1e3) / 1e12, 3)}
 
 
-def cpu_baseline(args):
-    """The oracle port (numpy restatement of the reference simulator) on the
-    host: steady-state decode of the cfg2 stream at its mean context (KV
-    length 176), 1 stream.  Sample: 6 decode steps."""
-    sys.path.insert(0, REPO)
-    from oracle import bfp_oracle as O
-    from oracle import synth as OS
-    model = OS.make_model(0)
-    model.cache_float_weights()
-    cfg = O.Cfg()
-    kv = O.new_kv(cfg, 304)
-    rng = np.random.default_rng(0)
-    for li in range(cfg.NL):       # a KV cache of 176 positions (values do not change the cost)
-        kv[li]["k"][:176] = O.fp_quantize_vec(rng.standard_normal(176 * 192)).reshape(176, 3, 64)
-        kv[li]["v"][:176] = O.fp_quantize_vec(rng.standard_normal(176 * 192)).reshape(176, 3, 64)
-    n = 6
-    t = time.perf_counter()
-    tok = 123
-    for s in range(n):
-        pos = 176 + s
-        h = model.embed_q(tok)
-        cs = O.rope_cos_sin(pos)
-        for li in range(cfg.NL):
-            h = O.fwd_layer(h, model.layers[li], pos, kv[li], pos, cfg, cs=cs)
-        tok = int(np.argmax(O.head_logits(h, model.norm_w_q, model.embed)))
-    dt = time.perf_counter() - t
-    return {"value": round(n / dt, 4), "unit": "tok/s", "cores": 1, "kind": "port",
-            "sample": f"{n} decode steps of one cfg2 stream at KV length 176..{176 + n - 1}, numpy oracle, 1 process"}
+# ---------------------------------------------------------------------------
+# CPU side: the oracle port (numpy restatement of the reference simulator),
+# one decode stream per host process.  The model is built once in the parent
+# and the workers fork from it (copy-on-write), which is why the GPU arm runs
+# these samples before it touches the GPU.
+_CPU_MODEL = None
 
 
-def run_reference(args, world, rank):
-    """--impl reference: the reference algorithm (oracle port) on host cores."""
-    if rank != 0:
-        return None
-    sys.path.insert(0, REPO)
+def _cpu_model():
+    global _CPU_MODEL
+    if _CPU_MODEL is None:
+        sys.path.insert(0, REPO)
+        from oracle import synth as OS
+        _CPU_MODEL = OS.make_model(0)
+        _CPU_MODEL.cache_float_weights()
+    return _CPU_MODEL
+
+
+def _cpu_stream(job):
+    """Worker: decode n_steps x per_step tokens of one stream from KV length
+    kv_len (cache filled with quantized N(0,1) values: the values do not
+    change the cost); returns the wall seconds of each step."""
+    kv_len, n_steps, per_step, seed = job
+    from threadpoolctl import threadpool_limits
     from oracle import bfp_oracle as O
-    from oracle import synth as OS
-    model = OS.make_model(0)
-    model.cache_float_weights()
+    threadpool_limits(1)
+    model = _cpu_model()
     cfg = O.Cfg()
-    prompt = OS.config_prompts(2)[0][0]
-    kv = O.new_kv(cfg, 304)
-    # prefill the 48-token prompt once (untimed), then time decode steps
-    h = None
-    for pos, tid in enumerate(prompt):
-        h = model.embed_q(tid)
-        cs = O.rope_cos_sin(pos)
-        for li in range(cfg.NL):
-            h = O.fwd_layer(h, model.layers[li], pos, kv[li], pos, cfg, cs=cs)
-    tok, pos = prompt[-1], len(prompt)
-    per_step = 2
+    kv = O.new_kv(cfg, kv_len + n_steps * per_step)
+    rng = np.random.default_rng(seed)
+    for li in range(cfg.NL):
+        for k in ("k", "v"):
+            kv[li][k][:kv_len] = O.fp_quantize_vec(rng.standard_normal(kv_len * 192)).reshape(kv_len, 3, 64)
+    tok, pos = 123 + seed, kv_len
     times = []
-    for it in range(args.warmup + args.steps):
+    for _ in range(n_steps):
         t = time.perf_counter()
         for _ in range(per_step):
             h = model.embed_q(tok)
@@ -427,23 +417,96 @@ def run_reference(args, world, rank):
                 h = O.fwd_layer(h, model.layers[li], pos, kv[li], pos, cfg, cs=cs)
             tok = int(np.argmax(O.head_logits(h, model.norm_w_q, model.embed)))
             pos += 1
-            if pos >= 304:
-                kv = O.new_kv(cfg, 304)
-                pos = 0
-        if it >= args.warmup:
-            times.append(time.perf_counter() - t)
-    step_s = statistics.mean(times)
-    v = per_step / step_s
+        times.append(time.perf_counter() - t)
+    return times
+
+
+def _host_info(procs):
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "usable": len(os.sched_getaffinity(0)), "cpu_model": model, "processes": procs}
+
+
+def _cpu_procs(args):
+    usable = len(os.sched_getaffinity(0))
+    return max(1, args.cpu_procs or min(32, usable))
+
+
+def _run_streams(jobs, procs):
+    """Runs the jobs on `procs` forked workers; returns their per-step times."""
+    import multiprocessing as mp
+    _cpu_model()
+    torch_mod = sys.modules.get("torch")
+    if torch_mod is not None and torch_mod.cuda.is_initialized():
+        raise RuntimeError("CPU baseline must run before the process initialises CUDA (workers fork)")
+    with mp.get_context("fork").Pool(procs) as pool:
+        return pool.map(_cpu_stream, jobs, chunksize=1)
+
+
+def cpu_baselines(args):
+    """The oracle port on the host cores (one stream per process).
+    cfg2: one stream per process decoding at KV length 176 (the cfg2 mean),
+    aggregate tok/s.  cfg3: the first 32 cfg3 sequences, each decoding 2
+    tokens at its mid-generation KV length (prompt + 64), aggregate tok/s."""
+    procs = _cpu_procs(args)
+    info = _host_info(procs)
+    steps2 = 3
+    t = time.perf_counter()
+    res2 = _run_streams([(176, steps2, 1, 10 + i) for i in range(procs)], procs)
+    wall2 = time.perf_counter() - t
+    v2 = procs * steps2 / max(sum(r) for r in res2)
+    sys.path.insert(0, REPO)
+    from oracle import synth as OS
+    prompts3, _ = OS.config_prompts(3)
+    jobs3 = [(len(p) + 64, 1, 2, 100 + i) for i, p in enumerate(prompts3[:32])]
+    t = time.perf_counter()
+    _run_streams(jobs3, procs)
+    wall3 = time.perf_counter() - t
+    v3 = 2 * len(jobs3) / wall3
+    return {
+        "cfg2": dict(value=round(v2, 3), unit="tok/s", cores=procs, kind="port",
+                     sample=f"{procs} processes x {steps2} decode steps of a cfg2-shaped stream at KV length 176 "
+                            f"(numpy oracle, 1 BLAS thread each; {wall2:.1f} s wall)", **info),
+        "cfg3": dict(value=round(v3, 3), unit="tok/s", cores=procs, kind="port",
+                     sample=f"first 32 cfg3 sequences x 2 decode steps at KV length prompt+64, {procs} processes "
+                            f"(numpy oracle, 1 BLAS thread each; {wall3:.1f} s wall)", **info),
+    }
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference algorithm (the numpy restatement of the
+    simulator under oracle/) on the host cores, rank 0 only: one cfg2 stream
+    per process, every process decoding `per_step` tokens per step from KV
+    length 48 (the end of the cfg2 prompt); a step's time is the slowest
+    process's, value = processes x per_step / mean step time."""
+    if rank != 0:
+        return None
+    procs = _cpu_procs(args)
+    per_step = 2
+    n = args.warmup + args.steps
+    res = _run_streams([(48, n, per_step, 20 + i) for i in range(procs)], procs)
+    step_s = [max(r[i] for r in res) for i in range(args.warmup, n)]
+    mean_s = statistics.mean(step_s)
+    v = procs * per_step / mean_s
+    info = _host_info(procs)
     return {"impl": "reference", "metric": "BFP decode tok/s (bs1, cfg2)", "value": round(v, 4), "unit": "tok/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 1),
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(mean_s * 1e3, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64/f64",
             "data": "synthetic",
-            "config": {"workload": "cfg2: 48-token prompt + greedy decode, bs1, KV<=304",
-                       "model": "SmolLM2-135M arch, seeded random BFP weights", "global_batch": 1, "seq_len": 304,
-                       "parallelism": "host"},
-            "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": 1, "kind": "port",
-                             "sample": f"{per_step} decode steps per timed step of the cfg2 stream "
-                                       "(numpy restatement of the reference simulator)"},
+            "config": {"workload": "cfg2: 48-token prompt + greedy decode, bs1 per stream, KV<=304",
+                       "model": "SmolLM2-135M arch, seeded random BFP weights", "global_batch": procs,
+                       "seq_len": 304, "parallelism": f"host processes x{procs}"},
+            "cpu_baseline": dict(value=round(v, 4), unit="tok/s", cores=procs, kind="port",
+                                 sample=f"{procs} processes, each {per_step} decode steps per timed step of a "
+                                        f"cfg2-shaped stream from KV length 48 (numpy restatement of the "
+                                        f"reference simulator, 1 BLAS thread each)", **info),
             "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -459,8 +522,10 @@ def main():
     ap.add_argument("--mm-reps", type=int, default=50, help="graph replays for the matmul roofline timing")
     ap.add_argument("--no-cfg5", action="store_true", help="skip the batch-64 / KV-2048 kernel profile")
     ap.add_argument("--no-cfg4", action="store_true", help="skip the matvec shape x batch sweep")
-    ap.add_argument("--sharded-head", action="store_true",
-                    help="with N > 1 GPUs, also time the single-stream decode with the vocabulary-sharded head")
+    ap.add_argument("--no-sharded-head", action="store_true",
+                    help="with N > 1 GPUs, skip the single-stream decode with the vocabulary-sharded head")
+    ap.add_argument("--cpu-procs", type=int, default=0,
+                    help="host processes of the CPU baselines (default: usable cores, at most 32)")
     ap.add_argument("--cfg4-batches", type=lambda s: [int(x) for x in s.split(",")], default=[1, 8, 64, 256, 1024],
                     help="batch sizes of the matvec sweep")
     args = ap.parse_args()
@@ -471,8 +536,9 @@ def main():
             print(json.dumps(res), flush=True)
         return
     world, rank, local = dist_init()
-    res = run_ours(args, world, rank, local)
+    res, detail = run_ours(args, world, rank, local)
     if rank == 0:
+        print(json.dumps({"detail": detail}), flush=True)
         print(json.dumps(res), flush=True)
     if world > 1:
         import torch.distributed as dist

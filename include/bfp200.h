@@ -263,16 +263,20 @@ int bfp200_fwd_layer(bfp200_handle* h, int layer, const double* h_in, const int3
  * caching allocator or fixed pool, or a latency-critical loop that cannot
  * take cudaMalloc/cudaFree's implicit device synchronisation.  Every pointer
  * is a DEVICE pointer on the current device, in the layouts of
- * bfp200_matvec; the call is asynchronous on `stream` (a cudaStream_t, NULL
- * for the default stream) and allocates nothing.  Its scratch (the matmul's
- * K-split accumulators and counters) is a fixed file-scope device array of
- * 2 MiB + 64 KiB that every GPU loading the library holds until exit:
- * D_out * batch must not exceed 262144 (larger sizes fail with
- * BFP200_EINVAL).  The first call on a device does a one-time set-up (it
- * looks up the scratch array's device address and sets kernel attributes),
- * so make that first call before any stream capture.  All calls share the
- * scratch: calls that overlap on the GPU (different streams, threads or
- * processes sharing the library) race and must be serialised by the caller. */
+ * bfp200_matvec; x_m and W_m must be 16-byte aligned and out_m 2-byte
+ * aligned (otherwise BFP200_EINVAL, before anything runs).  The call is
+ * asynchronous on `stream` (a cudaStream_t, NULL for the default stream) and
+ * allocates nothing.  Its scratch (the matmul's K-split accumulators and
+ * counters) is a fixed file-scope device array of 2 MiB + 64 KiB that every
+ * GPU loading the library holds until exit: D_out * batch must not exceed
+ * 262144 (larger sizes fail with BFP200_EINVAL).  The first call on a device
+ * does a one-time set-up (it looks up the scratch array's device address and
+ * sets kernel attributes), so make that first call before any stream
+ * capture, and after any cudaDeviceReset (a reset discards the set-up's
+ * results; the library does not notice).  Each process has its own copy of
+ * the scratch on each device, and every call in that process on that device
+ * shares it: calls that overlap on the GPU (different streams or threads of
+ * one process, same device) race and must be serialised by the caller. */
 int bfp200_matvec_noalloc(const int16_t* x_m, const int8_t* x_e, const int16_t* W_m, const int8_t* W_e, int D_out,
                           int D_in, int batch, int16_t* out_m, int8_t* out_e, void* stream);
 

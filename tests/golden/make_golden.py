@@ -18,6 +18,7 @@ import importlib.util
 import json
 import os
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -33,8 +34,16 @@ import inputs  # noqa: E402  (seeded input generators shared with the tests)
 REF_ROOT = os.environ["REF_ROOT"]          # the reference checkout
 
 
+_OUT_DIR = None
+
+
 def load_ref(name, max_ctx=64):
-    os.environ["OUT"] = "/tmp/ref_golden_out"
+    # the reference module writes its packer outputs under $OUT at import:
+    # point it at a private temporary directory
+    global _OUT_DIR
+    if _OUT_DIR is None:
+        _OUT_DIR = tempfile.mkdtemp(prefix="bfp200_ref_out_")
+    os.environ["OUT"] = _OUT_DIR
     os.environ["MAX_CTX"] = str(max_ctx)
     path = os.path.join(REF_ROOT, "rtl/vc707/host", name)
     spec = importlib.util.spec_from_file_location(name[:-3], path)

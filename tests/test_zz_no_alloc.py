@@ -47,3 +47,18 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     rc = L.bfp200_matvec_noalloc(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), 4096, 16, 65, x.data_ptr(),
                                  x.data_ptr(), None)
     assert rc == _lib.EINVAL and "exceeds" in _lib.last_error()
+
+
+def test_noalloc_rejects_misaligned_pointers():
+    # a pointer carved out of a caller's pool at a 2-byte offset is refused on
+    # the host (no kernel runs), so the CUDA context stays usable
+    import torch
+    from bfp200 import _lib
+    L = _lib.lib()
+    buf = torch.zeros(4096, dtype=torch.int16, device="cuda")
+    base = buf.data_ptr()
+    for xm_off, wm_off, om_off in [(2, 0, 0), (0, 2, 0), (0, 0, 1)]:
+        rc = L.bfp200_matvec_noalloc(base + xm_off, base, base + wm_off, base, 16, 16, 1, base + 64 + om_off,
+                                     base + 128, None)
+        assert rc == _lib.EINVAL and "aligned" in _lib.last_error()
+    torch.cuda.synchronize()

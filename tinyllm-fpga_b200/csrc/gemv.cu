@@ -81,7 +81,7 @@ size_t gemv_smem_bytes(int rg, int nc, int K, bool norm) { return gv_layout(rg, 
 // MAXU: K tiles per thread (NT <= MAXU * threads-per-row)
 template <int NC, int RG, int MODE, bool NORM, int MAXU>
 __global__ void __launch_bounds__(GV_THREADS)
-gemv_kernel(GemvArgs a) {
+bfp_gemv_small_kernel(GemvArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int ROWS = 16 * RG;
   constexpr int TPR = GV_THREADS / ROWS;                 // threads per row
@@ -357,7 +357,7 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<NC, RG, MODE, NORM, MAXU>, a);
+  return cudaLaunchKernelEx(&cfg, bfp_gemv_small_kernel<NC, RG, MODE, NORM, MAXU>, a);
 }
 
 // instantiation table: (NC, RG, MODE, NORM, MAXU)
@@ -405,7 +405,7 @@ cudaError_t init_gemv_attributes() {
   if (e != cudaSuccess) return e;
 #define GV_ATTR(nc, rg, md, nrm, mu)                                                        \
   {                                                                                         \
-    const void* f = (const void*)gemv_kernel<nc, rg, md, nrm, mu>;                          \
+    const void* f = (const void*)bfp_gemv_small_kernel<nc, rg, md, nrm, mu>;                          \
     cudaFuncAttributes fa;                                                                  \
     cudaError_t r = cudaFuncGetAttributes(&fa, f);                                          \
     if (r == cudaSuccess)                                                                   \

@@ -71,6 +71,14 @@ extern "C" int bfp200_matvec_noalloc(const int16_t* x_m, const int8_t* x_e, cons
       batch <= 0)
     return bfp200_set_error(BFP200_EINVAL,
                             "matvec_noalloc: bad arguments (device pointers, D_out and D_in multiples of 16, batch >= 1)");
+  // x_m rows are read 16 bytes at a time and W_m rows by bulk copies, which
+  // need 16-byte-aligned addresses; out_m takes 2-byte stores.  A caller that
+  // sub-allocates from its own pool can hand in offset pointers: reject them
+  // here, before any kernel could fault on them.
+  if (((reinterpret_cast<uintptr_t>(x_m) | reinterpret_cast<uintptr_t>(W_m)) & 15u) ||
+      (reinterpret_cast<uintptr_t>(out_m) & 1u))
+    return bfp200_set_error(BFP200_EINVAL,
+                            "matvec_noalloc: x_m and W_m must be 16-byte aligned and out_m 2-byte aligned");
   if ((size_t)D_out * (size_t)batch > NOALLOC_ACC_MAX)
     return bfp200_set_error(BFP200_EINVAL, "matvec_noalloc: D_out * batch = " +
                                                std::to_string((long long)D_out * batch) +
