@@ -280,6 +280,17 @@ int bfp200_fwd_layer(bfp200_handle* h, int layer, const double* h_in, const int3
 int bfp200_matvec_noalloc(const int16_t* x_m, const int8_t* x_e, const int16_t* W_m, const int8_t* W_e, int D_out,
                           int D_in, int batch, int16_t* out_m, int8_t* out_e, void* stream);
 
+/* bfp200_fwd_layer through the kernels a decode step uses for 1..4 columns
+ * (gen_smollm_blockfp_full.py:261-293, the same contract as bfp200_fwd_layer):
+ * at one column the fused attention-block launch plus the gate/up and down
+ * launches, at 2..4 columns the five small-batch launches.  Each kernel
+ * writes the stages it computes into the stage dump, so every intermediate
+ * tensor of the production decode path can be compared with the
+ * simulator's.  ncols must be 1..4 (BFP200_EINVAL otherwise). */
+int bfp200_fwd_layer_decode(bfp200_handle* h, int layer, const double* h_in, const int32_t* pos,
+                            const int32_t* kv_pos, int ncols, double* k_cache, double* v_cache, int max_ctx,
+                            double* h_out, double* stages);
+
 /* Stage dump layout of bfp200_fwd_layer (mirrors the N1..D dumps of
  * gen_smollm_blockfp_bfp.py:393-426): n1 q k v attn o h1 n2 g u mlp d, where
  * n1/n2/attn/mlp are the matvec inputs tile_quantize(.) decoded, q/k are

@@ -153,3 +153,49 @@ def test_tokens_cfg3_batched(decoder):
     assert decoder.uncertified_steps() == 0
     # batching does not change a sequence's stream
     assert decoder.generate(prompts[:3], n_gen) == out[:3]
+
+
+@pytest.mark.parametrize("ncols", [1, 2, 4])
+def test_decode_kernels_stages(layer_decoder, ncols):
+    """Every intermediate tensor of the kernels a decode step runs for 1..4
+    columns (the fused attention block + gate/up + down at one column, the
+    five small-batch kernels at 2..4) against the oracle's stages of
+    fwd_layer (:261-293), at positions on both sides of the warp and
+    staging boundaries."""
+    model = oracle_model()
+    cfg = O.Cfg()
+    rng = np.random.default_rng(40 + ncols)
+    pos = [0, 1, 31, 33, 48, 177, 303, 1000]
+    for p0 in range(0, len(pos), ncols):
+        ps = pos[p0:p0 + ncols]
+        ps = ps + [5] * (ncols - len(ps))
+        H, KC, VC = [], [], []
+        for p in ps:
+            H.append(O.fp_quantize_vec(inputs.outlier_normal(rng, 576)))
+            K = np.zeros((2048, 3, 64)); V = np.zeros((2048, 3, 64))
+            if p:
+                K[:p] = O.fp_quantize_vec(rng.standard_normal(p * 192)).reshape(p, 3, 64)
+                V[:p] = O.fp_quantize_vec(rng.standard_normal(p * 192)).reshape(p, 3, 64)
+            KC.append(K); VC.append(V)
+        kc, vc = np.stack(KC), np.stack(VC)
+        layer = 7 + p0
+        out, stages = layer_decoder.fwd_layer(layer, np.stack(H), ps, kc, vc, stages=True, decode_kernels=True)
+        for c, p in enumerate(ps):
+            kv = {"k": KC[c].copy(), "v": VC[c].copy()}
+            st = {}
+            want = O.fwd_layer(H[c], model.layers[layer], p, kv, p, cfg, stages=st)
+            g = stages[c]
+            ctx = (ncols, c, p)
+            assert np.array_equal(g["n1"], O.tile_decode(*O.tile_quantize(st["n1"]))), ctx
+            for nm in ("q", "k", "v"):
+                assert np.array_equal(g[nm], st[nm]), (nm,) + ctx
+            assert np.array_equal(g["attn"], O.tile_decode(*O.tile_quantize(st["attn"]))), ctx
+            for nm in ("o", "h1"):
+                assert np.array_equal(g[nm], st[nm]), (nm,) + ctx
+            assert np.array_equal(g["n2"], O.tile_decode(*O.tile_quantize(st["n2"]))), ctx
+            for nm in ("g", "u"):
+                assert np.array_equal(g[nm], st[nm]), (nm,) + ctx
+            assert np.array_equal(g["mlp"], O.tile_decode(*O.tile_quantize(st["mlp"]))), ctx
+            assert np.array_equal(g["d"], st["d"]), ctx
+            assert np.array_equal(out[c], want), ctx
+            assert np.array_equal(kc[c, p], kv["k"][p]) and np.array_equal(vc[c, p], kv["v"][p]), ctx

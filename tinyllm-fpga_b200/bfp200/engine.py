@@ -159,10 +159,12 @@ class Decoder:
         check(_lib.lib().bfp200_stage_dims(self._h, ptr(d)))
         return d
 
-    def fwd_layer(self, layer, h, pos, k_cache, v_cache, kv_pos=None, stages=False):
+    def fwd_layer(self, layer, h, pos, k_cache, v_cache, kv_pos=None, stages=False, decode_kernels=False):
         """h (ncols, D) grid doubles; k_cache/v_cache (ncols, max_ctx, H_KV, HD)
         float64, updated in place at kv_pos.  Returns h_out (and a list of
-        per-stage dicts if stages)."""
+        per-stage dicts if stages).  decode_kernels: run the kernels a decode
+        step uses for 1..4 columns (bfp200_fwd_layer_decode) instead of the
+        general batched path."""
         h = arr(h, np.float64)
         one = h.ndim == 1
         h2 = h.reshape(1, -1) if one else h
@@ -179,8 +181,9 @@ class Decoder:
         if stages:
             dims = self.stage_dims()
             st = np.empty(ncols * int(dims.sum()), np.float64)
-        check(_lib.lib().bfp200_fwd_layer(self._h, int(layer), ptr(h2), ptr(pos_a), ptr(kvp), ncols, ptr(kc),
-                                          ptr(vc), kc.shape[1], ptr(out), ptr(st)))
+        fn = _lib.lib().bfp200_fwd_layer_decode if decode_kernels else _lib.lib().bfp200_fwd_layer
+        check(fn(self._h, int(layer), ptr(h2), ptr(pos_a), ptr(kvp), ncols, ptr(kc), ptr(vc), kc.shape[1], ptr(out),
+                 ptr(st)))
         res = out[0] if one else out
         if not stages:
             return res

@@ -342,6 +342,14 @@ struct bfp200_handle {
   bool use_small = true;      // 1..4 columns: the fused small-batch kernels (gemv.cu)
   bool use_persist = false;   // 1..4 columns: decode steps in one persistent kernel (persist.cu), opt-in
   bool use_tc = true;         // >= 64 columns: matmuls on the tcgen05 tensor cores (tc.cu)
+  bool use_block = true;      // 1 column: the attention half of a layer in one cluster launch (layer1.cu)
+  bool block_ok = false;      // ... and its plan fits this configuration
+  L1Args block{};             // plan fields of that launch (og_*, ch)
+  // stage dump of the decode-path kernels (bfp200_fwd_layer_decode): device
+  // buffer [column][stage values] in bfp200_fwd_layer's stage layout, or null
+  DBuf<double> stage_buf;
+  double* stage_dbg = nullptr;
+  int stage_ld = 0;
   int smem_optin = 0;
   // weights
   DBuf<uint8_t> wm_qkv, wm_o, wm_gu, wm_d;
@@ -713,6 +721,16 @@ GemvArgs gemv_args(bfp200_handle* h, DevMat W, int ncols, int mode) {
   return a;
 }
 
+// Offset of stage s (n1 q k v attn o h1 n2 g u mlp d) within one column of
+// the stage dump.
+int stage_off(const bfp200_handle* h, int s) {
+  const int len[BFP200_NSTAGES] = {h->D, h->QD, h->KVD, h->KVD, h->QD, h->D, h->D, h->D, h->FFN, h->FFN, h->FFN, h->D};
+  int o = 0;
+  for (int i = 0; i < s; ++i) o += len[i];
+  return o;
+}
+int stage_stride(const bfp200_handle* h) { return stage_off(h, BFP200_NSTAGES); }
+
 int enqueue_gemv_qkv(bfp200_handle* h, int l, int ncols, bool pdl) {
   GemvArgs a = gemv_args(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), ncols, GV_QKV_ROPE);
   a.xm = h->h_m.p; a.xe = h->h_e.p; a.x_ld = h->D; a.x_lde = h->NTD;
@@ -720,6 +738,11 @@ int enqueue_gemv_qkv(bfp200_handle* h, int l, int ncols, bool pdl) {
   a.rope_cs = h->rope_cs.p; a.col_slot = h->col_slot.p; a.col_pos = h->col_pos.p;
   a.kv = h->kv(); a.layer = l; a.HQ = h->HQ; a.HKV = h->HKV;
   a.qr_m = h->qr_m.p; a.qr_e = h->qr_e.p;
+  if (h->stage_dbg) {
+    a.dbg_in = h->stage_dbg + stage_off(h, 0);
+    a.dbg_mid = h->stage_dbg + stage_off(h, 1);     // q | k | v rows are consecutive stages
+    a.dbg_ld = h->stage_ld;
+  }
   CK(launch_gemv(a, h->stream, pdl));
   return BFP200_OK;
 }
@@ -729,6 +752,7 @@ int enqueue_gemv_o(bfp200_handle* h, int l, int ncols, bool pdl, int16_t* om, in
   a.xm = h->a_m.p; a.xe = h->a_e.p; a.x_ld = h->QD; a.x_lde = h->QD / 16;
   a.rm = h->h_m.p; a.re = h->h_e.p;
   a.om = om; a.oe = oe; a.o_ld = h->D; a.o_lde = h->NTD;
+  if (h->stage_dbg) { a.dbg_mid = h->stage_dbg + stage_off(h, 5); a.dbg_ld = h->stage_ld; }
   CK(launch_gemv(a, h->stream, pdl));
   return BFP200_OK;
 }
@@ -738,6 +762,12 @@ int enqueue_gemv_gu(bfp200_handle* h, int l, int ncols, bool pdl) {
   a.xm = h->h1_m.p; a.xe = h->h1_e.p; a.x_ld = h->D; a.x_lde = h->NTD;
   a.norm = 1; a.gamma = h->g2.p + (size_t)l * h->D;
   a.om = h->mlp_m.p; a.oe = h->mlp_e.p; a.o_ld = h->FFN; a.o_lde = h->NTF;
+  if (h->stage_dbg) {
+    a.dbg_in = h->stage_dbg + stage_off(h, 7);
+    a.dbg_mid = h->stage_dbg + stage_off(h, 8);
+    a.dbg_mid2 = h->stage_dbg + stage_off(h, 9);
+    a.dbg_ld = h->stage_ld;
+  }
   CK(launch_gemv(a, h->stream, pdl));
   return BFP200_OK;
 }
@@ -747,12 +777,48 @@ int enqueue_gemv_d(bfp200_handle* h, int l, int ncols, bool pdl, int16_t* om, in
   a.xm = h->mlp_m.p; a.xe = h->mlp_e.p; a.x_ld = h->FFN; a.x_lde = h->NTF;
   a.rm = h->h1_m.p; a.re = h->h1_e.p;
   a.om = om; a.oe = oe; a.o_ld = h->D; a.o_lde = h->NTD;
+  if (h->stage_dbg) { a.dbg_mid = h->stage_dbg + stage_off(h, 11); a.dbg_ld = h->stage_ld; }
   CK(launch_gemv(a, h->stream, pdl));
   return BFP200_OK;
 }
 
+// One column: RMSNorm + Q/K/V + RoPE + KV write + attention + O + residual
+// in one cluster launch (h -> h1).
+int enqueue_attn_block(bfp200_handle* h, int l, bool pdl) {
+  L1Args a = h->block;
+  a.Wqkv = h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l);
+  a.Wo = h->mat(h->wm_o, h->we_o, h->GO, h->QD / 16, l);
+  a.gamma = h->g1.p + (size_t)l * h->D;
+  a.eps = h->cfg.eps;
+  a.hm = h->h_m.p; a.he = h->h_e.p;
+  a.h1m = h->h1_m.p; a.h1e = h->h1_e.p;
+  a.rope_cs = h->rope_cs.p;
+  a.col_slot = h->col_slot.p; a.col_pos = h->col_pos.p;
+  a.kv = h->kv();
+  a.layer = l;
+  a.pw_off = h->pw_off.p; a.pw_data = h->pw_data.p;
+  a.err = error_flag_device_ptr();
+  a.sqrt_hd = std::sqrt((double)h->HD);
+  int ex = 0;
+  a.inv_hd = std::frexp(a.sqrt_hd, &ex) == 0.5 ? std::ldexp(1.0, 1 - ex) : 0.0;
+  a.dbg = h->stage_dbg;                               // column 0: stages n1 .. h1
+  CK(launch_attn_block(a, h->stream, pdl));
+  return BFP200_OK;
+}
+
+bool attn_block_ok(bfp200_handle* h, int ncols) { return ncols == 1 && h->use_block && h->block_ok; }
+
 int enqueue_layer_small(bfp200_handle* h, int l, int ncols, bool first_pdl, bool early_kv) {
   const bool pdl = h->pdl;
+  if (attn_block_ok(h, ncols)) {
+    mark(h, PK_ATTENTION);
+    CKR(enqueue_attn_block(h, l, pdl && first_pdl));
+    mark(h, PK_MM_GU);
+    CKR(enqueue_gemv_gu(h, l, ncols, pdl));
+    mark(h, PK_MM_D);
+    CKR(enqueue_gemv_d(h, l, ncols, pdl, h->h_m.p, h->h_e.p));
+    return BFP200_OK;
+  }
   mark(h, PK_MM_QKV);
   CKR(enqueue_gemv_qkv(h, l, ncols, pdl && first_pdl));
   mark(h, PK_ATTENTION);
@@ -1062,7 +1128,17 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
   if (const char* e = std::getenv("BFP200_NO_SMALL")) h->use_small = !(e[0] == '1');
   if (const char* e = std::getenv("BFP200_PERSIST")) h->use_persist = e[0] == '1';
   if (const char* e = std::getenv("BFP200_NO_TC")) h->use_tc = !(e[0] == '1');
+  if (const char* e = std::getenv("BFP200_NO_BLOCK")) h->use_block = !(e[0] == '1');
   h->smem_optin = (int)prop.sharedMemPerBlockOptin;
+  {
+    int budget = 0;
+    const cudaError_t be = init_attn_block_attributes(h->smem_optin, &budget);
+    if (be != cudaSuccess) { delete h; return fail(BFP200_ECUDA, std::string("open: ") + cudaGetErrorString(be)); }
+    L1Args& b = h->block;
+    b.D = h->D; b.HQ = h->HQ; b.HKV = h->HKV;
+    b.kv.MAX_CTX = h->MAXC;
+    h->block_ok = h->HD == 64 && attn_block_plan(b, budget);
+  }
   cudaError_t ce = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
   if (ce != cudaSuccess) { delete h; return fail(BFP200_ECUDA, cudaGetErrorString(ce)); }
   std::vector<double> cs((size_t)h->MAXC * h->HD);
@@ -2022,10 +2098,28 @@ int bfp200_stage_dims(bfp200_handle* h, int32_t* dims) {
   return BFP200_OK;
 }
 
+static int fwd_layer_impl(bfp200_handle* h, int layer, const double* h_in, const int32_t* pos, const int32_t* kv_pos,
+                          int ncols, double* k_cache, double* v_cache, int max_ctx, double* h_out, double* stages,
+                          bool decode_kernels);
+
 int bfp200_fwd_layer(bfp200_handle* h, int layer, const double* h_in, const int32_t* pos, const int32_t* kv_pos,
                      int ncols, double* k_cache, double* v_cache, int max_ctx, double* h_out, double* stages) {
+  return fwd_layer_impl(h, layer, h_in, pos, kv_pos, ncols, k_cache, v_cache, max_ctx, h_out, stages, false);
+}
+
+int bfp200_fwd_layer_decode(bfp200_handle* h, int layer, const double* h_in, const int32_t* pos,
+                            const int32_t* kv_pos, int ncols, double* k_cache, double* v_cache, int max_ctx,
+                            double* h_out, double* stages) {
+  return fwd_layer_impl(h, layer, h_in, pos, kv_pos, ncols, k_cache, v_cache, max_ctx, h_out, stages, true);
+}
+
+static int fwd_layer_impl(bfp200_handle* h, int layer, const double* h_in, const int32_t* pos, const int32_t* kv_pos,
+                          int ncols, double* k_cache, double* v_cache, int max_ctx, double* h_out, double* stages,
+                          bool decode_kernels) {
   if (!h || !h_in || !pos || !kv_pos || !k_cache || !v_cache || !h_out || ncols <= 0)
     return fail(BFP200_EINVAL, "fwd_layer: null argument");
+  if (decode_kernels && !small_path_ok(h, ncols))
+    return fail(BFP200_EINVAL, "fwd_layer_decode: the decode-path kernels take 1..4 columns of this configuration");
   if (!h->have_image) return fail(BFP200_ESTATE, "fwd_layer before load_image");
   if (layer < 0 || layer >= h->NL) return fail(BFP200_EINVAL, "fwd_layer: layer out of range");
   if (ncols > h->cfg.max_seqs || max_ctx <= 0) return fail(BFP200_EINVAL, "fwd_layer: ncols > max_seqs");
@@ -2074,7 +2168,38 @@ int bfp200_fwd_layer(bfp200_handle* h, int layer, const double* h_in, const int3
   CK(cudaStreamSynchronize(h->stream));
   StageSink sink;
   sink.st.resize(BFP200_NSTAGES);
-  CKR(enqueue_layer(h, layer, ncols, stages ? &sink : nullptr, /*first_pdl=*/false));
+  if (decode_kernels) {
+    // the production 1..4-column kernels, each dumping the stages it computes
+    const int ld = stage_stride(h);
+    CK(h->stage_buf.ensure((size_t)ncols * ld));
+    CK(cudaMemsetAsync(h->stage_buf.p, 0, (size_t)ncols * ld * 8, h->stream));
+    h->stage_dbg = stages ? h->stage_buf.p : nullptr;
+    h->stage_ld = ld;
+    const int r = enqueue_layer_small(h, layer, ncols, /*first_pdl=*/false, /*early_kv=*/false);
+    h->stage_dbg = nullptr;
+    CKR(r);
+    if (stages) {
+      std::vector<double> buf((size_t)ncols * ld);
+      CK(cudaMemcpyAsync(buf.data(), h->stage_buf.p, buf.size() * 8, cudaMemcpyDeviceToHost, h->stream));
+      CK(cudaStreamSynchronize(h->stream));
+      int32_t dims[BFP200_NSTAGES];
+      bfp200_stage_dims(h, dims);
+      for (int st = 0; st < BFP200_NSTAGES; ++st) {
+        sink.st[st].assign((size_t)ncols * dims[st], 0.0);
+        for (int c = 0; c < ncols; ++c)
+          std::memcpy(sink.st[st].data() + (size_t)c * dims[st], buf.data() + (size_t)c * ld + stage_off(h, st),
+                      (size_t)dims[st] * 8);
+      }
+      // activations the kernels materialise: attn and h1 (multi-kernel path), mlp
+      if (!attn_block_ok(h, ncols)) {
+        CKR(download_decoded(h, h->a_m.p, h->a_e.p, h->QD, h->QD, 0, ncols, sink.st[4]));
+        CKR(download_decoded(h, h->h1_m.p, h->h1_e.p, h->D, h->D, 0, ncols, sink.st[6]));
+      }
+      CKR(download_decoded(h, h->mlp_m.p, h->mlp_e.p, h->FFN, h->FFN, 0, ncols, sink.st[10]));
+    }
+  } else {
+    CKR(enqueue_layer(h, layer, ncols, stages ? &sink : nullptr, /*first_pdl=*/false));
+  }
   std::vector<double> hout;
   CKR(download_decoded(h, h->h_m.p, h->h_e.p, D, D, 0, ncols, hout));
   std::memcpy(h_out, hout.data(), hout.size() * 8);

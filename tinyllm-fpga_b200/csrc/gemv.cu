@@ -173,6 +173,7 @@ bfp_gemv_small_kernel(GemvArgs a) {
           const int c = i / K, k = i % K;
           nm[i] = m[q];
           if ((k & 15) == 0) ne[c * NT + k / 16] = (int8_t)e[q];
+          if (a.dbg_in && blockIdx.x == 0 && c < a.ncols) a.dbg_in[(size_t)c * a.dbg_ld + k] = bfp_decode(m[q], e[q]);
         }
       }
     }
@@ -260,6 +261,7 @@ bfp_gemv_small_kernel(GemvArgs a) {
     int qe;
     int16_t qm = tile_quantize_16lanes(out_real, &qe);               // :233
     const size_t orow = (size_t)(g0 + go) * 16 + l16;
+    if (a.dbg_mid && valid) a.dbg_mid[(size_t)c * a.dbg_ld + orow] = bfp_decode(qm, qe);
     if constexpr (MODE == GV_RESIDUAL) {
       const double hv = valid ? bfp_decode(a.rm[(size_t)c * a.o_ld + orow], a.re[(size_t)c * a.o_lde + g0 + go]) : 0.0;
       const double y = __dadd_rn(hv, bfp_decode(qm, qe));            // fpq(h + o)
@@ -275,6 +277,10 @@ bfp_gemv_small_kernel(GemvArgs a) {
     int16_t gu_m[2];
     int gu_e[2], se, pe;
     tile_quantize_16lanes_n<2>(gu_r, gu_m, gu_e);                    // g, u = matvec (:288-289)
+    if (a.dbg_mid && valid) {
+      a.dbg_mid[(size_t)c * a.dbg_ld + (size_t)g0 / 2 * 16 + l16] = bfp_decode(gu_m[0], gu_e[0]);
+      a.dbg_mid2[(size_t)c * a.dbg_ld + (size_t)g0 / 2 * 16 + l16] = bfp_decode(gu_m[1], gu_e[1]);
+    }
     const double gv = bfp_decode(gu_m[0], gu_e[0]), uv = bfp_decode(gu_m[1], gu_e[1]);
     const double sv = __ddiv_rn(gv, __dadd_rn(1.0, exp(-gv)));       // silu_fp (:241-242)
     const int16_t sm = tile_quantize_16lanes(sv, &se);
@@ -314,6 +320,7 @@ bfp_gemv_small_kernel(GemvArgs a) {
                               : __dadd_rn(__dmul_rn(bv, cs), __dmul_rn(av, sn));
       int re;
       const int16_t rm = tile_quantize_16lanes(y, &re);
+      if (a.dbg_mid && valid) a.dbg_mid[(size_t)c * a.dbg_ld + unit * 64 + d] = bfp_decode(rm, re);
       if (valid) {
         if (unit < HQ) {
           a.qr_m[(size_t)c * HQ * 64 + unit * 64 + d] = rm;
@@ -325,6 +332,7 @@ bfp_gemv_small_kernel(GemvArgs a) {
         }
       }
     } else if (valid) {   // v heads: stored as produced (:272)
+      if (a.dbg_mid) a.dbg_mid[(size_t)c * a.dbg_ld + unit * 64 + d] = bfp_decode(qm, qe);
       const size_t base = (((size_t)slot * a.kv.NL + a.layer) * HKV + (unit - HQ - HKV)) * a.kv.MAX_CTX + pos;
       a.kv.vm[base * 64 + d] = qm;
       if (l16 == 0) a.kv.ve[base * 4 + rank] = (int8_t)qe;

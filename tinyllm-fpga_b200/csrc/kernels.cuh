@@ -84,7 +84,49 @@ struct GemvArgs {
   int layer = 0, HQ = 0, HKV = 0;
   int16_t* qr_m = nullptr;
   int8_t* qr_e = nullptr;
+  // stage dump (bfp200_fwd_layer_decode), or nullptr; column c at + c * dbg_ld:
+  // dbg_in: the normalised input (NORM, written by CTA 0); dbg_mid: the
+  // matvec output before the residual (GV_RESIDUAL), q | k | v after RoPE
+  // (GV_QKV_ROPE) or g (GV_SWIGLU); dbg_mid2: u (GV_SWIGLU)
+  double* dbg_in = nullptr;
+  double* dbg_mid = nullptr;
+  double* dbg_mid2 = nullptr;
+  int dbg_ld = 0;
 };
+
+// The attention half of a one-column decode layer in one launch of one
+// thread-block cluster (layer1.cu): RMSNorm + Q/K/V + RoPE + KV write +
+// attention + O + residual, h -> h1.
+struct L1Args {
+  DevMat Wqkv;                    // fused q | k | v rows of this layer (G = 4 (HQ + 2 HKV))
+  DevMat Wo;                      // G = D / 16
+  const double* gamma = nullptr;  // g1 of this layer, D doubles
+  double eps = 1e-5;
+  const int16_t* hm = nullptr;    // h (input), D mantissas + D/16 exponents
+  const int8_t* he = nullptr;
+  int16_t* h1m = nullptr;         // h1 (output)
+  int8_t* h1e = nullptr;
+  const double* rope_cs = nullptr;   // [MAX_CTX][32][cos, sin]
+  const int* col_slot = nullptr;     // column 0's KV slot and position
+  const int* col_pos = nullptr;
+  KvArena kv;
+  int layer = 0;
+  const int* pw_off = nullptr;       // numpy pairwise-sum plans per length
+  const unsigned short* pw_data = nullptr;
+  int* err = nullptr;                // bounded-wait error flag
+  int D = 0, HQ = 0, HKV = 0;
+  double sqrt_hd = 8.0, inv_hd = 0.125;   // inv_hd: exact 1/sqrt(HD), or 0 when not a power of two
+  // stage dump (bfp200_fwd_layer_decode), or nullptr: decoded n1, q, k, v,
+  // attn, o, h1 at the stage offsets of that entry point's layout
+  double* dbg = nullptr;
+  // filled by attn_block_plan
+  int og_other = 0, og_att = 0, ch = 0;
+};
+// Fills the plan fields; false when the configuration does not fit.
+bool attn_block_plan(L1Args& a, int smem_budget);
+size_t attn_block_smem(const L1Args& a);
+cudaError_t launch_attn_block(const L1Args& a, cudaStream_t s, bool pdl);
+cudaError_t init_attn_block_attributes(int smem_optin, int* dyn_budget);
 
 // Batched BFP matvec on the tcgen05 tensor cores (tc.cu), for >= 64 columns.
 // The weights are repacked once (launch_tc_pack) from DevMat into records of
