@@ -749,6 +749,7 @@ int enqueue_gemv_qkv(bfp200_handle* h, int l, int ncols, bool pdl) {
 
 int enqueue_gemv_o(bfp200_handle* h, int l, int ncols, bool pdl, int16_t* om, int8_t* oe) {
   GemvArgs a = gemv_args(h, h->mat(h->wm_o, h->we_o, h->GO, h->QD / 16, l), ncols, GV_RESIDUAL);
+  a.layer = l;
   a.xm = h->a_m.p; a.xe = h->a_e.p; a.x_ld = h->QD; a.x_lde = h->QD / 16;
   a.rm = h->h_m.p; a.re = h->h_e.p;
   a.om = om; a.oe = oe; a.o_ld = h->D; a.o_lde = h->NTD;
@@ -759,6 +760,7 @@ int enqueue_gemv_o(bfp200_handle* h, int l, int ncols, bool pdl, int16_t* om, in
 
 int enqueue_gemv_gu(bfp200_handle* h, int l, int ncols, bool pdl) {
   GemvArgs a = gemv_args(h, h->mat(h->wm_gu, h->we_gu, h->GGU, h->NTD, l), ncols, GV_SWIGLU);
+  a.layer = l;
   a.xm = h->h1_m.p; a.xe = h->h1_e.p; a.x_ld = h->D; a.x_lde = h->NTD;
   a.norm = 1; a.gamma = h->g2.p + (size_t)l * h->D;
   a.om = h->mlp_m.p; a.oe = h->mlp_e.p; a.o_ld = h->FFN; a.o_lde = h->NTF;
@@ -774,6 +776,7 @@ int enqueue_gemv_gu(bfp200_handle* h, int l, int ncols, bool pdl) {
 
 int enqueue_gemv_d(bfp200_handle* h, int l, int ncols, bool pdl, int16_t* om, int8_t* oe) {
   GemvArgs a = gemv_args(h, h->mat(h->wm_d, h->we_d, h->GD, h->NTF, l), ncols, GV_RESIDUAL);
+  a.layer = l;
   a.xm = h->mlp_m.p; a.xe = h->mlp_e.p; a.x_ld = h->FFN; a.x_lde = h->NTF;
   a.rm = h->h1_m.p; a.re = h->h1_e.p;
   a.om = om; a.oe = oe; a.o_ld = h->D; a.o_lde = h->NTD;
@@ -813,6 +816,9 @@ int enqueue_layer_small(bfp200_handle* h, int l, int ncols, bool first_pdl, bool
   if (attn_block_ok(h, ncols)) {
     mark(h, PK_ATTENTION);
     CKR(enqueue_attn_block(h, l, pdl && first_pdl));
+#ifdef BFP200_DOUBLE_BLOCK
+    CKR(enqueue_attn_block(h, l, pdl));   // measurement builds: the same launch again, with warm code
+#endif
     mark(h, PK_MM_GU);
     CKR(enqueue_gemv_gu(h, l, ncols, pdl));
     mark(h, PK_MM_D);

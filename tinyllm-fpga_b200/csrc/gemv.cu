@@ -15,6 +15,7 @@
 //     halves through distributed shared memory.
 #include "bfp_device.cuh"
 #include "kernels.cuh"
+#include "stamps.cuh"
 
 #include <cooperative_groups.h>
 
@@ -104,6 +105,8 @@ bfp_gemv_small_kernel(GemvArgs a) {
   __shared__ int s_lo[96], s_len[96];
   __shared__ double s_val[96];
 
+  constexpr int SK = MODE == GV_SWIGLU ? 1 : (MODE == GV_RESIDUAL ? 2 : 3);
+  BFP_STAMP(SK, a.layer, blockIdx.x, 0);
   gv_pdl_trigger();
   // ---- weights: registers and shared memory, before the dependency wait
   uint4 wh[MAXU], wl[MAXU];
@@ -123,6 +126,7 @@ bfp_gemv_small_kernel(GemvArgs a) {
   for (int i = tid; i < ROWS * NC; i += GV_THREADS) Ms[i] = -100000;
 
   gv_pdl_wait();
+  BFP_STAMP(SK, a.layer, blockIdx.x, 1);
   // ---- input columns (optionally RMS-normalised) into shared memory
   if constexpr (NORM) {
     constexpr int PER = 4;            // loads in flight per thread per round
@@ -190,6 +194,7 @@ bfp_gemv_small_kernel(GemvArgs a) {
     }
   }
   __syncthreads();
+  BFP_STAMP(SK, a.layer, blockIdx.x, 2);
   // ---- max tile exponent per (row, column) over the full K (:221-222)
   #pragma unroll
   for (int c = 0; c < NC; ++c) {
@@ -201,6 +206,7 @@ bfp_gemv_small_kernel(GemvArgs a) {
     atomicMax(&Ms[row * NC + c], m);
   }
   __syncthreads();
+  BFP_STAMP(SK, a.layer, blockIdx.x, 3);
   // ---- tile sums, per-tile floor shift, int64 accumulation (:219-228)
   long long acc[NC];
   int Mr[NC];
@@ -233,6 +239,7 @@ bfp_gemv_small_kernel(GemvArgs a) {
     for (int c = 0; c < NC; ++c) red[((size_t)warp * ROWS + row) * NC + c] = acc[c];
   }
   __syncthreads();
+  BFP_STAMP(SK, a.layer, blockIdx.x, 4);
 
   // ---- epilogue: 16 lanes per (row group, column) pair
   constexpr int NPAIR = (MODE == GV_SWIGLU ? 1 : RG) * NC;
@@ -424,5 +431,7 @@ cudaError_t init_gemv_attributes() {
 #undef GV_ATTR
   return e;
 }
+
+BFP_STAMP_READER(bfp200_stamps_gemv)
 
 }  // namespace bfp
