@@ -199,3 +199,28 @@ def test_decode_kernels_stages(layer_decoder, ncols):
             assert np.array_equal(g["d"], st["d"]), ctx
             assert np.array_equal(out[c], want), ctx
             assert np.array_equal(kc[c, p], kv["k"][p]) and np.array_equal(vc[c, p], kv["v"][p]), ctx
+
+
+def test_fwd_layer_33_columns():
+    """A layer at 33 columns (cfg3's share per GPU at 8 GPUs): the tensor-core
+    matmuls with the store, residual and SwiGLU epilogues on a ragged column
+    tile, against the oracle for every column."""
+    from bfp200 import BfpConfig, Decoder
+    model = oracle_model()
+    cfg = O.Cfg()
+    rng = np.random.default_rng(33)
+    ncols, ctx = 33, 200
+    pos = rng.integers(0, 190, ncols)
+    H = np.stack([O.fp_quantize_vec(inputs.outlier_normal(rng, 576)) for _ in range(ncols)])
+    kc = O.fp_quantize_vec(rng.standard_normal(ncols * ctx * 192)).reshape(ncols, ctx, 3, 64)
+    vc = O.fp_quantize_vec(rng.standard_normal(ncols * ctx * 192)).reshape(ncols, ctx, 3, 64)
+    for c in range(ncols):
+        kc[c, pos[c]:] = 0.0
+        vc[c, pos[c]:] = 0.0
+    with Decoder(BfpConfig(MAX_CTX=ctx, max_seqs=ncols)) as dec:
+        dec.load_image(full_image())
+        out = dec.fwd_layer(11, H, pos, kc.copy(), vc.copy())
+    for c in range(ncols):
+        kv = {"k": kc[c].copy(), "v": vc[c].copy()}
+        want = O.fwd_layer(H[c], model.layers[11], int(pos[c]), kv, int(pos[c]), cfg)
+        assert np.array_equal(out[c], want), c

@@ -166,3 +166,16 @@ def test_softmax_fp_tolerance(ops):
     rel = np.abs(got - want) / np.maximum(np.abs(want), np.finfo(float).tiny)
     assert rel.max() <= 4 * 2.0 ** -52
     assert (got == want).mean() > 0.85
+
+
+@pytest.mark.parametrize("shape", [(576, 576), (192, 576), (576, 1536)])
+def test_matvec_tensor_core_few_columns(ops, shape):
+    """16..63 columns run on the tensor cores too (a ragged last 16- or
+    32-column tile): every column against the oracle."""
+    D_out, D_in = shape
+    W_m, W_e = inputs.sweep_weights(D_out, D_in)
+    for B in (16, 17, 33, 48, 63):
+        X_m, X_e = inputs.sweep_x(D_in, B, D_out)
+        om, oe = ops.matvec(X_m, X_e, W_m, W_e)
+        Y = ops.tile_decode(om.reshape(-1), oe.reshape(-1)).reshape(B, D_out)
+        assert np.array_equal(Y, O.matvec_cols(X_m, X_e, W_m, W_e)), (shape, B)

@@ -341,7 +341,8 @@ struct bfp200_handle {
   bool use_clusters = true;   // K-split reduction through distributed shared memory
   bool use_small = true;      // 1..4 columns: the fused small-batch kernels (gemv.cu)
   bool use_persist = false;   // 1..4 columns: decode steps in one persistent kernel (persist.cu), opt-in
-  bool use_tc = true;         // >= 64 columns: matmuls on the tcgen05 tensor cores (tc.cu)
+  bool use_tc = true;         // >= tc_min_cols columns: matmuls on the tcgen05 tensor cores (tc.cu)
+  int tc_min_cols = 16;       // below: the dp2a matmul (one 16-column tile is the MMA's smallest N)
   bool use_block = true;      // 1 column: the attention half of a layer in one cluster launch (layer1.cu)
   bool block_ok = false;      // ... and its plan fits this configuration
   L1Args block{};             // plan fields of that launch (og_*, ch)
@@ -514,9 +515,9 @@ const uint8_t* tc_records_of(bfp200_handle* h, const DevMat& W) {
   return nullptr;
 }
 
-// >= 64 columns: the tcgen05 matmul (tc.cu)
+// >= tc_min_cols columns: the tcgen05 matmul (tc.cu)
 bool tc_path(bfp200_handle* h, const DevMat& W, int ncols, int epi) {
-  return h->use_tc && ncols >= 64 && tc_supported(W.NT, ncols) && !(epi == EPI_SWIGLU && W.G % 2);
+  return h->use_tc && ncols >= h->tc_min_cols && tc_supported(W.NT, ncols) && !(epi == EPI_SWIGLU && W.G % 2);
 }
 
 // Times every valid (columns per CTA, K split) candidate of one matmul call
@@ -1134,6 +1135,7 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
   if (const char* e = std::getenv("BFP200_NO_SMALL")) h->use_small = !(e[0] == '1');
   if (const char* e = std::getenv("BFP200_PERSIST")) h->use_persist = e[0] == '1';
   if (const char* e = std::getenv("BFP200_NO_TC")) h->use_tc = !(e[0] == '1');
+  if (const char* e = std::getenv("BFP200_TC_MIN_COLS")) h->tc_min_cols = std::max(1, std::atoi(e));
   if (const char* e = std::getenv("BFP200_NO_BLOCK")) h->use_block = !(e[0] == '1');
   h->smem_optin = (int)prop.sharedMemPerBlockOptin;
   {
@@ -1466,7 +1468,7 @@ static int generate_impl(bfp200_handle* h, const int32_t* prompt_ids, const int3
       if (!h->graph || h->graph_cols != n_seq || h->graph_ngen != n_gen || h->graph_temp != temp ||
           h->graph_topk != topk) {
         if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; }
-        if (!small_path_ok(h, n_seq) && h->use_tc && n_seq >= 64) {
+        if (!small_path_ok(h, n_seq) && h->use_tc && n_seq >= h->tc_min_cols) {
           // tensor-core configurations are chosen by timing, which a capture
           // cannot do: run the layer shapes once first (scratch outputs only)
           CKR(enqueue_layer_matmuls(h, 0, n_seq));

@@ -243,6 +243,33 @@ __device__ __forceinline__ double l1_matvec64(const uint8_t* wsm, const int8_t* 
   return out;
 }
 
+// attn_d = sum_t sm[t] * v[t][d], sequential in t (:280-281), over the
+// staged rows 0..nv-1 (int16 mantissas [t][64] and packed tile exponents
+// [t]) of dimension d = this thread.  Out of line: inside the kernel body
+// the loop competes for registers with everything live around it, and
+// spilled operands serialise it; as a call it gets its own allocation.
+__device__ __noinline__ double l1_attn_accumulate(const int16_t* vs, const unsigned* ves, const double* sc,
+                                                   int nv, int d) {
+  const int sh = 8 * (d >> 4);
+  const int16_t* vrow = vs + d;
+  double acc = 0.0;
+  int t = 0;
+  for (; t + 4 <= nv; t += 4) {
+    int m4[4], e4[4];
+    double s4[4];
+    #pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      m4[u] = vrow[(t + u) * A_HD];
+      e4[u] = (int)(int8_t)(ves[t + u] >> sh);
+      s4[u] = sc[t + u];
+    }
+    #pragma unroll
+    for (int u = 0; u < 4; ++u) acc = __dadd_rn(acc, __dmul_rn(s4[u], a_decode(m4[u], e4[u])));
+  }
+  for (; t < nv; ++t) acc = __dadd_rn(acc, __dmul_rn(sc[t], a_decode(vrow[t * A_HD], (int)(int8_t)(ves[t] >> sh))));
+  return acc;
+}
+
 // ---------------------------------------------------------------------------
 // The kernel.  Grid = one cluster of NU = HQ + 2 HKV CTAs.
 // ---------------------------------------------------------------------------
@@ -538,27 +565,10 @@ bfp_attn_block_kernel(L1Args a) {
     if (!dry) BFP_STAMP(0, a.layer, r, 8);
     // attn[h] += sm[t] * v[t], sequential in t (:280-281)
     if (tid < A_HD) {
-      const int sh = 8 * (tid >> 4);
-      const int16_t* vrow = reinterpret_cast<const int16_t*>(vs) + tid;
       const int nv = dry ? min(nin, 8) : nin;
       const int Tv = dry ? nv : Tp;
-      double acc = 0.0;
-      int t = 0;
-      for (; t + 4 <= nv; t += 4) {
-        int m4[4], e4[4];
-        double s4[4];
-        #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          m4[u] = vrow[(size_t)(t + u) * A_HD];
-          e4[u] = (int)(int8_t)(ves[t + u] >> sh);
-          s4[u] = sc[t + u];
-        }
-        #pragma unroll
-        for (int u = 0; u < 4; ++u) acc = __dadd_rn(acc, __dmul_rn(s4[u], a_decode(m4[u], e4[u])));
-      }
-      for (; t < nv; ++t)
-        acc = __dadd_rn(acc, __dmul_rn(sc[t], a_decode(vrow[(size_t)t * A_HD], (int)(int8_t)(ves[t] >> sh))));
-      for (; t < Tv; ++t) {                             // rows beyond the staged chunk
+      double acc = l1_attn_accumulate(reinterpret_cast<const int16_t*>(vs), ves, sc, nv, tid);
+      for (int t = nv; t < Tv; ++t) {                   // rows beyond the staged chunk
         const int m = t == pos ? rv[tid] : a.kv.vm[(kbase + t) * A_HD + tid];
         const int e = t == pos ? (int)rve[tid >> 4] : (int)a.kv.ve[(kbase + t) * 4 + (tid >> 4)];
         acc = __dadd_rn(acc, __dmul_rn(sc[t], a_decode(m, e)));
