@@ -53,3 +53,10 @@ def gpu_available():
         return torch.cuda.is_available()
     except Exception:
         return False
+
+
+def load_sampled():
+    """Sampled streams of the reference emulator (tests/golden/sampled.json):
+    [{temperature, top_k, seed, n_gen, tokens}] on the cfg1 prompt."""
+    with open(golden_path("sampled.json")) as f:
+        return json.load(f)

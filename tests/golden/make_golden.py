@@ -9,7 +9,7 @@ module level.  It is run once, in a container that has the reference, and its
 outputs are committed; the tests never need the reference itself.
 
 Usage:  python tests/golden/make_golden.py <part> [<part> ...]
-parts:  quant matvec layer tokens1 tokens2 tokens3:<i0>:<i1> image log2
+parts:  quant matvec layer tokens1 tokens2 tokens3:<i0>:<i1> image log2 sampled
 """
 from __future__ import annotations
 
@@ -165,6 +165,75 @@ def part_tokens(R, cfg_id, i0=None, i1=None):
         json.dump(out, f)
 
 
+# (temperature, top-k, seed) of the sampled-decode fixtures
+SAMPLED_CASES = [(0.8, 0, 1), (1.0, 50, 7), (0.6, 5, 3), (1.3, 1000, 11), (2.0, 1, 5)]
+SAMPLED_N_GEN = 12
+
+
+def load_ref_hw():
+    """rtl/vc707/host/sim_rtl_fp_hw.py, the hardware emulator whose main()
+    holds the temperature / top-k sampling loop (:196-216).  It imports
+    sim_blockfp from its own directory and seeds numpy at import."""
+    host = os.path.join(REF_ROOT, "rtl/vc707/host")
+    if host not in sys.path:
+        sys.path.insert(0, host)
+    spec = importlib.util.spec_from_file_location("sim_rtl_fp_hw", os.path.join(host, "sim_rtl_fp_hw.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def part_sampled(H):
+    """Sampled streams of the reference emulator: its own fwd_hw per layer
+    (sim_rtl_fp_hw.py:111-145) on the synthetic model, and its sampling loop
+    (:196-216, main() needs the HF checkpoint, so the loop is restated here
+    around the module's functions) with the global numpy generator seeded by
+    np.random.seed(SEED), the cfg1 prompt and SAMPLED_N_GEN tokens."""
+    model = synth.make_model(0)
+    c = model.cfg
+    prompt = [int(t) for t in synth.config_prompts(1)[0][0]]
+    n_steps = len(prompt) + SAMPLED_N_GEN
+    cfg = dict(D=c.D, H_Q=c.H_Q, H_KV=c.H_KV, HD=c.HD, FFN=c.FFN, NL=c.NL, MAX_CTX=n_steps)
+    layers = []
+    for li in range(c.NL):
+        d = {nm + "_me": model.layers[li][nm] for nm in synth.MATS}
+        d["g1"] = model.layers[li]["g1"]
+        d["g2"] = model.layers[li]["g2"]
+        layers.append(d)
+    embed, norm_w = model.embed, model.norm_w
+    out = []
+    for T, TOPK, SEED in SAMPLED_CASES:
+        t0 = time.time()
+        kv = [{"k": np.zeros((n_steps, c.H_KV, c.HD)), "v": np.zeros((n_steps, c.H_KV, c.HD))} for _ in range(c.NL)]
+        np.random.seed(SEED)
+        generated = list(prompt)
+        for step in range(n_steps):
+            tid = prompt[step] if step < len(prompt) else generated[-1]
+            h = H.fp_quantize(embed[tid].astype(np.float64))
+            for li in range(c.NL):
+                h = H.fwd_hw(h, layers[li], pos=step, kv=kv[li], kv_pos=step, cfg=cfg)
+            if step >= len(prompt) - 1:
+                h_normed = (h / np.sqrt(np.mean(h * h) + 1e-5)) * norm_w
+                logits = h_normed @ embed.T
+                scaled = logits / T
+                if TOPK > 0:
+                    idx = np.argsort(scaled)[-TOPK:]
+                    mask = np.full_like(scaled, -np.inf)
+                    mask[idx] = scaled[idx]
+                    scaled = mask
+                scaled -= scaled.max()
+                p = np.exp(scaled)
+                p = p / p.sum()
+                nid = int(np.random.choice(len(p), p=p))
+                if step >= len(prompt):
+                    generated.append(nid)
+        out.append({"temperature": T, "top_k": TOPK, "seed": SEED, "n_gen": SAMPLED_N_GEN, "tokens": generated})
+        print(f"sampled T={T} topk={TOPK} seed={SEED}: {time.time() - t0:.0f}s {generated[len(prompt):]}",
+              file=sys.stderr)
+    with open(os.path.join(HERE, "sampled.json"), "w") as f:
+        json.dump(out, f)
+
+
 def part_image(D):
     """Byte image through the reference packer's own functions
     (gen_smollm_blockfp_ddr.py:65-119), assembled in the region order of its
@@ -234,6 +303,8 @@ def main(argv):
             part_image(load_ref("gen_smollm_blockfp_ddr.py"))
         elif part == "log2":
             part_log2()
+        elif part == "sampled":
+            part_sampled(load_ref_hw())
         elif part.startswith("tokens"):
             cfg_id = int(part[6])
             if ":" in part:

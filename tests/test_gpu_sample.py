@@ -1,6 +1,8 @@
-"""Temperature / top-k sampling (sim_rtl_fp_hw.py:204-216) against the
-oracle's restatement with numpy's legacy generator: same seeds, same token
-streams; draws the fp64 head cannot certify are counted (none expected)."""
+"""Temperature / top-k sampling (sim_rtl_fp_hw.py:204-216): against the
+streams the reference emulator itself produced (tests/golden/sampled.json)
+and against the oracle's restatement with numpy's legacy generator: same
+seeds, same token streams; draws the fp64 head cannot certify are counted
+(none expected)."""
 import numpy as np
 import pytest
 
@@ -50,3 +52,18 @@ def test_full_model_sampled_prefix():
     assert got == O.generate_sampled(oracle_model(), prompts[0], 4, 0.9, 50, seed=1)
     assert dec.uncertified_steps() == 0
     dec.close()
+
+
+def test_full_model_sampled_reference_streams():
+    """Full SmolLM2-135M synthetic image, cfg1 prompt: every sampled stream the
+    reference emulator produced (several temperatures, top-k and seeds)."""
+    from bfp200 import BfpConfig, Decoder, synth
+    from common import load_sampled
+    prompts, _ = synth.config_prompts(1)
+    with Decoder(BfpConfig(MAX_CTX=32, max_seqs=2)) as dec:
+        dec.load_image(synth.synthetic_image(BfpConfig(), seed=0))
+        for case in load_sampled():
+            got = dec.generate_sampled(prompts, case["n_gen"], case["temperature"], case["top_k"],
+                                       seed=case["seed"])[0]
+            assert got == case["tokens"], case
+        assert dec.uncertified_steps() == 0

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 import inputs
-from common import golden_path, load_tokens, manifest, oracle_model, sha
+from common import golden_path, load_sampled, load_tokens, manifest, oracle_model, sha
 from oracle import bfp_oracle as O
 from oracle import synth
 
@@ -146,3 +146,15 @@ def test_config_prompts_match_product():
     from bfp200 import synth as PS
     for cfg_id in (1, 2, 3):
         assert PS.config_prompts(cfg_id) == synth.config_prompts(cfg_id)
+
+
+def test_sampled_streams_golden():
+    """The oracle's sampling loop (generate_sampled) reproduces the streams the
+    reference emulator's own fwd_hw and sampling loop (sim_rtl_fp_hw.py:
+    196-216, np.random.seed(SEED)) produced, for every (T, TOPK, SEED) case."""
+    model = oracle_model()
+    from oracle import synth
+    prompt = synth.config_prompts(1)[0][0]
+    for case in load_sampled()[1:3]:        # top-k 50 and 5 (the GPU tests run every case)
+        got = O.generate_sampled(model, prompt, case["n_gen"], case["temperature"], case["top_k"], case["seed"])
+        assert got == case["tokens"], case
