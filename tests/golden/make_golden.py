@@ -9,7 +9,10 @@ module level.  It is run once, in a container that has the reference, and its
 outputs are committed; the tests never need the reference itself.
 
 Usage:  python tests/golden/make_golden.py <part> [<part> ...]
-parts:  quant matvec layer tokens1 tokens2 tokens3:<i0>:<i1> image log2 sampled
+parts:  quant matvec layer tokens1 tokens2 tokens3:<i0>:<i1> merge3 image log2 sampled
+        (tokens3:<i0>:<i1> writes tokens_cfg3_<i0>_<i1>.json for sequences
+        i0..i1-1, so slices can run as parallel processes; merge3 joins every
+        slice into tokens_cfg3.json and removes the slices)
 """
 from __future__ import annotations
 
@@ -234,6 +237,21 @@ def part_sampled(H):
         json.dump(out, f)
 
 
+def part_merge3():
+    import glob
+    allt = {}
+    slices = sorted(glob.glob(os.path.join(HERE, "tokens_cfg3_*.json")))
+    for fn in slices:
+        with open(fn) as f:
+            for k, v in json.load(f).items():
+                allt[int(k)] = v
+    with open(os.path.join(HERE, "tokens_cfg3.json"), "w") as f:
+        json.dump({str(k): allt[k] for k in sorted(allt)}, f)
+    for fn in slices:
+        os.remove(fn)
+    print("cfg3 sequences:", len(allt), file=sys.stderr)
+
+
 def part_image(D):
     """Byte image through the reference packer's own functions
     (gen_smollm_blockfp_ddr.py:65-119), assembled in the region order of its
@@ -303,6 +321,8 @@ def main(argv):
             part_image(load_ref("gen_smollm_blockfp_ddr.py"))
         elif part == "log2":
             part_log2()
+        elif part == "merge3":
+            part_merge3()
         elif part == "sampled":
             part_sampled(load_ref_hw())
         elif part.startswith("tokens"):

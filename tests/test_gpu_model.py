@@ -141,13 +141,13 @@ def test_tokens_cfg2(decoder):
 
 
 def test_tokens_cfg3_batched(decoder):
-    """All 256 ragged sequences in one batch; the sequences the reference
-    simulator was run on must match exactly."""
+    """All 256 ragged sequences in one batch, each against the reference
+    simulator's own golden stream (tests/golden/tokens_cfg3.json)."""
     from bfp200 import synth
     prompts, n_gen = synth.config_prompts(3)
     out = decoder.generate(prompts, n_gen)
     gold = load_tokens(3)
-    assert len(gold) >= 8
+    assert len(gold) == 256
     for i, toks in gold.items():
         assert out[i] == toks, i
     assert decoder.uncertified_steps() == 0
