@@ -124,11 +124,16 @@ int bfp200_generate_multi(bfp200_handle* const* hs, int n_dev, const int32_t* pr
  * is set, and peers connect at communicator creation unless
  * NCCL_RUNTIME_CONNECT is set (the first exchange then never blocks the host
  * inside a graph capture).  Joining a group makes one exchange.  A sharded
- * handle's generate must be called on every rank with the
- * same arguments; its final wait polls with a limit of
- * $BFP200_NCCL_TIMEOUT_S seconds (default 120), after which it aborts the
- * communicator (ncclCommAbort) and returns BFP200_ETIMEOUT once the abort
- * has ended the exchange.
+ * handle's generate must be called on every rank with the same arguments;
+ * it runs one decode step at a time and waits for each with a poll limited
+ * to $BFP200_NCCL_TIMEOUT_S seconds (default 120).  Past the limit (a rank
+ * that never joins the step) or on an NCCL error it aborts the communicator
+ * (ncclCommAbort), waits at most 30 s for the stream to drain and returns
+ * BFP200_ETIMEOUT with the handle back to an unsharded head; if the stream
+ * does not drain, the call still returns BFP200_ETIMEOUT and the handle is
+ * marked unusable (later calls fail with BFP200_ESTATE) -- no call on this
+ * path waits without a limit.  ncclCommInitRank itself (bfp200_head_shard)
+ * blocks until every rank has joined.
  * Replaces: nothing in the reference (single FPGA, unsharded head :437-440). */
 #define BFP200_NCCL_ID_BYTES 128
 /* A fresh NCCL unique id (rank 0 makes it, every rank passes it to

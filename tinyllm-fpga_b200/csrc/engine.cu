@@ -394,6 +394,9 @@ struct bfp200_handle {
   // one record per column with the other ranks (xsend -> xrecv, all-gather)
   NcclComm comm = nullptr;
   int shard_n = 1, shard_rank = 0, v_lo = 0, v_hi = 0;
+  // set when work of an aborted exchange never left the stream: the handle
+  // can no longer be used (every call fails; the process should exit)
+  bool broken = false;
   DBuf<double> xsend, xrecv, xwarm;
   // sampling (bfp200_generate_sampled): full logits, scratch, uniforms, and
   // numpy's pairwise-sum plan for the vocabulary length
@@ -988,10 +991,26 @@ bool persist_ok(bfp200_handle* h, int ncols) {
 
 // Leaves any sharding (destroys the decode graph first: it holds the
 // communicator's all-gather) and joins `comm` as rank `rank` of `n`.
+// Polls the handle's stream until it is idle or `limit_s` seconds passed;
+// false on timeout (never blocks longer).
+bool bounded_drain(bfp200_handle* h, double limit_s) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(h->stream);
+    if (e != cudaErrorNotReady) return e == cudaSuccess;
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > limit_s) return false;
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
 int set_shard(bfp200_handle* h, NcclComm comm, int n, int rank) {
   DeviceGuard dguard(h->device);
   CK(dguard.err);
-  cudaStreamSynchronize(h->stream);
+  if (h->broken) return fail(BFP200_ESTATE, "handle unusable: an aborted exchange never left its stream");
+  if (!bounded_drain(h, 30.0)) {
+    h->broken = true;
+    return fail(BFP200_ETIMEOUT, "head_shard: the handle's stream did not drain (an exchange is stuck)");
+  }
   if (h->graph) { cudaGraphExecDestroy(h->graph); h->graph = nullptr; h->graph_cols = -1; }
   // local teardown (ncclCommAbort frees the communicator without waiting on
   // the other ranks; every exchange of this handle has completed or timed out)
@@ -1035,13 +1054,22 @@ int sync_stream(bfp200_handle* h) {
     nccl().async_error(h->comm, &ae);
     const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     if ((ae != NCCL_OK && ae != NCCL_IN_PROGRESS) || el > limit_s) {
+      const std::string why = ae != NCCL_OK && ae != NCCL_IN_PROGRESS
+                                  ? "sharded head: NCCL error " + nccl_err(ae)
+                                  : "sharded head: the exchange did not complete (a rank is missing)";
+      // the abort ends the waiting NCCL kernel; at most one decode step is
+      // ever queued behind it while sharded, so nothing else on the stream
+      // uses the freed communicator.  The drain is bounded as well: if the
+      // stream still does not empty, the handle is marked unusable instead
+      // of blocking the caller.
       nccl().comm_abort(h->comm);
       h->comm = nullptr;
-      cudaStreamSynchronize(h->stream);
+      if (!bounded_drain(h, 30.0)) {
+        h->broken = true;
+        return fail(BFP200_ETIMEOUT, why + "; the stream did not drain after the abort (handle unusable)");
+      }
       set_shard(h, nullptr, 1, 0);
-      return fail(BFP200_ETIMEOUT, ae != NCCL_OK && ae != NCCL_IN_PROGRESS
-                                       ? "sharded head: NCCL error " + nccl_err(ae)
-                                       : "sharded head: the exchange did not complete (a rank is missing)");
+      return fail(BFP200_ETIMEOUT, why);
     }
     std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
@@ -1356,6 +1384,7 @@ int bfp200_generate_sampled(bfp200_handle* h, const int32_t* prompt_ids, const i
 static int generate_impl(bfp200_handle* h, const int32_t* prompt_ids, const int32_t* prompt_lens, int n_seq,
                          int n_gen, int feed_mode, int32_t* out_tokens, const Sampling* smp) {
   if (!h || !out_tokens) return fail(BFP200_EINVAL, "generate: null argument");
+  if (h->broken) return fail(BFP200_ESTATE, "handle unusable: an aborted exchange never left its stream");
   if (smp && h->comm) return fail(BFP200_EINVAL, "sampling is not available with a sharded head");
   if (!h->have_image) return fail(BFP200_ESTATE, "generate before load_image");
   if (feed_mode != 0 && feed_mode != 1) return fail(BFP200_EINVAL, "feed_mode must be 0 (sim) or 1 (rtl)");
@@ -1503,7 +1532,17 @@ static int generate_impl(bfp200_handle* h, const int32_t* prompt_ids, const int3
         h->graph_temp = temp;
         h->graph_topk = topk;
       }
-      for (int i = 0; i < n_gen; ++i) CK(cudaGraphLaunch(h->graph, h->stream));
+      if (h->comm) {
+        // sharded: one step at a time, each waited for with the bounded poll,
+        // so a missing rank can never leave later steps queued behind an
+        // exchange that gets aborted
+        for (int i = 0; i < n_gen; ++i) {
+          CK(cudaGraphLaunch(h->graph, h->stream));
+          CKR(sync_stream(h));
+        }
+      } else {
+        for (int i = 0; i < n_gen; ++i) CK(cudaGraphLaunch(h->graph, h->stream));
+      }
       h->launch_count += h->graph_launches * n_gen;
     }
   }

@@ -42,6 +42,14 @@ namespace {
 constexpr int A_THREADS = 512;
 constexpr int A_HD = 64;
 constexpr int A_PLAN_MAX = 512;      // pairwise-sum plan entries kept in shared memory
+// First thread of the 64 that accumulate attn: warps 2 and 3.  Measured:
+// the same loop on warps 0 and 1 ran at twice the cycles per position on
+// warp 0 (warp 1 unaffected); warps 2 / 3 run it at the warp-1 rate.
+#ifndef BFP200_VW
+#define BFP200_VW 64
+#endif
+constexpr int A_VW = BFP200_VW;
+constexpr int A_SW = 0;              // the warp that runs the single-warp reductions
 
 __device__ __forceinline__ void a_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void a_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -402,7 +410,7 @@ bfp_attn_block_kernel(L1Args a) {
   }
   if (!dry && tid == 0 && !a_mbar_wait(&bar[0])) s_fail = 1;
   __syncthreads();
-  if (warp == 0) {
+  if (warp == A_SW) {
     const double sum = np_sum_warp(sq, D, s_lo, s_len, s_val);
     if (lane == 0) s_misc[0] = __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)D), a.eps));
   }
@@ -553,7 +561,7 @@ bfp_attn_block_kernel(L1Args a) {
     for (int w = 1; w < A_THREADS / 32; ++w) mx = s_misc[2 + w] > mx ? s_misc[2 + w] : mx;
     for (int t = tid; t < Tp; t += A_THREADS) sc[t] = exp(__dsub_rn(sc[t], mx));
     __syncthreads();
-    if (warp == 0) {
+    if (warp == A_SW) {
       const double S = np_sum_warp_plan(sc, T, plan, s_val);    // (dry: the entries past Tp are stale)
       if (lane == 0) s_misc[1] = S;
     }
@@ -564,13 +572,18 @@ bfp_attn_block_kernel(L1Args a) {
     __syncthreads();
     if (!dry) BFP_STAMP(0, a.layer, r, 8);
     // attn[h] += sm[t] * v[t], sequential in t (:280-281)
-    if (tid < A_HD) {
+    if (tid >= A_VW && tid < A_VW + A_HD) {
+      const int d = tid - A_VW;                         // this thread's dimension
       const int nv = dry ? min(nin, 8) : nin;
       const int Tv = dry ? nv : Tp;
-      double acc = l1_attn_accumulate(reinterpret_cast<const int16_t*>(vs), ves, sc, nv, tid);
+      if (!dry) { BFP_STAMP_T(A_VW, 3, a.layer, r, 0); BFP_STAMP_T(A_VW + 32, 3, a.layer, r, 4); }
+      double acc = l1_attn_accumulate(reinterpret_cast<const int16_t*>(vs), ves, sc, nv, d);
+#ifdef BFP200_STAMPS
+      if (!dry) { s_misc[20 + (d >> 5)] = acc; __syncwarp(); BFP_STAMP_T(A_VW, 3, a.layer, r, 2); BFP_STAMP_T(A_VW + 32, 3, a.layer, r, 6); }
+#endif
       for (int t = nv; t < Tv; ++t) {                   // rows beyond the staged chunk
-        const int m = t == pos ? rv[tid] : a.kv.vm[(kbase + t) * A_HD + tid];
-        const int e = t == pos ? (int)rve[tid >> 4] : (int)a.kv.ve[(kbase + t) * 4 + (tid >> 4)];
+        const int m = t == pos ? rv[d] : a.kv.vm[(kbase + t) * A_HD + d];
+        const int e = t == pos ? (int)rve[d >> 4] : (int)a.kv.ve[(kbase + t) * 4 + (d >> 4)];
         acc = __dadd_rn(acc, __dmul_rn(sc[t], a_decode(m, e)));
       }
       int e;
@@ -579,9 +592,10 @@ bfp_attn_block_kernel(L1Args a) {
       const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
       m = requant_mant(m, has_min && e < 127);           // tile_quantize(attn)   (:283)
       e = requant_exp(e, has_min);
-      attm[tid] = m;
-      if ((tid & 15) == 0) atte[tid >> 4] = (int8_t)e;
-      if (!dry && a.dbg) a.dbg[l1_stage_off(4, D, KVD) + r * 64 + tid] = bfp_decode(m, e);
+      attm[d] = m;
+      if ((d & 15) == 0) atte[d >> 4] = (int8_t)e;
+      if (!dry && a.dbg) a.dbg[l1_stage_off(4, D, KVD) + r * 64 + d] = bfp_decode(m, e);
+      if (!dry) { BFP_STAMP_T(A_VW, 3, a.layer, r, 3); BFP_STAMP_T(A_VW + 32, 3, a.layer, r, 7); }
     }
     __syncthreads();
     if (!dry) BFP_STAMP(0, a.layer, r, 9);

@@ -22,6 +22,15 @@ static __device__ unsigned long long g_stamp_ns[STAMP_N];
       g_stamp_ns[i_] = t_;                                                                           \
     }                                                                                                \
   } while (0)
+// the same, recorded by thread `th` instead of thread 0
+#define BFP_STAMP_T(th, kind, layer, cta, pt)                                                        \
+  do {                                                                                               \
+    if (threadIdx.x == (th) && (layer) < STAMP_LAYERS && (cta) < STAMP_CTAS) {                       \
+      unsigned long long c_;                                                                         \
+      asm volatile("mov.u64 %0, %%clock64;" : "=l"(c_) :: "memory");                                \
+      g_stamp_clk[((((layer) * STAMP_KINDS + (kind)) * STAMP_CTAS + (cta)) * STAMP_PTS + (pt))] = c_; \
+    }                                                                                                \
+  } while (0)
 #define BFP_STAMP_READER(name)                                                                       \
   extern "C" int name(unsigned long long* clk, unsigned long long* ns) {                             \
     if (cudaMemcpyFromSymbol(clk, bfp::g_stamp_clk, sizeof(bfp::g_stamp_clk)) != cudaSuccess) return -1; \
@@ -30,5 +39,6 @@ static __device__ unsigned long long g_stamp_ns[STAMP_N];
   }
 #else
 #define BFP_STAMP(kind, layer, cta, pt) do {} while (0)
+#define BFP_STAMP_T(th, kind, layer, cta, pt) do {} while (0)
 #define BFP_STAMP_READER(name)
 #endif
