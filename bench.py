@@ -272,7 +272,7 @@ def run_ours(args, world, rank, local):
         cfg5 = {"batch": 64, "pos": 2047, "kernel_ms": d5.profile_forward(64, 2047)}
         d5.close()
     del img
-    cfg4 = None if (args.no_cfg4 or rank != 0) else cfg4_sweep(args.cfg4_batches)   # per-GPU: rank 0
+    cfg4 = None if (args.no_cfg4 or rank != 0) else cfg4_sweep(args.cfg4_batches, pk)   # per-GPU: rank 0
     res = {
         "metric": "BFP decode tok/s (bs1, cfg2)", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
@@ -305,12 +305,16 @@ def run_ours(args, world, rank, local):
 CFG4_SHAPES = ((576, 576), (192, 576), (1536, 576), (576, 1536), (49152, 576))
 
 
-def cfg4_sweep(batches):
+def cfg4_sweep(batches, pk):
     """configs[3] (cfg4): the isolated BFP matvec over the model's weight
     shapes (D_out x D_in), mantissas uniform int16, tile exponents uniform in
     [-20, 4], inputs tile_quantize(N(0,1)), seed 4; device time per call
-    (bfp200_matvec_timed, weights and inputs resident, 10 repetitions) and
-    the rate it implies (weight GB/s, int16 MAC/s)."""
+    (bfp200_matvec_timed, weights and inputs resident, 10 repetitions) of the
+    kernel a decode step uses at that column count (small-batch GEMV at 1..4,
+    dp2a matmul at 5..15, tensor cores from 16), with its roofline fraction:
+    HBM (weight + activation bytes over the measured copy bandwidth) up to 8
+    columns, tensor (int16 MACs as 4 int8 limb MACs over twice the measured
+    bf16 rate) from 64."""
     from bfp200 import ops
     rng = np.random.default_rng(4)
     out = {}
@@ -322,8 +326,17 @@ def cfg4_sweep(batches):
         for b in batches:
             xm, xe = ops.tile_quantize(rng.standard_normal(b * din))
             _, _, ms = ops.matvec_timed(xm.reshape(b, nt, 16), xe.reshape(b, nt), W_m, W_e, reps=10)
-            row[str(b)] = {"us": round(ms * 1e3, 2), "weight_gbs": round(dout * din * 2.0625 / (ms / 1e3) / 1e9, 1),
-                           "tmacs": round(dout * din * b / (ms / 1e3) / 1e12, 3)}
+            s = ms / 1e3
+            kern = ("bfp_gemv_small_kernel" if b <= 4 else "bfp_matmul_kernel (dp2a)" if b < 16
+                    else "tc_matmul_kernel (tcgen05)")
+            byts = dout * din * 2.0625 + b * din * 2.0625 + b * dout * 2.0625
+            ent = {"kernel": kern, "us": round(ms * 1e3, 2), "weight_gbs": round(dout * din * 2.0625 / s / 1e9, 1),
+                   "tmacs": round(dout * din * b / s / 1e12, 3)}
+            if b <= 8:
+                ent["hbm_frac"] = round(byts / s / 1e9 / pk["hbm_gbs"], 4)
+            if b >= 64:
+                ent["tensor_frac"] = round(dout * din * b * 4 * 2 / s / 1e12 / (2 * pk["bf16_tflops"]), 5)
+            row[str(b)] = ent
         out[f"{dout}x{din}"] = row
     return out
 

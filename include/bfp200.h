@@ -199,9 +199,17 @@ int bfp200_uncertified_steps(bfp200_handle* h, long long* count);
 /* Device time of the last generate call's phases, in milliseconds. */
 int bfp200_last_timing(bfp200_handle* h, double* prefill_ms, double* decode_ms);
 
+/* Self-test of the device-side bounded waits: launches a kernel that waits
+ * for a flag nothing sets, gives up after limit_ms (1..2000) milliseconds,
+ * records the timeout in the library's device error flag like every other
+ * bounded wait (TMA barrier and tensor-memory waits), and returns; the call
+ * then reports BFP200_ETIMEOUT and the handle stays usable.  No reference
+ * counterpart: test support. */
+int bfp200_wait_probe(bfp200_handle* h, int limit_ms);
+
 /* Number of kernels the last bfp200_generate launched on the device (prefill
- * launches, plus one decode step's launches times n_gen, or the single
- * persistent launch).  No reference counterpart: measurement support. */
+ * launches, plus one decode step's launches times n_gen).  No reference
+ * counterpart: measurement support. */
 int bfp200_last_launches(bfp200_handle* h, long long* launches);
 
 /* Measurement: device time of one token's BFP matmuls (the 4 per layer of
@@ -231,7 +239,10 @@ int bfp200_tile_decode(bfp200_handle* h, const int16_t* m, const int8_t* e, size
  *   x_m [batch][D_in], x_e [batch][D_in/16]; W_m [D_out][D_in/16][16],
  *   W_e [D_out][D_in/16] (the reference's quantize_W layout);
  *   out_m [batch][D_out], out_e [batch][D_out/16] = tile_quantize of the
- *   result (decode gives the reference's fp_quantize_vec(out_real)). */
+ *   result (decode gives the reference's fp_quantize_vec(out_real)).
+ * Runs the kernel a decode step would use at this column count: the
+ * small-batch GEMV at 1..4 columns, the tensor-core matmul from 16, the dp2a
+ * matmul in between. */
 int bfp200_matvec(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, const int16_t* W_m, const int8_t* W_e,
                   int D_out, int D_in, int batch, int16_t* out_m, int8_t* out_e);
 

@@ -95,17 +95,18 @@ def test_rom_prompt_and_gamma_roms():
 
 @pytest.mark.parametrize("nseq", [1, 2, 3, 4])
 def test_small_batch_kernels_match_general_kernels(nseq, monkeypatch):
-    """1..4 columns: the persistent decode kernel (persist.cu, BFP200_PERSIST=1),
-    the graph-replayed small-batch kernels (gemv.cu, the default), the general
-    matmul path (BFP200_NO_SMALL) and the oracle agree."""
+    """1..4 columns: the graph-replayed decode kernels (the one-column
+    attention block and the small-batch GEMVs, the default), the same with
+    the attention block turned off (BFP200_NO_BLOCK), the general matmul path
+    (BFP200_NO_SMALL) and the oracle agree."""
     from bfp200 import BfpConfig, Decoder, synth
     cfg = BfpConfig(MAX_CTX=48, max_seqs=4, **SMALL)
     img = synth.synthetic_image(cfg, 5)
     rng = np.random.default_rng(50 + nseq)
     prompts = [rng.integers(0, 512, size=int(n)).tolist() for n in (3, 11, 1, 20)[:nseq]]
     results = []
-    for env in ({"BFP200_PERSIST": "1"}, {}, {"BFP200_NO_SMALL": "1"}):
-        for k in ("BFP200_PERSIST", "BFP200_NO_SMALL"):
+    for env in ({}, {"BFP200_NO_BLOCK": "1"}, {"BFP200_NO_SMALL": "1"}):
+        for k in ("BFP200_NO_BLOCK", "BFP200_NO_SMALL"):
             monkeypatch.delenv(k, raising=False)
         for k, v in env.items():
             monkeypatch.setenv(k, v)
@@ -120,24 +121,32 @@ def test_small_batch_kernels_match_general_kernels(nseq, monkeypatch):
         assert g == O.generate(model, p, 12, max_ctx=48, cfg=ocfg)
 
 
-def test_persistent_decode_long_context(monkeypatch):
-    """Persistent decode past one 256-position attention chunk (positions
-    0..299), against the graph-replayed kernels and the oracle."""
+def test_single_stream_long_context():
+    """One sequence decoded past 256 positions (positions 0..299) through the
+    one-column attention block, against the oracle."""
     from bfp200 import BfpConfig, Decoder, synth
     cfg = BfpConfig(MAX_CTX=300, max_seqs=2, **SMALL)
     img = synth.synthetic_image(cfg, 7)
-    prompts = [list(range(1, 41)), [7, 9]]
-    monkeypatch.setenv("BFP200_PERSIST", "1")
-    dec = Decoder(cfg)
-    dec.load_image(img)
-    fast = dec.generate(prompts, 258)
-    dec.close()
-    monkeypatch.delenv("BFP200_PERSIST")
-    dec = Decoder(cfg)
-    dec.load_image(img)
-    slow = dec.generate(prompts, 258)
-    dec.close()
-    assert fast == slow
+    prompt = [7, 9]
+    with Decoder(cfg) as dec:
+        dec.load_image(img)
+        got = dec.generate([prompt], 298)[0]
     ocfg = O.Cfg(**SMALL)
     model = OS.make_model(7, ocfg)
-    assert fast[1] == O.generate(model, prompts[1], 258, max_ctx=300, cfg=ocfg)
+    assert got == O.generate(model, prompt, 298, max_ctx=300, cfg=ocfg)
+
+
+def test_bounded_wait_times_out_and_handle_recovers():
+    """A device-side wait on a flag nothing sets gives up after its limit,
+    records the timeout in the library's error flag (the path every bounded
+    TMA-barrier / tensor-memory wait takes), the call returns BFP200_ETIMEOUT
+    and the handle keeps decoding with the same results."""
+    from bfp200 import BfpConfig, Decoder, synth, _lib
+    cfg = BfpConfig(MAX_CTX=48, max_seqs=2, **SMALL)
+    with Decoder(cfg) as dec:
+        dec.load_image(synth.synthetic_image(cfg, 5))
+        before = dec.generate([[1, 2, 3]], 4)
+        rc = _lib.lib().bfp200_wait_probe(dec.handle, 50)
+        assert rc == _lib.ETIMEOUT and "timed out" in _lib.last_error()
+        assert dec.generate([[1, 2, 3]], 4) == before
+        assert _lib.lib().bfp200_wait_probe(dec.handle, 50) == _lib.ETIMEOUT

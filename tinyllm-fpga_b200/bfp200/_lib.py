@@ -59,6 +59,7 @@ SIGNATURES = {
     "bfp200_rope_table": [_P, _I, _I, _D],
     "bfp200_fwd_layer": [_P, _I, _P, _P, _P, _I, _P, _P, _I, _P, _P],
     "bfp200_fwd_layer_decode": [_P, _I, _P, _P, _P, _I, _P, _P, _I, _P, _P],
+    "bfp200_wait_probe": [_P, _I],
     "bfp200_stage_dims": [_P, _P],
     "bfp200_time_matmuls": [_P, _I, _I, C.POINTER(_D), C.POINTER(_I)],
     "bfp200_profile_forward": [_P, _I, _I, _P, _P],

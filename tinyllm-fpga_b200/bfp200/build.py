@@ -14,7 +14,7 @@ from ._lib import LIB_DIR, LIB_PATH
 
 PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))   # tinyllm-fpga_b200/
 CSRC = os.path.join(PKG_ROOT, "csrc")
-SOURCES = ["kernels.cu", "gemv.cu", "layer1.cu", "persist.cu", "tc.cu", "sample.cu", "rtl.cu", "engine.cu", "noalloc.cu"]
+SOURCES = ["kernels.cu", "gemv.cu", "layer1.cu", "tc.cu", "sample.cu", "rtl.cu", "engine.cu", "noalloc.cu"]
 HEADERS = ["bfp_device.cuh", "kernels.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-shared"]

@@ -340,7 +340,6 @@ struct bfp200_handle {
   bool pdl = true;
   bool use_clusters = true;   // K-split reduction through distributed shared memory
   bool use_small = true;      // 1..4 columns: the fused small-batch kernels (gemv.cu)
-  bool use_persist = false;   // 1..4 columns: decode steps in one persistent kernel (persist.cu), opt-in
   bool use_tc = true;         // >= tc_min_cols columns: matmuls on the tcgen05 tensor cores (tc.cu)
   int tc_min_cols = 16;       // below: the dp2a matmul (one 16-column tile is the MMA's smallest N)
   bool use_block = true;      // 1 column: the attention half of a layer in one cluster launch (layer1.cu)
@@ -381,7 +380,6 @@ struct bfp200_handle {
   DBuf<int> col_slot, col_pos, col_kvpos, col_tok;
   DBuf<int> gen_out, dec_step, rtl_out;
   DBuf<long long> uncert_dev;
-  DBuf<unsigned> psync;
   // tensor-core records of the QKV, O, gate/up and down matrices, all layers
   DBuf<uint8_t> tc_rec[4];
   size_t tc_stride[4] = {0, 0, 0, 0};
@@ -959,36 +957,6 @@ int enqueue_forward(bfp200_handle* h, int ncols, bool head, bool decode = false)
   return BFP200_OK;
 }
 
-PersistArgs persist_args(bfp200_handle* h, int ncols, int n_gen) {
-  PersistArgs a;
-  a.D = h->D; a.HQ = h->HQ; a.HKV = h->HKV; a.FFN = h->FFN; a.NL = h->NL; a.V = h->V; a.MAXC = h->MAXC;
-  a.NTD = h->NTD; a.NTF = h->NTF;
-  a.ncols = ncols; a.n_gen = n_gen;
-  a.eps = h->cfg.eps; a.sqrt_hd = std::sqrt((double)h->HD); a.emb_norm_max = h->emb_norm_max;
-  a.wm_qkv = h->wm_qkv.p; a.wm_o = h->wm_o.p; a.wm_gu = h->wm_gu.p; a.wm_d = h->wm_d.p;
-  a.we_qkv = h->we_qkv.p; a.we_o = h->we_o.p; a.we_gu = h->we_gu.p; a.we_d = h->we_d.p;
-  a.g1 = h->g1.p; a.g2 = h->g2.p; a.nw = h->nw.p; a.rope_cs = h->rope_cs.p;
-  a.emb_m = h->emb_m.p; a.emb_e = h->emb_e.p;
-  a.pw_off = h->pw_off.p; a.pw_data = h->pw_data.p;
-  a.kv = h->kv();
-  a.h_m = h->h_m.p; a.h1_m = h->h1_m.p; a.qkv_m = h->qkv_m.p; a.a_m = h->a_m.p; a.mlp_m = h->mlp_m.p;
-  a.h_e = h->h_e.p; a.h1_e = h->h1_e.p; a.qkv_e = h->qkv_e.p; a.a_e = h->a_e.p; a.mlp_e = h->mlp_e.p;
-  a.part_val = h->part_val.p; a.part_sec = h->part_sec.p; a.part_idx = h->part_idx.p;
-  a.col_slot = h->col_slot.p; a.col_pos = h->col_pos.p; a.col_tok = h->col_tok.p;
-  a.gen_out = h->gen_out.p; a.uncert = h->uncert_dev.p;
-  a.sync = h->psync.p;
-  a.err = error_flag_device_ptr();
-  return a;
-}
-
-// 1..4 columns decode in the persistent kernel when its grid (one CTA per
-// SM) covers every phase's row groups and its shared memory fits.
-bool persist_ok(bfp200_handle* h, int ncols) {
-  if (!h->use_persist || ncols < 1 || ncols > 4) return false;
-  PersistArgs a = persist_args(h, ncols, 1);
-  return a.err != nullptr && persistent_plan(a, h->nsm, h->smem_optin);
-}
-
 // Leaves any sharding (destroys the decode graph first: it holds the
 // communicator's all-gather) and joins `comm` as rank `rank` of `n`.
 // Polls the handle's stream until it is idle or `limit_s` seconds passed;
@@ -1161,7 +1129,6 @@ int bfp200_open(const bfp200_cfg* cfg, int device, bfp200_handle** out) {
   if (const char* e = std::getenv("BFP200_NO_PDL")) h->pdl = !(e[0] == '1');
   if (const char* e = std::getenv("BFP200_NO_CLUSTER")) h->use_clusters = !(e[0] == '1');
   if (const char* e = std::getenv("BFP200_NO_SMALL")) h->use_small = !(e[0] == '1');
-  if (const char* e = std::getenv("BFP200_PERSIST")) h->use_persist = e[0] == '1';
   if (const char* e = std::getenv("BFP200_NO_TC")) h->use_tc = !(e[0] == '1');
   if (const char* e = std::getenv("BFP200_TC_MIN_COLS")) h->tc_min_cols = std::max(1, std::atoi(e));
   if (const char* e = std::getenv("BFP200_NO_BLOCK")) h->use_block = !(e[0] == '1');
@@ -1483,14 +1450,7 @@ static int generate_impl(bfp200_handle* h, const int32_t* prompt_ids, const int3
     CK(cudaMemcpyAsync(h->col_pos.p, dpos.data(), n_seq * 4, cudaMemcpyHostToDevice, h->stream));
     CK(cudaMemcpyAsync(h->col_tok.p, dtok.data(), n_seq * 4, cudaMemcpyHostToDevice, h->stream));
     CK(cudaMemsetAsync(h->dec_step.p, 0, 4, h->stream));
-    if (!smp && persist_ok(h, n_seq)) {
-      CK(h->psync.ensure(PERSIST_SYNC_WORDS));
-      CK(cudaMemsetAsync(h->psync.p, 0, PERSIST_SYNC_WORDS * sizeof(unsigned), h->stream));
-      PersistArgs pa = persist_args(h, n_seq, n_gen);
-      persistent_plan(pa, h->nsm, h->smem_optin);
-      CK(launch_persistent_decode(pa, h->nsm, h->stream));
-      ++h->launch_count;
-    } else {
+    {
       // one decode step captured once as a CUDA graph, replayed n_gen times
       const double temp = smp ? smp->temperature : 0.0;
       const int topk = smp ? smp->top_k : 0;
@@ -1708,6 +1668,19 @@ int bfp200_generate_sharded(bfp200_handle* const* hs, int n_dev, const int32_t* 
   return BFP200_OK;
 }
 
+int bfp200_wait_probe(bfp200_handle* h, int limit_ms) {
+  if (!h || limit_ms < 1 || limit_ms > 2000) return fail(BFP200_EINVAL, "wait_probe: limit_ms must be 1..2000");
+  DeviceGuard dguard(h->device);
+  CK(dguard.err);
+  DBuf<int> flag;
+  CK(flag.ensure(1));
+  CK(cudaMemsetAsync(flag.p, 0, sizeof(int), h->stream));
+  CK(launch_wait_probe(flag.p, (unsigned long long)limit_ms * 1000000ull, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  if (read_and_clear_error_flag(h->stream)) return fail(BFP200_ETIMEOUT, "a bounded device wait timed out");
+  return BFP200_OK;
+}
+
 int bfp200_uncertified_steps(bfp200_handle* h, long long* count) {
   if (!h || !count) return fail(BFP200_EINVAL, "null argument");
   *count = h->uncert;
@@ -1889,8 +1862,12 @@ static int matvec_impl(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, 
   W.wm = wm.p; W.we = we.p; W.G = G; W.NT = NT;
   DBuf<uint8_t> rec;
   DBuf<long long> acc; DBuf<unsigned> cnt;
-  const bool tc = tc_path(h, W, batch, EPI_STORE);
-  if (tc) {
+  // 1..4 columns: the decode path's small-batch GEMV; 16+: tensor cores;
+  // otherwise the dp2a matmul -- the kernels a decode step would run
+  const bool small = h->use_small && batch <= 4 && gemv_supported(GV_STORE, false, NT, batch);
+  const bool tc = !small && tc_path(h, W, batch, EPI_STORE);
+  if (small) {
+  } else if (tc) {
     CK(rec.ensure(tc_records_bytes(D_out, NT)));
     CK(launch_tc_pack(wm.p, we.p, D_out, NT, rec.p, h->stream));
   } else {
@@ -1903,6 +1880,16 @@ static int matvec_impl(bfp200_handle* h, const int16_t* x_m, const int8_t* x_e, 
   // the matvec only reads its inputs and writes its outputs: repeating it
   // (timing) leaves the same result
   auto run = [&]() -> int {
+    if (small) {
+      GemvArgs g;
+      g.W = W;
+      g.xm = dxm.p; g.xe = dxe.p; g.x_ld = D_in; g.x_lde = NT;
+      g.ncols = batch;
+      g.mode = GV_STORE;
+      g.om = dom.p; g.oe = doe.p; g.o_ld = D_out; g.o_lde = G;
+      CK(launch_gemv(g, h->stream, false));
+      return BFP200_OK;
+    }
     if (tc) return enqueue_tc(h, rec.p, W, dxm.p, dxe.p, D_in, NT, batch, EPI_STORE, dom.p, doe.p, D_out, G, nullptr,
                               nullptr);
     return enqueue_matmul(h, W, dxm.p, dxe.p, D_in, NT, batch, EPI_STORE, dom.p, doe.p, D_out, G, nullptr, nullptr,

@@ -2008,6 +2008,27 @@ int* error_flag_device_ptr() {
   return static_cast<int*>(p);
 }
 
+// Self-test of the bounded-wait path: spins on `flag` (which nothing sets)
+// for at most limit_ns nanoseconds of %globaltimer, then records the timeout
+// in the error flag exactly as the production waits do, and returns.
+__global__ void wait_probe_kernel(const volatile int* flag, unsigned long long limit_ns) {
+  if (threadIdx.x != 0) return;
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    if (*flag != 0) return;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > limit_ns) break;
+    __nanosleep(1000);
+  }
+  atomicExch(&g_error_flag, 5);
+}
+
+cudaError_t launch_wait_probe(const int* flag, unsigned long long limit_ns, cudaStream_t s) {
+  wait_probe_kernel<<<1, 32, 0, s>>>(flag, limit_ns);
+  return cudaGetLastError();
+}
+
 int read_and_clear_error_flag(cudaStream_t s) {
   int v = 0, z = 0;
   cudaMemcpyFromSymbolAsync(&v, g_error_flag, sizeof(int), 0, cudaMemcpyDeviceToHost, s);

@@ -154,42 +154,6 @@ bool tc_supported(int NT, int ncols);
 cudaError_t launch_tc_matmul(const TcArgs& a, cudaStream_t s, bool pdl);
 bool tc_config_valid(int NT, int ncb, int ks);
 
-// Persistent small-batch decode (persist.cu): one cooperative launch runs
-// n_gen decode steps of 1..4 columns (embedding, all layers, head, token
-// feedback).  The weight matrices are in DevMat layout, one per layer,
-// contiguous over layers.
-struct PersistArgs {
-  int D = 0, HQ = 0, HKV = 0, FFN = 0, NL = 0, V = 0, MAXC = 0, NTD = 0, NTF = 0;
-  int ncols = 0, n_gen = 0;
-  double eps = 1e-5, sqrt_hd = 8.0, emb_norm_max = 0.0;
-  const uint8_t *wm_qkv = nullptr, *wm_o = nullptr, *wm_gu = nullptr, *wm_d = nullptr;
-  const int8_t *we_qkv = nullptr, *we_o = nullptr, *we_gu = nullptr, *we_d = nullptr;
-  const double *g1 = nullptr, *g2 = nullptr, *nw = nullptr, *rope_cs = nullptr;
-  const int16_t* emb_m = nullptr;
-  const int8_t* emb_e = nullptr;
-  const int* pw_off = nullptr;
-  const unsigned short* pw_data = nullptr;
-  KvArena kv;
-  int16_t *h_m = nullptr, *h1_m = nullptr, *qkv_m = nullptr, *a_m = nullptr, *mlp_m = nullptr;
-  int8_t *h_e = nullptr, *h1_e = nullptr, *qkv_e = nullptr, *a_e = nullptr, *mlp_e = nullptr;
-  double *part_val = nullptr, *part_sec = nullptr;   // [2][4][grid] head partials
-  int* part_idx = nullptr;
-  int *col_slot = nullptr, *col_pos = nullptr, *col_tok = nullptr;   // in: step 0 columns; out: after n_gen
-  int* gen_out = nullptr;                            // [ncols][n_gen]
-  long long* uncert = nullptr;                       // += uncertified argmax decisions
-  unsigned* sync = nullptr;                          // PERSIST_SYNC_WORDS zeroed words
-  int* err = nullptr;                                // bounded-wait error flag
-  // role plan (persistent_plan): row groups per CTA of the QKV, O, gate/up
-  // (in g/u pairs) and down matvecs; each CTA keeps one role for the launch
-  int gpc[4] = {1, 1, 1, 1};
-};
-constexpr int PERSIST_SYNC_WORDS = 6 * 32;
-
-// Chooses the role plan for a grid of nctas CTAs (fills a.gpc); false when
-// no plan fits the grid and shared memory.
-bool persistent_plan(PersistArgs& a, int nctas, int smem_optin);
-size_t persistent_smem_bytes(const PersistArgs& a);
-cudaError_t launch_persistent_decode(const PersistArgs& a, int nctas, cudaStream_t s);
 // Device address of the flag that bounded waits set when they give up.
 int* error_flag_device_ptr();
 
@@ -216,6 +180,9 @@ bool gemv_supported(int mode, bool norm, int NT, int ncols);
 cudaError_t init_gemv_attributes();
 // Raises the dynamic shared memory limit of every kernel (call once per device).
 cudaError_t init_kernel_attributes();
+// Launches a kernel that waits (at most limit_ns) for *flag to become non-zero
+// and sets the bounded-wait error flag when it gives up (self-test).
+cudaError_t launch_wait_probe(const int* flag, unsigned long long limit_ns, cudaStream_t s);
 // Reads and clears the device flag a bounded wait sets when it gives up.
 int read_and_clear_error_flag(cudaStream_t s);
 
