@@ -269,6 +269,9 @@ struct DeviceGuard {
 // library itself does not depend on libnccl.  The types are NCCL's C ABI
 // (ncclUniqueId: 128 bytes by value; results and data types: C enums).
 // ---------------------------------------------------------------------------
+// a tuned tensor-core matmul configuration; all zero: the built-in choice
+struct TcChoice { int ncb = 0, ks = 0, ew = 0; };
+
 struct NcclUid { char internal[BFP200_NCCL_ID_BYTES]; };
 typedef struct ncclComm* NcclComm;
 constexpr int NCCL_OK = 0, NCCL_IN_PROGRESS = 7, NCCL_F64 = 8;
@@ -385,9 +388,9 @@ struct bfp200_handle {
   size_t tc_stride[4] = {0, 0, 0, 0};
   DBuf<unsigned> head_ctr;     // arrival counter of the single-launch head (left zeroed)
   HeadAdvance head_adv;        // set while a decode graph is captured: the head does the token feedback
-  // tensor-core matmul configuration (columns per CTA, K split) per
-  // (rows, K tiles, columns, epilogue), chosen by timing the candidates
-  std::map<std::tuple<int, int, int, int>, std::pair<int, int>> tc_cfg;
+  // tensor-core matmul configuration (columns per CTA, K split, epilogue
+  // warps) per (rows, K tiles, columns, epilogue), chosen by timing the candidates
+  std::map<std::tuple<int, int, int, int>, TcChoice> tc_cfg;
   // vocabulary-sharded head: this rank scans rows [v_lo, v_hi) and exchanges
   // one record per column with the other ranks (xsend -> xrecv, all-gather)
   NcclComm comm = nullptr;
@@ -521,39 +524,47 @@ bool tc_path(bfp200_handle* h, const DevMat& W, int ncols, int epi) {
   return h->use_tc && ncols >= h->tc_min_cols && tc_supported(W.NT, ncols) && !(epi == EPI_SWIGLU && W.G % 2);
 }
 
-// Times every valid (columns per CTA, K split) candidate of one matmul call
-// on its own arguments (the call only reads its inputs and writes its
-// outputs, so repeating it is harmless) and keeps the fastest.
+// Times every valid (columns per CTA, epilogue warps, K split) candidate of
+// one matmul call on its own arguments (the call only reads its inputs and
+// writes its outputs, so repeating it is harmless) and keeps the fastest.
+// The timed calls are chained the way a decode step chains its kernels
+// (programmatic dependent launch when the handle uses it): what counts is
+// the time from one kernel's dependency wait to the next's, not a lone
+// kernel's duration.
 int tc_tune(bfp200_handle* h, TcArgs t, const std::tuple<int, int, int, int>& key) {
   static const int KS[] = {1, 2, 3, 4, 6, 8};
+  static const int SHAPES[][2] = {{16, 16}, {16, 8}, {32, 16}};     // (columns per CTA, epilogue warps)
+  constexpr int REPS = 4;
   cudaEvent_t e0, e1;
   CK(cudaEventCreate(&e0));
   CK(cudaEventCreate(&e1));
   float best = -1.f;
-  std::pair<int, int> pick{0, 0};
-  for (int ncb : {16, 32})
+  TcChoice pick;
+  for (const auto& sh : SHAPES)
     for (int ks : KS) {
-      if (!tc_config_valid(t.NT, ncb, ks)) continue;
-      t.ncb = ncb;
+      if (!tc_config_valid(t.NT, sh[0], ks)) continue;
+      t.ncb = sh[0];
+      t.ew = sh[1];
       t.ks = ks;
-      if (launch_tc_matmul(t, h->stream, false) != cudaSuccess) { cudaGetLastError(); continue; }
+      if (launch_tc_matmul(t, h->stream, h->pdl) != cudaSuccess) { cudaGetLastError(); continue; }
       cudaEventRecord(e0, h->stream);
       bool ok = true;
-      for (int r = 0; r < 2 && ok; ++r) ok = launch_tc_matmul(t, h->stream, false) == cudaSuccess;
+      for (int r = 0; r < REPS && ok; ++r) ok = launch_tc_matmul(t, h->stream, h->pdl) == cudaSuccess;
       cudaEventRecord(e1, h->stream);
-      h->launch_count += 3;
+      h->launch_count += 1 + REPS;
       if (!ok) { cudaGetLastError(); continue; }
       if (cudaEventSynchronize(e1) != cudaSuccess) { cudaGetLastError(); continue; }
       float ms = 0.f;
       cudaEventElapsedTime(&ms, e0, e1);
-      if (best < 0.f || ms < best) { best = ms; pick = {ncb, ks}; }
+      if (best < 0.f || ms < best) { best = ms; pick = {sh[0], ks, sh[1]}; }
     }
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
-  h->tc_cfg[key] = pick;                 // {0, 0}: the built-in choice
+  h->tc_cfg[key] = pick;                 // {0, 0, 0}: the built-in choice
   if (const char* lg = std::getenv("BFP200_TC_LOG"); lg && *lg && *lg != '0')
-    std::fprintf(stderr, "bfp200: tensor-core matmul %d x %d at %d columns (epilogue %d): %d columns per CTA, K split %d, "
-                 "%.1f us\n", t.rows, t.NT * 16, t.ncols, t.mode, pick.first, pick.second, best * 1e3f / 2.f);
+    std::fprintf(stderr, "bfp200: tensor-core matmul %d x %d at %d columns (epilogue %d): %d columns per CTA, "
+                 "%d epilogue warps, K split %d, %.1f us\n", t.rows, t.NT * 16, t.ncols, t.mode, pick.ncb, pick.ew,
+                 pick.ks, best * 1e3f / REPS);
   return BFP200_OK;
 }
 
@@ -576,7 +587,7 @@ int enqueue_tc(bfp200_handle* h, const uint8_t* rec, DevMat W, const int16_t* xm
       it = h->tc_cfg.find(key);
     }
   }
-  if (it != h->tc_cfg.end()) { t.ncb = it->second.first; t.ks = it->second.second; }
+  if (it != h->tc_cfg.end()) { t.ncb = it->second.ncb; t.ks = it->second.ks; t.ew = it->second.ew; }
   CK(launch_tc_matmul(t, h->stream, h->pdl));
   return BFP200_OK;
 }

@@ -147,6 +147,7 @@ struct TcArgs {
   const int8_t* re = nullptr;
   int* err = nullptr;             // bounded-wait error flag
   int ncb = 0, ks = 0;            // columns per CTA (16 / 32) and K split (1..8); 0: built-in choice
+  int ew = 0;                     // epilogue warps: 16 (0) or 8 (16 columns per CTA, two CTAs per SM)
 };
 size_t tc_records_bytes(int rows, int NT);
 cudaError_t launch_tc_pack(const uint8_t* wm, const int8_t* we, int rows, int NT, uint8_t* rec, cudaStream_t s);

@@ -40,7 +40,27 @@ namespace bfp {
 
 namespace {
 
-constexpr int TC_THREADS = 576;     // warp 0 TMA, warp 1 MMA, warps 2..17 epilogue
+// CTA shape: NCB columns per CTA; warp 0 streams the records (TMA), warp 1
+// issues the MMAs, then EW epilogue warps, four per group of columns (one
+// per 32-lane quarter of tensor memory).  16 epilogue warps: the whole
+// tensor memory, one CTA per SM, CPT = NCB / 4 columns per thread -- the
+// shortest per-thread chains, for grids that leave SMs idle.  8 epilogue
+// warps (16 columns only): 256 tensor-memory columns and registers for two
+// CTAs per SM, 8 columns per thread, so that on grids larger than the GPU
+// one CTA's latency-bound phases (B staging, exponent maxima, the final
+// quantization) overlap the other's tile loop.
+template <int NCB, int EW>
+struct TcShape {
+  static_assert((EW == 16 && (NCB == 16 || NCB == 32)) || (EW == 8 && NCB == 16), "shape");
+  static constexpr int EPI_WARPS = EW;
+  static constexpr int THREADS = (2 + EW) * 32;
+  static constexpr int NQ = EW / 4;                        // column groups
+  static constexpr int CPT = NCB / NQ;                     // columns per epilogue thread (4 or 8)
+  static constexpr int CTAS_PER_SM = EW == 8 ? 2 : 1;
+  static constexpr unsigned TMEM_COLS = EW == 8 ? 256u : 512u;
+  static constexpr int D_STRIDE = (int)TMEM_COLS / 4;       // columns per D buffer (four buffers, >= 3 NCB)
+  static_assert(D_STRIDE >= 3 * NCB, "a D buffer holds 3 NCB columns");
+};
 constexpr int TC_M = 128;
 constexpr int TC_REC = 4096;            // bytes per (128-row block, K tile) record: Wl' and Wh rows
 constexpr int TC_SA = 4;                // record ring stages
@@ -119,6 +139,7 @@ __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[CPT]) {
   if constexpr (CPT == 8) tmem_ld8(taddr, r);
   else tmem_ld4(taddr, r);
 }
+
 
 // Per 128-row block: NT records, the rows' limb corrections tile by tile
 // ([NT][128] int32), their tile exponents tile by tile ([NT][128] int8) and
@@ -209,24 +230,26 @@ __device__ __forceinline__ long long ld_peer_s64(const long long* p, unsigned ra
 }
 
 // Warp roles: warp 0 streams the weight records (TMA), warp 1 issues the
-// MMAs, warps 2..17 are the epilogue: warp w reads TMEM lanes 32 (w % 4) ..
-// +31 (the rows) for column quarter (w - 2) / 4 (CPT = NCB / 4 columns per
-// thread).  Records pass through a ring of TC_SA stages (full: TMA bytes;
-// empty: the MMA's commit), D through TC_NB tensor-memory buffers of 128
-// columns (full: MMA commit; empty: the epilogue warps).  512 columns is the
-// whole of an SM's tensor memory: one CTA fits an SM (registers), and the
-// next kernel's CTAs allocate only after their dependency wait.
+// MMAs, warps 2.. are the epilogue: warp w reads TMEM lanes 32 (w % 4) ..
+// +31 (the rows) for column group (w - 2) / 4 (CPT columns per thread).
+// Records pass through a ring of TC_SA stages (full: TMA bytes; empty: the
+// MMA's commit), D through TC_NB tensor-memory buffers of D_STRIDE columns
+// (full: MMA commit; empty: the epilogue warps).  The CTAs resident on an SM
+// together allocate all of its tensor memory (512 columns), and the next
+// kernel's CTAs allocate only after their dependency wait, when this grid's
+// allocations are released.
 // Split K: gridDim.z CTAs form a cluster over the K tiles of one output
 // block; each computes the full max exponent, accumulates its own tiles,
 // and cluster rank 0 adds the others' int64 sums through distributed shared
 // memory (integer addition: exact in any order) before the epilogue.
 constexpr int TC_NB = 4;
-constexpr int TC_EPI_WARPS = 16;
 
-template <int NCB, int MODE>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <int NCB, int EW, int MODE>
+__global__ void __launch_bounds__(TcShape<NCB, EW>::THREADS, TcShape<NCB, EW>::CTAS_PER_SM)
 tc_matmul_kernel(TcArgs a) {
-  constexpr int CPT = NCB / 4;
+  using Shape = TcShape<NCB, EW>;
+  constexpr int CPT = Shape::CPT, NQ = Shape::NQ, EPIW = Shape::EPI_WARPS;
+  constexpr int TC_THREADS = Shape::THREADS;
   constexpr int N = 3 * NCB;
   extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -247,7 +270,7 @@ tc_matmul_kernel(TcArgs a) {
   int* xe_s = reinterpret_cast<int*>(smem + L.xe);           // [NT][NCB]
   int16_t* xe16_s = reinterpret_cast<int16_t*>(smem + L.xe16); // [NT][NCB], the same exponents as 16-bit lanes
   int* cx_s = reinterpret_cast<int*>(smem + L.cx);           // [ntl][NCB]
-  int* emin_s = reinterpret_cast<int*>(smem + L.emin);       // [NT][4]: min column exponent per column quarter
+  int* emin_s = reinterpret_cast<int*>(smem + L.emin);       // [NT][NQ]: min column exponent per column group
   long long* red = reinterpret_cast<long long*>(smem + L.red); // [NCB][128] (split K)
   const unsigned char* wex_s = smem + L.wex;                  // [128][NTP] tile exponents of the block's rows
   const int* cw_s = reinterpret_cast<const int*>(smem + L.cwt); // [ntl][128] limb corrections of this CTA's tiles
@@ -259,7 +282,7 @@ tc_matmul_kernel(TcArgs a) {
   // the previous kernel, so they stream before the wait
   if (tid == 0) {
     for (int s = 0; s < TC_SA; ++s) { mb_init(&rfull[s], 1); mb_init(&rempty[s], 1); }
-    for (int b = 0; b < TC_NB; ++b) { mb_init(&dfull[b], 1); mb_init(&dempty[b], TC_EPI_WARPS); }
+    for (int b = 0; b < TC_NB; ++b) { mb_init(&dfull[b], 1); mb_init(&dempty[b], EPIW); }
     mb_init(wbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     {
@@ -287,7 +310,8 @@ tc_matmul_kernel(TcArgs a) {
   // tensor memory only after the wait: a CTA waiting on its predecessor holds
   // none, so the predecessor's CTAs can always allocate theirs
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" :: "r"(su32(tptr)) : "memory");
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(su32(tptr)), "r"(Shape::TMEM_COLS)
+                 : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   // ---- B operand of every tile, column exponents and sums (columns c0 .. c0+NCB-1)
@@ -371,7 +395,7 @@ tc_matmul_kernel(TcArgs a) {
         mb_wait(&rfull[s], (unsigned)((t / TC_SA) & 1), a.err);
         if (t >= TC_NB) mb_wait(&dempty[b], (unsigned)(((t / TC_NB) - 1) & 1), a.err);
         tc_fence_after();
-        tc_mma(tbase + (uint32_t)(b * 128), smem_desc(ring + (size_t)s * TC_REC, 2048, 128),
+        tc_mma(tbase + (uint32_t)(b * Shape::D_STRIDE), smem_desc(ring + (size_t)s * TC_REC, 2048, 128),
                smem_desc(Z + (size_t)3 * t * NCB * 16, NCB * 16, 128), idesc);
         tc_commit(&dfull[b]);
         tc_commit(&rempty[s]);
@@ -397,7 +421,7 @@ tc_matmul_kernel(TcArgs a) {
           const uint2 x4 = *reinterpret_cast<const uint2*>(xr);
           m = __vmins2(x4.x, x4.y);
         }
-        emin_s[t * 4 + quarter] = min((int)(int16_t)(m & 0xFFFFu), (int)(int16_t)(m >> 16));
+        emin_s[t * NQ + quarter] = min((int)(int16_t)(m & 0xFFFFu), (int)(int16_t)(m >> 16));
       }
     }
     {
@@ -466,7 +490,7 @@ tc_matmul_kernel(TcArgs a) {
         }
       }
     }
-    asm volatile("bar.sync 1, %0;" :: "r"(TC_EPI_WARPS * 32) : "memory");     // emin_s complete
+    asm volatile("bar.sync 1, %0;" :: "r"(EPIW * 32) : "memory");     // emin_s complete
     #pragma unroll
     for (int j = 0; j < CPT; ++j) acc[j] = 0;
     for (int t = 0; t < ntl; ++t) {
@@ -475,7 +499,7 @@ tc_matmul_kernel(TcArgs a) {
       mb_wait(&dfull[b], (unsigned)((t / TC_NB) & 1), a.err);
       tc_fence_after();
       uint32_t hh[CPT], cr[CPT], ll[CPT];
-      const uint32_t tq = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 128 + cb);
+      const uint32_t tq = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * Shape::D_STRIDE + cb);
       tmem_ld<CPT>(tq, hh);
       tmem_ld<CPT>(tq + NCB, cr);
       tmem_ld<CPT>(tq + 2 * NCB, ll);
@@ -491,7 +515,7 @@ tc_matmul_kernel(TcArgs a) {
       // pairs is at most 16 (a bound from the row's largest max exponent and
       // the quarter's smallest column exponent), floor(S / 2^sh) =
       // hh * 2^(16-sh) + (w >> sh) exactly: two 32 x 32 -> 64-bit multiply-adds.
-      const int shb = MxMax - wer - emin_s[tg * 4 + quarter];
+      const int shb = MxMax - wer - emin_s[tg * NQ + quarter];
       if (__all_sync(0xffffffffu, shb <= 16)) {
         #pragma unroll
         for (int j = 0; j < CPT; j += 4) {
@@ -623,23 +647,32 @@ tc_matmul_kernel(TcArgs a) {
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" :: "r"(tbase) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tbase), "r"(Shape::TMEM_COLS) : "memory");
   }
 }
 
-template <int NCB, int MODE>
-cudaError_t launch_tc_t(const TcArgs& a, int ks, cudaStream_t s, bool pdl) {
+template <int NCB, int EW, int MODE>
+cudaError_t launch_tc_t(const TcArgs& a, int ks, int nsm, cudaStream_t s, bool pdl) {
+  using Shape = TcShape<NCB, EW>;
+  const dim3 grid((a.rows + TC_M - 1) / TC_M, (a.ncols + NCB - 1) / NCB, ks);
   const size_t smem = tc_layout(a.NT, NCB, (a.NT + ks - 1) / ks, ks > 1).total;
-  cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<NCB, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  // the two-CTAs-per-SM shape is for grids larger than the GPU; on fewer
+  // CTAs the sixteen-warp shape's shorter per-thread chains are faster
+  if (Shape::CTAS_PER_SM > 1 && (long)grid.x * grid.y * grid.z <= nsm) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(tc_matmul_kernel<NCB, EW, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
+  if (Shape::CTAS_PER_SM > 1) {      // all of the SM's unified memory as shared memory: room for both CTAs
+    e = cudaFuncSetAttribute(tc_matmul_kernel<NCB, EW, MODE>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+  }
   if (ks > 1) {
-    e = cudaFuncSetAttribute(tc_matmul_kernel<NCB, MODE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    e = cudaFuncSetAttribute(tc_matmul_kernel<NCB, EW, MODE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.rows + TC_M - 1) / TC_M, (a.ncols + NCB - 1) / NCB, ks);
-  cfg.blockDim = dim3(TC_THREADS);
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(Shape::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
@@ -658,7 +691,7 @@ cudaError_t launch_tc_t(const TcArgs& a, int ks, cudaStream_t s, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<NCB, MODE>, a);
+  return cudaLaunchKernelEx(&cfg, tc_matmul_kernel<NCB, EW, MODE>, a);
 }
 
 bool tc_config_fits(int NT, int ncb, int ks) {
@@ -693,20 +726,24 @@ bool tc_config_valid(int NT, int ncb, int ks) { return tc_config_fits(NT, ncb, k
 
 cudaError_t launch_tc_matmul(const TcArgs& a, cudaStream_t s, bool pdl) {
   int ncb = a.ncb, ks = a.ks;
-  if (ncb == 0 || ks == 0) {
-    int dev = 0, nsm = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    tc_default_config(a.rows, a.NT, a.ncols, nsm, &ncb, &ks);
-  }
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (ncb == 0 || ks == 0) tc_default_config(a.rows, a.NT, a.ncols, nsm, &ncb, &ks);
   if (!tc_config_fits(a.NT, ncb, ks)) return cudaErrorInvalidValue;
   if (a.mode == EPI_SWIGLU && (a.rows % 32)) return cudaErrorInvalidValue;
-  const bool w = ncb == 32;
+  const int ew = a.ew ? a.ew : 16;
+  if (ew != 16 && !(ew == 8 && ncb == 16)) return cudaErrorInvalidValue;
+  auto go = [&](auto mode_tag) -> cudaError_t {
+    constexpr int M = decltype(mode_tag)::value;
+    if (ncb == 32) return launch_tc_t<32, 16, M>(a, ks, nsm, s, pdl);
+    if (ew == 8) return launch_tc_t<16, 8, M>(a, ks, nsm, s, pdl);
+    return launch_tc_t<16, 16, M>(a, ks, nsm, s, pdl);
+  };
   switch (a.mode) {
-    case EPI_STORE: return w ? launch_tc_t<32, EPI_STORE>(a, ks, s, pdl) : launch_tc_t<16, EPI_STORE>(a, ks, s, pdl);
-    case EPI_RESIDUAL:
-      return w ? launch_tc_t<32, EPI_RESIDUAL>(a, ks, s, pdl) : launch_tc_t<16, EPI_RESIDUAL>(a, ks, s, pdl);
-    case EPI_SWIGLU: return w ? launch_tc_t<32, EPI_SWIGLU>(a, ks, s, pdl) : launch_tc_t<16, EPI_SWIGLU>(a, ks, s, pdl);
+    case EPI_STORE: return go(std::integral_constant<int, EPI_STORE>{});
+    case EPI_RESIDUAL: return go(std::integral_constant<int, EPI_RESIDUAL>{});
+    case EPI_SWIGLU: return go(std::integral_constant<int, EPI_SWIGLU>{});
   }
   return cudaErrorInvalidValue;
 }
