@@ -64,7 +64,7 @@ struct TcShape {
 constexpr int TC_M = 128;
 constexpr int TC_REC = 4096;            // bytes per (128-row block, K tile) record: Wl' and Wh rows
 constexpr int TC_SA = 4;                // record ring stages
-constexpr long long TC_SPIN = 1LL << 20;
+constexpr int TC_SPIN = 1 << 20;
 
 __device__ __forceinline__ unsigned su32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void pdl_wait_tc() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -81,7 +81,7 @@ __device__ __forceinline__ bool mb_try(unsigned long long* bar, unsigned parity)
 }
 // bounded wait; returns false (and raises the error flag) when it gives up
 __device__ __forceinline__ bool mb_wait(unsigned long long* bar, unsigned parity, int* err) {
-  long long it = 0;
+  int it = 0;
   while (!mb_try(bar, parity)) {
     if (++it > TC_SPIN) { atomicExch(err, 4); return false; }
   }
@@ -493,13 +493,23 @@ tc_matmul_kernel(TcArgs a) {
     asm volatile("bar.sync 1, %0;" :: "r"(EPIW * 32) : "memory");     // emin_s complete
     #pragma unroll
     for (int j = 0; j < CPT; ++j) acc[j] = 0;
+    // per-tile operands advance by pointer: the row's correction and tile
+    // exponent ([t][128] tables), the group's smallest column exponent, the
+    // columns' exponents and sums
+    const uint32_t tq0 = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)cb;
+    const int* cw_p = cw_s + row;
+    const int8_t* wt_p = wt_s + row;
+    const int* em_p = emin_s + t_lo * NQ + quarter;
+    const int* xe_p = xe_s + t_lo * NCB + cb;
+    const int* cx_p = cx_s + cb;
+    int b = 0;
+    unsigned ph = 0;
     for (int t = 0; t < ntl; ++t) {
-      const int b = t % TC_NB, tg = t_lo + t;
       // the three limb sums of tile t
-      mb_wait(&dfull[b], (unsigned)((t / TC_NB) & 1), a.err);
+      mb_wait(&dfull[b], ph, a.err);
       tc_fence_after();
       uint32_t hh[CPT], cr[CPT], ll[CPT];
-      const uint32_t tq = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * Shape::D_STRIDE + cb);
+      const uint32_t tq = tq0 + (uint32_t)(b * Shape::D_STRIDE);
       tmem_ld<CPT>(tq, hh);
       tmem_ld<CPT>(tq + NCB, cr);
       tmem_ld<CPT>(tq + 2 * NCB, ll);
@@ -507,45 +517,43 @@ tc_matmul_kernel(TcArgs a) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(su32(&dempty[b])) : "memory");
-      // the row's correction and exponent of tile t (tables in shared memory)
-      const int cw = cw_s[t * TC_M + row];
-      const int wer = (int)wt_s[t * TC_M + row];
-      // per-tile floor shift and int64 accumulation (:223-228).  S = 65536 hh + w
-      // with w = 256 cr + lo (|w| < 2^29).  When every shift of this warp's
-      // pairs is at most 16 (a bound from the row's largest max exponent and
-      // the quarter's smallest column exponent), floor(S / 2^sh) =
-      // hh * 2^(16-sh) + (w >> sh) exactly: two 32 x 32 -> 64-bit multiply-adds.
-      const int shb = MxMax - wer - emin_s[tg * NQ + quarter];
-      if (__all_sync(0xffffffffu, shb <= 16)) {
-        #pragma unroll
-        for (int j = 0; j < CPT; j += 4) {
-          const int4 e4 = *reinterpret_cast<const int4*>(xe_s + tg * NCB + cb + j);
-          const int4 x4 = *reinterpret_cast<const int4*>(cx_s + t * NCB + cb + j);
-          const int ev4[4] = {e4.x, e4.y, e4.z, e4.w}, cv4[4] = {x4.x, x4.y, x4.z, x4.w};
-          #pragma unroll
-          for (int q2 = 0; q2 < 4; ++q2) {
-            const int jj = j + q2;
-            const int sh = Mx[jj] - wer - ev4[q2];
-            const int w = (int)cr[jj] * 256 + ((int)ll[jj] + cw + cv4[q2]);
-            acc[jj] = mad_wide_s32(w >> sh, 1, mad_wide_s32((int)hh[jj], 0x10000 >> sh, acc[jj]));
-          }
-        }
-        continue;
-      }
-      // general shifts: S = ((256 hh + cr) * 256 + lo) in 64 bits (256 hh + cr fits int32)
+      const int cw = *cw_p;
+      const int wer = (int)*wt_p;
+      const int emn = *em_p;
+      int ev[CPT], cv[CPT];
       #pragma unroll
       for (int j = 0; j < CPT; j += 4) {
-        const int4 e4 = *reinterpret_cast<const int4*>(xe_s + tg * NCB + cb + j);
-        const int4 x4 = *reinterpret_cast<const int4*>(cx_s + t * NCB + cb + j);
-        const int ev4[4] = {e4.x, e4.y, e4.z, e4.w}, cv4[4] = {x4.x, x4.y, x4.z, x4.w};
+        const int4 e4 = *reinterpret_cast<const int4*>(xe_p + j);
+        const int4 x4 = *reinterpret_cast<const int4*>(cx_p + j);
+        ev[j] = e4.x; ev[j + 1] = e4.y; ev[j + 2] = e4.z; ev[j + 3] = e4.w;
+        cv[j] = x4.x; cv[j + 1] = x4.y; cv[j + 2] = x4.z; cv[j + 3] = x4.w;
+      }
+      cw_p += TC_M; wt_p += TC_M; em_p += NQ; xe_p += NCB; cx_p += NCB;
+      if (++b == TC_NB) { b = 0; ph ^= 1u; }
+      // per-tile floor shift and int64 accumulation (:223-228).  S = 65536 hh + w
+      // with w = 256 cr + ll + cw + cx = S - 65536 hh (|w| < 2^28).  For
+      // sh <= 16, floor(S / 2^sh) = hh * 2^(16-sh) + (w >> sh): two 32 x 32 ->
+      // 64-bit multiply-adds.  For sh >= 16, floor(S / 2^sh) =
+      // floor(floor(S / 2^16) / 2^(sh-16)) = (hh + (w >> 16)) >> (sh - 16), in
+      // 32 bits.  Shifts above ALIGN_MAX contribute nothing.  When every shift
+      // of this warp is at most 16 (a bound from the row's largest max
+      // exponent and the group's smallest column exponent) only the first form
+      // runs.
+      const int shb = MxMax - wer - emn;
+      if (__all_sync(0xffffffffu, shb <= 16)) {
         #pragma unroll
-        for (int q2 = 0; q2 < 4; ++q2) {
-          const int jj = j + q2;
-          const int sh = Mx[jj] - wer - ev4[q2];
-          const int lo = (int)ll[jj] + cw + cv4[q2];
-          const int u = (int)hh[jj] * 256 + (int)cr[jj];
-          const long long S = (long long)u * 256 + (long long)lo;
-          if (sh <= ALIGN_MAX) acc[jj] += S >> sh;
+        for (int j = 0; j < CPT; ++j) {
+          const int sh = Mx[j] - wer - ev[j];
+          const int w = (int)cr[j] * 256 + ((int)ll[j] + cw + cv[j]);
+          acc[j] = mad_wide_s32(w >> sh, 1, mad_wide_s32((int)hh[j], 0x10000 >> sh, acc[j]));
+        }
+      } else {
+        #pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+          const int sh = Mx[j] - wer - ev[j];
+          const int w = (int)cr[j] * 256 + ((int)ll[j] + cw + cv[j]);
+          if (sh <= 16) acc[j] = mad_wide_s32(w >> sh, 1, mad_wide_s32((int)hh[j], 0x10000 >> sh, acc[j]));
+          else if (sh <= ALIGN_MAX) acc[j] += ((int)hh[j] + (w >> 16)) >> (sh - 16);
         }
       }
     }
