@@ -346,16 +346,27 @@ def sharded_head_run(dec, prompts, n_gen, args, world, replica_tok_ms):
     the head split by vocabulary rows and the argmax exchanged by NCCL inside
     the library's decode graph.  Device time per generated token, max over
     ranks, next to the unsharded (replica) time."""
-    from bfp200.dist import shard_head_distributed
-    shard_head_distributed(dec)
-    for _ in range(max(1, args.warmup // 2)):
-        dec.generate(prompts, n_gen)
+    from bfp200.dist import check_peers, shard_head_distributed
+    err = None
     ms = []
-    for _ in range(max(1, args.steps // 2)):
-        dec.generate(prompts, n_gen)
-        ms.append(dec.last_timing()["decode_ms"] / n_gen)
-    dec.shard_head(None, 1, 0)
-    tok_ms = max_over_ranks(statistics.mean(ms), world)
+    try:
+        shard_head_distributed(dec)
+        nw, nt = max(1, args.warmup // 2), max(1, args.steps // 2)
+        for i in range(nw + nt):
+            check_peers(f"sharded{i}", timeout_s=60)    # a rank that left is noticed here, before the exchange
+            dec.generate(prompts, n_gen)
+            if i >= nw:
+                ms.append(dec.last_timing()["decode_ms"] / n_gen)
+    except Exception as e:            # the library's bounded waits end a stalled exchange with an error
+        err = f"{type(e).__name__}: {e}"[:200]
+    try:
+        dec.shard_head(None, 1, 0)
+    except Exception as e:
+        err = err or f"{type(e).__name__}: {e}"[:200]
+    # every rank takes the same collective steps, failed or not
+    tok_ms = max_over_ranks(statistics.mean(ms) if ms and err is None else float("inf"), world)
+    if err is not None or tok_ms == float("inf"):
+        return {"ranks": world, "error": err or "another rank failed"}
     return {"ranks": world, "decode_us_per_token": round(tok_ms * 1e3, 2),
             "replica_decode_us_per_token": round(replica_tok_ms * 1e3, 2),
             "vocab_rows_per_rank": 49152 // world, "exchange": "NCCL all-gather of 32 B per rank per step"}
@@ -379,7 +390,7 @@ def batched_roofline(dec, ncols, reps, pk, pk_kind):
     ms, n = dec.time_matmuls(ncols, reps)
     tops = LAYER_MACS * ncols * 4 * 2 / (ms / 1e3) / 1e12
     peak = 2 * pk["bf16_tflops"]
-    return {"kernel": "tc_matmul_kernel (tcgen05 kind::i8 limbs)" if ncols >= 64 else "bfp_matmul_kernel (dp2a)",
+    return {"kernel": "tc_matmul_kernel (tcgen05 kind::i8 limbs)" if ncols >= 16 else "bfp_matmul_kernel (dp2a)",
             "bound": "tensor", "achieved": round(tops, 2), "peak": round(peak, 1), "unit": "TOPS (int8)",
             "frac": round(tops / peak, 5), "traffic": None, "peak_kind": f"2 x bf16 ({pk_kind})",
             "ncols": ncols, "ms_per_step": round(ms, 4), "launches_per_step": n,

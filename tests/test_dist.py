@@ -121,3 +121,25 @@ def test_sharded_argmax_gloo_world2():
 ])
 def test_reduce_argmax(parts, want):
     assert bd.reduce_argmax(parts) == want
+
+
+def _leave_between_steps(rank, world):
+    """Rank 1 takes step 0, then leaves the job before step 1; rank 0 must
+    notice at its step-1 check, on the host, within the time limit."""
+    import time
+    bd.check_peers(0, timeout_s=30)
+    if rank == 1:
+        return "left"
+    t0 = time.monotonic()
+    try:
+        bd.check_peers(1, timeout_s=2)
+    except bd.PeerLost as e:
+        return ("lost", str(e), time.monotonic() - t0)
+    return ("not noticed",)
+
+
+def test_rank_leaving_between_steps_is_noticed_on_the_host():
+    out = _run(_leave_between_steps)
+    assert out[1] == "left"
+    assert out[0][0] == "lost", out
+    assert "rank(s) 1" in out[0][1] and out[0][2] < 20

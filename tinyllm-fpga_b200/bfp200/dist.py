@@ -120,5 +120,42 @@ def shard_head_distributed(decoder, group=None):
     decoder.shard_head(box[0], world, rank)
 
 
+class PeerLost(RuntimeError):
+    """A rank of the group did not reach the same step within the time limit."""
+
+
+def _group_store(group=None):
+    import torch.distributed as dist
+    if group is None:
+        from torch.distributed import distributed_c10d as c10d
+        return c10d._get_default_store()
+    raise ValueError("check_peers: pass store= for a non-default group")
+
+
+def check_peers(step, timeout_s=10.0, group=None, store=None, prefix="bfp200/alive"):
+    """Host-side liveness check between decode calls of a sharded head.
+
+    Every rank posts `<prefix>/<step>/<rank>` to the process group's store and
+    waits, at most `timeout_s`, for the keys of every other rank at the same
+    step.  A rank that has left the job (exited, crashed, or stopped decoding)
+    is noticed here, on the host and before this rank launches work that
+    holds a collective, instead of by an exchange on the GPU that would wait
+    for it.  Raises PeerLost naming the missing ranks."""
+    import datetime
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    st = store if store is not None else _group_store(group)
+    st.set(f"{prefix}/{step}/{rank}", "1")
+    others = [f"{prefix}/{step}/{r}" for r in range(world) if r != rank]
+    if not others:
+        return
+    try:
+        st.wait(others, datetime.timedelta(seconds=timeout_s))
+    except Exception as e:        # the store raises on its time limit
+        missing = [k.rsplit("/", 1)[1] for k in others if not st.check([k])]
+        raise PeerLost(f"step {step}: rank(s) {', '.join(missing) or '?'} did not arrive within {timeout_s} s") from e
+
+
 __all__ = ["partition_sequences", "generate_distributed", "reduce_argmax", "combine_argmax", "shard_rows",
-           "shard_head_distributed"]
+           "shard_head_distributed", "check_peers", "PeerLost"]
