@@ -13,8 +13,10 @@ does not shard, so N GPUs run N independent streams -- weak scaling).
 The same line carries ``bs256``: configs[2] = "cfg3", 256 ragged sequences
 x 128 tokens, sequences split over the ranks with no collectives.
 
-Further keys of the final line: ``roofline`` (the bs1 matvec kernels against
-the measured HBM copy bandwidth), ``path_roofline_frac`` (weight + KV bytes
+Further keys of the final line: ``roofline`` (the bs1 decode's dominant
+kernel, the per-layer attention block, against the measured HBM copy
+bandwidth, with the gate/up and down GEMV figures in ``roofline.gemv``),
+``path_roofline_frac`` (weight + KV bytes
 per token over the decode time), ``bs256`` (tok/s, ms per step, and the
 batched tensor-core matvecs' roofline), ``cpu_baseline`` (the oracle port on
 all usable host cores, rank 0 at N = 1) and, at N > 1, ``sharded_head``
@@ -71,6 +73,18 @@ def weight_bytes_per_token(cfg):
 
 def kv_bytes_per_position(cfg):
     return cfg.NL * 2 * cfg.H_KV * cfg.HD * 2 + cfg.NL * 2 * cfg.H_KV * cfg.HD // 16   # 23,760 B
+
+
+def attn_block_bytes(cfg, pos):
+    """Algorithmic bytes of one bfp_attn_block_kernel launch (one layer, one
+    column, KV position pos): Q/K/V and O weights (int16 mantissas + int8
+    exponents per 16), the f64 gamma, h in and h1 out (BFP), the cached K/V
+    rows 0..pos-1 read and row pos written."""
+    kvd = cfg.H_KV * cfg.HD
+    w = (cfg.D + 2 * kvd) * cfg.D + cfg.D * cfg.D
+    act = 2 * (cfg.D * 2 + cfg.D // 16)
+    kv_row = kv_bytes_per_position(cfg) // cfg.NL               # 792 B per layer and position
+    return w * 2 + w // 16 + cfg.D * 8 + act + kv_row * (pos + 1)
 
 
 class ClockSampler:
@@ -217,20 +231,40 @@ def run_ours(args, world, rank, local):
     last = dec.last_timing()
     decode_tok_ms = last["decode_ms"] / ngen2
 
-    # ---- roofline of the dominant kernel: the BFP matmul.  Its device time
-    # for one token's 120 launches (4 per layer) is measured with events on
-    # the library stream by replaying the decode-step matmuls.
+    # ---- roofline of the dominant kernel of the bs1 decode: the attention
+    # block (RMSNorm, Q/K/V, RoPE, KV write, attention, O, residual; one
+    # launch per layer, ~57% of a token's kernel time).  Its launch duration
+    # is measured with CUDA events around each launch of one serialised
+    # forward at KV position 176 (the cfg2 stream's mean); the other kernels
+    # of that forward give the gate/up and down GEMV figures.
     wbytes, hbytes = weight_bytes_per_token(cfg2)
-    mm_ms, mm_n = dec.time_matmuls(1, args.mm_reps)
-    mm = {"ms_per_token": mm_ms, "launches": mm_n}
-    achieved_gbs = wbytes / (mm["ms_per_token"] / 1e3) / 1e9
     peak = pk["hbm_gbs"]
-    roof = {"kernel": "bfp_gemv_small_kernel (fused QKV / O / gate-up / down matvecs, bs1)", "bound": "hbm", "achieved": round(achieved_gbs, 1),
-            "peak": peak, "unit": "GB/s", "frac": round(achieved_gbs / peak, 4), "traffic": GEMV_TRAFFIC_PER_TOKEN,
-            "traffic_unit": "bytes per token (120 launches, ncu dram__bytes_read.sum + dram__bytes_write.sum)",
-            "algorithmic_bytes": wbytes,
-            "peak_kind": pk_kind, "launches_per_token": mm["launches"],
-            "us_per_launch": round(mm["ms_per_token"] * 1e3 / mm["launches"], 3)}
+    prof1 = dec.profile_forward(1, 176)
+    a_ms, a_n = prof1["attention"]
+    a_us = a_ms * 1e3 / max(1, a_n)
+    a_bytes = attn_block_bytes(cfg2, 176)
+    a_gbs = a_bytes / (a_us * 1e-6) / 1e9
+    kvd = cfg2.H_KV * cfg2.HD
+    gemv = {}
+    for kind, rows, din in (("mm_gu", 2 * cfg2.FFN, cfg2.D), ("mm_d", cfg2.D, cfg2.FFN)):
+        ms_k, n_k = prof1[kind]
+        if n_k:
+            us_k = ms_k * 1e3 / n_k
+            b_k = rows * din * 2 + rows * din // 16
+            gemv[kind] = {"us_per_launch": round(us_k, 3), "achieved_gbs": round(b_k / (us_k * 1e-6) / 1e9, 1),
+                          "frac": round(b_k / (us_k * 1e-6) / 1e9 / peak, 4)}
+    # the matvec engine alone: one token's 120 matvecs (Q/K/V, O, gate/up,
+    # down) on the GEMV kernel, replayed from a graph between events
+    mm_ms, mm_n = dec.time_matmuls(1, args.mm_reps)
+    gemv["engine_120_matvecs"] = {"ms_per_token": round(mm_ms, 4), "achieved_gbs": round(wbytes / (mm_ms / 1e3) / 1e9, 1),
+                                  "frac": round(wbytes / (mm_ms / 1e3) / 1e9 / peak, 4)}
+    roof = {"kernel": "bfp_attn_block_kernel (RMSNorm + Q/K/V + RoPE + KV + attention + O + residual, bs1)",
+            "bound": "hbm", "achieved": round(a_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(a_gbs / peak, 4),
+            "traffic": ATTN_BLOCK_TRAFFIC_POS176,
+            "traffic_unit": "bytes per launch at KV position 176 (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+            "algorithmic_bytes": a_bytes, "peak_kind": pk_kind, "launches_per_token": a_n,
+            "us_per_launch": round(a_us, 3), "timing": "CUDA events around each launch of a serialised forward, KV 176",
+            "gemv": gemv}
     # whole-path roofline: weights + KV per token over the decode time
     mean_pos = 48 + ngen2 / 2
     path_bytes = wbytes + hbytes + kv_bytes_per_position(cfg2) * (mean_pos + 1)
@@ -256,7 +290,7 @@ def run_ours(args, world, rank, local):
         if part3:
             bs256["roofline"] = batched_roofline(dec, len(part3), max(1, args.mm_reps // 5), pk, pk_kind)
 
-    profile = {"bs1_pos176": dec.profile_forward(1, 176)}
+    profile = {"bs1_pos176": prof1}
     if not args.no_bs256 and part3:
         profile["bs256_pos100"] = dec.profile_forward(len(part3), 100)
     sharded = None
@@ -372,11 +406,11 @@ def sharded_head_run(dec, prompts, n_gen, args, world, replica_tok_ms):
             "vocab_rows_per_rank": 49152 // world, "exchange": "NCCL all-gather of 32 B per rank per step"}
 
 
-# DRAM bytes (read + write) of one token's 120 bfp_gemv_small_kernel launches, from an
-# ncu capture of one decode-graph replay (dram__bytes_read.sum +
-# dram__bytes_write.sum over the launches); the algorithmic weight bytes are
-# 218,972,160, the rest is activations, gammas and the RoPE table.
-GEMV_TRAFFIC_PER_TOKEN = 225_038_080
+# DRAM bytes (read + write) of one bfp_attn_block_kernel launch at KV position
+# 176, the mean of three launches of an ncu capture of a serialised forward
+# (dram__bytes_read.sum + dram__bytes_write.sum, writes 0); algorithmic bytes
+# at that position: 1,971,936 (the excess is about the kernel's code).
+ATTN_BLOCK_TRAFFIC_POS176 = 2_067_797
 
 LAYER_MACS = 106_168_320      # int16 MACs of one token's 4 x 30 layer matvecs (head excluded)
 
