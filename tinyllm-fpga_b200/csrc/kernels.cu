@@ -887,22 +887,27 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
 // dimension).  Per head: the same operations in the same order as
 // attention_kernel (scores four lanes per position, softmax_fp with numpy's
 // pairwise sum, sm[t] * v[t] accumulated sequentially in t).  Needs grp * 64
-// <= ATT_THREADS.
-constexpr int ATT_MAXG = ATT_THREADS / 64;
+// <= AG_THREADS.  Sized for occupancy: 192 threads (3 heads x 64 dimensions),
+// 48 registers and K / V staged AG_VCH positions at a time keep a CTA at
+// ~36 KB of shared memory, so six CTAs share an SM and a 256-sequence batch
+// (768 CTAs) runs in one wave on 148 SMs instead of two.
+constexpr int AG_THREADS = 192;
+constexpr int AG_MAXG = AG_THREADS / 64;
+constexpr int AG_VCH = 80;
 __host__ __device__ inline size_t att_group_sc_stride(int max_ctx) { return ((size_t)max_ctx + 1) & ~size_t(1); }
 
-__global__ void __launch_bounds__(ATT_THREADS)
+__global__ void __launch_bounds__(AG_THREADS, 6)
 attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
                        double sqrt_hd, double inv_hd, int16_t* am, int8_t* ae, const int* pw_off,
                        const unsigned short* pw_data, int early) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int HD = 64;
-  constexpr int VCH = att_vchunk(true);
-  __shared__ int s_qm[ATT_MAXG * HD];
-  __shared__ int s_qe[ATT_MAXG * 4];
-  __shared__ double s_red[ATT_THREADS / 32][ATT_MAXG];
-  __shared__ double s_mx[ATT_MAXG], s_sum[ATT_MAXG];
-  __shared__ double s_val[ATT_MAXG][160];
+  constexpr int VCH = AG_VCH;
+  __shared__ int s_qm[AG_MAXG * HD];
+  __shared__ int s_qe[AG_MAXG * 4];
+  __shared__ double s_red[AG_THREADS / 32][AG_MAXG];
+  __shared__ double s_mx[AG_MAXG], s_sum[AG_MAXG];
+  __shared__ double s_val[AG_MAXG][160];
   __shared__ unsigned short s_plan[ATT_PLAN_MAX];
   pdl_trigger();
   const int c = blockIdx.x, kvh = blockIdx.y;
@@ -923,7 +928,7 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
   {
     const uint4* ksrc = reinterpret_cast<const uint4*>(kv.km + kbase * HD);
     const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + kbase * HD);
-    for (int i = tid; i < nold * 8; i += ATT_THREADS) {
+    for (int i = tid; i < nold * 8; i += AG_THREADS) {
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(ks + att_kswz(i))),
                    "l"(ksrc + i) : "memory");
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(vs + i)),
@@ -931,7 +936,7 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
     }
     const unsigned* kesrc = reinterpret_cast<const unsigned*>(kv.ke + kbase * 4);
     const unsigned* vesrc = reinterpret_cast<const unsigned*>(kv.ve + kbase * 4);
-    for (int i = tid; i < nold; i += ATT_THREADS) {
+    for (int i = tid; i < nold; i += AG_THREADS) {
       asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"((unsigned)__cvta_generic_to_shared(kes + i)),
                    "l"(kesrc + i) : "memory");
       asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"((unsigned)__cvta_generic_to_shared(ves + i)),
@@ -944,14 +949,14 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
     const unsigned short* gp = pw_data + pw_off[T];
     const int np = 3 * (int)gp[0] + (int)gp[1];
     if (np <= ATT_PLAN_MAX) {
-      for (int i = tid; i < np; i += ATT_THREADS) s_plan[i] = gp[i];
+      for (int i = tid; i < np; i += AG_THREADS) s_plan[i] = gp[i];
       plan = s_plan;
     } else {
       plan = gp;
     }
   }
   if (early) pdl_wait();
-  for (int i = tid; i < grp * HD; i += ATT_THREADS) s_qm[i] = qr_m[(size_t)c * d.HQ * HD + (size_t)h0 * HD + i];
+  for (int i = tid; i < grp * HD; i += AG_THREADS) s_qm[i] = qr_m[(size_t)c * d.HQ * HD + (size_t)h0 * HD + i];
   if (tid < grp * 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h0 * 4 + tid];
   if (pos < VCH) {
     if (tid < 8) ks[att_kswz(pos * 8 + tid)] = reinterpret_cast<const uint4*>(kv.km + (kbase + pos) * HD)[tid];
@@ -967,7 +972,7 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
   for (int h = 0; h < grp; ++h) {
     const int* qp = s_qm + h * HD + jt * 16;
     double lmax = -INFINITY;
-    for (int t0 = 0; t0 < T; t0 += ATT_THREADS / 4) {
+    for (int t0 = 0; t0 < T; t0 += AG_THREADS / 4) {
       const int t = t0 + (tid >> 2);
       long long S = 0;
       int E = 0;
@@ -1015,12 +1020,12 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
   __syncthreads();
   if (tid < grp) {
     double mx = s_red[0][tid];
-    for (int w = 1; w < ATT_THREADS / 32; ++w) mx = s_red[w][tid] > mx ? s_red[w][tid] : mx;
+    for (int w = 1; w < AG_THREADS / 32; ++w) mx = s_red[w][tid] > mx ? s_red[w][tid] : mx;
     s_mx[tid] = mx;
   }
   __syncthreads();
   // softmax_fp (:245-247) per head
-  for (int i = tid; i < grp * T; i += ATT_THREADS) {
+  for (int i = tid; i < grp * T; i += AG_THREADS) {
     const int h = i / T, t = i - h * T;
     sc[h * scs + t] = exp(__dsub_rn(sc[h * scs + t], s_mx[h]));
   }
@@ -1030,7 +1035,7 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
     if (lane == 0) s_sum[warp] = S;
   }
   __syncthreads();
-  for (int i = tid; i < grp * T; i += ATT_THREADS) {
+  for (int i = tid; i < grp * T; i += AG_THREADS) {
     const int h = i / T, t = i - h * T;
     sc[h * scs + t] = __ddiv_rn(sc[h * scs + t], s_sum[h]);
   }
@@ -1044,9 +1049,9 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
     if (c0 > 0) {
       __syncthreads();
       const uint4* vsrc = reinterpret_cast<const uint4*>(kv.vm + (kbase + c0) * HD);
-      for (int i = tid; i < n * 8; i += ATT_THREADS) vs[i] = vsrc[i];
+      for (int i = tid; i < n * 8; i += AG_THREADS) vs[i] = vsrc[i];
       const unsigned* esrc = reinterpret_cast<const unsigned*>(kv.ve + (kbase + c0) * 4);
-      for (int i = tid; i < n; i += ATT_THREADS) ves[i] = esrc[i];
+      for (int i = tid; i < n; i += AG_THREADS) ves[i] = esrc[i];
     }
     __syncthreads();
     if (acc_thread) {
@@ -1090,10 +1095,9 @@ cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return cudaErrorInvalidDevice;
   const int grp = d.HQ / d.HKV;
-  if (d.HD == 64 && grp * d.HKV == d.HQ && grp * 64 <= ATT_THREADS && (long long)ncols * d.HKV >= 2LL * nsm) {
-    const size_t gsm = (((size_t)grp * att_group_sc_stride(d.MAX_CTX) * 8 + 15) & ~size_t(15)) +
-                       (size_t)att_vchunk(true) * 264;
-    return launch_ex(attention_group_kernel, dim3(ncols, d.HKV), dim3(ATT_THREADS), gsm, s, pdl, qr_m, qr_e, kv,
+  if (d.HD == 64 && grp * d.HKV == d.HQ && grp * 64 <= AG_THREADS && (long long)ncols * d.HKV >= 2LL * nsm) {
+    const size_t gsm = (((size_t)grp * att_group_sc_stride(d.MAX_CTX) * 8 + 15) & ~size_t(15)) + (size_t)AG_VCH * 264;
+    return launch_ex(attention_group_kernel, dim3(ncols, d.HKV), dim3(AG_THREADS), gsm, s, pdl, qr_m, qr_e, kv,
                      layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
   }
   return launch_ex(attention_kernel<true>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
