@@ -85,14 +85,15 @@ def test_fwd_layer_stages_and_batch(layer_decoder):
 def test_fwd_layer_batched_group_attention():
     """A layer at 112 columns, where attention runs one CTA per (column, KV
     head) for the three query heads sharing it, with positions on both sides
-    of the 128-row staging chunk; a spread of columns against the oracle."""
+    of the batched kernel's 80-row K/V staging chunk (and of 128); every
+    column against the oracle."""
     from bfp200 import BfpConfig, Decoder
     model = oracle_model()
     cfg = O.Cfg()
     rng = np.random.default_rng(11)
     ncols, ctx = 112, 320
     pos = rng.integers(0, 300, ncols)
-    pos[:5] = [0, 1, 127, 128, 299]
+    pos[:9] = [0, 1, 79, 80, 81, 127, 128, 160, 299]
     H = np.stack([O.fp_quantize_vec(inputs.outlier_normal(rng, 576)) for _ in range(ncols)])
     kc = O.fp_quantize_vec(rng.standard_normal(ncols * ctx * 192)).reshape(ncols, ctx, 3, 64)
     vc = O.fp_quantize_vec(rng.standard_normal(ncols * ctx * 192)).reshape(ncols, ctx, 3, 64)
@@ -102,7 +103,7 @@ def test_fwd_layer_batched_group_attention():
     with Decoder(BfpConfig(MAX_CTX=ctx, max_seqs=ncols)) as dec:
         dec.load_image(full_image())
         out = dec.fwd_layer(5, H, pos, kc.copy(), vc.copy())
-    for c in [0, 1, 2, 3, 4, 57, 111]:
+    for c in range(ncols):
         kv = {"k": kc[c].copy(), "v": vc[c].copy()}
         want = O.fwd_layer(H[c], model.layers[5], int(pos[c]), kv, int(pos[c]), cfg)
         assert np.array_equal(out[c], want), c

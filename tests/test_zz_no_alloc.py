@@ -2,14 +2,16 @@
 device memory (their own allocator or memory pool owns every byte, or they
 cannot take cudaMalloc's implicit synchronisation).  It must return exactly
 what the allocating entry point bfp200_matvec returns, call after call, with
-its scratch kept in the library's fixed device array.  This file is
-collected last on purpose."""
+its scratch kept in the library's fixed device array, and what the oracle's
+restatement of matvec_hw_golden (gen_smollm_blockfp_full.py:217-233)
+returns.  This file is collected last on purpose."""
 import ctypes as C
 
 import numpy as np
 import pytest
 
 import inputs
+from oracle import bfp_oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -37,6 +39,9 @@ def test_noalloc_matches_allocating_entry_point():
             torch.cuda.synchronize()
             assert np.array_equal(om.cpu().numpy(), want_m), (D_out, D_in, B, call)
             assert np.array_equal(oe.cpu().numpy(), want_e), (D_out, D_in, B, call)
+        # every column against the oracle
+        got = O.tile_decode(om.cpu().numpy().reshape(-1), oe.cpu().numpy().reshape(-1)).reshape(B, D_out)
+        assert np.array_equal(got, O.matvec_cols(X_m, X_e, W_m, W_e)), (D_out, D_in, B)
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
