@@ -1,4 +1,4 @@
-// tc.cu -- batched BFP matvec (>= 64 columns) on the tcgen05 tensor cores.
+// tc.cu -- batched BFP matvec (>= 16 columns) on the tcgen05 tensor cores.
 //
 // matvec_hw_golden (gen_smollm_blockfp_full.py:214-233) needs, for every
 // output row r, column c and 16-element K tile t, the exact tile sum
@@ -31,8 +31,8 @@
 // Per (row, column, tile) the epilogue needs S >> sh with sh = (max exponent
 // of the row and column) - (tile exponent).  The max exponents come first
 // (two pairs per instruction on packed 16-bit lanes); then every tile costs
-// two wide multiply-adds when its shifts are at most 16, the general 64-bit
-// shift otherwise.
+// two wide multiply-adds when its shifts are at most 16, a 32-bit shift of
+// floor(S / 2^16) above.
 #include "bfp_device.cuh"
 #include "kernels.cuh"
 
@@ -618,32 +618,44 @@ tc_matmul_kernel(TcArgs a) {
           if ((R & 15) == 0) a.oe[(size_t)col * a.o_lde + R / 16] = (int8_t)qe[j];
         }
       }
-    } else {   // EPI_SWIGLU: lanes 0-15 hold a gate group, lanes 16-31 its up group
-      // every lane runs the warp-wide quantizers; only the gate lanes' results are kept
-      const bool is_g = (lane & 16) == 0;
-      double other[CPT];
+    } else {   // EPI_SWIGLU: lanes 0-15 hold a gate group, lanes 16-31 its up group (the same output rows)
+      // Columns go in pairs (j, j+1): the low half-warp computes silu of
+      // column j's gate values, the high half-warp that of column j+1's
+      // (fetched from the low lanes), so every lane's exp, divide and
+      // quantization is kept; each half then forms its column's products with
+      // the up values and quantizes them as its own 16-row tile.  The same
+      // operations on the same values as one column at a time.
+      const bool lo = (lane & 16) == 0;
+      constexpr int CP = CPT / 2;
+      double sv[CP], up[CP];
       #pragma unroll
-      for (int j = 0; j < CPT; ++j) {
-        const double mine = bfp_decode(qm[j], qe[j]);
-        other[j] = __shfl_xor_sync(0xffffffffu, mine, 16);
-        v[j] = __ddiv_rn(mine, __dadd_rn(1.0, exp(-mine)));                             // silu_fp (:241-242)
+      for (int k = 0; k < CP; ++k) {
+        const double a0 = bfp_decode(qm[2 * k], qe[2 * k]);            // low: g of column j, high: u of j
+        const double a1 = bfp_decode(qm[2 * k + 1], qe[2 * k + 1]);    // low: g of j+1,      high: u of j+1
+        const double x0 = __shfl_xor_sync(0xffffffffu, a0, 16);        // low: u of j,        high: g of j
+        const double x1 = __shfl_xor_sync(0xffffffffu, a1, 16);        // low: u of j+1,      high: g of j+1
+        const double g = lo ? a0 : x1;
+        up[k] = lo ? x0 : a1;
+        sv[k] = __ddiv_rn(g, __dadd_rn(1.0, exp(-g)));                  // silu_fp (:241-242)
       }
-      tile_quantize_16lanes_n<CPT>(v, qm, qe);
+      int16_t sm[CP];
+      int se[CP];
+      tile_quantize_16lanes_n<CP>(sv, sm, se);
       #pragma unroll
-      for (int j = 0; j < CPT; ++j) v[j] = is_g ? __dmul_rn(bfp_decode(qm[j], qe[j]), other[j]) : 0.0;   // (:290)
-      tile_quantize_16lanes_n<CPT>(v, qm, qe);
+      for (int k = 0; k < CP; ++k) sv[k] = __dmul_rn(bfp_decode(sm[k], se[k]), up[k]);   // (:290)
+      tile_quantize_16lanes_n<CP>(sv, sm, se);
       const int ug = R / 32;                                                             // mlp group of the pair
       #pragma unroll
-      for (int j = 0; j < CPT; ++j) {
-        const int col = c0 + cb + j;
+      for (int k = 0; k < CP; ++k) {
+        const int col = c0 + cb + 2 * k + (lo ? 0 : 1);
         const bool valid = row_ok && col < a.ncols;
-        int16_t pm = qm[j];
-        int pe = qe[j];
-        const unsigned bal = __ballot_sync(0xffffffffu, is_g && valid && pm == (int16_t)-32768);
+        int16_t pm = sm[k];
+        int pe = se[k];
+        const unsigned bal = __ballot_sync(0xffffffffu, valid && pm == (int16_t)-32768);
         const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
         pm = requant_mant(pm, has_min && pe < 127);                                     // (:291)
         pe = requant_exp(pe, has_min);
-        if (is_g && valid) {
+        if (valid) {
           a.om[(size_t)col * a.o_ld + ug * 16 + (lane & 15)] = pm;
           if ((lane & 15) == 0) a.oe[(size_t)col * a.o_lde + ug] = (int8_t)pe;
         }
