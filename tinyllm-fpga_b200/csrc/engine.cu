@@ -662,13 +662,22 @@ int enqueue_layer(bfp200_handle* h, int l, int ncols, StageSink* sink, bool firs
   CKR(enqueue_matmul(h, h->mat(h->wm_qkv, h->we_qkv, h->GQKV, h->NTD, l), h->n_m.p, h->n_e.p, h->D, h->NTD, ncols,
                      EPI_STORE, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->RQKV / 16, nullptr, nullptr, acc, cnt, accld));
   if (sink) CKR(download_decoded(h, h->qkv_m.p, h->qkv_e.p, h->RQKV, h->KVD, h->QD + h->KVD, ncols, sink->st[3]));
-  // rope on q, k; KV write                                (:268-272)
-  mark(h, PK_ROPE_KV);
-  CK(launch_rope_kv(h->qkv_m.p, h->qkv_e.p, h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), h->rope_cs.p, d, ncols, s, pdl));
+  // rope on q, k; KV write                                (:268-272): folded into
+  // the batched group attention kernel in decode steps, where every column is
+  // its own sequence (a prefill's columns are positions of one sequence: their
+  // attention reads K / V rows other columns write, so those rows are written
+  // by a kernel of their own first) and no stage dump asks for the rotated q
+  const bool rope_in_attention = early_kv && !sink && attention_group_path(d, ncols);
+  if (!rope_in_attention) {
+    mark(h, PK_ROPE_KV);
+    CK(launch_rope_kv(h->qkv_m.p, h->qkv_e.p, h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), h->rope_cs.p, d, ncols, s,
+                      pdl));
+  }
   // attention -> tile_quantize(fpq(attn))                 (:273-283)
   mark(h, PK_ATTENTION);
   CK(launch_attention(h->qr_m.p, h->qr_e.p, h->kv(), l, h->cols(), d, ncols, h->a_m.p, h->a_e.p, s, pdl,
-                      h->pw_off.p, h->pw_data.p, early_kv));
+                      h->pw_off.p, h->pw_data.p, early_kv, rope_in_attention ? h->qkv_m.p : nullptr,
+                      rope_in_attention ? h->qkv_e.p : nullptr, h->rope_cs.p));
   if (sink) {
     CKR(download_decoded(h, h->qr_m.p, h->qr_e.p, h->QD, h->QD, 0, ncols, sink->st[1]));
     CKR(download_decoded(h, h->a_m.p, h->a_e.p, h->QD, h->QD, 0, ncols, sink->st[4]));

@@ -899,7 +899,8 @@ __host__ __device__ inline size_t att_group_sc_stride(int max_ctx) { return ((si
 __global__ void __launch_bounds__(AG_THREADS, 6)
 attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
                        double sqrt_hd, double inv_hd, int16_t* am, int8_t* ae, const int* pw_off,
-                       const unsigned short* pw_data, int early) {
+                       const unsigned short* pw_data, int early, const int16_t* qkv_m, const int8_t* qkv_e,
+                       const double* rope_cs) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int HD = 64;
   constexpr int VCH = AG_VCH;
@@ -956,13 +957,62 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
     }
   }
   if (early) pdl_wait();
-  for (int i = tid; i < grp * HD; i += AG_THREADS) s_qm[i] = qr_m[(size_t)c * d.HQ * HD + (size_t)h0 * HD + i];
-  if (tid < grp * 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h0 * 4 + tid];
-  if (pos < VCH) {
-    if (tid < 8) ks[att_kswz(pos * 8 + tid)] = reinterpret_cast<const uint4*>(kv.km + (kbase + pos) * HD)[tid];
-    else if (tid < 16) vs[pos * 8 + tid - 8] = reinterpret_cast<const uint4*>(kv.vm + (kbase + pos) * HD)[tid - 8];
-    else if (tid == 16) kes[pos] = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + pos) * 4);
-    else if (tid == 17) ves[pos] = *reinterpret_cast<const unsigned*>(kv.ve + (kbase + pos) * 4);
+  if (qkv_m) {
+    // RoPE of this CTA's grp query heads and its K head (rope_fp, :250-258,
+    // :268-269) and the KV write of position pos (:270-272), from the fused
+    // q | k | v matvec output: the same operations as rope_kv_kernel.  The
+    // scores buffer (unused until the scores) holds the decoded rows.
+    const int R = (d.HQ + 2 * d.HKV) * HD, RT = R / 16, H2 = HD / 2;
+    double* xs = sc;
+    for (int pass = 0; pass < 2; ++pass) {            // 0: the query heads (tid = head * 64 + dim); 1: the K head
+      const bool act = pass == 0 ? tid < grp * HD : tid < HD;
+      const int hl = tid / HD, dd = tid % HD;
+      const int row = (pass == 0 ? h0 + hl : d.HQ + kvh) * HD + dd;
+      xs[tid] = act ? bfp_decode(qkv_m[(size_t)c * R + row], qkv_e[(size_t)c * RT + row / 16]) : 0.0;
+      __syncthreads();
+      double out = 0.0;
+      if (act) {
+        const int jj = dd < H2 ? dd : dd - H2;
+        const double cs = rope_cs[((size_t)pos * H2 + jj) * 2 + 0];
+        const double sn = rope_cs[((size_t)pos * H2 + jj) * 2 + 1];
+        const double av = xs[hl * HD + jj], bv = xs[hl * HD + jj + H2];
+        out = dd < H2 ? __dsub_rn(__dmul_rn(av, cs), __dmul_rn(bv, sn))     // a*c - b*s
+                      : __dadd_rn(__dmul_rn(bv, cs), __dmul_rn(av, sn));    // b*c + a*s
+      }
+      int e;
+      const int16_t m = tile_quantize_16lanes(out, &e);
+      if (act && pass == 0) {
+        s_qm[hl * HD + dd] = m;
+        if ((dd & 15) == 0) s_qe[hl * 4 + dd / 16] = e;
+      } else if (act) {
+        kv.km[(kbase + pos) * HD + dd] = m;
+        if ((dd & 15) == 0) kv.ke[(kbase + pos) * 4 + dd / 16] = (int8_t)e;
+        if (pos < VCH) {
+          reinterpret_cast<int16_t*>(ks + att_kswz(pos * 8 + dd / 8))[dd & 7] = m;
+          if ((dd & 15) == 0) reinterpret_cast<int8_t*>(kes + pos)[dd / 16] = (int8_t)e;
+        }
+      }
+      __syncthreads();
+    }
+    if (tid < HD) {                                   // v row as produced by the matvec (kv['v'][kv_pos] = v, :272)
+      const int row = (d.HQ + d.HKV + kvh) * HD + tid;
+      const int16_t vm = qkv_m[(size_t)c * R + row];
+      kv.vm[(kbase + pos) * HD + tid] = vm;
+      if ((tid & 15) == 0) kv.ve[(kbase + pos) * 4 + tid / 16] = qkv_e[(size_t)c * RT + row / 16];
+      if (pos < VCH) {
+        reinterpret_cast<int16_t*>(vs + pos * 8)[tid] = vm;
+        if ((tid & 15) == 0) reinterpret_cast<int8_t*>(ves + pos)[tid / 16] = qkv_e[(size_t)c * RT + row / 16];
+      }
+    }
+  } else {
+    for (int i = tid; i < grp * HD; i += AG_THREADS) s_qm[i] = qr_m[(size_t)c * d.HQ * HD + (size_t)h0 * HD + i];
+    if (tid < grp * 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h0 * 4 + tid];
+    if (pos < VCH) {
+      if (tid < 8) ks[att_kswz(pos * 8 + tid)] = reinterpret_cast<const uint4*>(kv.km + (kbase + pos) * HD)[tid];
+      else if (tid < 16) vs[pos * 8 + tid - 8] = reinterpret_cast<const uint4*>(kv.vm + (kbase + pos) * HD)[tid - 8];
+      else if (tid == 16) kes[pos] = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + pos) * 4);
+      else if (tid == 17) ves[pos] = *reinterpret_cast<const unsigned*>(kv.ve + (kbase + pos) * 4);
+    }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
@@ -1078,15 +1128,26 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
   }
 }
 
+bool attention_group_path(Dims d, int ncols) {
+  int dev = 0, nsm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return false;
+  const int grp = d.HQ / d.HKV;
+  return ncols > 4 && d.HD == 64 && grp * d.HKV == d.HQ && grp * 64 <= AG_THREADS &&
+         (long long)ncols * d.HKV >= 2LL * nsm;
+}
+
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
                              int ncols, int16_t* am, int8_t* ae, cudaStream_t s, bool pdl, const int* pw_off,
-                             const unsigned short* pw_data, bool early_kv) {
+                             const unsigned short* pw_data, bool early_kv, const int16_t* qkv_m, const int8_t* qkv_e,
+                             const double* rope_cs) {
   const bool lanes4 = ncols > 4;
   const size_t smem = (((size_t)d.MAX_CTX * 8 + 15) & ~size_t(15)) + (size_t)att_vchunk(lanes4) * 264;
   if (!pw_off || !pw_data) return cudaErrorInvalidValue;      // the pairwise-sum plans are required
   const double sq = std::sqrt((double)d.HD);
   int ex = 0;
   const double inv = std::frexp(sq, &ex) == 0.5 ? std::ldexp(1.0, 1 - ex) : 0.0;   // 1/sq, exact, or 0
+  if (qkv_m && !attention_group_path(d, ncols)) return cudaErrorInvalidValue;   // RoPE folds into the group kernel only
   if (!lanes4)
     return launch_ex(attention_kernel<false>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv,
                      layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
@@ -1098,7 +1159,8 @@ cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv
   if (d.HD == 64 && grp * d.HKV == d.HQ && grp * 64 <= AG_THREADS && (long long)ncols * d.HKV >= 2LL * nsm) {
     const size_t gsm = (((size_t)grp * att_group_sc_stride(d.MAX_CTX) * 8 + 15) & ~size_t(15)) + (size_t)AG_VCH * 264;
     return launch_ex(attention_group_kernel, dim3(ncols, d.HKV), dim3(AG_THREADS), gsm, s, pdl, qr_m, qr_e, kv,
-                     layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
+                     layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0, qkv_m, qkv_e,
+                     rope_cs);
   }
   return launch_ex(attention_kernel<true>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv, layer,
                    cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);

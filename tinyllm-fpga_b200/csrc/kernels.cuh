@@ -197,10 +197,16 @@ cudaError_t launch_rope_kv(const int16_t* qkv_m, const int8_t* qkv_e, int16_t* q
 // early_kv: every column's K/V rows below its position were written by
 // earlier launches (a decode step), so they are read before the dependency
 // wait.
+// qkv_m (non-null): the batched group kernel applies RoPE and writes the KV
+// row itself from the fused q | k | v output (no rope_kv launch); only where
+// attention_group_path() holds.
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
                              ColDesc cols, Dims d, int ncols, int16_t* am, int8_t* ae,
                              cudaStream_t s, bool pdl, const int* pw_off = nullptr,
-                             const unsigned short* pw_data = nullptr, bool early_kv = false);
+                             const unsigned short* pw_data = nullptr, bool early_kv = false,
+                             const int16_t* qkv_m = nullptr, const int8_t* qkv_e = nullptr,
+                             const double* rope_cs = nullptr);
+bool attention_group_path(Dims d, int ncols);
 cudaError_t launch_embed(const int16_t* emb_m, const int8_t* emb_e, const int* tokens, int D,
                          int ncols, int16_t* hm, int8_t* he, cudaStream_t s, bool pdl);
 cudaError_t launch_head_prep(const int16_t* hm, const int8_t* he, const double* norm_w, double eps,
