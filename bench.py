@@ -11,7 +11,9 @@ is one full generate call (prefill + 256 decode steps).  ``value`` =
 generated tokens/s over all ranks (each rank decodes its own replica: bs1
 does not shard, so N GPUs run N independent streams -- weak scaling).
 The same line carries ``bs256``: configs[2] = "cfg3", 256 ragged sequences
-x 128 tokens, sequences split over the ranks with no collectives.
+x 128 tokens, sequences split over the ranks with no collectives (strong
+scaling), and at N > 1 ``bs256_weak``: every rank serves the whole cfg3
+batch (256 sequences per GPU, 256 N in all -- weak scaling).
 
 Further keys of the final line: ``roofline`` (the bs1 decode's dominant
 kernel, the per-layer attention block, against the measured HBM copy
@@ -290,6 +292,21 @@ def run_ours(args, world, rank, local):
         if part3:
             bs256["roofline"] = batched_roofline(dec, len(part3), max(1, args.mm_reps // 5), pk, pk_kind)
 
+    # ---- bs256, weak scaling: every rank serves all 256 cfg3 sequences
+    bs256_weak = None
+    if world > 1 and not args.no_bs256:
+        dec.generate(prompts3, ngen3)                   # warm-up (graphs at 256 columns)
+        barrier(world)
+        w_ms = []
+        for _ in range(max(1, args.steps // 4)):
+            dec.generate(prompts3, ngen3)
+            t = dec.last_timing()
+            w_ms.append(t["prefill_ms"] + t["decode_ms"])
+        barrier(world)
+        w_step = max_over_ranks(statistics.mean(w_ms), world)
+        bs256_weak = {"value": round(world * len(prompts3) * ngen3 / (w_step / 1e3), 1), "unit": "tok/s",
+                      "ms_per_step": round(w_step, 3), "sequences_per_gpu": len(prompts3), "scaling": "weak"}
+
     profile = {"bs1_pos176": prof1}
     if not args.no_bs256 and part3:
         profile["bs256_pos100"] = dec.profile_forward(len(part3), 100)
@@ -323,6 +340,7 @@ def run_ours(args, world, rank, local):
                 "d2h_bytes_per_step": (48 + ngen2) * 4 + 8},
         "gpu_launches": int(sum_over_ranks(launches, world)),
         "bs256": bs256,
+        "bs256_weak": bs256_weak,
         "sharded_head": sharded,
         "uncertified_steps": uncert,
         "image_build_s": round(build_s, 1),
