@@ -429,24 +429,34 @@ def sharded_head_run(dec, prompts, n_gen, args, world, replica_tok_ms):
 # (dram__bytes_read.sum + dram__bytes_write.sum, writes 0); algorithmic bytes
 # at that position: 1,971,936 (the excess is about the kernel's code).
 ATTN_BLOCK_TRAFFIC_POS176 = 2_067_797
+# DRAM bytes of one layer's four batched matvecs at 256 columns (Q/K/V, O,
+# gate/up, down; reads only, the outputs stay in L2) from one ncu capture,
+# times 30 layers
+TC_STEP_TRAFFIC_256 = 30 * (1_780_480 + 1_568_768 + 4_615_424 + 3_517_440)
 
 LAYER_MACS = 106_168_320      # int16 MACs of one token's 4 x 30 layer matvecs (head excluded)
 
 
 def batched_roofline(dec, ncols, reps, pk, pk_kind):
     """The batched matvecs of one decode step at this rank's column count:
-    tcgen05 kind::i8 (>= 64 columns) or the dp2a kernel.  Algorithmic work =
+    tcgen05 kind::i8 (>= 16 columns) or the dp2a kernel.  Algorithmic work =
     the int16 MACs, counted as 4 int8 limb MACs each (2 ops per MAC), against
     the int8 dense peak taken as twice the measured bf16 GEMM rate (the
-    nominal int8 : bf16 ratio of B200)."""
+    nominal int8 : bf16 ratio of B200).  ``traffic``: DRAM bytes of the
+    step's 120 launches from one ncu capture at 256 columns (cold cache:
+    weight records + input columns), reported at that column count only."""
     ms, n = dec.time_matmuls(ncols, reps)
     tops = LAYER_MACS * ncols * 4 * 2 / (ms / 1e3) / 1e12
     peak = 2 * pk["bf16_tflops"]
-    return {"kernel": "tc_matmul_kernel (tcgen05 kind::i8 limbs)" if ncols >= 16 else "bfp_matmul_kernel (dp2a)",
-            "bound": "tensor", "achieved": round(tops, 2), "peak": round(peak, 1), "unit": "TOPS (int8)",
-            "frac": round(tops / peak, 5), "traffic": None, "peak_kind": f"2 x bf16 ({pk_kind})",
-            "ncols": ncols, "ms_per_step": round(ms, 4), "launches_per_step": n,
-            "int16_macs_per_s": round(LAYER_MACS * ncols / (ms / 1e3) / 1e12, 3)}
+    out = {"kernel": "tc_matmul_kernel (tcgen05 kind::i8 limbs)" if ncols >= 16 else "bfp_matmul_kernel (dp2a)",
+           "bound": "tensor", "achieved": round(tops, 2), "peak": round(peak, 1), "unit": "TOPS (int8)",
+           "frac": round(tops / peak, 5), "traffic": None, "peak_kind": f"2 x bf16 ({pk_kind})",
+           "ncols": ncols, "ms_per_step": round(ms, 4), "launches_per_step": n,
+           "int16_macs_per_s": round(LAYER_MACS * ncols / (ms / 1e3) / 1e12, 3)}
+    if ncols == 256 and n == 120:
+        out["traffic"] = TC_STEP_TRAFFIC_256
+        out["traffic_unit"] = "bytes per step, 120 launches (ncu dram__bytes_read.sum + dram__bytes_write.sum, 256 columns)"
+    return out
 
 
 # ---------------------------------------------------------------------------
