@@ -86,9 +86,10 @@ def test_release_rom_fixture_format():
     """The reference's release ROM files (real SmolLM2 gammas): every tile is
     normalised (max |m| in [16384, 32767]) and the prompt is the 8-token
     'Once upon a time' encoding."""
-    rel = os.path.join(os.environ.get("REF_ROOT", os.path.join(os.sep, "nonexistent")), "rtl/vc707/release")
+    ref = os.environ.get("BFP200_REFERENCE", os.path.join(os.path.dirname(REPO), "reference"))
+    rel = os.path.join(ref, "rtl", "vc707", "release")
     if not os.path.isdir(rel):
-        pytest.skip("reference checkout not present (set REF_ROOT)")
+        pytest.skip("reference checkout not present (set BFP200_REFERENCE)")
     roms = image.read_roms(rel, "lbfp_full_")
     assert roms[6].tolist() == [34, 50, 14669, 5728, 34, 50, 1758, 9148]
     m = roms[0].astype(np.int16).astype(np.int64).reshape(-1, 16)
