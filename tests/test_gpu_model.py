@@ -109,6 +109,34 @@ def test_fwd_layer_batched_group_attention():
         assert np.array_equal(out[c], want), c
 
 
+def test_fwd_layer_long_arena_attention():
+    """A layer at 20 columns in a 2048-position arena, where attention
+    streams each (column, KV head)'s K / V rows through a ring of 64-row
+    chunks: positions on both sides of the chunk boundaries and up to the
+    last position; every column against the oracle."""
+    from bfp200 import BfpConfig, Decoder
+    model = oracle_model()
+    cfg = O.Cfg()
+    rng = np.random.default_rng(12)
+    ncols, ctx = 20, 2048
+    pos = np.array([0, 1, 62, 63, 64, 65, 127, 128, 319, 320, 383, 384, 385, 1000, 1023, 1024, 1535, 2046, 2047, 700])
+    H = np.stack([O.fp_quantize_vec(inputs.outlier_normal(rng, 576)) for _ in range(ncols)])
+    kc = np.zeros((ncols, ctx, 3, 64))
+    vc = np.zeros((ncols, ctx, 3, 64))
+    for c in range(ncols):
+        p = int(pos[c])
+        if p:
+            kc[c, :p] = O.fp_quantize_vec(rng.standard_normal(p * 192)).reshape(p, 3, 64)
+            vc[c, :p] = O.fp_quantize_vec(rng.standard_normal(p * 192)).reshape(p, 3, 64)
+    with Decoder(BfpConfig(MAX_CTX=ctx, max_seqs=ncols)) as dec:
+        dec.load_image(full_image())
+        out = dec.fwd_layer(9, H, pos, kc.copy(), vc.copy())
+    for c in range(ncols):
+        kv = {"k": kc[c].copy(), "v": vc[c].copy()}
+        want = O.fwd_layer(H[c], model.layers[9], int(pos[c]), kv, int(pos[c]), cfg)
+        assert np.array_equal(out[c], want), (c, int(pos[c]))
+
+
 @pytest.fixture(scope="module")
 def decoder():
     from bfp200 import BfpConfig, Decoder

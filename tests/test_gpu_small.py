@@ -47,6 +47,21 @@ def test_small_model_full_context():
     dec.close()
 
 
+def test_small_model_long_arena_decode():
+    """A KV arena of 1024 positions and more than four sequences: batched
+    attention streams K / V in 64-row chunks; 90 decode steps from prompts
+    of 30-48 tokens cross the chunk boundaries 64 and 128 (the chunks below
+    the last one stream before the dependency wait).  3 query heads per KV
+    head, as in the full model."""
+    dec, model, ocfg = _pair(4, 1024, 6, H_Q=3, D=192, FFN=384)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, 512, size=n).tolist() for n in (30, 40, 47, 48, 45, 33)]
+    got = dec.generate(prompts, 90)
+    for p, g in zip(prompts, got):
+        assert g == O.generate(model, p, 90, max_ctx=1024, cfg=ocfg)
+    dec.close()
+
+
 def test_error_paths():
     from bfp200 import BfpConfig, BfpError, Decoder, _lib, synth
     cfg = BfpConfig(MAX_CTX=16, max_seqs=2, **SMALL)

@@ -1128,13 +1128,257 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
   }
 }
 
+// Batched GQA attention for long KV arenas (>= AL_MIN_CTX positions): one CTA
+// per (column, KV head) as in attention_group_kernel, so the grp query heads
+// sharing a KV head read its rows once, with the K and V rows streamed
+// through a ring of AL_STAGES shared-memory chunks of AL_P rows by cp.async
+// copies issued AL_STAGES - 1 chunks ahead of their use: first the K chunks
+// (scores), then the V chunks (the sequential accumulation), so the first V
+// rows are in flight during the last scores and the softmax.
+//   scores: thread (head, j) forms the score of row j of every K chunk for
+//     its head: four exact 16-element tile sums by dp2a (q in registers as
+//     16-bit pairs, the K row split into its high and low byte planes), one
+//     rounding (exact_tile_dot4);
+//   accumulation: thread j < 64 carries dimension j of every query head of
+//     the group (grp independent chains, each V element decoded once).
+// The same values and the same operations in the same order as
+// attention_group_kernel (:273-283).
+constexpr int AL_THREADS = 192;
+constexpr int AL_P = 64;                                  // rows per chunk
+constexpr int AL_STAGES = 6;
+constexpr int AL_STAGE_BYTES = AL_P * 128 + AL_P * 4;     // the rows, then their tile-exponent words
+constexpr int AL_MIN_CTX = 1024;
+__host__ __device__ inline size_t att_long_smem(int grp, int max_ctx) {
+  return (((size_t)grp * att_group_sc_stride(max_ctx) * 8 + 15) & ~size_t(15)) + (size_t)AL_STAGES * AL_STAGE_BYTES;
+}
+
+__device__ __forceinline__ int al_dp2a_lo_ss(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int al_dp2a_hi_ss(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int al_dp2a_lo_su(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int al_dp2a_hi_su(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+// exact sum_k x[k] y[k] over one 16-element tile: x as eight 16-bit pairs
+// (x0: elements 0..7, x1: 8..15), y as two uint4 of int16 split into signed
+// high bytes and unsigned low bytes (y = 256 hi + lo); each 32-bit partial
+// holds at most 16 products of 2^15 x 2^8
+__device__ __forceinline__ long long al_tile_sum(const uint4 x0, const uint4 x1, const uint4 k0, const uint4 k1) {
+  const unsigned h0 = __byte_perm(k0.x, k0.y, 0x7531), h1 = __byte_perm(k0.z, k0.w, 0x7531);
+  const unsigned h2 = __byte_perm(k1.x, k1.y, 0x7531), h3 = __byte_perm(k1.z, k1.w, 0x7531);
+  const unsigned l0 = __byte_perm(k0.x, k0.y, 0x6420), l1 = __byte_perm(k0.z, k0.w, 0x6420);
+  const unsigned l2 = __byte_perm(k1.x, k1.y, 0x6420), l3 = __byte_perm(k1.z, k1.w, 0x6420);
+  int A = 0, B = 0;
+  A = al_dp2a_lo_ss(x0.x, h0, A); A = al_dp2a_hi_ss(x0.y, h0, A);
+  A = al_dp2a_lo_ss(x0.z, h1, A); A = al_dp2a_hi_ss(x0.w, h1, A);
+  A = al_dp2a_lo_ss(x1.x, h2, A); A = al_dp2a_hi_ss(x1.y, h2, A);
+  A = al_dp2a_lo_ss(x1.z, h3, A); A = al_dp2a_hi_ss(x1.w, h3, A);
+  B = al_dp2a_lo_su(x0.x, l0, B); B = al_dp2a_hi_su(x0.y, l0, B);
+  B = al_dp2a_lo_su(x0.z, l1, B); B = al_dp2a_hi_su(x0.w, l1, B);
+  B = al_dp2a_lo_su(x1.x, l2, B); B = al_dp2a_hi_su(x1.y, l2, B);
+  B = al_dp2a_lo_su(x1.z, l3, B); B = al_dp2a_hi_su(x1.w, l3, B);
+  return ((long long)A << 8) + (long long)B;
+}
+
+__global__ void __launch_bounds__(AL_THREADS, 2)
+attention_long_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
+                      double sqrt_hd, double inv_hd, int16_t* am, int8_t* ae, const int* pw_off,
+                      const unsigned short* pw_data, int early) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int HD = 64;
+  __shared__ __align__(16) int16_t s_q[AG_MAXG * HD];
+  __shared__ int s_qe[AG_MAXG * 4];
+  __shared__ double s_red[AL_THREADS / 32];
+  __shared__ double s_mx[AG_MAXG], s_sum[AG_MAXG];
+  __shared__ double s_val[AG_MAXG][160];
+  __shared__ unsigned short s_plan[ATT_PLAN_MAX];
+  pdl_trigger();
+  const int c = blockIdx.x, kvh = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = d.HQ / d.HKV, h0 = kvh * grp;
+  const int hh = tid / HD, j = tid % HD;                 // scores: this thread's head and row
+  const bool act = hh < grp;                             // whole warps
+  const size_t scs = att_group_sc_stride(d.MAX_CTX);
+  double* sc = reinterpret_cast<double*>(smem);                                       // [grp][scs]
+  unsigned char* ring = smem + (((size_t)grp * scs * 8 + 15) & ~size_t(15));          // [AL_STAGES][AL_STAGE_BYTES]
+  if (!early) pdl_wait();
+  const int slot = cols.slot[c], pos = cols.pos[c];
+  const int T = pos + 1;
+  const int nk = (T + AL_P - 1) / AL_P, njobs = 2 * nk;
+  const size_t kbase = (((size_t)slot * d.NL + layer) * d.HKV + kvh) * d.MAX_CTX;
+  // job q: K chunk q (q < nk) or V chunk q - nk, into stage q % AL_STAGES; K
+  // rows land swizzled (conflict-free row reads), V rows as they are.  The
+  // exponent words are copied in whole 16-byte units (rows up to the next
+  // multiple of 4, inside the arena: MAX_CTX % 4 == 0).  Every thread commits
+  // one group per job, empty past the last.
+  auto issue = [&](int q) {
+    if (q < njobs) {
+      const bool isk = q < nk;
+      const int r0 = (isk ? q : q - nk) * AL_P, n = min(AL_P, T - r0);
+      unsigned char* st = ring + (size_t)(q % AL_STAGES) * AL_STAGE_BYTES;
+      const uint4* src = reinterpret_cast<const uint4*>((isk ? kv.km : kv.vm) + (kbase + r0) * HD);
+      const uint4* esrc = reinterpret_cast<const uint4*>((isk ? kv.ke : kv.ve) + (kbase + r0) * 4);
+      const int nu = n * 8, ne = (n + 3) / 4;
+      for (int i = tid; i < nu + ne; i += AL_THREADS) {
+        const bool row = i < nu;
+        unsigned char* dst = row ? st + (size_t)(isk ? att_kswz(i) : i) * 16 : st + AL_P * 128 + (size_t)(i - nu) * 16;
+        const uint4* s = row ? src + i : esrc + (i - nu);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"((unsigned)__cvta_generic_to_shared(dst)),
+                     "l"(s) : "memory");
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  // numpy's pairwise-sum plan for this length (host-built, constant)
+  const unsigned short* plan;
+  {
+    const unsigned short* gp = pw_data + pw_off[T];
+    const int np = 3 * (int)gp[0] + (int)gp[1];
+    if (np <= ATT_PLAN_MAX) {
+      for (int i = tid; i < np; i += AL_THREADS) s_plan[i] = gp[i];
+      plan = s_plan;
+    } else {
+      plan = gp;
+    }
+  }
+  int q0 = 0;
+  if (early) {
+    // a decode step: rows below pos come from earlier launches, so the K
+    // chunks before the last one stream before the dependency wait; the
+    // chunks holding row pos (written by the previous kernel) after it
+    for (; q0 < min(AL_STAGES - 1, nk - 1); ++q0) issue(q0);
+    pdl_wait();
+  }
+  for (; q0 < AL_STAGES - 1; ++q0) issue(q0);
+  for (int i = tid; i < grp * HD; i += AL_THREADS) s_q[i] = qr_m[(size_t)c * d.HQ * HD + (size_t)h0 * HD + i];
+  if (tid < grp * 4) s_qe[tid] = qr_e[(size_t)c * d.HQ * 4 + h0 * 4 + tid];
+  __syncthreads();
+  uint4 qv[8];                                           // q of this thread's head, 16-bit pairs
+  #pragma unroll
+  for (int u = 0; u < 8; ++u) qv[u] = reinterpret_cast<const uint4*>(s_q + (act ? hh : 0) * HD)[u];
+  int qe[4];
+  #pragma unroll
+  for (int jt = 0; jt < 4; ++jt) qe[jt] = s_qe[(act ? hh : 0) * 4 + jt];
+
+  const bool pow2_hd = inv_hd != 0.0;
+  double lmax = -INFINITY;
+  double acc[AG_MAXG] = {0.0, 0.0, 0.0};
+  for (int jb = 0; jb < njobs; ++jb) {
+    asm volatile("cp.async.wait_group %0;" :: "n"(AL_STAGES - 2) : "memory");
+    __syncthreads();                                     // chunk jb visible; chunk jb - 1's stage free
+    issue(jb + AL_STAGES - 1);
+    const unsigned char* st = ring + (size_t)(jb % AL_STAGES) * AL_STAGE_BYTES;
+    const unsigned* ex = reinterpret_cast<const unsigned*>(st + AL_P * 128);
+    if (jb < nk) {
+      // scores[t] = float(np.dot(q, k_t)) / math.sqrt(HD) (:278)
+      const int r0 = jb * AL_P;
+      if (act && j < T - r0) {
+        const uint4* ks = reinterpret_cast<const uint4*>(st);
+        uint4 kk[8];
+        #pragma unroll
+        for (int u = 0; u < 8; ++u) kk[u] = ks[j * 8 + (u ^ (j & 7))];
+        const unsigned ke4 = ex[j];
+        long long S[4];
+        int E[4];
+        #pragma unroll
+        for (int jt = 0; jt < 4; ++jt) {
+          S[jt] = al_tile_sum(qv[2 * jt], qv[2 * jt + 1], kk[2 * jt], kk[2 * jt + 1]);
+          E[jt] = qe[jt] + (int)(int8_t)(ke4 >> (8 * jt));
+        }
+        const double dot = exact_tile_dot4(S, E);
+        const double v = pow2_hd ? __dmul_rn(dot, inv_hd) : __ddiv_rn(dot, sqrt_hd);
+        sc[(size_t)hh * scs + r0 + j] = v;
+        lmax = v > lmax ? v : lmax;
+      }
+    } else {
+      if (jb == nk) {
+        // softmax_fp (:245-247) per head: warps 2h and 2h + 1 hold head h
+        for (int off = 16; off; off >>= 1) {
+          const double o = __shfl_xor_sync(0xffffffffu, lmax, off);
+          lmax = o > lmax ? o : lmax;
+        }
+        if (lane == 0) s_red[warp] = lmax;
+        __syncthreads();
+        if (tid < grp) s_mx[tid] = s_red[2 * tid + 1] > s_red[2 * tid] ? s_red[2 * tid + 1] : s_red[2 * tid];
+        __syncthreads();
+        for (int i = tid; i < grp * T; i += AL_THREADS) {
+          const int h = i / T, t = i - h * T;
+          sc[h * scs + t] = exp(__dsub_rn(sc[h * scs + t], s_mx[h]));
+        }
+        __syncthreads();
+        if (warp < grp) {
+          const double S = np_sum_warp_plan(sc + warp * scs, T, plan, s_val[warp]);
+          if (lane == 0) s_sum[warp] = S;
+        }
+        __syncthreads();
+        for (int i = tid; i < grp * T; i += AL_THREADS) {
+          const int h = i / T, t = i - h * T;
+          sc[h * scs + t] = __ddiv_rn(sc[h * scs + t], s_sum[h]);
+        }
+        __syncthreads();
+      }
+      // attn[h] += sm[t] * v[t], sequential in t (:280-281): thread j < 64
+      // holds dimension j of every head of the group
+      const int r0 = (jb - nk) * AL_P, n = min(AL_P, T - r0);
+      if (tid < HD) {
+        const int16_t* vrow = reinterpret_cast<const int16_t*>(st) + tid;
+        const int sh = 8 * (tid >> 4);
+        const double* sm0 = sc + r0;
+        #pragma unroll 4
+        for (int t = 0; t < n; ++t) {
+          const int e = (int)(int8_t)(ex[t] >> sh);
+          const double vv = bfp_decode(vrow[(size_t)t * HD], e);
+          #pragma unroll
+          for (int h = 0; h < AG_MAXG; ++h)
+            if (h < grp) acc[h] = __dadd_rn(acc[h], __dmul_rn(sm0[(size_t)h * scs + t], vv));
+        }
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");       // (only empty groups remain)
+  if (tid < HD) {                                        // warps 0 and 1: the quantizer's 16-lane tiles
+    #pragma unroll
+    for (int h = 0; h < AG_MAXG; ++h) {
+      if (h >= grp) break;
+      int e;
+      int16_t m = tile_quantize_16lanes(acc[h], &e);          // fpq(attn)   (:282)
+      const unsigned bal = __ballot_sync(0xffffffffu, m == (int16_t)-32768);
+      const bool has_min = ((bal >> (lane & 16)) & 0xFFFFu) != 0;
+      m = requant_mant(m, has_min && e < 127);               // tile_quantize(attn) (:283)
+      e = requant_exp(e, has_min);
+      const size_t hq = (size_t)c * d.HQ + h0 + h;
+      am[hq * HD + tid] = m;
+      if ((tid & 15) == 0) ae[hq * 4 + tid / 16] = (int8_t)e;
+    }
+  }
+}
+
+// The long-arena kernel: batched columns, 64-dim heads, every query head of a
+// group in one CTA, an arena of at least AL_MIN_CTX positions whose exponent
+// rows start on 16-byte boundaries (MAX_CTX % 4 == 0), and shared memory for
+// the group's scores plus the ring.
+bool attention_long_path(Dims d, int ncols) {
+  int dev = 0, optin = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return false;
+  const int grp = d.HKV > 0 ? d.HQ / d.HKV : 0;
+  return ncols > 4 && d.HD == 64 && grp > 0 && grp * d.HKV == d.HQ && grp * 64 <= AL_THREADS &&
+         d.MAX_CTX >= AL_MIN_CTX && d.MAX_CTX % 4 == 0 && att_long_smem(grp, d.MAX_CTX) + 8192 <= (size_t)optin;
+}
+
 bool attention_group_path(Dims d, int ncols) {
   int dev = 0, nsm = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return false;
   const int grp = d.HQ / d.HKV;
   return ncols > 4 && d.HD == 64 && grp * d.HKV == d.HQ && grp * 64 <= AG_THREADS &&
-         (long long)ncols * d.HKV >= 2LL * nsm;
+         (long long)ncols * d.HKV >= 2LL * nsm && !attention_long_path(d, ncols);
 }
 
 cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer, ColDesc cols, Dims d,
@@ -1148,6 +1392,11 @@ cudaError_t launch_attention(const int16_t* qr_m, const int8_t* qr_e, KvArena kv
   int ex = 0;
   const double inv = std::frexp(sq, &ex) == 0.5 ? std::ldexp(1.0, 1 - ex) : 0.0;   // 1/sq, exact, or 0
   if (qkv_m && !attention_group_path(d, ncols)) return cudaErrorInvalidValue;   // RoPE folds into the group kernel only
+  if (lanes4 && attention_long_path(d, ncols) && !(((uintptr_t)kv.ke | (uintptr_t)kv.ve | (uintptr_t)kv.km | (uintptr_t)kv.vm) & 15)) {
+    const int grp = d.HQ / d.HKV;
+    return launch_ex(attention_long_kernel, dim3(ncols, d.HKV), dim3(AL_THREADS), att_long_smem(grp, d.MAX_CTX), s, pdl,
+                     qr_m, qr_e, kv, layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
+  }
   if (!lanes4)
     return launch_ex(attention_kernel<false>, dim3(ncols, d.HQ), dim3(ATT_THREADS), smem, s, pdl, qr_m, qr_e, kv,
                      layer, cols, d, sq, inv, am, ae, pw_off, pw_data, (pdl && early_kv) ? 1 : 0);
@@ -2128,6 +2377,7 @@ cudaError_t init_kernel_attributes() {
   set((const void*)attention_kernel<false>);
   set((const void*)attention_kernel<true>);
   set((const void*)attention_group_kernel);
+  set((const void*)attention_long_kernel);
   set((const void*)rmsnorm_fp_kernel);
   set((const void*)softmax_fp_kernel);
   set((const void*)np_sum_kernel);
