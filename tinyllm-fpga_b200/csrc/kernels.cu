@@ -1329,7 +1329,7 @@ attention_long_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int l
         const int16_t* vrow = reinterpret_cast<const int16_t*>(st) + tid;
         const int sh = 8 * (tid >> 4);
         const double* sm0 = sc + r0;
-        #pragma unroll 4
+        #pragma unroll 16     // loads and decodes of 16 rows ahead of their adds
         for (int t = 0; t < n; ++t) {
           const int e = (int)(int8_t)(ex[t] >> sh);
           const double vv = bfp_decode(vrow[(size_t)t * HD], e);

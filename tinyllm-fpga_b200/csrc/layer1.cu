@@ -262,17 +262,19 @@ __device__ __noinline__ double l1_attn_accumulate(const int16_t* vs, const unsig
   const int16_t* vrow = vs + d;
   double acc = 0.0;
   int t = 0;
-  for (; t + 4 <= nv; t += 4) {
-    int m4[4], e4[4];
-    double s4[4];
+  // 16 rows' loads and decodes issued ahead of their 16 dependent adds
+  // (groups of 4: +23 us per token)
+  for (; t + 16 <= nv; t += 16) {
+    int m16[16], e16[16];
+    double s16[16];
     #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      m4[u] = vrow[(t + u) * A_HD];
-      e4[u] = (int)(int8_t)(ves[t + u] >> sh);
-      s4[u] = sc[t + u];
+    for (int u = 0; u < 16; ++u) {
+      m16[u] = vrow[(t + u) * A_HD];
+      e16[u] = (int)(int8_t)(ves[t + u] >> sh);
+      s16[u] = sc[t + u];
     }
     #pragma unroll
-    for (int u = 0; u < 4; ++u) acc = __dadd_rn(acc, __dmul_rn(s4[u], a_decode(m4[u], e4[u])));
+    for (int u = 0; u < 16; ++u) acc = __dadd_rn(acc, __dmul_rn(s16[u], a_decode(m16[u], e16[u])));
   }
   for (; t < nv; ++t) acc = __dadd_rn(acc, __dmul_rn(sc[t], a_decode(vrow[t * A_HD], (int)(int8_t)(ves[t] >> sh))));
   return acc;
@@ -578,7 +580,7 @@ bfp_attn_block_kernel(L1Args a) {
     // attn[h] += sm[t] * v[t], sequential in t (:280-281)
     if (tid >= A_VW && tid < A_VW + A_HD) {
       const int d = tid - A_VW;                         // this thread's dimension
-      const int nv = dry ? min(nin, 8) : nin;
+      const int nv = dry ? min(nin, 16) : nin;            // (dry: one whole group of the loop)
       const int Tv = dry ? nv : Tp;
       if (!dry) { BFP_STAMP_T(A_VW, 3, a.layer, r, 0); BFP_STAMP_T(A_VW + 32, 3, a.layer, r, 4); }
       double acc = l1_attn_accumulate(reinterpret_cast<const int16_t*>(vs), ves, sc, nv, d);
