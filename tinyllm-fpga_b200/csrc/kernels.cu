@@ -881,6 +881,39 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   }
 }
 
+__device__ __forceinline__ int al_dp2a_lo_ss(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int al_dp2a_hi_ss(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int al_dp2a_lo_su(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int al_dp2a_hi_su(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+// exact sum_k x[k] y[k] over one 16-element tile: x as eight 16-bit pairs
+// (x0: elements 0..7, x1: 8..15), y as two uint4 of int16 split into signed
+// high bytes and unsigned low bytes (y = 256 hi + lo); each 32-bit partial
+// holds at most 16 products of 2^15 x 2^8
+__device__ __forceinline__ long long al_tile_sum(const uint4 x0, const uint4 x1, const uint4 k0, const uint4 k1) {
+  const unsigned h0 = __byte_perm(k0.x, k0.y, 0x7531), h1 = __byte_perm(k0.z, k0.w, 0x7531);
+  const unsigned h2 = __byte_perm(k1.x, k1.y, 0x7531), h3 = __byte_perm(k1.z, k1.w, 0x7531);
+  const unsigned l0 = __byte_perm(k0.x, k0.y, 0x6420), l1 = __byte_perm(k0.z, k0.w, 0x6420);
+  const unsigned l2 = __byte_perm(k1.x, k1.y, 0x6420), l3 = __byte_perm(k1.z, k1.w, 0x6420);
+  int A = 0, B = 0;
+  A = al_dp2a_lo_ss(x0.x, h0, A); A = al_dp2a_hi_ss(x0.y, h0, A);
+  A = al_dp2a_lo_ss(x0.z, h1, A); A = al_dp2a_hi_ss(x0.w, h1, A);
+  A = al_dp2a_lo_ss(x1.x, h2, A); A = al_dp2a_hi_ss(x1.y, h2, A);
+  A = al_dp2a_lo_ss(x1.z, h3, A); A = al_dp2a_hi_ss(x1.w, h3, A);
+  B = al_dp2a_lo_su(x0.x, l0, B); B = al_dp2a_hi_su(x0.y, l0, B);
+  B = al_dp2a_lo_su(x0.z, l1, B); B = al_dp2a_hi_su(x0.w, l1, B);
+  B = al_dp2a_lo_su(x1.x, l2, B); B = al_dp2a_hi_su(x1.y, l2, B);
+  B = al_dp2a_lo_su(x1.z, l3, B); B = al_dp2a_hi_su(x1.w, l3, B);
+  return ((long long)A << 8) + (long long)B;
+}
+
 // Batched GQA attention with one CTA per (column, KV head): the grp query
 // heads that share a KV head use one staged copy of its K / V rows, and their
 // grp x 64 sequential accumulations run side by side (a thread per head and
@@ -904,7 +937,7 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int HD = 64;
   constexpr int VCH = AG_VCH;
-  __shared__ int s_qm[AG_MAXG * HD];
+  __shared__ __align__(16) int16_t s_qm[AG_MAXG * HD];
   __shared__ int s_qe[AG_MAXG * 4];
   __shared__ double s_red[AG_THREADS / 32][AG_MAXG];
   __shared__ double s_mx[AG_MAXG], s_sum[AG_MAXG];
@@ -1016,37 +1049,34 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
-  // scores (:278), four lanes per (head, position), one 16-element tile each
+  // scores (:278), four lanes per position, one 16-element tile each: every
+  // K row is fetched once for the grp query heads (exact tile sums by dp2a,
+  // q read as 16-bit pairs)
   const bool pow2_hd = inv_hd != 0.0;
   const int jt = tid & 3, qb = lane & ~3;
-  for (int h = 0; h < grp; ++h) {
-    const int* qp = s_qm + h * HD + jt * 16;
-    double lmax = -INFINITY;
-    for (int t0 = 0; t0 < T; t0 += AG_THREADS / 4) {
-      const int t = t0 + (tid >> 2);
-      long long S = 0;
-      int E = 0;
-      if (t < T) {
-        uint4 k0, k1;
-        unsigned ke4;
-        if (t < n0) {
-          k0 = ks[t * 8 + ((2 * jt) ^ (t & 7))];
-          k1 = ks[t * 8 + ((2 * jt + 1) ^ (t & 7))];
-          ke4 = kes[t];
-        } else {
-          const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
-          k0 = kr[2 * jt];
-          k1 = kr[2 * jt + 1];
-          ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
-        }
-        const unsigned w[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-        #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          S += (long long)qp[2 * u] * (int)(int16_t)(w[u] & 0xFFFF);
-          S += (long long)qp[2 * u + 1] * (int)(int16_t)(w[u] >> 16);
-        }
-        E = s_qe[h * 4 + jt] + (int)(int8_t)(ke4 >> (8 * jt));
+  double lmax[AG_MAXG] = {-INFINITY, -INFINITY, -INFINITY};
+  for (int t0 = 0; t0 < T; t0 += AG_THREADS / 4) {
+    const int t = t0 + (tid >> 2);
+    uint4 k0 = make_uint4(0, 0, 0, 0), k1 = make_uint4(0, 0, 0, 0);
+    unsigned ke4 = 0;
+    if (t < T) {
+      if (t < n0) {
+        k0 = ks[t * 8 + ((2 * jt) ^ (t & 7))];
+        k1 = ks[t * 8 + ((2 * jt + 1) ^ (t & 7))];
+        ke4 = kes[t];
+      } else {
+        const uint4* kr = reinterpret_cast<const uint4*>(kv.km + (kbase + t) * HD);
+        k0 = kr[2 * jt];
+        k1 = kr[2 * jt + 1];
+        ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
       }
+    }
+    #pragma unroll
+    for (int h = 0; h < AG_MAXG; ++h) {
+      if (h >= grp) break;                              // (uniform)
+      const uint4* qp = reinterpret_cast<const uint4*>(s_qm + h * HD + jt * 16);
+      const long long S = al_tile_sum(qp[0], qp[1], k0, k1);
+      const int E = s_qe[h * 4 + jt] + (int)(int8_t)(ke4 >> (8 * jt));
       long long S4[4];
       int E4[4];
       #pragma unroll
@@ -1058,14 +1088,19 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
         const double dot = exact_tile_dot4(S4, E4);
         const double v = pow2_hd ? __dmul_rn(dot, inv_hd) : __ddiv_rn(dot, sqrt_hd);
         sc[h * scs + t] = v;
-        lmax = v > lmax ? v : lmax;
+        lmax[h] = v > lmax[h] ? v : lmax[h];
       }
     }
+  }
+  #pragma unroll
+  for (int h = 0; h < AG_MAXG; ++h) {
+    if (h >= grp) break;
+    double m = lmax[h];
     for (int off = 16; off; off >>= 1) {
-      const double o = __shfl_xor_sync(0xffffffffu, lmax, off);
-      lmax = o > lmax ? o : lmax;
+      const double o = __shfl_xor_sync(0xffffffffu, m, off);
+      m = o > m ? o : m;
     }
-    if (lane == 0) s_red[warp][h] = lmax;
+    if (lane == 0) s_red[warp][h] = m;
   }
   __syncthreads();
   if (tid < grp) {
@@ -1150,39 +1185,6 @@ constexpr int AL_STAGE_BYTES = AL_P * 128 + AL_P * 4;     // the rows, then thei
 constexpr int AL_MIN_CTX = 1024;
 __host__ __device__ inline size_t att_long_smem(int grp, int max_ctx) {
   return (((size_t)grp * att_group_sc_stride(max_ctx) * 8 + 15) & ~size_t(15)) + (size_t)AL_STAGES * AL_STAGE_BYTES;
-}
-
-__device__ __forceinline__ int al_dp2a_lo_ss(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-__device__ __forceinline__ int al_dp2a_hi_ss(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-__device__ __forceinline__ int al_dp2a_lo_su(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-__device__ __forceinline__ int al_dp2a_hi_su(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-// exact sum_k x[k] y[k] over one 16-element tile: x as eight 16-bit pairs
-// (x0: elements 0..7, x1: 8..15), y as two uint4 of int16 split into signed
-// high bytes and unsigned low bytes (y = 256 hi + lo); each 32-bit partial
-// holds at most 16 products of 2^15 x 2^8
-__device__ __forceinline__ long long al_tile_sum(const uint4 x0, const uint4 x1, const uint4 k0, const uint4 k1) {
-  const unsigned h0 = __byte_perm(k0.x, k0.y, 0x7531), h1 = __byte_perm(k0.z, k0.w, 0x7531);
-  const unsigned h2 = __byte_perm(k1.x, k1.y, 0x7531), h3 = __byte_perm(k1.z, k1.w, 0x7531);
-  const unsigned l0 = __byte_perm(k0.x, k0.y, 0x6420), l1 = __byte_perm(k0.z, k0.w, 0x6420);
-  const unsigned l2 = __byte_perm(k1.x, k1.y, 0x6420), l3 = __byte_perm(k1.z, k1.w, 0x6420);
-  int A = 0, B = 0;
-  A = al_dp2a_lo_ss(x0.x, h0, A); A = al_dp2a_hi_ss(x0.y, h0, A);
-  A = al_dp2a_lo_ss(x0.z, h1, A); A = al_dp2a_hi_ss(x0.w, h1, A);
-  A = al_dp2a_lo_ss(x1.x, h2, A); A = al_dp2a_hi_ss(x1.y, h2, A);
-  A = al_dp2a_lo_ss(x1.z, h3, A); A = al_dp2a_hi_ss(x1.w, h3, A);
-  B = al_dp2a_lo_su(x0.x, l0, B); B = al_dp2a_hi_su(x0.y, l0, B);
-  B = al_dp2a_lo_su(x0.z, l1, B); B = al_dp2a_hi_su(x0.w, l1, B);
-  B = al_dp2a_lo_su(x1.x, l2, B); B = al_dp2a_hi_su(x1.y, l2, B);
-  B = al_dp2a_lo_su(x1.z, l3, B); B = al_dp2a_hi_su(x1.w, l3, B);
-  return ((long long)A << 8) + (long long)B;
 }
 
 __global__ void __launch_bounds__(AL_THREADS, 2)
