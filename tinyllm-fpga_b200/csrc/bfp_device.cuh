@@ -487,6 +487,40 @@ __device__ __forceinline__ double np_sum_warp(const double* a, int n, int* s_lo,
   return np_sum_warp_generic(a, n, s_lo, s_len, s_val);
 }
 
+// d = c + a.h0*b.b0 + a.h1*b.b1 (lo) / a.h0*b.b2 + a.h1*b.b3 (hi); a: 2 x s16
+__device__ __forceinline__ int dp2a_lo_ss(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int dp2a_hi_ss(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int dp2a_lo_su(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int dp2a_hi_su(unsigned a, unsigned b, int c) {
+  int d; asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+// Exact sum_k x[k] y[k] over one 16-element tile of int16 values: x as eight 16-bit pairs
+// (x0: elements 0..7, x1: 8..15), y as two uint4 of int16 split into signed
+// high bytes and unsigned low bytes (y = 256 hi + lo); each 32-bit partial
+// holds at most 16 products of 2^15 x 2^8
+__device__ __forceinline__ long long tile_sum16_dp2a(const uint4 x0, const uint4 x1, const uint4 k0, const uint4 k1) {
+  const unsigned h0 = __byte_perm(k0.x, k0.y, 0x7531), h1 = __byte_perm(k0.z, k0.w, 0x7531);
+  const unsigned h2 = __byte_perm(k1.x, k1.y, 0x7531), h3 = __byte_perm(k1.z, k1.w, 0x7531);
+  const unsigned l0 = __byte_perm(k0.x, k0.y, 0x6420), l1 = __byte_perm(k0.z, k0.w, 0x6420);
+  const unsigned l2 = __byte_perm(k1.x, k1.y, 0x6420), l3 = __byte_perm(k1.z, k1.w, 0x6420);
+  int A = 0, B = 0;
+  A = dp2a_lo_ss(x0.x, h0, A); A = dp2a_hi_ss(x0.y, h0, A);
+  A = dp2a_lo_ss(x0.z, h1, A); A = dp2a_hi_ss(x0.w, h1, A);
+  A = dp2a_lo_ss(x1.x, h2, A); A = dp2a_hi_ss(x1.y, h2, A);
+  A = dp2a_lo_ss(x1.z, h3, A); A = dp2a_hi_ss(x1.w, h3, A);
+  B = dp2a_lo_su(x0.x, l0, B); B = dp2a_hi_su(x0.y, l0, B);
+  B = dp2a_lo_su(x0.z, l1, B); B = dp2a_hi_su(x0.w, l1, B);
+  B = dp2a_lo_su(x1.x, l2, B); B = dp2a_hi_su(x1.y, l2, B);
+  B = dp2a_lo_su(x1.z, l3, B); B = dp2a_hi_su(x1.w, l3, B);
+  return ((long long)A << 8) + (long long)B;
+}
+
 // ---------------------------------------------------------------------------
 // Correct rounding of (signed 128-bit integer) * 2^scale to double.
 // ---------------------------------------------------------------------------

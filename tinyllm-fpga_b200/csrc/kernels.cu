@@ -19,20 +19,6 @@ namespace bfp {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// d = c + a.h0*b.b0 + a.h1*b.b1 (lo) / a.h0*b.b2 + a.h1*b.b3 (hi); a: 2 x s16
-__device__ __forceinline__ int dp2a_lo_ss(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-__device__ __forceinline__ int dp2a_hi_ss(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-__device__ __forceinline__ int dp2a_lo_su(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-__device__ __forceinline__ int dp2a_hi_su(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
   return (unsigned)__cvta_generic_to_shared(p);
 }
@@ -881,39 +867,6 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
   }
 }
 
-__device__ __forceinline__ int al_dp2a_lo_ss(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-__device__ __forceinline__ int al_dp2a_hi_ss(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-__device__ __forceinline__ int al_dp2a_lo_su(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-__device__ __forceinline__ int al_dp2a_hi_su(unsigned a, unsigned b, int c) {
-  int d; asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-// exact sum_k x[k] y[k] over one 16-element tile: x as eight 16-bit pairs
-// (x0: elements 0..7, x1: 8..15), y as two uint4 of int16 split into signed
-// high bytes and unsigned low bytes (y = 256 hi + lo); each 32-bit partial
-// holds at most 16 products of 2^15 x 2^8
-__device__ __forceinline__ long long al_tile_sum(const uint4 x0, const uint4 x1, const uint4 k0, const uint4 k1) {
-  const unsigned h0 = __byte_perm(k0.x, k0.y, 0x7531), h1 = __byte_perm(k0.z, k0.w, 0x7531);
-  const unsigned h2 = __byte_perm(k1.x, k1.y, 0x7531), h3 = __byte_perm(k1.z, k1.w, 0x7531);
-  const unsigned l0 = __byte_perm(k0.x, k0.y, 0x6420), l1 = __byte_perm(k0.z, k0.w, 0x6420);
-  const unsigned l2 = __byte_perm(k1.x, k1.y, 0x6420), l3 = __byte_perm(k1.z, k1.w, 0x6420);
-  int A = 0, B = 0;
-  A = al_dp2a_lo_ss(x0.x, h0, A); A = al_dp2a_hi_ss(x0.y, h0, A);
-  A = al_dp2a_lo_ss(x0.z, h1, A); A = al_dp2a_hi_ss(x0.w, h1, A);
-  A = al_dp2a_lo_ss(x1.x, h2, A); A = al_dp2a_hi_ss(x1.y, h2, A);
-  A = al_dp2a_lo_ss(x1.z, h3, A); A = al_dp2a_hi_ss(x1.w, h3, A);
-  B = al_dp2a_lo_su(x0.x, l0, B); B = al_dp2a_hi_su(x0.y, l0, B);
-  B = al_dp2a_lo_su(x0.z, l1, B); B = al_dp2a_hi_su(x0.w, l1, B);
-  B = al_dp2a_lo_su(x1.x, l2, B); B = al_dp2a_hi_su(x1.y, l2, B);
-  B = al_dp2a_lo_su(x1.z, l3, B); B = al_dp2a_hi_su(x1.w, l3, B);
-  return ((long long)A << 8) + (long long)B;
-}
-
 // Batched GQA attention with one CTA per (column, KV head): the grp query
 // heads that share a KV head use one staged copy of its K / V rows, and their
 // grp x 64 sequential accumulations run side by side (a thread per head and
@@ -1075,7 +1028,7 @@ attention_group_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int 
     for (int h = 0; h < AG_MAXG; ++h) {
       if (h >= grp) break;                              // (uniform)
       const uint4* qp = reinterpret_cast<const uint4*>(s_qm + h * HD + jt * 16);
-      const long long S = al_tile_sum(qp[0], qp[1], k0, k1);
+      const long long S = tile_sum16_dp2a(qp[0], qp[1], k0, k1);
       const int E = s_qe[h * 4 + jt] + (int)(int8_t)(ke4 >> (8 * jt));
       long long S4[4];
       int E4[4];
@@ -1289,7 +1242,7 @@ attention_long_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int l
         int E[4];
         #pragma unroll
         for (int jt = 0; jt < 4; ++jt) {
-          S[jt] = al_tile_sum(qv[2 * jt], qv[2 * jt + 1], kk[2 * jt], kk[2 * jt + 1]);
+          S[jt] = tile_sum16_dp2a(qv[2 * jt], qv[2 * jt + 1], kk[2 * jt], kk[2 * jt + 1]);
           E[jt] = qe[jt] + (int)(int8_t)(ke4 >> (8 * jt));
         }
         const double dot = exact_tile_dot4(S, E);

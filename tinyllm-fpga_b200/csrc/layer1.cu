@@ -326,7 +326,7 @@ bfp_attn_block_kernel(L1Args a) {
   unsigned* kes = reinterpret_cast<unsigned*>(smem + L.kes);
   uint4* vs = reinterpret_cast<uint4*>(smem + L.vs);
   unsigned* ves = reinterpret_cast<unsigned*>(smem + L.ves);
-  __shared__ int s_qm[64];
+  __shared__ __align__(16) int16_t s_qm[64];
   __shared__ int s_qe[4];
   __shared__ int s_fail;
 
@@ -539,15 +539,8 @@ bfp_attn_block_kernel(L1Args a) {
       int E[4];
       #pragma unroll
       for (int jt = 0; jt < 4; ++jt) {
-        const unsigned w[8] = {kk[2 * jt].x, kk[2 * jt].y, kk[2 * jt].z, kk[2 * jt].w,
-                               kk[2 * jt + 1].x, kk[2 * jt + 1].y, kk[2 * jt + 1].z, kk[2 * jt + 1].w};
-        long long sacc = 0;
-        #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          sacc += (long long)s_qm[jt * 16 + 2 * u] * (int)(int16_t)(w[u] & 0xFFFF);
-          sacc += (long long)s_qm[jt * 16 + 2 * u + 1] * (int)(int16_t)(w[u] >> 16);
-        }
-        S[jt] = sacc;
+        const uint4* qp = reinterpret_cast<const uint4*>(s_qm) + 2 * jt;   // q of tile jt, 16-bit pairs
+        S[jt] = tile_sum16_dp2a(qp[0], qp[1], kk[2 * jt], kk[2 * jt + 1]);
         E[jt] = s_qe[jt] + (int)(int8_t)(ke4 >> (8 * jt));
       }
       const double dot = exact_tile_dot4(S, E);
