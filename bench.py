@@ -428,7 +428,7 @@ def sharded_head_run(dec, prompts, n_gen, args, world, replica_tok_ms):
 # 176, the mean of three launches of an ncu capture of a serialised forward
 # (dram__bytes_read.sum + dram__bytes_write.sum, writes 0); algorithmic bytes
 # at that position: 1,971,936 (the excess is about the kernel's code).
-ATTN_BLOCK_TRAFFIC_POS176 = 2_067_797
+ATTN_BLOCK_TRAFFIC_POS176 = 2_064_896
 # DRAM bytes of one layer's four batched matvecs at 256 columns (Q/K/V, O,
 # gate/up, down; reads only, the outputs stay in L2) from one ncu capture,
 # times 30 layers
