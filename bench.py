@@ -322,6 +322,16 @@ def run_ours(args, world, rank, local):
         d5.load_image(img)
         cfg5 = {"batch": 64, "pos": 2047, "kernel_ms": d5.profile_forward(64, 2047)}
         d5.close()
+        # attention's HBM rate: the K / V rows 0..2047 of every sequence and
+        # layer (mantissas + tile exponents) per 30 launches, against the
+        # measured copy bandwidth
+        att_ms, att_n = cfg5["kernel_ms"]["attention"]
+        att_bytes = 64 * 2048 * kv_bytes_per_position(BfpConfig())
+        if att_ms > 0:
+            gbs = att_bytes / (att_ms / 1e3) / 1e9
+            cfg5["attention_hbm"] = {"kernel": "attention_long_kernel", "bytes_per_forward": att_bytes,
+                                     "achieved_gbs": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 4),
+                                     "peak_kind": pk_kind}
     del img
     cfg4 = None if (args.no_cfg4 or rank != 0) else cfg4_sweep(args.cfg4_batches, pk)   # per-GPU: rank 0
     res = {
