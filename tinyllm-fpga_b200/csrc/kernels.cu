@@ -656,7 +656,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
                  double sqrt_hd, double inv_hd, int16_t* am, int8_t* ae, const int* pw_off,
                  const unsigned short* pw_data, int early) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ int s_qm[64];
+  __shared__ __align__(16) int16_t s_qm[64];          // q as 16-bit pairs (dp2a tile sums)
   __shared__ int s_qe[4];
   __shared__ double s_red[ATT_THREADS / 32];
   __shared__ double s_bcast;
@@ -752,15 +752,8 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
       int E[4];
       #pragma unroll
       for (int jt = 0; jt < 4; ++jt) {
-        const unsigned w[8] = {kk[2 * jt].x, kk[2 * jt].y, kk[2 * jt].z, kk[2 * jt].w,
-                               kk[2 * jt + 1].x, kk[2 * jt + 1].y, kk[2 * jt + 1].z, kk[2 * jt + 1].w};
-        long long sacc = 0;
-        #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          sacc += (long long)s_qm[jt * 16 + 2 * u] * (int)(int16_t)(w[u] & 0xFFFF);
-          sacc += (long long)s_qm[jt * 16 + 2 * u + 1] * (int)(int16_t)(w[u] >> 16);
-        }
-        S[jt] = sacc;
+        const uint4* qp = reinterpret_cast<const uint4*>(s_qm) + 2 * jt;
+        S[jt] = tile_sum16_dp2a(qp[0], qp[1], kk[2 * jt], kk[2 * jt + 1]);
         E[jt] = s_qe[jt] + (int)(int8_t)(ke4 >> (8 * jt));
       }
       const double dot = exact_tile_dot4(S, E);
@@ -770,7 +763,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
     }
   } else {
     const int jt = tid & 3, qb = lane & ~3;
-    const int* qp = s_qm + jt * 16;
+    const uint4* qp = reinterpret_cast<const uint4*>(s_qm) + 2 * jt;
     for (int t0 = 0; t0 < T; t0 += ATT_THREADS / 4) {
       const int t = t0 + (tid >> 2);
       long long S = 0;
@@ -788,12 +781,7 @@ attention_kernel(const int16_t* qr_m, const int8_t* qr_e, KvArena kv, int layer,
           k1 = kr[2 * jt + 1];
           ke4 = *reinterpret_cast<const unsigned*>(kv.ke + (kbase + t) * 4);
         }
-        const unsigned w[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-        #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          S += (long long)qp[2 * u] * (int)(int16_t)(w[u] & 0xFFFF);
-          S += (long long)qp[2 * u + 1] * (int)(int16_t)(w[u] >> 16);
-        }
+        S = tile_sum16_dp2a(qp[0], qp[1], k0, k1);
         E = s_qe[jt] + (int)(int8_t)(ke4 >> (8 * jt));
       }
       long long S4[4];
