@@ -240,8 +240,10 @@ __device__ __forceinline__ long long ld_peer_s64(const long long* p, unsigned ra
 // allocations are released.
 // Split K: gridDim.z CTAs form a cluster over the K tiles of one output
 // block; each computes the full max exponent, accumulates its own tiles,
-// and cluster rank 0 adds the others' int64 sums through distributed shared
-// memory (integer addition: exact in any order) before the epilogue.
+// and the final phase is shared out by row quarter: rank (q mod ks) adds the
+// other CTAs' int64 sums of rows 32q..32q+31 through distributed shared
+// memory (integer addition: exact in any order) and runs their epilogue, so
+// the clip / quantize / store work of a split runs on up to four SMs.
 constexpr int TC_NB = 4;
 
 template <int NCB, int EW, int MODE>
@@ -480,7 +482,7 @@ tc_matmul_kernel(TcArgs a) {
     if constexpr (MODE == EPI_RESIDUAL) {
       // the residual input, loaded now so its latency hides behind the tiles
       const int R = blk * TC_M + row;
-      if (kr == 0 && R < a.rows) {
+      if (kr == q % ks && R < a.rows) {              // this CTA finalises row quarter q
         #pragma unroll
         for (int j = 0; j < CPT; ++j) {
           const int col = c0 + cb + j;
@@ -562,19 +564,23 @@ tc_matmul_kernel(TcArgs a) {
       for (int j = 0; j < CPT; ++j) red[(cb + j) * TC_M + row] = acc[j];
     }
   }
-  // ---- split K: cluster rank 0 adds the other CTAs' sums (DSMEM); the
-  // second barrier keeps every CTA's shared memory alive until it is read
+  // ---- split K: the rank that finalises a row quarter adds the other CTAs'
+  // sums of those rows (DSMEM); the second barrier keeps every CTA's shared
+  // memory alive until it is read
+  const bool fin = warp >= 2 && kr == (warp & 3) % ks;
   if (ks > 1) {
     cluster_sync_all();
-    if (kr == 0 && warp >= 2) {
+    if (fin) {
       const int q = warp & 3, quarter = (warp - 2) >> 2, row = q * 32 + lane, cb = quarter * CPT;
-      for (int r = 1; r < ks; ++r)
+      for (int r = 0; r < ks; ++r) {
+        if (r == kr) continue;
         #pragma unroll
         for (int j = 0; j < CPT; ++j) acc[j] += ld_peer_s64(red + (cb + j) * TC_M + row, (unsigned)r);
+      }
     }
     cluster_sync_all();
   }
-  if (warp >= 2 && kr == 0) {
+  if (fin) {
     const int q = warp & 3, quarter = (warp - 2) >> 2;
     const int row = q * 32 + lane, R = blk * TC_M + row;
     const int cb = quarter * CPT;
