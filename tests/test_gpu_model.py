@@ -184,6 +184,20 @@ def test_tokens_cfg3_batched(decoder):
     assert decoder.generate(prompts[:3], n_gen) == out[:3]
 
 
+def test_tokens_cfg3_rank_share(decoder):
+    """The first 33 cfg3 sequences in one batch -- one GPU's share of the
+    8-way sequence split: the tuned tensor-core matmuls at 33 columns (K
+    split across a cluster) and the per-head batched attention, each stream
+    against the reference simulator's golden tokens."""
+    from bfp200 import synth
+    prompts, n_gen = synth.config_prompts(3)
+    out = decoder.generate(prompts[:33], n_gen)
+    gold = load_tokens(3)
+    for i in range(33):
+        assert out[i] == gold[i], i
+    assert decoder.uncertified_steps() == 0
+
+
 @pytest.mark.parametrize("ncols", [1, 2, 4])
 def test_decode_kernels_stages(layer_decoder, ncols):
     """Every intermediate tensor of the kernels a decode step runs for 1..4
