@@ -500,15 +500,15 @@ __device__ __forceinline__ int dp2a_lo_su(unsigned a, unsigned b, int c) {
 __device__ __forceinline__ int dp2a_hi_su(unsigned a, unsigned b, int c) {
   int d; asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
 }
-// Exact sum_k x[k] y[k] over one 16-element tile of int16 values: x as eight 16-bit pairs
-// (x0: elements 0..7, x1: 8..15), y as two uint4 of int16 split into signed
-// high bytes and unsigned low bytes (y = 256 hi + lo); each 32-bit partial
-// holds at most 16 products of 2^15 x 2^8
-__device__ __forceinline__ long long tile_sum16_dp2a(const uint4 x0, const uint4 x1, const uint4 k0, const uint4 k1) {
-  const unsigned h0 = __byte_perm(k0.x, k0.y, 0x7531), h1 = __byte_perm(k0.z, k0.w, 0x7531);
-  const unsigned h2 = __byte_perm(k1.x, k1.y, 0x7531), h3 = __byte_perm(k1.z, k1.w, 0x7531);
-  const unsigned l0 = __byte_perm(k0.x, k0.y, 0x6420), l1 = __byte_perm(k0.z, k0.w, 0x6420);
-  const unsigned l2 = __byte_perm(k1.x, k1.y, 0x6420), l3 = __byte_perm(k1.z, k1.w, 0x6420);
+// Exact sum_k x[k] y[k] over one 16-element tile of int16 values, x and y
+// each as two uint4 of eight 16-bit values (elements 0..7, 8..15).  y is
+// split into signed high bytes and unsigned low bytes (y = 256 hi + lo) and
+// each half summed by dp2a in 32 bits (at most 16 products of 2^15 x 2^8).
+__device__ __forceinline__ long long tile_sum16_dp2a(const uint4 x0, const uint4 x1, const uint4 y0, const uint4 y1) {
+  const unsigned h0 = __byte_perm(y0.x, y0.y, 0x7531), h1 = __byte_perm(y0.z, y0.w, 0x7531);
+  const unsigned h2 = __byte_perm(y1.x, y1.y, 0x7531), h3 = __byte_perm(y1.z, y1.w, 0x7531);
+  const unsigned l0 = __byte_perm(y0.x, y0.y, 0x6420), l1 = __byte_perm(y0.z, y0.w, 0x6420);
+  const unsigned l2 = __byte_perm(y1.x, y1.y, 0x6420), l3 = __byte_perm(y1.z, y1.w, 0x6420);
   int A = 0, B = 0;
   A = dp2a_lo_ss(x0.x, h0, A); A = dp2a_hi_ss(x0.y, h0, A);
   A = dp2a_lo_ss(x0.z, h1, A); A = dp2a_hi_ss(x0.w, h1, A);
